@@ -1,0 +1,126 @@
+/*
+ * mlvc_b200.h - C ABI of the B200 (sm_100a) inference backend for mlvc's
+ * FP16 convolution stack.
+ *
+ * The backend executes the reference's AOT graph parts (graph schema 3:
+ * aot/<part>/graph.pb + weights.bin, proto/mlvc_model.proto:30-83) on one
+ * GPU.  Each entry point replaces one member of the reference backend
+ * contract in runtime/include/mlvc/runtime/backend.hpp; the mapping is given
+ * beside every declaration.  All functions return 0 on success and -1 on
+ * failure; mlvc_b200_last_error() then returns the message of the exception
+ * the C++ layer raised (the reference C ABI's convention,
+ * codec/src/c_api.cpp:60-88).  Calls on one backend must come from one host
+ * thread at a time (backend.hpp: one instance per session, one stream).
+ *
+ * Host tensors are NCHW, FP16 as raw IEEE binary16 bits (dtype 0) or INT32
+ * (dtype 1), exactly as mlvc::Tensor (core/include/mlvc/core/tensor.hpp).
+ */
+#ifndef MLVC_B200_H
+#define MLVC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLVC_B200_ABI_VERSION 1
+
+typedef struct mlvc_b200_backend mlvc_b200_backend;
+
+typedef struct mlvc_b200_tensor {
+    int32_t dtype;     /* 0 = FP16, 1 = INT32 */
+    int32_t rank;      /* 0..4 */
+    int64_t shape[4];  /* NCHW */
+    void* data;        /* host memory */
+    size_t bytes;      /* capacity (outputs) / size (inputs) */
+} mlvc_b200_tensor;
+
+/* mlvc::StateTensorBinding (backend.hpp:34-40): graph output `output_index`
+ * feeds graph input `input_index` of the next run and stays on the device. */
+typedef struct mlvc_b200_state_binding {
+    size_t input_index;
+    size_t output_index;
+} mlvc_b200_state_binding;
+
+int mlvc_b200_abi_version(void);
+
+/* Thread-local message of the last failing call ("" if none). */
+const char* mlvc_b200_last_error(void);
+
+/* Backend factory: replaces the "driver-cubin" factory registered through
+ * register_backend() (backends/driver_cubin/src/backend.cpp:129-137) with
+ * BackendOptions::device_id (backend.hpp:24-32). */
+int mlvc_b200_create(int device_id, mlvc_b200_backend** out);
+void mlvc_b200_destroy(mlvc_b200_backend* backend);
+
+/* Planning-only instance (no reference counterpart): no GPU is touched;
+ * load / load_memory decode, validate and plan the graph for a device with
+ * `sm_count` SMs and `smem_optin_bytes` of shared memory per block, and the
+ * step_* queries report the chosen kernels.  Execution calls fail. */
+int mlvc_b200_create_offline(int sm_count, int smem_optin_bytes, mlvc_b200_backend** out);
+
+/* InferenceBackend::name() (backend.hpp:52). Returns "b200". */
+const char* mlvc_b200_name(const mlvc_b200_backend* backend);
+
+/* InferenceBackend::load(model_name, ModelExecutionConfig) (backend.hpp:55-56),
+ * reading <model_dir>/aot/<model_name>/{graph.pb,weights.bin} like
+ * load_aot_graph (runtime/src/aot_graph.cpp:291-317). */
+int mlvc_b200_load(mlvc_b200_backend* backend, const char* model_dir, const char* model_name,
+                   const mlvc_b200_state_binding* bindings, size_t binding_count);
+
+/* Same as mlvc_b200_load with the two assets in memory (the reference's
+ * ModelAssetReader indirection, core/include/mlvc/core/assets.hpp:16-24). */
+int mlvc_b200_load_memory(mlvc_b200_backend* backend, const void* graph_pb, size_t graph_bytes,
+                          const void* weights, size_t weights_bytes, const mlvc_b200_state_binding* bindings,
+                          size_t binding_count);
+
+/* Host-visible graph inputs / outputs (state-bound tensors removed, graph
+ * order kept; backend.hpp:58-60).  `info->data` is left NULL; `name` points to
+ * storage owned by the backend. */
+size_t mlvc_b200_input_count(const mlvc_b200_backend* backend);
+size_t mlvc_b200_output_count(const mlvc_b200_backend* backend);
+int mlvc_b200_input_info(const mlvc_b200_backend* backend, size_t index, mlvc_b200_tensor* info, const char** name);
+int mlvc_b200_output_info(const mlvc_b200_backend* backend, size_t index, mlvc_b200_tensor* info,
+                          const char** name);
+
+/* InferenceBackend::run(inputs) -> outputs (backend.hpp:58-60): synchronous.
+ * `outputs[i].data` must hold output_info(i).bytes. */
+int mlvc_b200_run(mlvc_b200_backend* backend, const mlvc_b200_tensor* inputs, size_t input_count,
+                  mlvc_b200_tensor* outputs, size_t output_count);
+
+/* InferenceBackend::reset_state() (backend.hpp:62): zero every bound state. */
+int mlvc_b200_reset_state(mlvc_b200_backend* backend);
+
+/* BufferedCodecBackend slot path (backend.hpp:79-96), tensor form:
+ * configure_codec_io(slots) / codec_slot_count / decoder_inputs(slot) /
+ * submit_decoder(slot) / wait_codec_slot(slot).  Slot buffers are pinned host
+ * memory owned by the backend, valid until the slot is resubmitted; a slot
+ * must be waited before its buffers are reused (cuda_graph_executor.cpp:243-290). */
+int mlvc_b200_configure_slots(mlvc_b200_backend* backend, size_t slot_count);
+size_t mlvc_b200_slot_count(const mlvc_b200_backend* backend);
+void* mlvc_b200_slot_input(mlvc_b200_backend* backend, size_t slot, size_t input_index);
+const void* mlvc_b200_slot_output(const mlvc_b200_backend* backend, size_t slot, size_t output_index);
+int mlvc_b200_submit(mlvc_b200_backend* backend, size_t slot);
+int mlvc_b200_wait_slot(mlvc_b200_backend* backend, size_t slot);
+
+/* Measurement hooks (no reference counterpart; the reference times whole
+ * runs with steady_clock, codec/src/pipeline.cpp:341-415).  enqueue replays
+ * the captured schedule on the backend's stream with the device-resident
+ * inputs of the previous run; time_steps launches every step separately
+ * between CUDA events and returns the mean milliseconds per step. */
+int mlvc_b200_enqueue(mlvc_b200_backend* backend);
+int mlvc_b200_synchronize(mlvc_b200_backend* backend);
+void* mlvc_b200_stream(const mlvc_b200_backend* backend);
+size_t mlvc_b200_step_count(const mlvc_b200_backend* backend);
+int mlvc_b200_step_info(const mlvc_b200_backend* backend, size_t index, const char** kernel, const char** nodes,
+                        double* flops, double* bytes, uint32_t* grid, uint32_t* block, uint32_t* smem);
+int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, float* ms_per_step);
+int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend);
+size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MLVC_B200_H */

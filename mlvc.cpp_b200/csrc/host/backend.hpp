@@ -1,0 +1,134 @@
+// The B200 inference backend: one loaded graph part on one device.
+//
+// Host-side mirror of the reference contracts it replaces:
+//   * InferenceBackend::load / run / reset_state
+//     (runtime/include/mlvc/runtime/backend.hpp:48-63)
+//   * the fixed-shape buffered slot path of BufferedCodecBackend
+//     (runtime/include/mlvc/runtime/backend.hpp:79-96), here with tensor slots
+//     (pinned host inputs/outputs per slot, submit / wait)
+//   * AotGraph's load -> plan -> capture -> replay life cycle
+//     (backends/driver_cubin/src/model_loader.cpp:11-63,
+//      cuda_graph_executor.cpp:31-412).
+#pragma once
+
+#include "driver.hpp"
+#include "graph.hpp"
+
+#include <cuda.h>
+
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace mlvc_b200 {
+
+struct HostTensorRef {
+    int dtype;  // 0 = FP16 (uint16 bits), 1 = INT32
+    int rank;
+    int64_t shape[4];
+    void* data;
+    size_t bytes;
+};
+
+struct StateBinding {
+    size_t input_index;
+    size_t output_index;
+};
+
+struct StepInfo {
+    std::string kernel;
+    std::string nodes;   // graph node indices covered by the step
+    uint32_t grid = 0, block = 0, smem = 0;
+    double flops = 0.0;  // algorithmic work
+    double bytes = 0.0;  // algorithmic HBM bytes (one read of each input, one write of each output)
+};
+
+class Backend {
+public:
+    explicit Backend(int device_id);
+    // Planning-only instance: no device is touched; load_bytes() decodes,
+    // validates and plans the graph (kernel choice, fusion, weight preparation)
+    // for a machine with `sm_count` SMs and `smem_optin` bytes of shared memory
+    // per block, so the host logic can be tested without a GPU.
+    Backend(int sm_count, int smem_optin, bool /*offline*/);
+    ~Backend();
+    Backend(const Backend&) = delete;
+    Backend& operator=(const Backend&) = delete;
+
+    void load(const std::string& model_dir, const std::string& part, const std::vector<StateBinding>& bindings);
+    void load_bytes(const uint8_t* graph, size_t graph_size, const uint8_t* weights, size_t weights_size,
+                    const std::vector<StateBinding>& bindings);
+
+    size_t input_count() const { return ext_inputs_.size(); }
+    size_t output_count() const { return ext_outputs_.size(); }
+    const TensorDesc& input_desc(size_t i) const;
+    const TensorDesc& output_desc(size_t i) const;
+
+    void run(const HostTensorRef* inputs, size_t n_in, HostTensorRef* outputs, size_t n_out);
+    void reset_state();
+
+    // Slot path: pinned host staging per slot, asynchronous submit, wait.
+    void configure_slots(size_t count);
+    size_t slot_count() const;
+    void* slot_input(size_t slot, size_t i);
+    const void* slot_output(size_t slot, size_t i) const;
+    void submit(size_t slot);
+    void wait_slot(size_t slot);
+
+    // Device-resident replay of the whole schedule (no host copies) for
+    // timing; optional per-step event timing.
+    void enqueue();
+    void synchronize();
+    std::vector<float> time_steps(int iterations);
+    const std::vector<StepInfo>& steps() const { return step_info_; }
+    int kernel_launches_per_run() const;
+    CUstream stream() const { return stream_; }
+    CUcontext context() const { return ctx_; }
+    size_t device_bytes() const;
+
+private:
+    struct Value;
+    struct Step;
+    struct Slot;
+
+    void plan();
+    void build_schedule();
+    void capture();
+    void check_status();
+    void launch_steps(CUstream s);
+    CUfunction fn(const char* name);
+
+    int device_ = 0;
+    CUdevice dev_ = 0;
+    CUcontext ctx_ = nullptr;
+    CUstream stream_ = nullptr;
+    CUmodule module_ = nullptr;
+    CUdeviceptr status_ptr_ = 0;
+    int sm_count_ = 148;
+    int max_smem_optin_ = 227 * 1024;
+
+    GraphDesc graph_;
+    std::vector<uint8_t> weights_host_;
+    std::vector<StateBinding> bindings_;
+    std::vector<size_t> ext_inputs_;   // indices into graph_.inputs
+    std::vector<size_t> ext_outputs_;  // indices into graph_.outputs
+
+    std::vector<Value> values_;
+    std::vector<Step> steps_;
+    std::vector<StepInfo> step_info_;
+    std::vector<Slot> slots_;
+
+    DeviceBuffer weights_dev_, prepped_dev_, arena_dev_;
+    std::vector<DeviceBuffer> input_dev_, input_stage_dev_, output_stage_dev_, state_dev_;
+    std::vector<uint8_t> prepped_host_;
+
+    CUgraph graph_handle_ = nullptr;
+    CUgraphExec graph_exec_ = nullptr;
+    bool state_ready_ = false;
+    bool loaded_ = false;
+    bool offline_ = false;
+};
+
+}  // namespace mlvc_b200

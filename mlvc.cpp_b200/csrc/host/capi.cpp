@@ -1,0 +1,272 @@
+// extern "C" layer over mlvc_b200::Backend (declarations and the reference
+// interface each entry replaces: include/mlvc_b200.h).  Exceptions never
+// cross the boundary: they become -1 plus a thread-local message.
+#include "../../../include/mlvc_b200.h"
+
+#include "backend.hpp"
+
+#include <exception>
+#include <memory>
+#include <string>
+#include <vector>
+
+struct mlvc_b200_backend {
+    std::unique_ptr<mlvc_b200::Backend> impl;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <typename F>
+int guarded(F&& f)
+{
+    try {
+        f();
+        g_last_error.clear();
+        return 0;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+    } catch (...) {
+        g_last_error = "mlvc-b200: unknown error";
+    }
+    return -1;
+}
+
+std::vector<mlvc_b200::StateBinding> to_bindings(const mlvc_b200_state_binding* b, size_t n)
+{
+    std::vector<mlvc_b200::StateBinding> out;
+    for (size_t i = 0; i < n; ++i)
+        out.push_back({b[i].input_index, b[i].output_index});
+    return out;
+}
+
+void describe(const mlvc_b200::TensorDesc& d, mlvc_b200_tensor* info)
+{
+    info->dtype = d.dtype == mlvc_b200::DType::kInt32 ? 1 : 0;
+    info->rank = static_cast<int32_t>(d.shape.size());
+    for (int i = 0; i < 4; ++i)
+        info->shape[i] = i < info->rank ? d.shape[i] : 1;
+    info->data = nullptr;
+    info->bytes = static_cast<size_t>(mlvc_b200::element_count(d.shape)) * mlvc_b200::dtype_size(d.dtype);
+}
+
+mlvc_b200::Backend& require(const mlvc_b200_backend* b)
+{
+    if (!b || !b->impl)
+        throw std::runtime_error("mlvc-b200: null backend handle");
+    return *b->impl;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mlvc_b200_abi_version(void) { return MLVC_B200_ABI_VERSION; }
+
+const char* mlvc_b200_last_error(void) { return g_last_error.c_str(); }
+
+int mlvc_b200_create(int device_id, mlvc_b200_backend** out)
+{
+    return guarded([&] {
+        if (!out)
+            throw std::runtime_error("mlvc-b200: null output handle");
+        auto h = std::make_unique<mlvc_b200_backend>();
+        h->impl = std::make_unique<mlvc_b200::Backend>(device_id);
+        *out = h.release();
+    });
+}
+
+int mlvc_b200_create_offline(int sm_count, int smem_optin_bytes, mlvc_b200_backend** out)
+{
+    return guarded([&] {
+        if (!out || sm_count <= 0 || smem_optin_bytes <= 0)
+            throw std::runtime_error("mlvc-b200: invalid planning target");
+        auto h = std::make_unique<mlvc_b200_backend>();
+        h->impl = std::make_unique<mlvc_b200::Backend>(sm_count, smem_optin_bytes, true);
+        *out = h.release();
+    });
+}
+
+void mlvc_b200_destroy(mlvc_b200_backend* backend) { delete backend; }
+
+const char* mlvc_b200_name(const mlvc_b200_backend*) { return "b200"; }
+
+int mlvc_b200_load(mlvc_b200_backend* backend, const char* model_dir, const char* model_name,
+                   const mlvc_b200_state_binding* bindings, size_t binding_count)
+{
+    return guarded([&] {
+        if (!model_dir || !model_name)
+            throw std::runtime_error("mlvc-b200: null model path");
+        require(backend).load(model_dir, model_name, to_bindings(bindings, binding_count));
+    });
+}
+
+int mlvc_b200_load_memory(mlvc_b200_backend* backend, const void* graph_pb, size_t graph_bytes, const void* weights,
+                          size_t weights_bytes, const mlvc_b200_state_binding* bindings, size_t binding_count)
+{
+    return guarded([&] {
+        require(backend).load_bytes(static_cast<const uint8_t*>(graph_pb), graph_bytes,
+                                    static_cast<const uint8_t*>(weights), weights_bytes,
+                                    to_bindings(bindings, binding_count));
+    });
+}
+
+size_t mlvc_b200_input_count(const mlvc_b200_backend* backend)
+{
+    return backend && backend->impl ? backend->impl->input_count() : 0;
+}
+
+size_t mlvc_b200_output_count(const mlvc_b200_backend* backend)
+{
+    return backend && backend->impl ? backend->impl->output_count() : 0;
+}
+
+int mlvc_b200_input_info(const mlvc_b200_backend* backend, size_t index, mlvc_b200_tensor* info, const char** name)
+{
+    return guarded([&] {
+        const auto& d = require(backend).input_desc(index);
+        if (info)
+            describe(d, info);
+        if (name)
+            *name = d.name.c_str();
+    });
+}
+
+int mlvc_b200_output_info(const mlvc_b200_backend* backend, size_t index, mlvc_b200_tensor* info, const char** name)
+{
+    return guarded([&] {
+        const auto& d = require(backend).output_desc(index);
+        if (info)
+            describe(d, info);
+        if (name)
+            *name = d.name.c_str();
+    });
+}
+
+int mlvc_b200_run(mlvc_b200_backend* backend, const mlvc_b200_tensor* inputs, size_t input_count,
+                  mlvc_b200_tensor* outputs, size_t output_count)
+{
+    return guarded([&] {
+        std::vector<mlvc_b200::HostTensorRef> in(input_count), out(output_count);
+        for (size_t i = 0; i < input_count; ++i) {
+            const auto& t = inputs[i];
+            in[i] = {t.dtype, t.rank, {t.shape[0], t.shape[1], t.shape[2], t.shape[3]}, t.data, t.bytes};
+        }
+        for (size_t i = 0; i < output_count; ++i) {
+            const auto& t = outputs[i];
+            out[i] = {t.dtype, t.rank, {t.shape[0], t.shape[1], t.shape[2], t.shape[3]}, t.data, t.bytes};
+        }
+        require(backend).run(in.data(), in.size(), out.data(), out.size());
+        for (size_t i = 0; i < output_count; ++i) {
+            auto& t = outputs[i];
+            t.dtype = out[i].dtype;
+            t.rank = out[i].rank;
+            for (int r = 0; r < 4; ++r)
+                t.shape[r] = r < t.rank ? out[i].shape[r] : 1;
+            t.bytes = out[i].bytes;
+        }
+    });
+}
+
+int mlvc_b200_reset_state(mlvc_b200_backend* backend)
+{
+    return guarded([&] { require(backend).reset_state(); });
+}
+
+int mlvc_b200_configure_slots(mlvc_b200_backend* backend, size_t slot_count)
+{
+    return guarded([&] { require(backend).configure_slots(slot_count); });
+}
+
+size_t mlvc_b200_slot_count(const mlvc_b200_backend* backend)
+{
+    return backend && backend->impl ? backend->impl->slot_count() : 0;
+}
+
+void* mlvc_b200_slot_input(mlvc_b200_backend* backend, size_t slot, size_t input_index)
+{
+    void* p = nullptr;
+    guarded([&] { p = require(backend).slot_input(slot, input_index); });
+    return p;
+}
+
+const void* mlvc_b200_slot_output(const mlvc_b200_backend* backend, size_t slot, size_t output_index)
+{
+    const void* p = nullptr;
+    guarded([&] { p = require(backend).slot_output(slot, output_index); });
+    return p;
+}
+
+int mlvc_b200_submit(mlvc_b200_backend* backend, size_t slot)
+{
+    return guarded([&] { require(backend).submit(slot); });
+}
+
+int mlvc_b200_wait_slot(mlvc_b200_backend* backend, size_t slot)
+{
+    return guarded([&] { require(backend).wait_slot(slot); });
+}
+
+int mlvc_b200_enqueue(mlvc_b200_backend* backend)
+{
+    return guarded([&] { require(backend).enqueue(); });
+}
+
+int mlvc_b200_synchronize(mlvc_b200_backend* backend)
+{
+    return guarded([&] { require(backend).synchronize(); });
+}
+
+void* mlvc_b200_stream(const mlvc_b200_backend* backend)
+{
+    return backend && backend->impl ? static_cast<void*>(backend->impl->stream()) : nullptr;
+}
+
+size_t mlvc_b200_step_count(const mlvc_b200_backend* backend)
+{
+    return backend && backend->impl ? backend->impl->steps().size() : 0;
+}
+
+int mlvc_b200_step_info(const mlvc_b200_backend* backend, size_t index, const char** kernel, const char** nodes,
+                        double* flops, double* bytes, uint32_t* grid, uint32_t* block, uint32_t* smem)
+{
+    return guarded([&] {
+        const auto& s = require(backend).steps().at(index);
+        if (kernel)
+            *kernel = s.kernel.c_str();
+        if (nodes)
+            *nodes = s.nodes.c_str();
+        if (flops)
+            *flops = s.flops;
+        if (bytes)
+            *bytes = s.bytes;
+        if (grid)
+            *grid = s.grid;
+        if (block)
+            *block = s.block;
+        if (smem)
+            *smem = s.smem;
+    });
+}
+
+int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, float* ms_per_step)
+{
+    return guarded([&] {
+        const auto t = require(backend).time_steps(iterations);
+        for (size_t i = 0; i < t.size(); ++i)
+            ms_per_step[i] = t[i];
+    });
+}
+
+int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend)
+{
+    return backend && backend->impl ? backend->impl->kernel_launches_per_run() : -1;
+}
+
+size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend)
+{
+    return backend && backend->impl ? backend->impl->device_bytes() : 0;
+}
+
+}  // extern "C"

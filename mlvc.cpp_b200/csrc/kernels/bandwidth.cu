@@ -1,0 +1,327 @@
+// Bandwidth-bound kernels on channels-last FP16 tensors: elementwise unary and
+// broadcast binary operators, strided copies (slice / concat / layout
+// conversion), gather, pixel (un)shuffle, stand-alone ReGLU, depthwise and
+// generic grouped direct convolution.
+//
+// Arithmetic and rounding points follow the reference operators one for one:
+// unary/binary  backends/driver_cubin/kernels/elementwise.cu:1-79,
+// ReGLU         backends/driver_cubin/kernels/activation.cu:1-7,
+// gather        backends/driver_cubin/kernels/tensor_ops.cu:1-14,
+// pixel shuffle backends/driver_cubin/kernels/tensor_ops.cu:62-116 (CRD order),
+// depthwise     backends/driver_cubin/kernels/depthwise_conv.cu:1-173 (FP32
+//               FMA accumulation from the bias, one FP16 rounding).
+// The grids are sized as a multiple of the SM count by the host, and each
+// thread walks a grid-stride loop; contiguous paths move 16 bytes per access.
+#include "sm100.cuh"
+
+namespace mlvc_b200 {
+
+__device__ __forceinline__ float unary_op(float x, int op, float alpha, float lo, float hi)
+{
+    switch (op) {
+    case 0: return x >= 0.0f ? x : alpha * x;
+    case 1: return fminf(fmaxf(x, lo), hi);
+    case 2: return 1.0f / (1.0f + expf(-x));
+    case 3: return 1.0f / x;
+    default: return nearbyintf(x);
+    }
+}
+
+__device__ __forceinline__ float binary_op(float a, float b, int op)
+{
+    return op == 0 ? a + b : (op == 1 ? a * b : a - b);
+}
+
+// ------------------------------------------------------------- unary
+extern "C" __global__ void mlvc_unary_f16(const __grid_constant__ ElementwiseParams p)
+{
+    const long long vecs = p.count / 8;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < vecs; i += stride) {
+        uint4 v = reinterpret_cast<const uint4*>(p.a)[i];
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float x0, x1;
+            unpack_h2(w[k], x0, x1);
+            w[k] = pack_h2(unary_op(x0, p.op, p.alpha, p.lo, p.hi), unary_op(x1, p.op, p.alpha, p.lo, p.hi));
+        }
+        reinterpret_cast<uint4*>(p.out)[i] = v;
+    }
+    for (long long i = vecs * 8 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count;
+         i += stride)
+        p.out[i] = __float2half_rn(unary_op(__half2float(p.a[i]), p.op, p.alpha, p.lo, p.hi));
+}
+
+// ------------------------------------------------------------ binary
+// Same-shape operands: 16-byte vectors.
+extern "C" __global__ void mlvc_binary_same_f16(const __grid_constant__ ElementwiseParams p)
+{
+    const long long vecs = p.count / 8;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < vecs; i += stride) {
+        uint4 va = reinterpret_cast<const uint4*>(p.a)[i];
+        const uint4 vb = reinterpret_cast<const uint4*>(p.b)[i];
+        uint32_t* wa = reinterpret_cast<uint32_t*>(&va);
+        const uint32_t* wb = reinterpret_cast<const uint32_t*>(&vb);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float a0, a1, b0, b1;
+            unpack_h2(wa[k], a0, a1);
+            unpack_h2(wb[k], b0, b1);
+            wa[k] = pack_h2(binary_op(a0, b0, p.op), binary_op(a1, b1, p.op));
+        }
+        reinterpret_cast<uint4*>(p.out)[i] = va;
+    }
+    for (long long i = vecs * 8 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count;
+         i += stride)
+        p.out[i] = __float2half_rn(binary_op(__half2float(p.a[i]), __half2float(p.b[i]), p.op));
+}
+
+// General broadcast: output is dense in (n, h, w, c) order, operands are
+// addressed through per-dimension strides (0 on broadcast dimensions).
+extern "C" __global__ void mlvc_binary_bcast_f16(const __grid_constant__ ElementwiseParams p)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
+        long long r = i;
+        const long long c = r % p.dims[3];
+        r /= p.dims[3];
+        const long long w = r % p.dims[2];
+        r /= p.dims[2];
+        const long long h = r % p.dims[1];
+        const long long n = r / p.dims[1];
+        const float a = __half2float(p.a[n * p.sa[0] + h * p.sa[1] + w * p.sa[2] + c * p.sa[3]]);
+        const float b = __half2float(p.b[n * p.sb[0] + h * p.sb[1] + w * p.sb[2] + c * p.sb[3]]);
+        p.out[i] = __float2half_rn(binary_op(a, b, p.op));
+    }
+}
+
+// -------------------------------------------------------------- copies
+extern "C" __global__ void mlvc_strided_copy_f16(const __grid_constant__ CopyParams p)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
+        long long r = i;
+        const long long i3 = r % p.dims[3];
+        r /= p.dims[3];
+        const long long i2 = r % p.dims[2];
+        r /= p.dims[2];
+        const long long i1 = r % p.dims[1];
+        const long long i0 = r / p.dims[1];
+        p.dst[i0 * p.ds[0] + i1 * p.ds[1] + i2 * p.ds[2] + i3 * p.ds[3]] =
+            p.src[i0 * p.ss[0] + i1 * p.ss[1] + i2 * p.ss[2] + i3 * p.ss[3]];
+    }
+}
+
+// Same as above, moving 8 consecutive elements (16 bytes) per step; used when
+// the innermost extent is a multiple of 8 and contiguous on both sides.
+extern "C" __global__ void mlvc_strided_copy_v8_f16(const __grid_constant__ CopyParams p)
+{
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    const long long inner = p.dims[3] / 8;
+    const long long total = p.count / 8;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+        long long r = i;
+        const long long i3 = (r % inner) * 8;
+        r /= inner;
+        const long long i2 = r % p.dims[2];
+        r /= p.dims[2];
+        const long long i1 = r % p.dims[1];
+        const long long i0 = r / p.dims[1];
+        *reinterpret_cast<uint4*>(p.dst + i0 * p.ds[0] + i1 * p.ds[1] + i2 * p.ds[2] + i3) =
+            *reinterpret_cast<const uint4*>(p.src + i0 * p.ss[0] + i1 * p.ss[1] + i2 * p.ss[2] + i3);
+    }
+}
+
+// NCHW (plane-major) <-> NHWC transpose of one [C, HW] matrix per image
+// through a 32x33 shared tile, both sides coalesced.
+extern "C" __global__ void mlvc_transpose_f16(const __grid_constant__ CopyParams p)
+{
+    // dims: [images, rows, cols]; src is [rows][cols], dst is [cols][rows]
+    __shared__ mlvc_half tile[32][33];
+    const int rows = p.dims[1], cols = p.dims[2];
+    const long long img = blockIdx.z;
+    const mlvc_half* src = p.src + img * p.ss[0];
+    mlvc_half* dst = p.dst + img * p.ds[0];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
+        const int r = r0 + dy, c = c0 + threadIdx.x;
+        if (r < rows && c < cols)
+            tile[dy][threadIdx.x] = src[static_cast<long long>(r) * cols + c];
+    }
+    __syncthreads();
+    for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
+        const int c = c0 + dy, r = r0 + threadIdx.x;
+        if (r < rows && c < cols)
+            dst[static_cast<long long>(c) * rows + r] = tile[threadIdx.x][dy];
+    }
+}
+
+extern "C" __global__ void mlvc_gather_rows_f16(const __grid_constant__ GatherParams p)
+{
+    int row = p.index[0];
+    if (row < 0)
+        row += p.rows;
+    if (row < 0 || row >= p.rows)
+        return;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.row_elems; i += stride)
+        p.dst[i] = p.src[row * p.row_elems + i];
+}
+
+// --------------------------------------------------------- pixel ops
+// DepthToSpace (CRD, PyTorch pixel_shuffle) on NHWC: output pixel (y, x)
+// channel c reads input pixel (y / r, x / r) channel c*r*r + (y%r)*r + x%r.
+extern "C" __global__ void mlvc_depth_to_space_f16(const __grid_constant__ PixelShuffleParams p)
+{
+    const int r = p.r, oc = p.c / (r * r), ow = p.w * r, oh = p.h * r;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
+        long long t = i;
+        const int c = static_cast<int>(t % oc);
+        t /= oc;
+        const int x = static_cast<int>(t % ow);
+        t /= ow;
+        const int y = static_cast<int>(t % oh);
+        const long long n = t / oh;
+        const int ic = c * r * r + (y % r) * r + (x % r);
+        p.dst[i] = p.src[((n * p.h + y / r) * p.w + x / r) * p.c + ic];
+    }
+}
+
+// SpaceToDepth (PyTorch pixel_unshuffle) on NHWC: output channel
+// c*r*r + dy*r + dx of pixel (y, x) reads input pixel (y*r+dy, x*r+dx) channel c.
+extern "C" __global__ void mlvc_space_to_depth_f16(const __grid_constant__ PixelShuffleParams p)
+{
+    const int r = p.r, oh = p.h / r, ow = p.w / r, oc = p.c * r * r;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
+        long long t = i;
+        const int c = static_cast<int>(t % oc);
+        t /= oc;
+        const int x = static_cast<int>(t % ow);
+        t /= ow;
+        const int y = static_cast<int>(t % oh);
+        const long long n = t / oh;
+        const int ic = c / (r * r), off = c % (r * r);
+        p.dst[i] = p.src[((n * p.h + y * r + off / r) * p.w + x * r + off % r) * p.c + ic];
+    }
+}
+
+// ------------------------------------------------------------- ReGLU
+extern "C" __global__ void mlvc_reglu_f16(const __grid_constant__ RegluParams p)
+{
+    const long long total = p.pixels * p.c;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+        const long long px = i / p.c;
+        const int c = static_cast<int>(i % p.c);
+        const float g = __half2float(p.src[px * 2 * p.c + c]);
+        const float l = __half2float(p.src[px * 2 * p.c + p.c + c]);
+        const float cg = round_h(fminf(fmaxf(g, p.lo), p.hi));
+        p.dst[i] = __float2half_rn(cg * l);
+    }
+}
+
+// --------------------------------------------------------- depthwise
+// One thread produces 8 consecutive channels of one output pixel (16-byte
+// loads of input and weights); weights are [kh*kw][C].  Requires C % 8 == 0.
+extern "C" __global__ void mlvc_depthwise_v8_f16(const __grid_constant__ DirectConvParams p)
+{
+    const int cv = p.oc / 8;
+    const long long total = static_cast<long long>(p.n) * p.oh * p.ow * cv;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+        long long t = i;
+        const int c8 = static_cast<int>(t % cv) * 8;
+        t /= cv;
+        const int ox = static_cast<int>(t % p.ow);
+        t /= p.ow;
+        const int oy = static_cast<int>(t % p.oh);
+        const long long n = t / p.oh;
+        float acc[8];
+        if (p.bias) {
+            const uint4 bv = *reinterpret_cast<const uint4*>(p.bias + c8);
+            const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                unpack_h2(bw[k], acc[2 * k], acc[2 * k + 1]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                acc[k] = 0.0f;
+        }
+        for (int ky = 0; ky < p.kh; ++ky) {
+            const int iy = oy * p.sh + ky - p.ph;
+            if (iy < 0 || iy >= p.ih)
+                continue;
+            for (int kx = 0; kx < p.kw; ++kx) {
+                const int ix = ox * p.sw + kx - p.pw;
+                if (ix < 0 || ix >= p.iw)
+                    continue;
+                const uint4 xv = *reinterpret_cast<const uint4*>(p.x + ((n * p.ih + iy) * p.iw + ix) * p.ic + c8);
+                const uint4 wv = *reinterpret_cast<const uint4*>(p.w + (ky * p.kw + kx) * p.oc + c8);
+                const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv);
+                const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float x0, x1, w0, w1;
+                    unpack_h2(xw[k], x0, x1);
+                    unpack_h2(ww[k], w0, w1);
+                    acc[2 * k] = fmaf(x0, w0, acc[2 * k]);
+                    acc[2 * k + 1] = fmaf(x1, w1, acc[2 * k + 1]);
+                }
+            }
+        }
+        uint4 ov;
+        uint32_t* o = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            o[k] = pack_h2(acc[2 * k], acc[2 * k + 1]);
+        *reinterpret_cast<uint4*>(p.y + i * 8) = ov;
+    }
+}
+
+// Generic grouped direct convolution (fallback for shapes the tensor-core
+// kernels do not cover).  Weights are [OC][kh][kw][ICg]; optional fused
+// LeakyReLU / residual with the graph's double rounding.
+extern "C" __global__ void mlvc_conv_direct_f16(const __grid_constant__ DirectConvParams p)
+{
+    const long long total = static_cast<long long>(p.n) * p.oh * p.ow * p.oc;
+    const int icg = p.ic / p.groups, ocg = p.oc / p.groups;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+        long long t = i;
+        const int o = static_cast<int>(t % p.oc);
+        t /= p.oc;
+        const int ox = static_cast<int>(t % p.ow);
+        t /= p.ow;
+        const int oy = static_cast<int>(t % p.oh);
+        const long long n = t / p.oh;
+        const int g = o / ocg;
+        float acc = p.bias ? __half2float(p.bias[o]) : 0.0f;
+        for (int ky = 0; ky < p.kh; ++ky) {
+            const int iy = oy * p.sh + ky - p.ph;
+            if (iy < 0 || iy >= p.ih)
+                continue;
+            for (int kx = 0; kx < p.kw; ++kx) {
+                const int ix = ox * p.sw + kx - p.pw;
+                if (ix < 0 || ix >= p.iw)
+                    continue;
+                const mlvc_half* xr = p.x + ((n * p.ih + iy) * p.iw + ix) * p.ic + g * icg;
+                const mlvc_half* wr = p.w + ((static_cast<long long>(o) * p.kh + ky) * p.kw + kx) * icg;
+                for (int c = 0; c < icg; ++c)
+                    acc = fmaf(__half2float(xr[c]), __half2float(wr[c]), acc);
+            }
+        }
+        float v = round_h(acc);
+        if (p.epilogue == kEpiLeaky)
+            v = v < 0.0f ? round_h(v * p.alpha) : v;
+        else if (p.epilogue == kEpiResidual)
+            v = v + __half2float(p.residual[i]);
+        p.y[i] = __float2half_rn(v);
+    }
+}
+
+}  // namespace mlvc_b200

@@ -1,0 +1,513 @@
+// Tensor-core convolutions for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Both kernels compute, on channels-last (NHWC) FP16 activations,
+//     out[p, n] = epilogue( sum_k A[p, k] * B[n, k] + bias[n] )
+// with FP32 accumulation in tensor memory and one FP16 rounding of the conv
+// result, followed by the fused operator and its own rounding, which is the
+// operator-by-operator rounding of the AOT graph (reference semantics:
+// backends/cpu/src/kernels_scalar.cpp:180-192; fused patterns from
+// backends/driver_cubin/src/fusion_registry.cpp:711-800 and 893-1036).
+//
+//  * mlvc_conv1x1_tc: 1x1 conv = GEMM M = pixels, N = out channels, K = in
+//    channels.  A is streamed by TMA in 128x64 panels (128-byte swizzle), the
+//    whole weight slice of the CTA's N tile stays resident in shared memory.
+//  * mlvc_convkxk_tc: k x k conv (stride 1 or 2, symmetric pad) as implicit
+//    GEMM.  For every 64-channel slice the CTA loads ONE halo block covering
+//    all taps (kh input rows x (128 + halo) pixels, interleaved 8x16-byte core
+//    matrices, zero fill outside the image from the TMA bounds check) and
+//    feeds every tap to the tensor core by offsetting the matrix descriptor's
+//    start address by whole pixels.  Weight panels (64 channels of one tap)
+//    stream through their own ring or stay resident when they fit.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer, warps 2..5 = epilogue (one TMEM lane quadrant each).  Persistent:
+// each CTA walks tiles t = blockIdx.x + i * gridDim.x, and gridDim.x is a
+// multiple of n_tiles so a CTA keeps one N tile.  Accumulators are double
+// buffered in TMEM so the epilogue of tile i overlaps the MMAs of tile i+1.
+#include "sm100.cuh"
+
+namespace mlvc_b200 {
+
+constexpr int kThreads = 192;
+constexpr int kBM = 128;
+constexpr int kMaxStages = 8;
+constexpr unsigned int kErrWaitProducer = 0x1u;
+constexpr unsigned int kErrWaitMma = 0x2u;
+constexpr unsigned int kErrWaitEpilogue = 0x4u;
+
+struct TcShared {
+    uint64_t a_full[kMaxStages];
+    uint64_t a_empty[kMaxStages];
+    uint64_t b_full[kMaxStages];
+    uint64_t b_empty[kMaxStages];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort_flag;
+    float bias[256];
+};
+static_assert(sizeof(TcShared) <= kTcHeaderBytes, "TcShared must fit the header reserved by the host");
+
+__device__ __forceinline__ uint32_t tmem_cols_for(int bn)
+{
+    uint32_t need = static_cast<uint32_t>(2 * bn);
+    uint32_t c = 32;
+    while (c < need)
+        c <<= 1;
+    return c;
+}
+
+// ----------------------------------------------------------- epilogue
+// One thread owns one output pixel (TMEM lane) of the tile and walks its
+// columns 16 at a time.
+__device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcShared& sh, uint32_t tmem_acc,
+                                              int quadrant, int lane, long long pixel, bool valid, int n_tile)
+{
+    const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16);
+    if (p.epilogue == kEpiReglu) {
+        const int half = p.BN / 2;
+        mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * half;
+        for (int c0 = 0; c0 < half; c0 += 16) {
+            float g[16], l[16];
+            tmem_ld16(lane_addr + c0, g);
+            tmem_ld16(lane_addr + half + c0, l);
+            uint32_t packed[8];
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+                float r2[2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const float gv = round_h(g[i + j] + sh.bias[c0 + i + j]);
+                    const float lv = round_h(l[i + j] + sh.bias[half + c0 + i + j]);
+                    const float cg = round_h(fminf(fmaxf(gv, p.clip_lo), p.clip_hi));
+                    r2[j] = cg * lv;
+                }
+                packed[i / 2] = pack_h2(r2[0], r2[1]);
+            }
+            if (valid) {
+                uint4* d = reinterpret_cast<uint4*>(dst + c0);
+                d[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                d[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            }
+        }
+        return;
+    }
+    mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * p.BN;
+    const mlvc_half* res = p.residual ? p.residual + pixel * p.ldr + n_tile * p.BN : nullptr;
+    for (int c0 = 0; c0 < p.BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(lane_addr + c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            v[i] = round_h(v[i] + sh.bias[c0 + i]);
+        if (p.epilogue == kEpiLeaky) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                v[i] = v[i] < 0.0f ? round_h(v[i] * p.alpha) : v[i];
+        } else if (p.epilogue == kEpiResidual && valid) {
+            const uint4* r = reinterpret_cast<const uint4*>(res + c0);
+            const int col = n_tile * p.BN + c0;
+            const uint4 zero = make_uint4(0, 0, 0, 0);
+            const uint4 r0 = col + 8 <= p.n_valid ? r[0] : zero, r1 = col + 16 <= p.n_valid ? r[1] : zero;
+            const uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float ra, rb;
+                unpack_h2(rr[i], ra, rb);
+                v[2 * i] += ra;
+                v[2 * i + 1] += rb;
+            }
+        }
+        if (valid) {
+            uint32_t packed[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                packed[i] = pack_h2(v[2 * i], v[2 * i + 1]);
+            uint4* d = reinterpret_cast<uint4*>(dst + c0);
+            const int col = n_tile * p.BN + c0;  // channels beyond n_valid are padding rows
+            if (col + 8 <= p.n_valid)
+                d[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            if (col + 16 <= p.n_valid)
+                d[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
+    }
+}
+
+__device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& sh, int warp, int lane,
+                                              int n_tile, int first_tile, int tile_step, int total_tiles,
+                                              bool kxk)
+{
+    const int quadrant = warp & 3;
+    const int et = (warp - 2) * 32 + lane;  // 0..127
+    for (int i = et; i < p.BN; i += 128) {
+        const int col = n_tile * p.BN + i;
+        sh.bias[i] = (p.bias && col < p.N) ? __half2float(p.bias[col]) : 0.0f;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    uint32_t acc = 0, acc_phase = 0;
+    for (int t = first_tile; t < total_tiles; t += tile_step) {
+        if (!mbar_wait(&sh.tmem_full[acc], acc_phase, &sh.abort_flag, kErrWaitEpilogue))
+            return;
+        tc_fence_after();
+        const int m_tile = t / p.n_tiles;
+        const int row = quadrant * 32 + lane;
+        long long pixel;
+        bool valid;
+        if (!kxk) {
+            pixel = static_cast<long long>(m_tile) * kBM + row;
+            valid = pixel < p.M;
+        } else {
+            const int tiles_per_row = (p.out_w + kBM - 1) / kBM;
+            const int oy = m_tile / tiles_per_row;
+            const int ox = (m_tile % tiles_per_row) * kBM + row;
+            valid = ox < p.out_w;
+            pixel = static_cast<long long>(oy) * p.out_w + ox;
+        }
+        epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, lane, pixel, valid, n_tile);
+        tc_fence_before();
+        mbar_arrive(&sh.tmem_empty[acc]);
+        acc ^= 1u;
+        acc_phase ^= (acc == 0) ? 1u : 0u;
+    }
+}
+
+// --------------------------------------------------------------- setup
+__device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvTcParams& p, int warp)
+{
+    TcShared* sh = reinterpret_cast<TcShared*>(smem_raw);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMaxStages; ++s) {
+            mbar_init(&sh->a_full[s], 1);
+            mbar_init(&sh->a_empty[s], 1);
+            mbar_init(&sh->b_full[s], 1);
+            mbar_init(&sh->b_empty[s], 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&sh->tmem_full[s], 1);
+            mbar_init(&sh->tmem_empty[s], 128);
+        }
+        mbar_init(&sh->drain, 1);
+        sh->abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && elect_one()) {
+        tma_prefetch_desc(&p.map_a0);
+        tma_prefetch_desc(&p.map_b);
+    }
+    if (warp == 1)
+        tmem_alloc(&sh->tmem_base, tmem_cols_for(p.BN));
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    return sh;
+}
+
+__device__ __forceinline__ void teardown(const ConvTcParams& p, TcShared* sh, int warp, bool mma_thread,
+                                         uint32_t issued_mma)
+{
+    // An aborted MMA issuer drains its outstanding tcgen05.mma before TMEM is freed.
+    if (mma_thread && sh->abort_flag && issued_mma) {
+        umma_commit(&sh->drain);
+        volatile int never = 0;
+        mbar_wait(&sh->drain, 0, &never, kErrWaitMma);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(sh->tmem_base, tmem_cols_for(p.BN));
+    }
+}
+
+// Producer-side drain: wait (bounded) for every TMA this thread armed, so no
+// bulk copy is still writing shared memory when an aborted CTA exits.
+__device__ __forceinline__ void drain_armed(uint64_t* bars, const uint32_t* armed_parity, const bool* armed, int n)
+{
+    volatile int never = 0;
+    for (int s = 0; s < n; ++s)
+        if (armed[s])
+            mbar_wait(&bars[s], armed_parity[s], &never, kErrWaitProducer);
+}
+
+// ===================================================== 1x1 conv (GEMM)
+extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_conv1x1_tc(const __grid_constant__ ConvTcParams p)
+{
+    extern __shared__ __align__(1024) uint8_t smem_dyn[];
+    // 1024-byte alignment for the swizzled operand tiles.
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    TcShared* sh = setup_shared(base, p, warp);
+    uint8_t* b_smem = base + ((sizeof(TcShared) + 1023) & ~size_t(1023));
+    const int k_panels = (p.K + 63) / 64;  // channels past K read as TMA zero fill
+    const size_t b_panel_bytes = static_cast<size_t>(p.BN) * 128;
+    uint8_t* a_smem = b_smem + b_panel_bytes * k_panels;
+    constexpr uint32_t kAPanelBytes = kBM * 128;
+
+    const int total_tiles = p.m_tiles * p.n_tiles;
+    const int n_tile = blockIdx.x % p.n_tiles;
+    const int first = blockIdx.x, step = gridDim.x;
+    bool mma_thread = false;
+    uint32_t issued = 0;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            bool armed[kMaxStages] = {};
+            uint32_t armed_parity[kMaxStages] = {};
+            bool b_armed = true;
+            mbar_arrive_expect_tx(&sh->b_full[0], static_cast<uint32_t>(b_panel_bytes * k_panels));
+            for (int kp = 0; kp < k_panels; ++kp)
+                tma_load_2d(b_smem + kp * b_panel_bytes, &p.map_b, &sh->b_full[0], kp * 64, n_tile * p.BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {
+                const int m_tile = t / p.n_tiles;
+                for (int kp = 0; kp < k_panels; ++kp) {
+                    if (!mbar_wait(&sh->a_empty[stage], phase ^ 1u, &sh->abort_flag, kErrWaitProducer))
+                        break;
+                    mbar_arrive_expect_tx(&sh->a_full[stage], kAPanelBytes);
+                    tma_load_2d(a_smem + stage * kAPanelBytes, &p.map_a0, &sh->a_full[stage], kp * 64, m_tile * kBM);
+                    armed[stage] = true;
+                    armed_parity[stage] = phase;
+                    if (++stage == p.a_stages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (sh->abort_flag) {
+                drain_armed(sh->a_full, armed_parity, armed, p.a_stages);
+                const uint32_t zero = 0;
+                drain_armed(sh->b_full, &zero, &b_armed, 1);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            mma_thread = true;
+            const uint32_t idesc = idesc_f16_f32(kBM, static_cast<uint32_t>(p.BN));
+            if (mbar_wait(&sh->b_full[0], 0, &sh->abort_flag, kErrWaitMma)) {
+                tc_fence_after();
+                int stage = 0;
+                uint32_t phase = 0, acc = 0, acc_phase = 0;
+                const uint32_t b_addr = smem_u32(b_smem), a_addr = smem_u32(a_smem);
+                for (int t = first; t < total_tiles; t += step) {
+                    if (!mbar_wait(&sh->tmem_empty[acc], acc_phase ^ 1u, &sh->abort_flag, kErrWaitMma))
+                        break;
+                    tc_fence_after();
+                    const uint32_t d = sh->tmem_base + acc * static_cast<uint32_t>(p.BN);
+                    bool ok = true;
+                    for (int kp = 0; kp < k_panels; ++kp) {
+                        if (!mbar_wait(&sh->a_full[stage], phase, &sh->abort_flag, kErrWaitMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_st = a_addr + stage * kAPanelBytes;
+                        const uint32_t b_st = b_addr + static_cast<uint32_t>(kp * b_panel_bytes);
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint64_t ad = smem_desc(a_st + ks * 32, 16, 1024, 2);
+                            const uint64_t bd = smem_desc(b_st + ks * 32, 16, 1024, 2);
+                            umma_f16(d, ad, bd, idesc, (kp | ks) != 0);
+                            ++issued;
+                        }
+                        umma_commit(&sh->a_empty[stage]);
+                        if (++stage == p.a_stages) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok)
+                        break;
+                    umma_commit(&sh->tmem_full[acc]);
+                    acc ^= 1u;
+                    acc_phase ^= (acc == 0) ? 1u : 0u;
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        epilogue_role(p, *sh, warp, lane, n_tile, first, step, total_tiles, false);
+    }
+    teardown(p, sh, warp, mma_thread, issued);
+}
+
+// ===================================================== k x k conv
+// Halo layout in shared memory for one 64-channel slice:
+//   [parity q][chunk j (8 channels)][row r][pixel x] x 16 bytes
+// so that for a fixed (q, row) the pixels of one chunk sit at a 16-byte
+// stride (the rows of an interleaved core matrix) and consecutive chunks are
+// LBO = kh * halo_px * 16 bytes apart.
+extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const __grid_constant__ ConvTcParams p)
+{
+    extern __shared__ __align__(1024) uint8_t smem_dyn[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    TcShared* sh = setup_shared(base, p, warp);
+    if (warp == 0 && elect_one() && p.stride == 2)
+        tma_prefetch_desc(&p.map_a1);
+
+    const int parities = p.stride;  // 1 or 2 halo views
+    const int k_panels = p.in_c / 64;
+    const int taps = p.kh * p.kw;
+    const uint32_t chunk_bytes = static_cast<uint32_t>(p.kh * p.halo_px * 16);  // LBO
+    const uint32_t halo_bytes = static_cast<uint32_t>(parities * 8) * chunk_bytes;
+    const uint32_t halo_stride = (halo_bytes + 1023u) & ~1023u;
+    const uint32_t b_panel_bytes = static_cast<uint32_t>(p.BN) * 128u;
+    uint8_t* b_smem = base + ((sizeof(TcShared) + 1023) & ~size_t(1023));
+    const int b_slots = p.b_resident ? taps * k_panels : p.b_stages;
+    uint8_t* a_smem = b_smem + static_cast<size_t>(b_slots) * b_panel_bytes;
+
+    const int tiles_per_row = (p.out_w + kBM - 1) / kBM;
+    const int total_tiles = p.m_tiles * p.n_tiles;
+    const int n_tile = blockIdx.x % p.n_tiles;
+    const int first = blockIdx.x, step = gridDim.x;
+    bool mma_thread = false;
+    uint32_t issued = 0;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            bool a_armed[kMaxStages] = {}, b_armed[kMaxStages] = {};
+            uint32_t a_par[kMaxStages] = {}, b_par[kMaxStages] = {};
+            if (p.b_resident) {
+                mbar_arrive_expect_tx(&sh->b_full[0], b_panel_bytes * taps * k_panels);
+                for (int kp = 0; kp < k_panels; ++kp)
+                    for (int tap = 0; tap < taps; ++tap)
+                        tma_load_2d(b_smem + static_cast<size_t>(kp * taps + tap) * b_panel_bytes, &p.map_b,
+                                    &sh->b_full[0], tap * p.in_c + kp * 64, n_tile * p.BN);
+                b_armed[0] = true;
+            }
+            int as = 0, bs = 0;
+            uint32_t aph = 0, bph = 0;
+            for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {
+                const int m_tile = t / p.n_tiles;
+                const int oy = m_tile / tiles_per_row;
+                const int ox0 = (m_tile % tiles_per_row) * kBM;
+                const int iy0 = oy * p.stride - p.pad;
+                // first halo pixel (stride 1) or pixel pair (stride 2)
+                const int x0 = (p.stride == 1) ? ox0 - p.pad : ox0 + p.px_min;
+                for (int kp = 0; kp < k_panels; ++kp) {
+                    if (!mbar_wait(&sh->a_empty[as], aph ^ 1u, &sh->abort_flag, kErrWaitProducer))
+                        break;
+                    mbar_arrive_expect_tx(&sh->a_full[as], halo_bytes);
+                    uint8_t* dst = a_smem + static_cast<size_t>(as) * halo_stride;
+                    for (int q = 0; q < parities; ++q)
+                        for (int j = 0; j < 8; ++j)
+                            tma_load_3d(dst + (q * 8 + j) * chunk_bytes, q ? &p.map_a1 : &p.map_a0, &sh->a_full[as],
+                                        kp * 64 + j * 8, x0, iy0);
+                    a_armed[as] = true;
+                    a_par[as] = aph;
+                    if (++as == p.a_stages) {
+                        as = 0;
+                        aph ^= 1u;
+                    }
+                    if (!p.b_resident) {
+                        for (int tap = 0; tap < taps; ++tap) {
+                            if (!mbar_wait(&sh->b_empty[bs], bph ^ 1u, &sh->abort_flag, kErrWaitProducer))
+                                break;
+                            mbar_arrive_expect_tx(&sh->b_full[bs], b_panel_bytes);
+                            tma_load_2d(b_smem + static_cast<size_t>(bs) * b_panel_bytes, &p.map_b, &sh->b_full[bs],
+                                        tap * p.in_c + kp * 64, n_tile * p.BN);
+                            b_armed[bs] = true;
+                            b_par[bs] = bph;
+                            if (++bs == p.b_stages) {
+                                bs = 0;
+                                bph ^= 1u;
+                            }
+                        }
+                    }
+                }
+            }
+            if (sh->abort_flag) {
+                drain_armed(sh->a_full, a_par, a_armed, p.a_stages);
+                drain_armed(sh->b_full, b_par, b_armed, p.b_resident ? 1 : p.b_stages);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (elect_one()) {
+            mma_thread = true;
+            const uint32_t idesc = idesc_f16_f32(kBM, static_cast<uint32_t>(p.BN));
+            bool ok = true;
+            if (p.b_resident)
+                ok = mbar_wait(&sh->b_full[0], 0, &sh->abort_flag, kErrWaitMma);
+            int as = 0, bs = 0;
+            uint32_t aph = 0, bph = 0, acc = 0, acc_phase = 0;
+            const uint32_t a_addr = smem_u32(a_smem), b_addr = smem_u32(b_smem);
+            for (int t = first; ok && t < total_tiles; t += step) {
+                if (!mbar_wait(&sh->tmem_empty[acc], acc_phase ^ 1u, &sh->abort_flag, kErrWaitMma))
+                    break;
+                tc_fence_after();
+                const uint32_t d = sh->tmem_base + acc * static_cast<uint32_t>(p.BN);
+                bool first_mma = true;
+                for (int kp = 0; ok && kp < k_panels; ++kp) {
+                    if (!mbar_wait(&sh->a_full[as], aph, &sh->abort_flag, kErrWaitMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t halo = a_addr + as * halo_stride;
+                    for (int ky = 0; ok && ky < p.kh; ++ky) {
+                        for (int kx = 0; kx < p.kw; ++kx) {
+                            const int tap = ky * p.kw + kx;
+                            uint32_t b_panel;
+                            if (p.b_resident) {
+                                b_panel = b_addr + static_cast<uint32_t>(kp * taps + tap) * b_panel_bytes;
+                            } else {
+                                if (!mbar_wait(&sh->b_full[bs], bph, &sh->abort_flag, kErrWaitMma)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                b_panel = b_addr + bs * b_panel_bytes;
+                            }
+                            int q, xoff;
+                            if (p.stride == 1) {
+                                q = 0;
+                                xoff = kx;
+                            } else {
+                                const int dlt = kx - p.pad;                 // input offset of this tap
+                                q = dlt & 1;                                 // parity (two's complement)
+                                xoff = ((dlt - q) >> 1) - p.px_min;          // pair offset inside the halo
+                            }
+                            const uint32_t a_tap = halo + static_cast<uint32_t>(q * 8) * chunk_bytes +
+                                                   static_cast<uint32_t>(ky * p.halo_px + xoff) * 16u;
+#pragma unroll
+                            for (int ks = 0; ks < 4; ++ks) {
+                                const uint64_t ad = smem_desc(a_tap + ks * 2 * chunk_bytes, chunk_bytes, 128, 0);
+                                const uint64_t bd = smem_desc(b_panel + ks * 32, 16, 1024, 2);
+                                umma_f16(d, ad, bd, idesc, first_mma ? 0u : 1u);
+                                first_mma = false;
+                                ++issued;
+                            }
+                            if (!p.b_resident) {
+                                umma_commit(&sh->b_empty[bs]);
+                                if (++bs == p.b_stages) {
+                                    bs = 0;
+                                    bph ^= 1u;
+                                }
+                            }
+                        }
+                    }
+                    umma_commit(&sh->a_empty[as]);
+                    if (++as == p.a_stages) {
+                        as = 0;
+                        aph ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+                umma_commit(&sh->tmem_full[acc]);
+                acc ^= 1u;
+                acc_phase ^= (acc == 0) ? 1u : 0u;
+            }
+        }
+        __syncwarp();
+    } else {
+        epilogue_role(p, *sh, warp, lane, n_tile, first, step, total_tiles, true);
+    }
+    teardown(p, sh, warp, mma_thread, issued);
+}
+
+}  // namespace mlvc_b200

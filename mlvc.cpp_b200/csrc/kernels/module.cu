@@ -1,0 +1,8 @@
+// Single translation unit for the embedded sm_100a cubin: every kernel of the
+// backend, resolved by name from the host through cuModuleGetFunction.
+#include "sm100.cuh"
+
+extern "C" __device__ unsigned int mlvc_b200_status = 0;
+
+#include "conv_tc.cu"
+#include "bandwidth.cu"

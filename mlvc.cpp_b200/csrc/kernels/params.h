@@ -1,0 +1,122 @@
+// Kernel parameter blocks shared by the host runtime (C++) and the sm_100a
+// kernels.  Every kernel takes exactly one of these structs by value
+// (`const __grid_constant__`), so the host launches it with a single
+// kernelParams entry and CUDA-graph capture copies it once.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#include <cuda_fp16.h>
+typedef __half mlvc_half;
+#else
+typedef uint16_t mlvc_half;
+#endif
+
+namespace mlvc_b200 {
+
+// Shared-memory bytes reserved at the start of a tensor-core conv CTA for
+// barriers, the TMEM address and the bias slice (operand tiles follow,
+// 1024-byte aligned).
+constexpr int kTcHeaderBytes = 2048;
+
+// Epilogue kinds of the tensor-core conv kernels.  Rounding follows the graph:
+// the conv result is rounded to FP16 first, then the fused operator is applied
+// and rounded again.
+enum Epilogue : int {
+    kEpiBias = 0,      // y = fp16(acc + bias)
+    kEpiLeaky = 1,     // y = leaky(fp16(acc + bias))
+    kEpiResidual = 2,  // y = fp16(fp16(acc + bias) + r)
+    kEpiReglu = 3,     // columns [0, BN/2) gate, [BN/2, BN) linear of the same channels
+};
+
+// Shared by the 1x1 GEMM and the k x k implicit-GEMM conv kernels.
+struct ConvTcParams {
+    CUtensorMap map_a0;  // activations (1x1: [M rows, K]; kxk: parity 0 view)
+    CUtensorMap map_a1;  // kxk stride-2: parity 1 view (unused otherwise)
+    CUtensorMap map_b;   // prepared weights [N rows, K = taps * IC] (K-major)
+    const mlvc_half* bias;      // [N] in prepared column order, may be null
+    const mlvc_half* residual;  // NHWC [M, ldr] or null
+    mlvc_half* out;             // NHWC [M, ldo]
+    int M, N, K;                // GEMM extents (K = taps * IC); N counts prepared (padded) weight rows
+    int n_valid;                // output channels actually stored (<= N, multiple of 8)
+    int BN;                     // columns per N tile (multiple of 16, <= 256)
+    int n_tiles, m_tiles;       // tile counts
+    int ldo, out_col0;          // output row stride / first channel written
+    int ldr;                    // residual row stride
+    int epilogue;               // Epilogue
+    float alpha, clip_lo, clip_hi;
+    int a_stages;               // A ring depth (1x1: 16 KB panels; kxk: halo blocks)
+    int b_resident;             // kxk: 1 = all weight panels resident in smem
+    int b_stages;               // kxk: B ring depth when not resident
+    // kxk geometry (ignored by the 1x1 kernel)
+    int in_h, in_w, in_c;
+    int out_h, out_w;
+    int kh, kw, stride, pad;
+    int halo_px;                // pixels (or pixel pairs) per halo row
+    int px_min;                 // leftmost halo offset relative to the tile start (<= 0)
+};
+
+struct ElementwiseParams {
+    const mlvc_half* a;
+    const mlvc_half* b;
+    mlvc_half* out;
+    long long count;    // output elements
+    int op;             // unary: 0 leaky 1 clip 2 sigmoid 3 reciprocal 4 round; binary: 0 add 1 mul 2 sub
+    float alpha, lo, hi;
+    // broadcast binary: output logical dims (n, c, h, w) in physical NHWC order and per-operand strides
+    int dims[4];        // n, h, w, c extents of the output (physical order)
+    long long sa[4];    // element strides of `a` for (n, h, w, c)
+    long long sb[4];
+};
+
+// Generic strided copy over up to 4 logical dimensions (physical order of the
+// output): slice, concat pieces, layout conversion.
+struct CopyParams {
+    const mlvc_half* src;
+    mlvc_half* dst;
+    int dims[4];
+    long long ss[4];
+    long long ds[4];
+    long long count;
+};
+
+struct GatherParams {
+    const mlvc_half* src;
+    const int32_t* index;
+    mlvc_half* dst;
+    long long row_elems;
+    int rows;
+};
+
+// Depthwise / generic grouped direct convolution on NHWC tensors.
+struct DirectConvParams {
+    const mlvc_half* x;
+    const mlvc_half* w;     // depthwise: [kh*kw][C]; generic: [OC][kh][kw][ICg]
+    const mlvc_half* bias;  // [OC] or null
+    const mlvc_half* residual;
+    mlvc_half* y;
+    int n, ih, iw, ic, oh, ow, oc;
+    int kh, kw, sh, sw, ph, pw, groups;
+    int epilogue;
+    float alpha;
+};
+
+struct PixelShuffleParams {
+    const mlvc_half* src;
+    mlvc_half* dst;
+    int n, h, w, c;  // input NHWC extents
+    int r;           // block size
+    long long count;
+};
+
+struct RegluParams {
+    const mlvc_half* src;  // NHWC [P, 2C]
+    mlvc_half* dst;        // NHWC [P, C]
+    long long pixels;
+    int c;
+    float lo, hi;
+};
+
+}  // namespace mlvc_b200

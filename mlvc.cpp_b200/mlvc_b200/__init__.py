@@ -1,0 +1,248 @@
+"""Python host mirror of the reference backend interface over libmlvc_b200.so.
+
+`Backend` follows mlvc::InferenceBackend (runtime/include/mlvc/runtime/
+backend.hpp:48-63): load(model_name, state bindings) -> run(inputs) ->
+reset_state(), plus the slot path of BufferedCodecBackend (backend.hpp:79-96)
+in tensor form.  Tensors are NCHW numpy arrays (float16 or int32), the same
+contract as mlvc::Tensor.  Every call goes through the C ABI declared in
+include/mlvc_b200.h; failures raise RuntimeError with the library's message.
+
+There is no fallback: if the native library is missing or the device is not
+an sm_100 GPU, construction fails.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+_PKG_ROOT = Path(__file__).resolve().parent.parent
+LIB_PATH = _PKG_ROOT / "lib" / "libmlvc_b200.so"
+_lib = None
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("rank", ctypes.c_int32), ("shape", ctypes.c_int64 * 4),
+                ("data", ctypes.c_void_p), ("bytes", ctypes.c_size_t)]
+
+
+class StateBinding(ctypes.Structure):
+    _fields_ = [("input_index", ctypes.c_size_t), ("output_index", ctypes.c_size_t)]
+
+
+EXPORTS = {
+    "mlvc_b200_abi_version": ([], ctypes.c_int),
+    "mlvc_b200_last_error": ([], ctypes.c_char_p),
+    "mlvc_b200_create": ([ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "mlvc_b200_create_offline": ([ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "mlvc_b200_destroy": ([ctypes.c_void_p], None),
+    "mlvc_b200_name": ([ctypes.c_void_p], ctypes.c_char_p),
+    "mlvc_b200_load": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(StateBinding),
+                        ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_load_memory": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+                               ctypes.POINTER(StateBinding), ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_input_count": ([ctypes.c_void_p], ctypes.c_size_t),
+    "mlvc_b200_output_count": ([ctypes.c_void_p], ctypes.c_size_t),
+    "mlvc_b200_input_info": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(Tensor),
+                              ctypes.POINTER(ctypes.c_char_p)], ctypes.c_int),
+    "mlvc_b200_output_info": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(Tensor),
+                               ctypes.POINTER(ctypes.c_char_p)], ctypes.c_int),
+    "mlvc_b200_run": ([ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.c_size_t, ctypes.POINTER(Tensor),
+                       ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_reset_state": ([ctypes.c_void_p], ctypes.c_int),
+    "mlvc_b200_configure_slots": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_slot_count": ([ctypes.c_void_p], ctypes.c_size_t),
+    "mlvc_b200_slot_input": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t], ctypes.c_void_p),
+    "mlvc_b200_slot_output": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t], ctypes.c_void_p),
+    "mlvc_b200_submit": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_wait_slot": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_enqueue": ([ctypes.c_void_p], ctypes.c_int),
+    "mlvc_b200_synchronize": ([ctypes.c_void_p], ctypes.c_int),
+    "mlvc_b200_stream": ([ctypes.c_void_p], ctypes.c_void_p),
+    "mlvc_b200_step_count": ([ctypes.c_void_p], ctypes.c_size_t),
+    "mlvc_b200_step_info": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_char_p),
+                             ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_double),
+                             ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint32),
+                             ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
+    "mlvc_b200_time_steps": ([ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)], ctypes.c_int),
+    "mlvc_b200_kernel_launches": ([ctypes.c_void_p], ctypes.c_int),
+    "mlvc_b200_device_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
+}
+
+
+def lib():
+    """Loads the in-tree native library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"mlvc-b200 native library not built: {LIB_PATH} (run python mlvc.cpp_b200/build.py)")
+        l = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in EXPORTS.items():
+            f = getattr(l, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = l
+    return _lib
+
+
+def _check(rc):
+    if rc != 0:
+        raise RuntimeError(lib().mlvc_b200_last_error().decode())
+
+
+def _np_dtype(code):
+    return np.float16 if code == 0 else np.int32
+
+
+class Backend:
+    """One B200 backend instance bound to one device (BackendOptions::device_id)."""
+
+    def __init__(self, device_id: int = 0, plan_only_for=None):
+        """plan_only_for=(sm_count, smem_optin_bytes) creates a planning-only
+        instance that never touches a GPU (mlvc_b200_create_offline)."""
+        self._h = ctypes.c_void_p()
+        if plan_only_for is None:
+            _check(lib().mlvc_b200_create(device_id, ctypes.byref(self._h)))
+        else:
+            _check(lib().mlvc_b200_create_offline(int(plan_only_for[0]), int(plan_only_for[1]), ctypes.byref(self._h)))
+        self._in, self._out = [], []
+
+    def close(self):
+        if self._h:
+            lib().mlvc_b200_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def name(self):
+        return lib().mlvc_b200_name(self._h).decode()
+
+    # ------------------------------------------------------------ load
+    def load(self, model_dir, model_name, state_bindings=()):
+        b = (StateBinding * max(1, len(state_bindings)))(*[StateBinding(i, o) for i, o in state_bindings])
+        _check(lib().mlvc_b200_load(self._h, str(model_dir).encode(), model_name.encode(), b, len(state_bindings)))
+        self._describe()
+
+    def load_memory(self, graph_pb: bytes, weights: bytes, state_bindings=()):
+        b = (StateBinding * max(1, len(state_bindings)))(*[StateBinding(i, o) for i, o in state_bindings])
+        g = ctypes.create_string_buffer(graph_pb, len(graph_pb))
+        w = ctypes.create_string_buffer(weights, max(1, len(weights)))
+        _check(lib().mlvc_b200_load_memory(self._h, g, len(graph_pb), w, len(weights), b, len(state_bindings)))
+        self._describe()
+
+    def _describe(self):
+        L = lib()
+        self._in, self._out = [], []
+        for count, info, dst in ((L.mlvc_b200_input_count, L.mlvc_b200_input_info, self._in),
+                                 (L.mlvc_b200_output_count, L.mlvc_b200_output_info, self._out)):
+            for i in range(count(self._h)):
+                t, name = Tensor(), ctypes.c_char_p()
+                _check(info(self._h, i, ctypes.byref(t), ctypes.byref(name)))
+                dst.append((name.value.decode(), _np_dtype(t.dtype), tuple(t.shape[:t.rank])))
+
+    @property
+    def inputs(self):
+        return list(self._in)
+
+    @property
+    def outputs(self):
+        return list(self._out)
+
+    # ------------------------------------------------------------- run
+    def run(self, inputs):
+        if len(inputs) != len(self._in):
+            raise RuntimeError("mlvc-b200: graph input count mismatch")
+        keep = []
+        tin = (Tensor * max(1, len(inputs)))()
+        for k, (arr, (_, dt, shape)) in enumerate(zip(inputs, self._in)):
+            a = np.ascontiguousarray(arr)
+            keep.append(a)
+            tin[k].dtype = 0 if a.dtype == np.float16 else 1 if a.dtype == np.int32 else -1
+            tin[k].rank = a.ndim
+            for r in range(a.ndim):
+                tin[k].shape[r] = a.shape[r]
+            tin[k].data = a.ctypes.data
+            tin[k].bytes = a.nbytes
+        outs = [np.empty(shape, dt) for _, dt, shape in self._out]
+        tout = (Tensor * max(1, len(outs)))()
+        for k, o in enumerate(outs):
+            tout[k].data = o.ctypes.data
+            tout[k].bytes = o.nbytes
+        _check(lib().mlvc_b200_run(self._h, tin, len(inputs), tout, len(outs)))
+        return outs
+
+    def reset_state(self):
+        _check(lib().mlvc_b200_reset_state(self._h))
+
+    # ----------------------------------------------------------- slots
+    def configure_slots(self, n):
+        _check(lib().mlvc_b200_configure_slots(self._h, n))
+
+    def slot_input(self, slot, i):
+        """numpy view of the pinned host buffer of input i in `slot`."""
+        ptr = lib().mlvc_b200_slot_input(self._h, slot, i)
+        if not ptr:
+            raise RuntimeError(lib().mlvc_b200_last_error().decode())
+        _, dt, shape = self._in[i]
+        n = int(np.prod(shape)) * np.dtype(dt).itemsize
+        return np.frombuffer((ctypes.c_char * n).from_address(ptr), dt).reshape(shape)
+
+    def slot_output(self, slot, i):
+        ptr = lib().mlvc_b200_slot_output(self._h, slot, i)
+        if not ptr:
+            raise RuntimeError(lib().mlvc_b200_last_error().decode())
+        _, dt, shape = self._out[i]
+        n = int(np.prod(shape)) * np.dtype(dt).itemsize
+        return np.frombuffer((ctypes.c_char * n).from_address(ptr), dt).reshape(shape)
+
+    def submit(self, slot):
+        _check(lib().mlvc_b200_submit(self._h, slot))
+
+    def wait_slot(self, slot):
+        _check(lib().mlvc_b200_wait_slot(self._h, slot))
+
+    # ----------------------------------------------------- measurement
+    def enqueue(self):
+        _check(lib().mlvc_b200_enqueue(self._h))
+
+    def synchronize(self):
+        _check(lib().mlvc_b200_synchronize(self._h))
+
+    @property
+    def stream(self):
+        return lib().mlvc_b200_stream(self._h)
+
+    def steps(self):
+        L = lib()
+        out = []
+        for i in range(L.mlvc_b200_step_count(self._h)):
+            k, n = ctypes.c_char_p(), ctypes.c_char_p()
+            fl, by = ctypes.c_double(), ctypes.c_double()
+            g, b, s = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+            _check(L.mlvc_b200_step_info(self._h, i, ctypes.byref(k), ctypes.byref(n), ctypes.byref(fl),
+                                         ctypes.byref(by), ctypes.byref(g), ctypes.byref(b), ctypes.byref(s)))
+            out.append(dict(kernel=k.value.decode(), nodes=n.value.decode(), flops=fl.value, bytes=by.value,
+                            grid=g.value, block=b.value, smem=s.value))
+        return out
+
+    def time_steps(self, iterations=10):
+        n = lib().mlvc_b200_step_count(self._h)
+        buf = (ctypes.c_float * max(1, n))()
+        _check(lib().mlvc_b200_time_steps(self._h, iterations, buf))
+        return list(buf[:n])
+
+    @property
+    def kernel_launches(self):
+        return lib().mlvc_b200_kernel_launches(self._h)
+
+    @property
+    def device_bytes(self):
+        return lib().mlvc_b200_device_bytes(self._h)

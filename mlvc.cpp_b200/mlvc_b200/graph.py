@@ -1,0 +1,357 @@
+"""Builder for mlvc AOT graph bundles (aot/<part>/graph.pb + weights.bin).
+
+The on-disk contract is the reference's graph schema 3
+(proto/mlvc_model.proto:30-83) as validated by runtime/src/aot_graph.cpp:110-283:
+tensor IDs are dense from 1, weights live 256-byte aligned in weights.bin,
+runtime tensors carry a 256-byte aligned arena slot whose `birth` is the index
+of the producing node, inputs have no storage, and both SHA-256 fields are 32
+bytes.  The reference produces such bundles by tracing a PyTorch module
+(tools/python/mlvc_tools/aot.py:233-278); this builder emits the same operator
+vocabulary directly, which lets the benchmark and the GPU tests generate their
+seeded synthetic models on a machine that has no PyTorch model code.
+
+The protobuf wire format is written by hand (varints, length-delimited
+submessages, packed repeated scalars) so this module has no dependency on a
+generated protobuf class.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import struct
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+ALIGN = 256
+DTYPE_CODE = {"fp16": 1, "int32": 2, "int64": 3}
+DTYPE_BYTES = {"fp16": 2, "int32": 4, "int64": 8}
+OP_CODE = dict(Add=1, Sub=2, Mul=3, Clip=4, Concat=5, Conv=6, DepthToSpace=7, Gather=8, LeakyRelu=9,
+               Reciprocal=10, Round=11, Sigmoid=12, Slice=13, SpaceToDepth=14)
+
+
+def _align(v: int) -> int:
+    return (v + ALIGN - 1) // ALIGN * ALIGN
+
+
+# ---------------------------------------------------------------- wire writer
+def _varint(v: int) -> bytes:
+    if v < 0:
+        v &= (1 << 64) - 1
+    out = bytearray()
+    while True:
+        b = v & 0x7F
+        v >>= 7
+        if v:
+            out.append(b | 0x80)
+        else:
+            out.append(b)
+            return bytes(out)
+
+
+def _key(field_no: int, wire: int) -> bytes:
+    return _varint(field_no << 3 | wire)
+
+
+def _f_varint(field_no, v):
+    return _key(field_no, 0) + _varint(v) if v else b""
+
+
+def _f_bytes(field_no, data: bytes):
+    return _key(field_no, 2) + _varint(len(data)) + data
+
+
+def _f_packed(field_no, values):
+    values = list(values)
+    if not values:
+        return b""
+    return _f_bytes(field_no, b"".join(_varint(int(v)) for v in values))
+
+
+def _zigzag(v: int) -> int:
+    return (v << 1) ^ (v >> 31)
+
+
+@dataclass
+class _Tensor:
+    name: str
+    dtype: str
+    shape: list
+    kind: str  # "input" | "weight" | "value"
+    data: np.ndarray | None = None
+    producer: int = -1
+    last_use: int = -1
+    tid: int = 0
+
+
+@dataclass
+class _Node:
+    op: str
+    inputs: list
+    output: str
+    attrs: dict = field(default_factory=dict)
+
+
+class GraphBuilder:
+    """Emits one graph part.  Tensors are referenced by name."""
+
+    def __init__(self):
+        self.tensors: dict[str, _Tensor] = {}
+        self.nodes: list[_Node] = []
+        self.inputs: list[str] = []
+        self.outputs: list[str] = []
+        self._lit = 0
+
+    # -------------------------------------------------------------- values
+    def input(self, name, shape, dtype="fp16"):
+        self.tensors[name] = _Tensor(name, dtype, list(shape), "input")
+        self.inputs.append(name)
+        return name
+
+    def weight(self, name, array):
+        array = np.ascontiguousarray(array)
+        dtype = {np.dtype(np.float16): "fp16", np.dtype(np.int64): "int64"}[array.dtype]
+        self.tensors[name] = _Tensor(name, dtype, list(array.shape), "weight", array)
+        return name
+
+    def literal(self, values, dtype=np.int64):
+        name = f"literal_{self._lit:05d}"
+        self._lit += 1
+        return self.weight(name, np.asarray(values, dtype).reshape(-1))
+
+    def _emit(self, op, inputs, shape, attrs=None, dtype="fp16", name=None):
+        index = len(self.nodes)
+        name = name or f"value_{index:05d}"
+        self.tensors[name] = _Tensor(name, dtype, list(shape), "value", producer=index)
+        self.nodes.append(_Node(op, list(inputs), name, attrs or {}))
+        return name
+
+    def shape(self, name):
+        return list(self.tensors[name].shape)
+
+    # ----------------------------------------------------------------- ops
+    def conv(self, x, w, b=None, stride=(1, 1), pad=(0, 0), groups=1, name=None):
+        n, ic, ih, iw = self.shape(x)
+        oc, icg, kh, kw = self.shape(w)
+        if icg * groups != ic:
+            raise ValueError("conv channel mismatch")
+        oh = (ih + 2 * pad[0] - kh) // stride[0] + 1
+        ow = (iw + 2 * pad[1] - kw) // stride[1] + 1
+        attrs = dict(strides=list(stride), pads=list(pad) * 2, dilations=[1, 1], groups=groups)
+        return self._emit("Conv", [x, w] + ([b] if b is not None else []), [n, oc, oh, ow], attrs, name=name)
+
+    def _binary(self, op, a, b, name=None):
+        shape = list(np.broadcast_shapes(tuple(self.shape(a)), tuple(self.shape(b))))
+        return self._emit(op, [a, b], shape, name=name)
+
+    def add(self, a, b, name=None):
+        return self._binary("Add", a, b, name)
+
+    def sub(self, a, b, name=None):
+        return self._binary("Sub", a, b, name)
+
+    def mul(self, a, b, name=None):
+        return self._binary("Mul", a, b, name)
+
+    def leaky_relu(self, x, alpha=0.01, name=None):
+        return self._emit("LeakyRelu", [x], self.shape(x), dict(alpha=alpha), name=name)
+
+    def clip(self, x, lo=None, hi=None, name=None):
+        ins = [x, self.literal([lo], np.float16) if lo is not None else "",
+               self.literal([hi], np.float16) if hi is not None else ""]
+        while ins and ins[-1] == "":
+            ins.pop()
+        return self._emit("Clip", ins, self.shape(x), name=name)
+
+    def unary(self, op, x, name=None):
+        return self._emit(op, [x], self.shape(x), name=name)
+
+    def slice(self, x, axis, start, end, step=1, name=None):
+        shape = self.shape(x)
+        start, end, step = slice(start, end, step).indices(shape[axis])
+        shape[axis] = len(range(start, end, step))
+        ins = [x] + [self.literal([v]) for v in (start, end, axis, step)]
+        return self._emit("Slice", ins, shape, name=name)
+
+    def concat(self, xs, axis, name=None):
+        shape = self.shape(xs[0])
+        shape[axis] = sum(self.shape(v)[axis] for v in xs)
+        return self._emit("Concat", list(xs), shape, dict(axis=axis), name=name)
+
+    def gather(self, data, index, name=None):
+        shape = [1] + self.shape(data)[1:]
+        return self._emit("Gather", [data, index], shape, dict(axis=0), name=name)
+
+    def depth_to_space(self, x, r, name=None):
+        n, c, h, w = self.shape(x)
+        return self._emit("DepthToSpace", [x], [n, c // (r * r), h * r, w * r], dict(block_size=r), name=name)
+
+    def space_to_depth(self, x, r, name=None):
+        n, c, h, w = self.shape(x)
+        return self._emit("SpaceToDepth", [x], [n, c * r * r, h // r, w // r], dict(block_size=r), name=name)
+
+    def output(self, value, name):
+        """Marks `value` as a graph output, renaming it to `name`."""
+        if value != name:
+            t = self.tensors.pop(value)
+            t.name = name
+            self.tensors[name] = t
+            for node in self.nodes:
+                node.inputs = [name if v == value else v for v in node.inputs]
+                if node.output == value:
+                    node.output = name
+            self.outputs = [name if v == value else v for v in self.outputs]
+        self.outputs.append(name)
+        return name
+
+    # ------------------------------------------------------------ finalise
+    def _plan_arena(self):
+        for index, node in enumerate(self.nodes):
+            for v in node.inputs:
+                if v:
+                    self.tensors[v].last_use = max(self.tensors[v].last_use, index)
+        values = [t for t in self.tensors.values() if t.kind == "value"]
+        events = []
+        for t in values:
+            size = _align(int(np.prod(t.shape)) * DTYPE_BYTES[t.dtype])
+            death = len(self.nodes) if t.name in self.outputs else max(t.last_use, t.producer)
+            events.append((t.producer, death, size, t))
+        live, end, plan = [], 0, {}
+        for birth, death, size, t in sorted(events, key=lambda e: (e[0], e[3].name)):
+            live = [e for e in live if e[0] >= birth]  # (death, offset, size)
+            taken = sorted((o, o + s) for _, o, s in live)
+            offset, cursor = None, 0
+            for lo, hi in taken:  # first gap that fits
+                if lo - cursor >= size:
+                    offset = cursor
+                    break
+                cursor = max(cursor, hi)
+            if offset is None:
+                offset = cursor
+            end = max(end, offset + size)
+            live.append((death, offset, size))
+            plan[t.name] = (offset, size, birth, death)
+        return plan, end
+
+    def finish(self, checkpoint_sha256: bytes = b"\0" * 32):
+        used = set(self.inputs) | set(self.outputs)
+        for node in self.nodes:
+            used.update(v for v in node.inputs if v)
+            used.add(node.output)
+        names = sorted(n for n in self.tensors if n in used)
+        ids = {n: i for i, n in enumerate(names, 1)}
+        weights = bytearray()
+        woff = {}
+        for n in names:
+            t = self.tensors[n]
+            if t.kind == "weight":
+                weights.extend(b"\0" * (_align(len(weights)) - len(weights)))
+                woff[n] = len(weights)
+                weights.extend(t.data.tobytes())
+        plan, arena_bytes = self._plan_arena()
+        out = bytearray()
+        out += _f_varint(1, 3)
+        out += _f_bytes(2, checkpoint_sha256)
+        for n in names:
+            t = self.tensors[n]
+            body = _f_varint(1, ids[n]) + _f_bytes(2, n.encode()) + _f_varint(3, DTYPE_CODE[t.dtype])
+            body += _f_packed(4, t.shape)
+            if t.kind == "weight":
+                body += _f_bytes(6, _f_varint(1, woff[n]) + _f_varint(2, t.data.nbytes))
+            elif t.kind == "value":
+                o, s, b, d = plan[n]
+                body += _f_bytes(5, _f_varint(1, o) + _f_varint(2, s) + _f_varint(3, b) + _f_varint(4, d))
+            out += _f_bytes(3, body)
+        out += _f_packed(4, [ids[n] for n in self.inputs])
+        out += _f_packed(5, [ids[n] for n in self.outputs])
+        for node in self.nodes:
+            body = _f_varint(1, OP_CODE[node.op])
+            body += _f_packed(2, [ids[v] if v else 0 for v in node.inputs])
+            body += _f_packed(3, [ids[node.output]])
+            a = node.attrs
+            if node.op == "Conv":
+                body += _f_bytes(4, _f_packed(1, a["strides"]) + _f_packed(2, a["pads"]) +
+                                 _f_packed(3, a["dilations"]) + _f_varint(4, a["groups"]))
+            elif node.op in ("Concat", "Gather"):
+                body += _f_bytes(5, _f_varint(1, _zigzag(int(a["axis"]))))
+            elif node.op == "LeakyRelu":
+                body += _f_bytes(6, _key(1, 5) + struct.pack("<f", a["alpha"]))
+            elif node.op in ("DepthToSpace", "SpaceToDepth"):
+                body += _f_bytes(7, _f_varint(1, a["block_size"]))
+            out += _f_bytes(6, body)
+        out += _f_varint(7, arena_bytes)
+        out += _f_varint(8, ALIGN)
+        out += _f_varint(9, len(weights))
+        out += _f_bytes(10, hashlib.sha256(weights).digest())
+        return bytes(out), bytes(weights)
+
+    def save(self, model_dir, part):
+        graph, weights = self.finish()
+        d = Path(model_dir) / "aot" / part
+        d.mkdir(parents=True, exist_ok=True)
+        (d / "graph.pb").write_bytes(graph)
+        (d / "weights.bin").write_bytes(weights)
+        return d
+
+
+# ------------------------------------------------------ synthetic workloads
+def _fp16(a):
+    return np.asarray(a, np.float32).astype(np.float16)
+
+
+def kaiming_normal(rng, shape):
+    fan_in = int(np.prod(shape[1:]))
+    return _fp16(rng.standard_normal(shape, dtype=np.float32) * np.float32(np.sqrt(2.0 / fan_in)))
+
+
+def small_bias(rng, n):
+    return _fp16(rng.uniform(-0.1, 0.1, n).astype(np.float32))
+
+
+def build_conv3x3(seed=0, channels=64, height=184, width=320):
+    """Config 1: one FP16 3x3 s1 p1 conv C->C with bias.  W ~ N(0, sqrt(2/(9C))),
+    b ~ U(-0.1, 0.1), x ~ N(0, 1), all drawn from one seeded generator."""
+    rng = np.random.default_rng(seed)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, channels, height, width])
+    w = gb.weight("conv.weight", kaiming_normal(rng, (channels, channels, 3, 3)))
+    b = gb.weight("conv.bias", small_bias(rng, channels))
+    gb.output(gb.conv(x, w, b, (1, 1), (1, 1)), "y")
+    inputs = [_fp16(rng.standard_normal((1, channels, height, width), dtype=np.float32))]
+    return gb, inputs
+
+
+def build_block_stack(seed=0, channels=128, height=92, width=160, blocks=8):
+    """Config 2: pixel_unshuffle(2) -> `blocks` x [1x1 C->2C + LeakyReLU(0.01);
+    depthwise 3x3 (2C); 1x1 2C->C + residual; 1x1 C->4C -> ReGLU (clip(gate, 0, 1)
+    * linear) -> 1x1 2C->C + residual] -> pixel_shuffle(2).  Input [1, C/4, 2H, 2W]
+    ~ N(0, 1); Kaiming-normal weights; biases U(-0.1, 0.1)."""
+    rng = np.random.default_rng(seed)
+    c = channels
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c // 4, height * 2, width * 2])
+    h = gb.space_to_depth(x, 2)
+    for i in range(blocks):
+        p = f"block{i}."
+        w1 = gb.weight(p + "expand.weight", kaiming_normal(rng, (2 * c, c, 1, 1)))
+        b1 = gb.weight(p + "expand.bias", small_bias(rng, 2 * c))
+        wd = gb.weight(p + "dw.weight", kaiming_normal(rng, (2 * c, 1, 3, 3)))
+        bd = gb.weight(p + "dw.bias", small_bias(rng, 2 * c))
+        w2 = gb.weight(p + "project.weight", kaiming_normal(rng, (c, 2 * c, 1, 1)))
+        b2 = gb.weight(p + "project.bias", small_bias(rng, c))
+        w3 = gb.weight(p + "ffn_in.weight", kaiming_normal(rng, (4 * c, c, 1, 1)))
+        b3 = gb.weight(p + "ffn_in.bias", small_bias(rng, 4 * c))
+        w4 = gb.weight(p + "ffn_out.weight", kaiming_normal(rng, (c, 2 * c, 1, 1)))
+        b4 = gb.weight(p + "ffn_out.bias", small_bias(rng, c))
+        t = gb.leaky_relu(gb.conv(h, w1, b1), 0.01)
+        t = gb.conv(t, wd, bd, (1, 1), (1, 1), groups=2 * c)
+        h = gb.add(h, gb.conv(t, w2, b2))
+        f = gb.conv(h, w3, b3)
+        g = gb.slice(f, 1, 0, 2 * c)
+        lin = gb.slice(f, 1, 2 * c, 4 * c)
+        f = gb.mul(gb.clip(g, 0.0, 1.0), lin)
+        h = gb.add(h, gb.conv(f, w4, b4))
+    gb.output(gb.depth_to_space(h, 2), "y")
+    inputs = [_fp16(rng.standard_normal((1, c // 4, height * 2, width * 2), dtype=np.float32))]
+    return gb, inputs

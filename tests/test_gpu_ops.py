@@ -1,0 +1,279 @@
+"""Operator parity on the B200: each case is a one-operator (or one fused
+chain) graph run through the product's C ABI (load -> run) and compared with
+the CPU oracle on the same seeded inputs.
+
+Conv cases mirror the reference's kernel tests (tests/unit/cutlass_kernel_tests.cpp:
+GEMM shapes M=OC, N=H*W, K=IC at :345-348 with the LCG inputs of :26-34, the
+spatial convs of :355-358 on a 13x17 image, pixel (un)shuffle order for
+factors 2 and 8 at :43-89) plus the shapes of the benchmark workloads.
+Tolerance for convolutions: max-abs 2e-2 and relative L2 1e-3 against FP32
+accumulation; elementwise, layout and data-movement operators are bit-exact.
+"""
+
+import numpy as np
+import pytest
+
+from helpers import bits_equal, compare, conv_graph, lcg_fast
+from mlvc_b200 import Backend
+from mlvc_b200.graph import GraphBuilder
+from oracle.graph_oracle import GraphOracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def device():
+    return 0
+
+
+def run_both(gb, inputs, conv_impl="c", state_bindings=()):
+    graph, weights = gb.finish()
+    be = Backend(0)
+    be.load_memory(graph, weights, state_bindings)
+    got = be.run(inputs)
+    want = GraphOracle(graph, weights, conv_impl).run(inputs)
+    return got, want, be
+
+
+# ------------------------------------------------------------ convolutions
+GEMM_SHAPES = [  # (OC, H, W, IC): reference shapes (OC, HW, IC) with HW = H*W
+    (136, 23, 40, 24), (136, 23, 40, 72), (136, 23, 40, 128), (128, 16, 16, 32), (8, 2, 4, 8), (256, 24, 40, 512),
+    # benchmark block-stack shapes
+    (256, 92, 160, 128), (128, 92, 160, 256), (512, 92, 160, 128), (64, 13, 17, 64),
+]
+
+
+@pytest.mark.parametrize("oc,h,w,ic", GEMM_SHAPES)
+@pytest.mark.parametrize("epilogue", [None, "leaky", "residual"])
+def test_conv1x1(oc, h, w, ic, epilogue):
+    x = lcg_fast(ic * h * w, 1).reshape(1, ic, h, w)
+    wt = lcg_fast(oc * ic, 2).reshape(oc, ic, 1, 1)
+    b = lcg_fast(oc, 3)
+    gb = conv_graph(x.shape, wt, b, epilogue=epilogue)
+    inputs = [x]
+    if epilogue == "residual":
+        inputs.append(lcg_fast(oc * h * w, 4).reshape(1, oc, h, w))
+    got, want, be = run_both(gb, inputs)
+    compare(got[0], want[0])
+    kernels = {s["kernel"] for s in be.steps()}
+    assert "mlvc_conv1x1_tc" in kernels, kernels
+
+
+@pytest.mark.parametrize("c,h,w", [(128, 92, 160), (64, 13, 17), (256, 8, 8)])
+def test_conv1x1_reglu(c, h, w):
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((1, c, h, w), dtype=np.float32).astype(np.float16)
+    wt = (rng.standard_normal((4 * c, c, 1, 1), dtype=np.float32) * np.sqrt(2.0 / c)).astype(np.float16)
+    b = rng.uniform(-0.1, 0.1, 4 * c).astype(np.float16)
+    gb = conv_graph(x.shape, wt, b, epilogue="reglu")
+    got, want, be = run_both(gb, [x])
+    compare(got[0], want[0])
+    steps = be.steps()
+    assert len([s for s in steps if s["kernel"] != "mlvc_transpose_f16"]) == 1, steps
+
+
+SPATIAL = [  # (IC, OC, stride, kernel, pad, H, W)
+    (24, 24, 1, 3, 1, 13, 17), (40, 264, 2, 3, 1, 13, 17), (8, 8, 2, 2, 0, 13, 17), (128, 256, 2, 2, 0, 13, 17),
+    (64, 64, 1, 3, 1, 13, 17), (64, 128, 2, 3, 1, 13, 17), (64, 64, 1, 3, 1, 46, 300), (128, 64, 1, 3, 1, 9, 140),
+    (64, 64, 1, 1, 0, 13, 17), (64, 96, 2, 3, 1, 24, 258),
+]
+
+
+@pytest.mark.parametrize("ic,oc,stride,k,pad,h,w", SPATIAL)
+def test_conv_spatial(ic, oc, stride, k, pad, h, w):
+    x = lcg_fast(ic * h * w, 5).reshape(1, ic, h, w)
+    wt = lcg_fast(oc * ic * k * k, 6).reshape(oc, ic, k, k)
+    b = lcg_fast(oc, 7)
+    gb = conv_graph(x.shape, wt, b, (stride, stride), (pad, pad))
+    got, want, be = run_both(gb, [x])
+    compare(got[0], want[0])
+    if ic % 64 == 0 and oc % 16 == 0 and k > 1:
+        assert "mlvc_convkxk_tc" in {s["kernel"] for s in be.steps()}
+
+
+@pytest.mark.parametrize("epilogue", ["leaky", "residual"])
+def test_conv3x3_fused(epilogue):
+    x = lcg_fast(64 * 20 * 33, 8).reshape(1, 64, 20, 33)
+    wt = lcg_fast(64 * 64 * 9, 9).reshape(64, 64, 3, 3)
+    b = lcg_fast(64, 10)
+    gb = conv_graph(x.shape, wt, b, (1, 1), (1, 1), epilogue=epilogue)
+    inputs = [x] + ([lcg_fast(64 * 20 * 33, 11).reshape(1, 64, 20, 33)] if epilogue == "residual" else [])
+    got, want, _ = run_both(gb, inputs)
+    compare(got[0], want[0])
+
+
+def test_conv3x3_config1_full():
+    """Config 1 at its real size (3x3 64->64 @ 184x320), FP32-GEMM oracle."""
+    from mlvc_b200.graph import build_conv3x3
+    gb, inputs = build_conv3x3(0)
+    got, want, be = run_both(gb, inputs, conv_impl="gemm")
+    compare(got[0], want[0])
+    assert "mlvc_convkxk_tc" in {s["kernel"] for s in be.steps()}
+
+
+@pytest.mark.parametrize("c,h,w,stride", [(256, 92, 160, 1), (64, 13, 17, 1), (64, 13, 17, 2), (24, 7, 9, 1)])
+def test_depthwise(c, h, w, stride):
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((1, c, h, w), dtype=np.float32).astype(np.float16)
+    wt = (rng.standard_normal((c, 1, 3, 3), dtype=np.float32) * 0.3).astype(np.float16)
+    b = rng.uniform(-0.1, 0.1, c).astype(np.float16)
+    gb = conv_graph(x.shape, wt, b, (stride, stride), (1, 1), groups=c)
+    got, want, _ = run_both(gb, [x])
+    compare(got[0], want[0])
+
+
+def test_grouped_conv():
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((1, 12, 9, 10), dtype=np.float32).astype(np.float16)
+    wt = (rng.standard_normal((6, 4, 3, 3), dtype=np.float32) * 0.3).astype(np.float16)
+    gb = conv_graph(x.shape, wt, None, (1, 1), (1, 1), groups=3)
+    got, want, _ = run_both(gb, [x])
+    compare(got[0], want[0])
+
+
+def test_conv_rgb_input():
+    """IC = 3 (the codec's first conv) takes the direct fallback."""
+    rng = np.random.default_rng(5)
+    x = rng.random((1, 3, 16, 24), dtype=np.float32).astype(np.float16)
+    wt = (rng.standard_normal((32, 3, 3, 3), dtype=np.float32) * 0.3).astype(np.float16)
+    b = rng.uniform(-0.1, 0.1, 32).astype(np.float16)
+    gb = conv_graph(x.shape, wt, b, (2, 2), (1, 1))
+    got, want, _ = run_both(gb, [x])
+    compare(got[0], want[0])
+
+
+# ---------------------------------------------------- elementwise / layout
+def _rand(shape, seed, scale=1.0):
+    return (np.random.default_rng(seed).standard_normal(shape, dtype=np.float32) * scale).astype(np.float16)
+
+
+@pytest.mark.parametrize("op", ["add", "sub", "mul"])
+@pytest.mark.parametrize("bshape", [(1, 24, 6, 10), (1, 24, 1, 1), (1, 1, 6, 10), (1,), (24, 1, 1)])
+def test_binary(op, bshape):
+    gb = GraphBuilder()
+    a = gb.input("a", [1, 24, 6, 10])
+    if bshape == (1, 24, 6, 10):
+        b = gb.input("b", list(bshape))
+        inputs = [_rand((1, 24, 6, 10), 1), _rand(bshape, 2)]
+    else:
+        b = gb.weight("b", _rand(bshape, 2))
+        inputs = [_rand((1, 24, 6, 10), 1)]
+    gb.output(getattr(gb, op)(a, b), "y")
+    got, want, _ = run_both(gb, inputs)
+    bits_equal(got[0], want[0])
+
+
+@pytest.mark.parametrize("op", ["LeakyRelu", "Clip", "Sigmoid", "Reciprocal", "Round"])
+def test_unary(op):
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 16, 9, 11])
+    if op == "LeakyRelu":
+        y = gb.leaky_relu(x, 0.2)
+    elif op == "Clip":
+        y = gb.clip(x, -0.5, 0.75)
+    else:
+        y = gb.unary(op, x)
+    gb.output(y, "y")
+    inputs = [_rand((1, 16, 9, 11), 3, 4.0)]
+    got, want, _ = run_both(gb, inputs)
+    if op == "Sigmoid":  # expf may differ by an FP32 ulp between libm and CUDA
+        compare(got[0], want[0], max_abs=1e-3, rel_l2=1e-3)
+    else:
+        bits_equal(got[0], want[0])
+
+
+def test_slice_concat_gather():
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 32, 8, 12])
+    q = gb.input("q", [1], "int32")
+    table = gb.weight("table", _rand((5, 32, 1, 1), 9))
+    s1 = gb.slice(x, 1, 8, 24)            # channel slice
+    s2 = gb.slice(x, 3, 1, 12, 2)         # strided width slice
+    s3 = gb.slice(x, 2, 0, 4)
+    cat = gb.concat([s1, gb.slice(x, 1, 0, 8)], 1)
+    scale = gb.gather(table, q)
+    y = gb.mul(x, scale)
+    gb.output(cat, "cat")
+    gb.output(s2, "s2")
+    gb.output(gb.concat([s3, s3], 2), "cat_h")
+    gb.output(y, "scaled")
+    inputs = [_rand((1, 32, 8, 12), 5), np.array([3], np.int32)]
+    got, want, _ = run_both(gb, inputs)
+    for g, w_ in zip(got, want):
+        bits_equal(g, w_)
+
+
+@pytest.mark.parametrize("factor", [2, 8])
+def test_pixel_shuffle_order(factor):
+    """Native CRD channel order, factors 2 and 8 (reference cutlass_kernel_tests.cpp:43-89):
+    unshuffle then shuffle must restore the input, and both match the oracle."""
+    c, h, w = 3, factor * 2, factor * 3
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, h, w])
+    u = gb.space_to_depth(x, factor)
+    gb.output(u, "unshuffled")
+    gb.output(gb.depth_to_space(u, factor), "restored")
+    inputs = [np.arange(c * h * w, dtype=np.float32).reshape(1, c, h, w).astype(np.float16)]
+    got, want, _ = run_both(gb, inputs)
+    bits_equal(got[0], want[0])
+    bits_equal(got[1], inputs[0])
+
+
+def test_reglu_standalone():
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 48, 5, 7])
+    g = gb.slice(x, 1, 0, 24)
+    lin = gb.slice(x, 1, 24, 48)
+    gb.output(gb.mul(gb.clip(g, 0.0, 1.0), lin), "y")
+    got, want, be = run_both(gb, [_rand((1, 48, 5, 7), 6)])
+    bits_equal(got[0], want[0])
+    assert "mlvc_reglu_f16" in {s["kernel"] for s in be.steps()}
+
+
+def test_state_binding_and_slots():
+    """State binding (reference backend.hpp:34-46): output `feature` feeds input
+    `ref` of the next run; reset_state zeroes it.  The slot path must give the
+    same numbers as run()."""
+    rng = np.random.default_rng(8)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 64, 6, 10])
+    ref = gb.input("ref", [1, 64, 6, 10])
+    w = gb.weight("w", (rng.standard_normal((64, 64, 1, 1), dtype=np.float32) * 0.1).astype(np.float16))
+    feat = gb.add(gb.conv(x, w), ref)
+    gb.output(gb.leaky_relu(feat, 0.1), "y")
+    gb.output(feat, "feature")
+    graph, weights = gb.finish()
+    be = Backend(0)
+    be.load_memory(graph, weights, [(1, 1)])
+    with pytest.raises(RuntimeError, match="reset_state"):
+        be.run([_rand((1, 64, 6, 10), 1)])
+    be.reset_state()
+    oracle = GraphOracle(graph, weights)
+    state = np.zeros((1, 64, 6, 10), np.float16)
+    frames = [_rand((1, 64, 6, 10), 10 + i) for i in range(3)]
+    outs = []
+    for f in frames:
+        (y,) = be.run([f])
+        want_y, want_feat = oracle.run([f, state])
+        compare(y, want_y)
+        state = want_feat
+        outs.append(y)
+    be.reset_state()
+    be.configure_slots(2)
+    for i, f in enumerate(frames):
+        slot = i % 2
+        be.slot_input(slot, 0)[...] = f
+        be.submit(slot)
+        be.wait_slot(slot)
+        bits_equal(be.slot_output(slot, 0), outs[i])
+
+
+def test_rejects_bad_input_shape():
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 8, 4, 4])
+    gb.output(gb.leaky_relu(x), "y")
+    graph, weights = gb.finish()
+    be = Backend(0)
+    be.load_memory(graph, weights)
+    with pytest.raises(RuntimeError, match="shape"):
+        be.run([np.zeros((1, 8, 4, 5), np.float16)])
