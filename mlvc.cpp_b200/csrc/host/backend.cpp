@@ -606,7 +606,8 @@ void Backend::plan()
                     halo_px = 128 + max_pair - px_min;
                 }
                 const int parities = stride;
-                const int halo_bytes = parities * 8 * KH * halo_px * 16;
+                const int chunk_bytes = static_cast<int>(align_up(static_cast<size_t>(KH) * halo_px * 16, 128));
+                const int halo_bytes = parities * 8 * chunk_bytes;
                 const int halo_stride = static_cast<int>(align_up(halo_bytes, 1024));
                 const bool halo_ok = halo_px <= 256 && (stride == 1 || IW >= 2);
                 int BN = 0, a_st = 0, b_st = 0, resident = 0;

@@ -34,6 +34,7 @@ constexpr int kMaxStages = 8;
 constexpr unsigned int kErrWaitProducer = 0x1u;
 constexpr unsigned int kErrWaitMma = 0x2u;
 constexpr unsigned int kErrWaitEpilogue = 0x4u;
+constexpr unsigned int kErrAlign = 0x8u;
 
 struct TcShared {
     uint64_t a_full[kMaxStages];
@@ -351,7 +352,12 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
     const int parities = p.stride;  // 1 or 2 halo views
     const int k_panels = p.in_c / 64;
     const int taps = p.kh * p.kw;
-    const uint32_t chunk_bytes = static_cast<uint32_t>(p.kh * p.halo_px * 16);  // LBO
+    // One chunk = kh rows x halo_px pixels x 16 bytes written by one TMA copy;
+    // chunk starts are padded to 128 bytes (the TMA destination alignment) and
+    // that padded stride is the descriptor's leading byte offset.
+    const uint32_t chunk_payload = static_cast<uint32_t>(p.kh * p.halo_px * 16);
+    const uint32_t chunk_bytes = (chunk_payload + 127u) & ~127u;  // LBO
+    const uint32_t halo_tx = static_cast<uint32_t>(parities * 8) * chunk_payload;
     const uint32_t halo_bytes = static_cast<uint32_t>(parities * 8) * chunk_bytes;
     const uint32_t halo_stride = (halo_bytes + 1023u) & ~1023u;
     const uint32_t b_panel_bytes = static_cast<uint32_t>(p.BN) * 128u;
@@ -390,8 +396,13 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
                 for (int kp = 0; kp < k_panels; ++kp) {
                     if (!mbar_wait(&sh->a_empty[as], aph ^ 1u, &sh->abort_flag, kErrWaitProducer))
                         break;
-                    mbar_arrive_expect_tx(&sh->a_full[as], halo_bytes);
                     uint8_t* dst = a_smem + static_cast<size_t>(as) * halo_stride;
+                    if (smem_u32(dst) & 127u) {  // never expected: refuse rather than fault
+                        atomicOr(&mlvc_b200_status, kErrAlign);
+                        sh->abort_flag = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&sh->a_full[as], halo_tx);
                     for (int q = 0; q < parities; ++q)
                         for (int j = 0; j < 8; ++j)
                             tma_load_3d(dst + (q * 8 + j) * chunk_bytes, q ? &p.map_a1 : &p.map_a0, &sh->a_full[as],

@@ -210,8 +210,7 @@ def test_pixel_shuffle_order(factor):
     c, h, w = 3, factor * 2, factor * 3
     gb = GraphBuilder()
     x = gb.input("x", [1, c, h, w])
-    u = gb.space_to_depth(x, factor)
-    gb.output(u, "unshuffled")
+    u = gb.output(gb.space_to_depth(x, factor), "unshuffled")
     gb.output(gb.depth_to_space(u, factor), "restored")
     inputs = [np.arange(c * h * w, dtype=np.float32).reshape(1, c, h, w).astype(np.float16)]
     got, want, _ = run_both(gb, inputs)
