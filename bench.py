@@ -1,0 +1,359 @@
+#!/usr/bin/env python3
+"""Throughput benchmark of the B200 FP16 conv-stack backend.
+
+Workload (the benchmark this backend is measured on
+at N=1): the 8-block depthwise residual stack, C=128 @ 92x160 between
+pixel_unshuffle(2) and pixel_shuffle(2), input [1, 32, 184, 320] FP16,
+Kaiming-normal weights and N(0, 1) input from seed 0 (synthetic: no
+checkpoints exist for this network).  One step = one frame through the stack.
+`--workload conv3x3` runs configs[0] (one 3x3 64->64 conv @ 184x320) instead.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N>1 runs under torchrun, one process and one independent backend per GPU (the
+stack has no cross-GPU exchange: frames of different streams are independent),
+timed on the device, max over ranks.  `--impl reference` times the reference's
+own CPU backend (compiled from its sources into oracle/_ref) on the host cores.
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT, ROOT / "mlvc.cpp_b200"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+from mlvc_b200.graph import build_block_stack, build_conv3x3  # noqa: E402
+
+METRIC = "conv-stack frames/s (config 2 block stack; stand-in for 1080p MLVC decode frames/s)"
+UNIT = "frames/s"
+FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def workload(name):
+    if name == "conv3x3":
+        gb, inputs = build_conv3x3(0)
+        desc = ("config1-conv3x3: one FP16 3x3 s1 p1 conv 64->64 @184x320, W~N(0,sqrt(2/576)), b~U(-0.1,0.1), "
+                "x~N(0,1), seed 0")
+        metric = METRIC.replace("config 2 block stack", "config 1 single 3x3 conv")
+    else:
+        gb, inputs = build_block_stack(0)
+        desc = ("config2-block-stack: pixel_unshuffle(2) -> 8 x [1x1 128->256 +LeakyReLU(0.01); dw3x3 256; "
+                "1x1 256->128 +residual; 1x1 128->512 -> ReGLU(clip[0,1]) -> 1x1 256->128 +residual] -> "
+                "pixel_shuffle(2); input [1,32,184,320] fp16 ~N(0,1); Kaiming-normal weights, seed 0")
+        metric = METRIC
+    graph, weights = gb.finish()
+    return graph, weights, inputs, desc, metric
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return d.get("hbm_gbs"), d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM traffic of the dominant kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "ncu_traffic.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text())
+        except ValueError:
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu_index)],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9 and f[1].replace(".", "").isdigit():
+                    rows.append(f)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# ------------------------------------------------------------------ CPU
+def reference_backend_frames_per_s(graph, weights, inputs, frames, warmup, threads):
+    """Times the reference CPU backend (oracle/_ref) running the same graph."""
+    from oracle.ref_backend import RefCpuBackend  # reference arm / CPU baseline only
+    with tempfile.TemporaryDirectory() as d:
+        part = Path(d) / "aot" / "stack"
+        part.mkdir(parents=True)
+        (part / "graph.pb").write_bytes(graph)
+        (part / "weights.bin").write_bytes(weights)
+        ref = RefCpuBackend(d, "stack", threads)
+        for _ in range(warmup):
+            ref.run(inputs)
+        times = []
+        for _ in range(frames):
+            t0 = time.perf_counter()
+            ref.run(inputs)
+            times.append(time.perf_counter() - t0)
+        ref.close()
+    return frames / sum(times), times
+
+
+def run_reference_arm(args, rank, world):
+    graph, weights, inputs, desc, metric = workload(args.workload)
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    fps, times = reference_backend_frames_per_s(graph, weights, inputs, args.steps, args.warmup, threads)
+    line = {
+        "impl": "reference", "metric": metric, "value": fps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": desc, "global_batch": 1, "parallelism": "cpu-threads"},
+        "cpu_baseline": {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": f"{args.steps} frames of the workload, reference backends/cpu (AVX2, fusion on)"},
+        "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU
+def run_b200_arm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from mlvc_b200 import Backend
+
+    torch.cuda.set_device(local_rank)
+    graph, weights, inputs, desc, metric = workload(args.workload)
+    be = Backend(local_rank)
+    be.load_memory(graph, weights)
+    outs = be.run(inputs)  # inputs now resident on the device
+    if not all(np.isfinite(o.astype(np.float32)).all() for o in outs):
+        raise RuntimeError("non-finite output")
+    stream = torch.cuda.ExternalStream(be.stream)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=f"cuda:{local_rank}")
+
+    def flush_l2():
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
+
+    for _ in range(args.warmup):
+        flush_l2()
+        be.enqueue()
+    be.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    be.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = vis.split(",")[local_rank] if vis else local_rank
+    with ClockSampler(gpu_index) as clocks:
+        for i in range(args.steps):
+            flush_l2()  # cold L2 at the start of every frame (untimed)
+            starts[i].record(stream)
+            be.enqueue()
+            ends[i].record(stream)
+        be.synchronize()
+    torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # ---- end to end through the public slot API: H2D + replay + D2H per frame
+    be.configure_slots(2)
+    in_bytes = sum(int(np.prod(s)) * np.dtype(d).itemsize for _, d, s in be.inputs)
+    out_bytes = sum(int(np.prod(s)) * np.dtype(d).itemsize for _, d, s in be.outputs)
+    for slot in range(2):
+        for k, arr in enumerate(inputs):
+            be.slot_input(slot, k)[...] = arr
+    for i in range(max(1, args.warmup)):
+        be.submit(i % 2)
+        be.wait_slot(i % 2)
+    e_st = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_en = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        slot = i % 2
+        flush_l2()
+        e_st[i].record(stream)
+        be.submit(slot)
+        e_en[i].record(stream)
+        be.wait_slot(slot)
+    torch.cuda.synchronize()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_st, e_en))
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * args.steps / (float(t.item()) / 1000.0)
+    # output still correct after the slot loop
+    first = be.slot_output((args.steps - 1) % 2, 0)
+    if not np.array_equal(first.view(np.uint16), outs[0].view(np.uint16)):
+        raise RuntimeError("slot path output differs from run()")
+
+    # ---- per-kernel timings: in-stack (warm) shares and cold-L2 launches
+    steps = be.steps()
+    warm = be.time_steps(20, 0)
+    cold = be.time_steps(10, FLUSH_BYTES)
+    per_kernel = {}
+    for s, w_ms, c_ms in zip(steps, warm, cold):
+        k = per_kernel.setdefault(s["kernel"], {"launches": 0, "warm_ms": 0.0, "cold_ms": 0.0, "bytes": 0.0,
+                                                "flops": 0.0})
+        k["launches"] += 1
+        k["warm_ms"] += w_ms
+        k["cold_ms"] += c_ms
+        k["bytes"] += s["bytes"]
+        k["flops"] += s["flops"]
+    total_warm = sum(v["warm_ms"] for v in per_kernel.values())
+    dom_name, dom = max(per_kernel.items(), key=lambda kv: kv[1]["warm_ms"])
+    hbm, tflops_peak, peak_kind = measured_peaks()
+    intensity = dom["flops"] / max(dom["bytes"], 1.0)
+    ridge = tflops_peak * 1e12 / (hbm * 1e9)
+    if intensity >= ridge:
+        achieved = dom["flops"] / (dom["cold_ms"] / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s"}
+    else:
+        achieved = dom["bytes"] / (dom["cold_ms"] / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_kind"] = peak_kind
+    roof["kernel"] = dom_name
+    roof["launches_per_step"] = dom["launches"]
+    roof["algorithmic_bytes_per_launch"] = dom["bytes"] / dom["launches"]
+    roof["algorithmic_flops_per_launch"] = dom["flops"] / dom["launches"]
+    roof["avg_launch_us_cold_l2"] = 1e3 * dom["cold_ms"] / dom["launches"]
+    roof["avg_launch_us_in_stack"] = 1e3 * dom["warm_ms"] / dom["launches"]
+    roof["share_in_stack"] = dom["warm_ms"] / total_warm
+    tr = ncu_traffic().get(args.workload, {}).get(dom_name)
+    roof["traffic"] = tr
+    kernels = {k: {"launches": v["launches"], "share": v["warm_ms"] / total_warm,
+                   "us_in_stack": 1e3 * v["warm_ms"], "us_cold_l2": 1e3 * v["cold_ms"],
+                   "tflops_cold": v["flops"] / (v["cold_ms"] / 1e3) / 1e12 if v["flops"] else 0.0,
+                   "gbs_cold": v["bytes"] / (v["cold_ms"] / 1e3) / 1e9}
+               for k, v in per_kernel.items()}
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": desc, "global_batch": world, "parallelism": f"replicas x{world} (no collective)",
+                       "l2": "flushed before every timed frame (256 MiB fill, untimed)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": in_bytes * world,
+                    "d2h_bytes_per_step": out_bytes * world,
+                    "path": "mlvc_b200 slot API: pinned H2D + graph replay + pinned D2H per frame"},
+            "gpu_launches": be.kernel_launches * args.steps,
+            "roofline": roof,
+            "kernels": kernels,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            try:
+                fps, times = reference_backend_frames_per_s(graph, weights, inputs, args.cpu_frames, 1, threads)
+                line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
+                                        "sample": f"{args.cpu_frames} frames of the same workload on the reference "
+                                                  f"backends/cpu (AVX2, fusion on), {sum(times):.1f} s"}
+            except Exception as e:  # reported, never silently replaced
+                line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
+                                        "sample": f"unavailable: {e}"}
+    be.close()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["block_stack", "conv3x3"], default="block_stack")
+    ap.add_argument("--cpu-frames", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local_rank}"))
+    line = run_b200_arm(args, rank, world, local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

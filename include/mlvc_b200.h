@@ -109,14 +109,16 @@ int mlvc_b200_wait_slot(mlvc_b200_backend* backend, size_t slot);
  * runs with steady_clock, codec/src/pipeline.cpp:341-415).  enqueue replays
  * the captured schedule on the backend's stream with the device-resident
  * inputs of the previous run; time_steps launches every step separately
- * between CUDA events and returns the mean milliseconds per step. */
+ * between CUDA events and returns the mean milliseconds per step (with
+ * flush_bytes > 0, each step is preceded by an untimed memset of that many
+ * bytes so it starts from a cold L2). */
 int mlvc_b200_enqueue(mlvc_b200_backend* backend);
 int mlvc_b200_synchronize(mlvc_b200_backend* backend);
 void* mlvc_b200_stream(const mlvc_b200_backend* backend);
 size_t mlvc_b200_step_count(const mlvc_b200_backend* backend);
 int mlvc_b200_step_info(const mlvc_b200_backend* backend, size_t index, const char** kernel, const char** nodes,
                         double* flops, double* bytes, uint32_t* grid, uint32_t* block, uint32_t* smem);
-int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, float* ms_per_step);
+int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, size_t flush_bytes, float* ms_per_step);
 int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend);
 size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend);
 

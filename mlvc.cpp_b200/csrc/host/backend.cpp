@@ -201,6 +201,7 @@ Backend::~Backend()
     weights_dev_.reset();
     prepped_dev_.reset();
     arena_dev_.reset();
+    flush_dev_.reset();
     input_dev_.clear();
     input_stage_dev_.clear();
     output_stage_dev_.clear();
@@ -1446,17 +1447,24 @@ void Backend::synchronize()
     check_status();
 }
 
-std::vector<float> Backend::time_steps(int iterations)
+std::vector<float> Backend::time_steps(int iterations, size_t flush_bytes)
 {
     if (offline_)
         throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
     ContextGuard guard(ctx_);
-    std::vector<Event> ev(steps_.size() + 1);
+    // With flush_bytes > 0 every step runs after a memset of a buffer larger
+    // than L2, i.e. from a cold cache, and only the step itself is timed.
+    if (flush_bytes && flush_dev_.bytes() < flush_bytes)
+        flush_dev_ = DeviceBuffer(flush_bytes);
+    std::vector<Event> ev(2 * steps_.size());
     std::vector<double> acc(steps_.size(), 0.0);
     for (int it = 0; it < iterations; ++it) {
-        check(cuEventRecord(ev[0].get(), stream_), "cuEventRecord");
         for (size_t k = 0; k < steps_.size(); ++k) {
             auto& st = steps_[k];
+            if (flush_bytes)
+                check(cuMemsetD8Async(flush_dev_.get(), static_cast<unsigned char>(it + k), flush_bytes, stream_),
+                      "cuMemsetD8Async(flush)");
+            check(cuEventRecord(ev[2 * k].get(), stream_), "cuEventRecord");
             if (st.type == Step::kCopy) {
                 check(cuMemcpyDtoDAsync(st.dst, st.src, st.bytes, stream_), "cuMemcpyDtoDAsync");
             } else {
@@ -1465,12 +1473,12 @@ std::vector<float> Backend::time_steps(int iterations)
                                      args, nullptr),
                       st.kernel.c_str());
             }
-            check(cuEventRecord(ev[k + 1].get(), stream_), "cuEventRecord");
+            check(cuEventRecord(ev[2 * k + 1].get(), stream_), "cuEventRecord");
         }
         check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
         for (size_t k = 0; k < steps_.size(); ++k) {
             float ms = 0.0f;
-            check(cuEventElapsedTime(&ms, ev[k].get(), ev[k + 1].get()), "cuEventElapsedTime");
+            check(cuEventElapsedTime(&ms, ev[2 * k].get(), ev[2 * k + 1].get()), "cuEventElapsedTime");
             acc[k] += ms;
         }
     }

@@ -81,7 +81,7 @@ public:
     // timing; optional per-step event timing.
     void enqueue();
     void synchronize();
-    std::vector<float> time_steps(int iterations);
+    std::vector<float> time_steps(int iterations, size_t flush_bytes);
     const std::vector<StepInfo>& steps() const { return step_info_; }
     int kernel_launches_per_run() const;
     CUstream stream() const { return stream_; }
@@ -120,7 +120,7 @@ private:
     std::vector<StepInfo> step_info_;
     std::vector<Slot> slots_;
 
-    DeviceBuffer weights_dev_, prepped_dev_, arena_dev_;
+    DeviceBuffer weights_dev_, prepped_dev_, arena_dev_, flush_dev_;
     std::vector<DeviceBuffer> input_dev_, input_stage_dev_, output_stage_dev_, state_dev_;
     std::vector<uint8_t> prepped_host_;
 

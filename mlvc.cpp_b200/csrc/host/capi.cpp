@@ -250,10 +250,10 @@ int mlvc_b200_step_info(const mlvc_b200_backend* backend, size_t index, const ch
     });
 }
 
-int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, float* ms_per_step)
+int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, size_t flush_bytes, float* ms_per_step)
 {
     return guarded([&] {
-        const auto t = require(backend).time_steps(iterations);
+        const auto t = require(backend).time_steps(iterations, flush_bytes);
         for (size_t i = 0; i < t.size(); ++i)
             ms_per_step[i] = t[i];
     });

@@ -67,7 +67,8 @@ EXPORTS = {
                              ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_double),
                              ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint32),
                              ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
-    "mlvc_b200_time_steps": ([ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)], ctypes.c_int),
+    "mlvc_b200_time_steps": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.POINTER(ctypes.c_float)],
+                             ctypes.c_int),
     "mlvc_b200_kernel_launches": ([ctypes.c_void_p], ctypes.c_int),
     "mlvc_b200_device_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
 }
@@ -233,10 +234,12 @@ class Backend:
                             grid=g.value, block=b.value, smem=s.value))
         return out
 
-    def time_steps(self, iterations=10):
+    def time_steps(self, iterations=10, flush_bytes=0):
+        """Mean ms per step, each step launched alone between CUDA events on the
+        backend's stream; flush_bytes > 0 flushes L2 before every step."""
         n = lib().mlvc_b200_step_count(self._h)
         buf = (ctypes.c_float * max(1, n))()
-        _check(lib().mlvc_b200_time_steps(self._h, iterations, buf))
+        _check(lib().mlvc_b200_time_steps(self._h, iterations, flush_bytes, buf))
         return list(buf[:n])
 
     @property

@@ -1,0 +1,88 @@
+"""ctypes driver for the reference's own CPU backend (oracle/_ref/libmlvc_ref_cpu.so).
+
+TEST INFRASTRUCTURE ONLY: the checker in tests/ and the timed reference arm
+and CPU baseline of bench.py.  The library is the reference's backends/cpu
+sources compiled unchanged (oracle/Makefile) plus ref_shim/, driven through
+the reference InferenceBackend contract (runtime/include/mlvc/runtime/
+backend.hpp:48-63): create -> load -> reset_state -> run.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "_ref" / "libmlvc_ref_cpu.so"
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"reference CPU backend not built: {LIB_PATH} (make -C oracle ref)")
+        L = ctypes.CDLL(str(LIB_PATH))
+        vp, cp, sz = ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t
+        L.mlvc_ref_create.restype = vp
+        L.mlvc_ref_create.argtypes = [cp, ctypes.c_int, cp, sz]
+        L.mlvc_ref_load.argtypes = [vp, cp, ctypes.c_int, vp, vp, vp, cp, sz]
+        L.mlvc_ref_reset_state.argtypes = [vp, cp, sz]
+        L.mlvc_ref_run.argtypes = [vp, ctypes.c_int, vp, vp, vp, vp, cp, sz]
+        L.mlvc_ref_output_count.argtypes = [vp]
+        L.mlvc_ref_output_info.restype = ctypes.c_int64
+        L.mlvc_ref_output_info.argtypes = [vp, ctypes.c_int, vp, vp, vp]
+        L.mlvc_ref_output_copy.argtypes = [vp, ctypes.c_int, vp, sz]
+        L.mlvc_ref_destroy.argtypes = [vp]
+        _lib = L
+    return _lib
+
+
+class RefCpuBackend:
+    def __init__(self, model_dir, part, threads=0, state_bindings=()):
+        L = lib()
+        err = ctypes.create_string_buffer(1024)
+        self._h = L.mlvc_ref_create(str(model_dir).encode(), int(threads), err, 1024)
+        if not self._h:
+            raise RuntimeError(err.value.decode())
+        n = len(state_bindings)
+        si = (ctypes.c_uint64 * max(1, n))(*[b[0] for b in state_bindings])
+        so = (ctypes.c_uint64 * max(1, n))(*[b[1] for b in state_bindings])
+        shapes = (ctypes.c_int64 * max(4, 4 * n))(*[d for b in state_bindings for d in b[2]])
+        if L.mlvc_ref_load(self._h, part.encode(), n, si, so, shapes, err, 1024) != 0:
+            raise RuntimeError(err.value.decode())
+        if n and L.mlvc_ref_reset_state(self._h, err, 1024) != 0:
+            raise RuntimeError(err.value.decode())
+
+    def run(self, inputs):
+        L = lib()
+        arrs = [np.ascontiguousarray(a) for a in inputs]
+        n = len(arrs)
+        data = (ctypes.c_void_p * max(1, n))(*[a.ctypes.data for a in arrs])
+        dts = (ctypes.c_int * max(1, n))(*[0 if a.dtype == np.float16 else 1 for a in arrs])
+        ranks = (ctypes.c_int * max(1, n))(*[a.ndim for a in arrs])
+        flat = [d for a in arrs for d in a.shape]
+        shapes = (ctypes.c_int64 * max(1, len(flat)))(*flat)
+        err = ctypes.create_string_buffer(1024)
+        if L.mlvc_ref_run(self._h, n, data, dts, ranks, shapes, err, 1024) != 0:
+            raise RuntimeError(err.value.decode())
+        outs = []
+        for i in range(L.mlvc_ref_output_count(self._h)):
+            dt, rk, s4 = ctypes.c_int(), ctypes.c_int(), (ctypes.c_int64 * 4)()
+            nb = L.mlvc_ref_output_info(self._h, i, ctypes.byref(dt), ctypes.byref(rk), s4)
+            o = np.empty(tuple(s4[:rk.value]), np.float16 if dt.value == 0 else np.int32)
+            L.mlvc_ref_output_copy(self._h, i, o.ctypes.data, nb)
+            outs.append(o)
+        return outs
+
+    def close(self):
+        if self._h:
+            lib().mlvc_ref_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
