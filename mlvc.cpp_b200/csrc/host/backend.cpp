@@ -1291,6 +1291,41 @@ size_t Backend::device_bytes() const
     return t;
 }
 
+bool Backend::read_value(const std::string& name, void* dst, size_t bytes)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    for (size_t id = 1; id < values_.size(); ++id) {
+        const Value& v = values_[id];
+        if (!v.present || graph_.tensors[id].name != name)
+            continue;
+        if (!v.addr || v.kind == Value::kNone)
+            return false;
+        if (bytes < v.bytes)
+            throw std::runtime_error("mlvc-b200: read_value buffer too small");
+        ContextGuard guard(ctx_);
+        check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
+        std::vector<uint8_t> tmp(v.bytes);
+        const bool staged = v.kind == Value::kInput && v.nhwc && !input_stage_dev_.empty();
+        (void)staged;
+        check(cuMemcpyDtoH(tmp.data(), v.addr, v.bytes), "cuMemcpyDtoH(read_value)");
+        const auto d = dims4(v.shape);
+        if (v.nhwc && d[1] > 1 && d[2] * d[3] > 1) {  // NHWC -> NCHW
+            const auto* src = reinterpret_cast<const uint16_t*>(tmp.data());
+            auto* out = static_cast<uint16_t*>(dst);
+            const long long C = d[1], HW = d[2] * d[3];
+            for (long long n = 0; n < d[0]; ++n)
+                for (long long p = 0; p < HW; ++p)
+                    for (long long c = 0; c < C; ++c)
+                        out[(n * C + c) * HW + p] = src[(n * HW + p) * C + c];
+        } else {
+            std::memcpy(dst, tmp.data(), v.bytes);
+        }
+        return true;
+    }
+    throw std::runtime_error("mlvc-b200: no tensor named " + name);
+}
+
 void Backend::check_status()
 {
     unsigned int status = 0;

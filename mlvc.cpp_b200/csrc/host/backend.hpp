@@ -87,6 +87,11 @@ public:
     CUstream stream() const { return stream_; }
     CUcontext context() const { return ctx_; }
     size_t device_bytes() const;
+    // Copies a tensor the last run materialised on the device (graph inputs,
+    // outputs and every intermediate a step wrote; chain-internal values of a
+    // fused step are never materialised) to host memory in NCHW order.
+    // Returns false when the tensor does not exist on the device.
+    bool read_value(const std::string& name, void* dst, size_t bytes);
 
 private:
     struct Value;

@@ -264,6 +264,17 @@ int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend)
     return backend && backend->impl ? backend->impl->kernel_launches_per_run() : -1;
 }
 
+int mlvc_b200_read_tensor(mlvc_b200_backend* backend, const char* name, void* dst, size_t bytes, int* found)
+{
+    return guarded([&] {
+        if (!name || !dst)
+            throw std::runtime_error("mlvc-b200: null argument");
+        const bool ok = require(backend).read_value(name, dst, bytes);
+        if (found)
+            *found = ok ? 1 : 0;
+    });
+}
+
 size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend)
 {
     return backend && backend->impl ? backend->impl->device_bytes() : 0;

@@ -71,6 +71,8 @@ EXPORTS = {
                              ctypes.c_int),
     "mlvc_b200_kernel_launches": ([ctypes.c_void_p], ctypes.c_int),
     "mlvc_b200_device_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
+    "mlvc_b200_read_tensor": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_size_t,
+                               ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
 }
 
 
@@ -245,6 +247,14 @@ class Backend:
     @property
     def kernel_launches(self):
         return lib().mlvc_b200_kernel_launches(self._h)
+
+    def read_tensor(self, name, shape, dtype=np.float16):
+        """NCHW copy of a tensor the last run materialised, or None when it only
+        exists inside a fused step."""
+        out = np.empty(shape, dtype)
+        found = ctypes.c_int(0)
+        _check(lib().mlvc_b200_read_tensor(self._h, name.encode(), out.ctypes.data, out.nbytes, ctypes.byref(found)))
+        return out if found.value else None
 
     @property
     def device_bytes(self):

@@ -81,3 +81,54 @@ def conv_graph(x_shape, w, b=None, stride=(1, 1), pad=(0, 0), groups=1, epilogue
         y = gb.mul(gb.clip(g, 0.0, 1.0), lin)
     gb.output(y, "y")
     return gb
+
+
+# FP16 spacing grows with magnitude (2^-7 at |x| = 8, 2^-5 at 32), so an
+# absolute bound only means something near unit scale.  The per-op contract
+# (max-abs 2e-2, rel-L2 1e-3 against FP32 accumulation) is applied with the
+# absolute bound scaled by max(1, |expected| / 8): 2e-2 at |x| <= 8, i.e.
+# about 2.5 FP16 ulps, and the same 2.5 ulps above.
+def compare_scaled(actual, expected, max_abs=MAX_ABS, rel_l2=REL_L2):
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    assert a.shape == e.shape, (a.shape, e.shape)
+    assert np.isfinite(a).all(), "non-finite output"
+    scale = np.maximum(1.0, np.abs(e) / 8.0)
+    err = float((np.abs(a - e) / scale).max()) if a.size else 0.0
+    rl = float(np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30))
+    assert err <= max_abs and rl <= rel_l2, f"scaled max-abs {err:.3g} (<= {max_abs}), rel-L2 {rl:.3g} (<= {rel_l2})"
+    return err, rl
+
+
+# Whole-graph limits when rounding differences compound through many layers:
+# the reference's own tensor conformance rule (docs/codec-compatibility.md:
+# FP16 tensors max-abs <= 0.25), scaled as above, with rel-L2 1e-3.
+STACK_MAX_ABS = 0.25
+
+
+def per_op_parity(backend, graph, weights, inputs, conv_impl="c"):
+    """Checks every tensor the GPU materialised against the oracle applied to the
+    GPU's own inputs of that step (so errors do not compound across steps).
+    Chain-internal values of fused steps are recomputed by the oracle from the
+    GPU's chain input.  Returns the number of checked tensors."""
+    from oracle.graph_oracle import GraphOracle
+    o = GraphOracle(graph, weights, conv_impl)
+    vals = dict(o.consts)
+    for tid, arr in zip(o.g.inputs, inputs):
+        vals[tid] = np.asarray(arr)
+    checked = 0
+    for node in o.g.nodes:
+        out_t = o.tensors[node.outputs[0]]
+        want = o._exec(node, vals, out_t)
+        dt = np.int32 if out_t.dtype == 2 else np.float16
+        got = backend.read_tensor(out_t.name, tuple(out_t.shape), dt)
+        if got is not None:
+            try:
+                compare_scaled(got, want)
+            except AssertionError as e:
+                raise AssertionError(f"node {out_t.name}: {e}") from None
+            vals[node.outputs[0]] = got
+            checked += 1
+        else:
+            vals[node.outputs[0]] = want
+    return checked
