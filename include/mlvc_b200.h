@@ -124,7 +124,10 @@ size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend);
 
 /* Debug dump of one named tensor of the last run, NCHW on the host: the
  * reference's --debug-dir tensor dumps (codec/src/pipeline.cpp:225-266).
- * *found is 0 for tensors that exist only inside a fused step. */
+ * Requires mlvc_b200_set_debug_tensors(backend, 1) before load, which keeps
+ * every materialised tensor in its own arena slot.  *found is 0 for tensors
+ * that exist only inside a fused step. */
+int mlvc_b200_set_debug_tensors(mlvc_b200_backend* backend, int enable);
 int mlvc_b200_read_tensor(mlvc_b200_backend* backend, const char* name, void* dst, size_t bytes, int* found);
 
 #ifdef __cplusplus

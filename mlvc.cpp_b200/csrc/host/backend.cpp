@@ -1147,6 +1147,10 @@ void Backend::build_schedule()
         if (v.kind == Value::kArena)
             v.last = total;
     }
+    if (keep_all_values_)
+        for (auto& v : values_)
+            if (v.kind == Value::kArena)
+                v.last = total;
     // Greedy first-fit arena over [first, last] intervals (256-byte slots).
     std::vector<uint32_t> order;
     for (size_t id = 1; id < values_.size(); ++id)
@@ -1291,10 +1295,19 @@ size_t Backend::device_bytes() const
     return t;
 }
 
+void Backend::set_keep_all_values(bool keep)
+{
+    if (loaded_)
+        throw std::runtime_error("mlvc-b200: debug tensor mode must be set before load()");
+    keep_all_values_ = keep;
+}
+
 bool Backend::read_value(const std::string& name, void* dst, size_t bytes)
 {
     if (offline_)
         throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    if (!keep_all_values_)
+        throw std::runtime_error("mlvc-b200: tensor read-back needs debug tensor mode (set before load)");
     for (size_t id = 1; id < values_.size(); ++id) {
         const Value& v = values_[id];
         if (!v.present || graph_.tensors[id].name != name)
@@ -1306,8 +1319,6 @@ bool Backend::read_value(const std::string& name, void* dst, size_t bytes)
         ContextGuard guard(ctx_);
         check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
         std::vector<uint8_t> tmp(v.bytes);
-        const bool staged = v.kind == Value::kInput && v.nhwc && !input_stage_dev_.empty();
-        (void)staged;
         check(cuMemcpyDtoH(tmp.data(), v.addr, v.bytes), "cuMemcpyDtoH(read_value)");
         const auto d = dims4(v.shape);
         if (v.nhwc && d[1] > 1 && d[2] * d[3] > 1) {  // NHWC -> NCHW

@@ -92,6 +92,9 @@ public:
     // fused step are never materialised) to host memory in NCHW order.
     // Returns false when the tensor does not exist on the device.
     bool read_value(const std::string& name, void* dst, size_t bytes);
+    // Before load(): give every materialised tensor its own arena slot so
+    // read_value() sees all of them after a run (costs memory; debug only).
+    void set_keep_all_values(bool keep);
 
 private:
     struct Value;
@@ -134,6 +137,7 @@ private:
     bool state_ready_ = false;
     bool loaded_ = false;
     bool offline_ = false;
+    bool keep_all_values_ = false;
 };
 
 }  // namespace mlvc_b200

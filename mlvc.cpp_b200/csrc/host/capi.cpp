@@ -264,6 +264,11 @@ int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend)
     return backend && backend->impl ? backend->impl->kernel_launches_per_run() : -1;
 }
 
+int mlvc_b200_set_debug_tensors(mlvc_b200_backend* backend, int enable)
+{
+    return guarded([&] { require(backend).set_keep_all_values(enable != 0); });
+}
+
 int mlvc_b200_read_tensor(mlvc_b200_backend* backend, const char* name, void* dst, size_t bytes, int* found)
 {
     return guarded([&] {

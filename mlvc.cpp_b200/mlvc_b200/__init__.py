@@ -71,6 +71,7 @@ EXPORTS = {
                              ctypes.c_int),
     "mlvc_b200_kernel_launches": ([ctypes.c_void_p], ctypes.c_int),
     "mlvc_b200_device_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
+    "mlvc_b200_set_debug_tensors": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
     "mlvc_b200_read_tensor": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_size_t,
                                ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
 }
@@ -103,14 +104,17 @@ def _np_dtype(code):
 class Backend:
     """One B200 backend instance bound to one device (BackendOptions::device_id)."""
 
-    def __init__(self, device_id: int = 0, plan_only_for=None):
+    def __init__(self, device_id: int = 0, plan_only_for=None, debug_tensors=False):
         """plan_only_for=(sm_count, smem_optin_bytes) creates a planning-only
-        instance that never touches a GPU (mlvc_b200_create_offline)."""
+        instance that never touches a GPU (mlvc_b200_create_offline).
+        debug_tensors keeps every intermediate readable with read_tensor()."""
         self._h = ctypes.c_void_p()
         if plan_only_for is None:
             _check(lib().mlvc_b200_create(device_id, ctypes.byref(self._h)))
         else:
             _check(lib().mlvc_b200_create_offline(int(plan_only_for[0]), int(plan_only_for[1]), ctypes.byref(self._h)))
+        if debug_tensors:
+            _check(lib().mlvc_b200_set_debug_tensors(self._h, 1))
         self._in, self._out = [], []
 
     def close(self):
