@@ -1230,15 +1230,21 @@ void Backend::build_schedule()
         if (!values_[id].addr)
             throw std::runtime_error("mlvc-b200: unresolved graph output address");
 
+    // The dynamic shared-memory limit is a property of the function, shared by
+    // every step that launches it: set it once to the largest request.
+    std::map<std::string, unsigned> smem_max;
+    for (const auto& st : steps_)
+        if (st.type == Step::kKernel)
+            smem_max[st.kernel] = std::max(smem_max[st.kernel], st.smem);
+    for (const auto& [name, bytes] : smem_max)
+        if (bytes > 48 * 1024)
+            check(cuFuncSetAttribute(fn(name.c_str()), CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                     static_cast<int>(bytes)),
+                  "cuFuncSetAttribute(smem)");
     step_info_.clear();
     for (auto& st : steps_) {
-        if (st.type == Step::kKernel) {
+        if (st.type == Step::kKernel)
             st.f = fn(st.kernel.c_str());
-            if (st.smem > 48 * 1024)
-                check(cuFuncSetAttribute(st.f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
-                                         static_cast<int>(st.smem)),
-                      "cuFuncSetAttribute(smem)");
-        }
         if (st.build)
             st.build(st);
         st.info.kernel = st.kernel;
