@@ -300,9 +300,12 @@ def _fp16(a):
     return np.asarray(a, np.float32).astype(np.float16)
 
 
-def kaiming_normal(rng, shape):
+def kaiming_normal(rng, shape, gain=np.sqrt(2.0)):
+    """He/Kaiming normal, fan-in mode: N(0, gain^2 / fan_in).  gain sqrt(2) is the
+    ReLU-family gain (torch.nn.init.kaiming_normal_ default); gain 1 is the
+    linear gain."""
     fan_in = int(np.prod(shape[1:]))
-    return _fp16(rng.standard_normal(shape, dtype=np.float32) * np.float32(np.sqrt(2.0 / fan_in)))
+    return _fp16(rng.standard_normal(shape, dtype=np.float32) * np.float32(gain / np.sqrt(fan_in)))
 
 
 def small_bias(rng, n):
@@ -326,7 +329,15 @@ def build_block_stack(seed=0, channels=128, height=92, width=160, blocks=8):
     """Config 2: pixel_unshuffle(2) -> `blocks` x [1x1 C->2C + LeakyReLU(0.01);
     depthwise 3x3 (2C); 1x1 2C->C + residual; 1x1 C->4C -> ReGLU (clip(gate, 0, 1)
     * linear) -> 1x1 2C->C + residual] -> pixel_shuffle(2).  Input [1, C/4, 2H, 2W]
-    ~ N(0, 1); Kaiming-normal weights; biases U(-0.1, 0.1)."""
+    ~ N(0, 1); biases U(-0.1, 0.1).
+
+    Kaiming-normal weights with the gain of the operator that follows each conv:
+    sqrt(2) for the expand conv (followed by LeakyReLU, the case He
+    initialisation is derived for), 1 for the convs feeding linear operators
+    (depthwise -> project, project/ffn_out -> residual add, ffn_in -> ReGLU).
+    With sqrt(2) everywhere the un-normalised residual stream grows about 6x in
+    variance per block and overflows FP16 (inf) inside block 7, which would make
+    the workload's output meaningless; with these gains it stays in range."""
     rng = np.random.default_rng(seed)
     c = channels
     gb = GraphBuilder()
@@ -334,15 +345,15 @@ def build_block_stack(seed=0, channels=128, height=92, width=160, blocks=8):
     h = gb.space_to_depth(x, 2)
     for i in range(blocks):
         p = f"block{i}."
-        w1 = gb.weight(p + "expand.weight", kaiming_normal(rng, (2 * c, c, 1, 1)))
+        w1 = gb.weight(p + "expand.weight", kaiming_normal(rng, (2 * c, c, 1, 1), np.sqrt(2.0)))
         b1 = gb.weight(p + "expand.bias", small_bias(rng, 2 * c))
-        wd = gb.weight(p + "dw.weight", kaiming_normal(rng, (2 * c, 1, 3, 3)))
+        wd = gb.weight(p + "dw.weight", kaiming_normal(rng, (2 * c, 1, 3, 3), 1.0))
         bd = gb.weight(p + "dw.bias", small_bias(rng, 2 * c))
-        w2 = gb.weight(p + "project.weight", kaiming_normal(rng, (c, 2 * c, 1, 1)))
+        w2 = gb.weight(p + "project.weight", kaiming_normal(rng, (c, 2 * c, 1, 1), 1.0))
         b2 = gb.weight(p + "project.bias", small_bias(rng, c))
-        w3 = gb.weight(p + "ffn_in.weight", kaiming_normal(rng, (4 * c, c, 1, 1)))
+        w3 = gb.weight(p + "ffn_in.weight", kaiming_normal(rng, (4 * c, c, 1, 1), 1.0))
         b3 = gb.weight(p + "ffn_in.bias", small_bias(rng, 4 * c))
-        w4 = gb.weight(p + "ffn_out.weight", kaiming_normal(rng, (c, 2 * c, 1, 1)))
+        w4 = gb.weight(p + "ffn_out.weight", kaiming_normal(rng, (c, 2 * c, 1, 1), 1.0))
         b4 = gb.weight(p + "ffn_out.bias", small_bias(rng, c))
         t = gb.leaky_relu(gb.conv(h, w1, b1), 0.01)
         t = gb.conv(t, wd, bd, (1, 1), (1, 1), groups=2 * c)

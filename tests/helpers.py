@@ -97,9 +97,14 @@ def compare_scaled(actual, expected, max_abs=MAX_ABS, rel_l2=REL_L2, magnitude=N
     assert np.isfinite(a).all(), "non-finite output"
     m = np.abs(e) if magnitude is None else np.maximum(np.abs(e), magnitude)
     scale = np.maximum(1.0, m / 8.0)
-    err = float((np.abs(a - e) / scale).max()) if a.size else 0.0
+    se = np.abs(a - e) / scale
+    err = float(se.max()) if a.size else 0.0
     rl = float(np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30))
-    assert err <= max_abs and rl <= rel_l2, f"scaled max-abs {err:.3g} (<= {max_abs}), rel-L2 {rl:.3g} (<= {rel_l2})"
+    if not (err <= max_abs and rl <= rel_l2):
+        i = np.unravel_index(int(np.argmax(se)), se.shape)
+        raise AssertionError(f"scaled max-abs {err:.3g} (<= {max_abs}), rel-L2 {rl:.3g} (<= {rel_l2}); "
+                             f"{int((se > max_abs).sum())} of {se.size} over; worst at {tuple(int(v) for v in i)}: "
+                             f"got {a[i]!r} want {e[i]!r} magnitude {m[i]!r}")
     return err, rl
 
 
@@ -133,7 +138,13 @@ def per_op_parity(backend, graph, weights, inputs, conv_impl="c"):
             try:
                 compare_scaled(got, want, magnitude=mag)
             except AssertionError as e:
-                raise AssertionError(f"node {out_t.name}: {e}") from None
+                ctx = ""
+                if node.op in (1, 2, 3):
+                    d = np.abs(got.astype(np.float64) - want.astype(np.float64))
+                    i = np.unravel_index(int(np.argmax(d)), d.shape)
+                    ctx = "; operands " + ", ".join(
+                        repr(np.broadcast_to(np.asarray(vals[k]), want.shape)[i]) for k in node.inputs)
+                raise AssertionError(f"node {out_t.name} (op {node.op}): {e}{ctx}") from None
             vals[node.outputs[0]] = got
             checked += 1
         else:
