@@ -128,6 +128,19 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+def replica_throughput(local_ms, steps, world, device="cpu"):
+    """Whole-job frames/s of `world` independent replicas that each ran `steps`
+    frames in `local_ms` device milliseconds: the slowest rank bounds the job
+    (max over ranks; needs an initialised process group when world > 1)."""
+    import torch
+    t = torch.tensor([float(local_ms)], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    return world * steps / (ms_max / 1000.0), ms_max
+
+
 # ------------------------------------------------------------------ CPU
 def reference_backend_frames_per_s(graph, weights, inputs, frames, warmup, threads):
     """Times the reference CPU backend (oracle/_ref) running the same graph."""
@@ -210,12 +223,7 @@ def run_b200_arm(args, rank, world, local_rank):
         be.synchronize()
     torch.cuda.synchronize()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local_rank}")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.barrier()
-    ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1000.0)
+    value, ms_max = replica_throughput(ms, args.steps, world, f"cuda:{local_rank}")
 
     # ---- end to end through the public slot API: H2D + replay + D2H per frame
     be.configure_slots(2)
@@ -240,10 +248,7 @@ def run_b200_arm(args, rank, world, local_rank):
         be.wait_slot(slot)
     torch.cuda.synchronize()
     e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_st, e_en))
-    t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = world * args.steps / (float(t.item()) / 1000.0)
+    e2e_value, _ = replica_throughput(e2e_ms, args.steps, world, f"cuda:{local_rank}")
     # output still correct after the slot loop
     first = be.slot_output((args.steps - 1) % 2, 0)
     if not np.array_equal(first.view(np.uint16), outs[0].view(np.uint16)):

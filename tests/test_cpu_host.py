@@ -1,0 +1,218 @@
+"""Host-side logic without a GPU: the graph wire format (builder <-> protobuf
+schema <-> the product's C++ decoder), graph validation errors, the C ABI
+surface, the planner's kernel routing and fusion decisions (planning-only
+backend), and the multi-replica throughput reduction over gloo ranks."""
+
+import os
+import re
+import socket
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import mlvc_b200
+from mlvc_b200 import Backend
+from mlvc_b200.graph import GraphBuilder, build_block_stack, build_conv3x3
+from oracle.graph_oracle import GraphOracle
+from oracle.wire_schema import parse_graph
+
+ROOT = Path(__file__).resolve().parents[1]
+GOLDEN = ROOT / "tests" / "golden"
+B200 = (148, 232448)  # SMs, opt-in shared memory per block
+
+
+def plan(graph, weights, target=B200):
+    be = Backend(plan_only_for=target)
+    be.load_memory(graph, weights)
+    return be
+
+
+# ------------------------------------------------------------- C ABI
+def test_c_abi_exports_every_declared_symbol():
+    header = (ROOT / "include" / "mlvc_b200.h").read_text()
+    names = set(re.findall(r"\b(mlvc_b200_[a-z0-9_]+)\s*\(", header))
+    assert len(names) >= 30
+    lib = mlvc_b200.lib()
+    for n in sorted(names):
+        assert hasattr(lib, n), n
+    assert lib.mlvc_b200_abi_version() == 1
+
+
+def test_library_has_no_link_time_driver_dependency():
+    import subprocess
+    out = subprocess.run(["ldd", str(mlvc_b200.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "libcuda" not in out and "libcudart" not in out
+
+
+@pytest.mark.skipif(os.path.exists("/dev/nvidiactl"), reason="a GPU driver is present")
+def test_create_without_driver_fails_loudly():
+    with pytest.raises(RuntimeError, match="cuInit"):
+        Backend(0)
+
+
+def test_planning_only_backend_refuses_execution():
+    gb, inputs = build_conv3x3(0, 64, 16, 24)
+    be = plan(*gb.finish())
+    with pytest.raises(RuntimeError, match="planning-only"):
+        be.run(inputs)
+
+
+# ------------------------------------------------------- wire format
+def test_builder_graph_parses_with_protobuf_schema():
+    gb, _ = build_block_stack(seed=0, channels=32, height=8, width=12, blocks=2)
+    graph, weights = gb.finish()
+    g = parse_graph(graph)
+    assert g.schema_version == 3 and len(g.checkpoint_sha256) == 32 and len(g.weights_sha256) == 32
+    assert g.arena_alignment == 256 and g.weights_bytes == len(weights)
+    ops = [n.op for n in g.nodes]
+    assert ops[0] == 14 and ops[-1] == 7 and ops.count(6) == 10
+    # every runtime value is born at its producing node
+    by_id = {t.id: t for t in g.tensors}
+    for i, n in enumerate(g.nodes):
+        assert by_id[n.outputs[0]].arena.birth == i
+
+
+@pytest.mark.parametrize("case", ["example_q", "block_stack_tiny", "spatial_convs"])
+def test_decoder_accepts_reference_compiled_graphs(case):
+    """Graphs emitted by the reference's own AOT compiler decode, validate and plan."""
+    d = GOLDEN / case / "aot" / "model"
+    be = plan((d / "graph.pb").read_bytes(), (d / "weights.bin").read_bytes())
+    o = GraphOracle.from_dir(GOLDEN / case, "model")
+    assert [n for n, _, _ in be.inputs] == o.input_names()
+    assert [n for n, _, _ in be.outputs] == o.output_names()
+    assert be.steps()
+
+
+def _corrupt(graph, mutate):
+    g = parse_graph(graph)
+    mutate(g)
+    return g.SerializeToString()
+
+
+BAD = {
+    "schema": lambda g: setattr(g, "schema_version", 2),
+    "provenance": lambda g: setattr(g, "weights_sha256", b"short"),
+    "arena alignment": lambda g: setattr(g, "arena_alignment", 128),
+    "tensor rank": lambda g: g.tensors[0].shape.extend([1, 1, 1, 1]),
+    "dilation": lambda g: [n.conv.dilations.__setitem__(0, 2) for n in g.nodes if n.op == 6][:1],
+    "asymmetric pad": lambda g: [n.conv.pads.__setitem__(0, 0) for n in g.nodes if n.op == 6][:1],
+    "unknown op": lambda g: setattr(g.nodes[0], "op", 15),
+    "birth": lambda g: setattr(g.tensors[[t.WhichOneof("storage") for t in g.tensors].index("arena")].arena,
+                               "birth", 7),
+    "empty outputs": lambda g: g.ClearField("outputs"),
+}
+
+
+@pytest.mark.parametrize("what", sorted(BAD))
+def test_decoder_rejects_malformed_graphs(what):
+    gb, _ = build_conv3x3(0, 64, 8, 8)
+    graph, weights = gb.finish()
+    bad = _corrupt(graph, BAD[what])
+    with pytest.raises(RuntimeError, match="invalid AOT graph"):
+        plan(bad, weights)
+
+
+def test_decoder_rejects_truncation_and_weight_size():
+    gb, _ = build_conv3x3(0, 64, 8, 8)
+    graph, weights = gb.finish()
+    with pytest.raises(RuntimeError, match="invalid AOT graph"):
+        plan(graph[: len(graph) // 2], weights)
+    with pytest.raises(RuntimeError, match="weights size"):
+        plan(graph, weights[:-2])
+
+
+def test_state_binding_validation():
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 8, 4, 4])
+    r = gb.input("ref", [1, 8, 4, 4])
+    gb.output(gb.add(x, r), "y")
+    graph, weights = gb.finish()
+    be = Backend(plan_only_for=B200)
+    with pytest.raises(RuntimeError, match="state binding"):
+        be.load_memory(graph, weights, [(5, 0)])
+
+
+# ----------------------------------------------------------- planner
+def _kernels(be):
+    return [s["kernel"] for s in be.steps()]
+
+
+def test_plan_block_stack_fuses_like_the_reference():
+    """Conv+LeakyReLU, Conv+Add and Conv+Slice+Slice+Clip+Mul collapse into the
+    tensor-core conv epilogue (fusion_registry.cpp:711-1036)."""
+    gb, _ = build_block_stack(seed=0)
+    be = plan(*gb.finish())
+    k = _kernels(be)
+    assert k.count("mlvc_conv1x1_tc") == 32
+    assert k.count("mlvc_depthwise_v8_f16") == 8
+    assert "mlvc_unary_f16" not in k and "mlvc_binary_same_f16" not in k and "mlvc_reglu_f16" not in k
+    nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_conv1x1_tc"]
+    assert "6-10" in nodes  # conv + slice + slice + clip + mul
+    flops = sum(s["flops"] for s in be.steps())
+    assert abs(flops - 39.13e9) / 39.13e9 < 0.01  # config-2 algorithmic FLOPs
+
+
+def test_plan_conv3x3_uses_halo_kernel():
+    gb, _ = build_conv3x3(0)
+    be = plan(*gb.finish())
+    steps = [s for s in be.steps() if s["kernel"] == "mlvc_convkxk_tc"]
+    assert len(steps) == 1 and steps[0]["flops"] == 4341104640.0
+    assert steps[0]["smem"] <= 232448
+
+
+@pytest.mark.parametrize("ic,oc,k,stride,expect", [
+    (64, 64, 3, 1, "mlvc_convkxk_tc"), (128, 256, 2, 2, "mlvc_convkxk_tc"), (64, 128, 3, 2, "mlvc_convkxk_tc"),
+    (24, 24, 3, 1, "mlvc_conv_direct_f16"), (3, 32, 3, 2, "mlvc_conv_direct_f16"),
+    (24, 136, 1, 1, "mlvc_conv1x1_tc"), (8, 8, 1, 1, "mlvc_conv1x1_tc"),
+])
+def test_plan_conv_routing(ic, oc, k, stride, expect):
+    gb = GraphBuilder()
+    x = gb.input("x", [1, ic, 13, 17])
+    w = gb.weight("w", np.zeros((oc, ic, k, k), np.float16))
+    gb.output(gb.conv(x, w, None, (stride, stride), ((k - 1) // 2 if stride == 1 else (1 if k == 3 else 0),) * 2), "y")
+    assert expect in _kernels(plan(*gb.finish()))
+
+
+def test_plan_smaller_smem_target_still_plans():
+    gb, _ = build_block_stack(seed=0, channels=128, height=23, width=40, blocks=1)
+    be = plan(*gb.finish(), target=(20, 100 * 1024))
+    assert all(s["smem"] <= 100 * 1024 for s in be.steps())
+
+
+# ------------------------------------------------- replicas over gloo
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _replica_rank(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import bench
+    # each rank is an independent replica: plan its own copy of the graph
+    gb, _ = build_block_stack(seed=0, channels=32, height=8, width=12, blocks=1)
+    be = plan(*gb.finish())
+    assert be.steps()
+    value, ms_max = bench.replica_throughput(10.0 * (rank + 1), 50, world)
+    q.put((rank, value, ms_max))
+    dist.destroy_process_group()
+
+
+def test_replica_throughput_gloo_two_ranks():
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_replica_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    for _, value, ms_max in res:
+        assert ms_max == 20.0  # max over ranks
+        assert value == pytest.approx(2 * 50 / 0.020)
