@@ -349,34 +349,83 @@ void Backend::plan()
     std::vector<size_t> prepped_for_weight;  // not used yet
     (void)prepped_for_weight;
 
-    // ---- input boundary: NCHW host layout -> device layout
+    // ---- boundary: NCHW host layout <-> NHWC device layout.  A SpaceToDepth
+    // that is the only consumer of a graph input, and a DepthToSpace that
+    // produces a graph output from a private tensor, are folded into the
+    // conversion kernel (one pass over the data instead of two).
+    std::vector<bool> absorbed(graph_.nodes.size(), false);
+    auto needs_conversion = [&](const Value& v) {
+        const auto d = dims4(v.shape);
+        return v.nhwc && d[1] > 1 && d[2] * d[3] > 1;
+    };
+    auto boundary_step = [&](uint32_t host_id, uint32_t dev_id, int r, bool to_host, size_t k) {
+        Step s;
+        s.kernel = "mlvc_boundary_f16";
+        s.info.kernel = s.kernel;
+        s.info.nodes = std::string(to_host ? "output:" : "input:") + graph_.tensors[host_id].name +
+                       (r > 1 ? (to_host ? "+depth_to_space" : "+space_to_depth") : "");
+        s.info.bytes = 2.0 * values_[host_id].bytes;
+        if (to_host)
+            s.reads = {dev_id};
+        else
+            s.writes = {dev_id};
+        const auto dd = dims4(values_[dev_id].shape);  // device tensor, logical NCHW extents
+        const int tiles_x = static_cast<int>((dd[3] + 31) / 32);
+        s.grid = static_cast<unsigned>(dd[0] * dd[2] * tiles_x);
+        s.block = 256;
+        s.smem = static_cast<unsigned>((dd[1] / (r * r)) * r * (32 * r + 1) * 2);
+        s.build = [this, dev_id, dd, r, to_host, k](Step& st) {
+            BoundaryParams p{};
+            const CUdeviceptr stage = to_host ? output_stage_dev_.at(k).get() : input_stage_dev_.at(k).get();
+            p.src = reinterpret_cast<const mlvc_half*>(to_host ? values_[dev_id].addr : stage);
+            p.dst = reinterpret_cast<mlvc_half*>(to_host ? stage : values_[dev_id].addr);
+            p.n = static_cast<int>(dd[0]);
+            p.c = static_cast<int>(dd[1]);
+            p.h = static_cast<int>(dd[2]);
+            p.w = static_cast<int>(dd[3]);
+            p.r = r;
+            p.to_host = to_host ? 1 : 0;
+            st.set(p);
+        };
+        return s;
+    };
     for (size_t k = 0; k < ext_inputs_.size(); ++k) {
         const uint32_t id = graph_.inputs[ext_inputs_[k]];
         const Value& v = values_[id];
-        const auto d = dims4(v.shape);
-        if (v.nhwc && d[1] > 1 && d[2] * d[3] > 1) {
-            Step s;
-            s.kernel = "mlvc_transpose_f16";
-            s.writes = {id};
-            s.info.nodes = "input:" + graph_.tensors[id].name;
-            s.info.bytes = 2.0 * v.bytes;
-            const size_t k_copy = k;
-            s.build = [this, id, d, k_copy](Step& st) {
-                CopyParams p{};
-                p.src = reinterpret_cast<const mlvc_half*>(input_stage_dev_.at(k_copy).get());
-                p.dst = reinterpret_cast<mlvc_half*>(values_[id].addr);
-                p.dims[0] = static_cast<int>(d[0]);
-                p.dims[1] = static_cast<int>(d[1]);
-                p.dims[2] = static_cast<int>(d[2] * d[3]);
-                p.ss[0] = p.ds[0] = d[1] * d[2] * d[3];
-                st.set(p);
-                st.grid = static_cast<unsigned>((d[2] * d[3] + 31) / 32);
-                st.grid_y = static_cast<unsigned>((d[1] + 31) / 32);
-                st.grid_z = static_cast<unsigned>(d[0]);
-                st.block = 32;
-                st.block_y = 8;
-            };
-            steps_.push_back(std::move(s));
+        if (!needs_conversion(v))
+            continue;
+        uint32_t dev_id = id;
+        int r = 1;
+        if (v.consumers == 1 && !v.graph_output) {
+            for (size_t j = 0; j < graph_.nodes.size(); ++j) {
+                const NodeDesc& n = graph_.nodes[j];
+                if (n.op == Op::kSpaceToDepth && n.inputs[0] == id && v.shape[2] % n.block == 0 &&
+                    v.shape[3] % n.block == 0) {
+                    absorbed[j] = true;
+                    dev_id = n.output;
+                    r = n.block;
+                }
+            }
+        }
+        steps_.push_back(boundary_step(id, dev_id, r, false, k));
+    }
+    std::vector<std::pair<uint32_t, int>> output_source(ext_outputs_.size(), {0, 1});
+    for (size_t k = 0; k < ext_outputs_.size(); ++k) {
+        const uint32_t id = graph_.outputs[ext_outputs_[k]];
+        output_source[k] = {id, 1};
+        if (!needs_conversion(values_[id]))
+            continue;
+        for (size_t j = 0; j < graph_.nodes.size(); ++j) {
+            const NodeDesc& n = graph_.nodes[j];
+            if (n.output != id || n.op != Op::kDepthToSpace)
+                continue;
+            const uint32_t t = n.inputs[0];
+            if (values_[t].nhwc && values_[t].consumers == 1 && !values_[t].graph_output &&
+                values_[t].kind != Value::kInput && values_[t].kind != Value::kState && values_[id].consumers == 0) {
+                absorbed[j] = true;
+                output_source[k] = {t, n.block};
+                absorbed_outputs_.push_back(id);
+            }
         }
     }
 
@@ -421,6 +470,10 @@ void Backend::plan()
 
     for (size_t i = 0; i < nodes.size();) {
         const NodeDesc& n = nodes[i];
+        if (absorbed[i]) {
+            ++i;
+            continue;
+        }
         if (n.op == Op::kConv) {
             const uint32_t x_id = n.inputs[0], w_id = n.inputs[1];
             const uint32_t b_id = n.inputs.size() > 2 ? n.inputs[2] : 0;
@@ -500,24 +553,40 @@ void Backend::plan()
                 const int K = IC, NN = (OC + 15) / 16 * 16;  // weight rows padded to a multiple of 16
                 const int k_panels = (K + 63) / 64;
                 const int m_tiles = (IH * IW + 127) / 128;
-                // Candidate N tiles: divide NN, fit the resident weight slice plus two A
-                // stages.  Take the largest one that still yields a tile per SM; else the
-                // smallest (>= 64) for the most parallelism.
+                // Candidate N tiles divide NN and keep the CTA's weight slice resident.
+                // Prefer a footprint that lets two CTAs share an SM (<= 113 KB of smem,
+                // 2 x BN TMEM columns <= 512): one CTA's epilogue then overlaps the
+                // other's loads and MMAs.  Among those, the largest BN that still
+                // gives one tile per SM; otherwise fall back to one CTA per SM.
+                constexpr int kTwoCtaSmem = 233472 / 2 - 1024;
                 std::vector<int> cands;
                 for (int bn = std::min(256, NN); bn >= 16; bn -= 16)
                     if (NN % bn == 0 && (!reglu || bn % 32 == 0) &&
                         header + k_panels * bn * 128 + 2 * 16384 <= smem_cap)
                         cands.push_back(bn);
-                int best = 0;
+                auto stages_for = [&](int bn, int cap) { return (cap - header - 1024 - k_panels * bn * 128) / 16384; };
+                int best = 0, ctas_per_sm = 1;
                 for (int bn : cands)
-                    if (m_tiles * (NN / bn) >= sm_count_) {
+                    if (bn <= 128 && stages_for(bn, kTwoCtaSmem) >= 2 && m_tiles * (NN / bn) >= sm_count_) {
                         best = bn;
+                        ctas_per_sm = 2;
                         break;
                     }
                 if (!best)
                     for (int bn : cands)
-                        if (bn >= 64 || bn == cands.front())
+                        if (bn <= 128 && stages_for(bn, kTwoCtaSmem) >= 2) {
                             best = bn;
+                            ctas_per_sm = 2;
+                            break;
+                        }
+                if (!best)
+                    for (int bn : cands)
+                        if (m_tiles * (NN / bn) >= sm_count_) {
+                            best = bn;
+                            break;
+                        }
+                if (!best && !cands.empty())
+                    best = cands.back() >= 64 ? cands.back() : cands.front();
                 if (best) {
                     const int BN = best, n_tiles = NN / BN;
                     std::vector<uint16_t> wp(static_cast<size_t>(NN) * K, 0), bp(NN, 0);
@@ -532,8 +601,11 @@ void Backend::plan()
                     }
                     const size_t w_off = prep(wp.data(), wp.size() * 2);
                     const size_t b_off = prep(bp.data(), bp.size() * 2);
-                    const int a_stages = std::min(8, (smem_cap - header - k_panels * BN * 128) / 16384);
-                    const int grid = n_tiles * std::max(1, std::min(m_tiles, sm_count_ / n_tiles));
+                    const int a_stages =
+                        std::min(8, ctas_per_sm == 2 ? stages_for(BN, kTwoCtaSmem)
+                                                     : (smem_cap - header - k_panels * BN * 128) / 16384);
+                    const int slots = sm_count_ * ctas_per_sm;
+                    const int grid = n_tiles * std::max(1, std::min(m_tiles, slots / n_tiles));
                     s.kernel = "mlvc_conv1x1_tc";
                     s.info.kernel = s.kernel;
                     s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 + 1024);
@@ -751,8 +823,14 @@ void Backend::plan()
                     for (int k = 0; k < KH * KW; ++k)
                         wp[static_cast<size_t>(k) * OC + c] = w[static_cast<size_t>(c) * KH * KW + k];
                 w_off = prep(wp.data(), wp.size() * 2);
-                s.kernel = "mlvc_depthwise_v8_f16";
-                work = static_cast<long long>(N) * OH * OW * (OC / 8);
+                const bool dw3 = KH == 3 && KW == 3 && SH == SW && (SH == 1 || SH == 2) && PH == PW && PH <= 1;
+                if (dw3) {
+                    s.kernel = "mlvc_depthwise3x3_f16";
+                    work = static_cast<long long>(N) * ((OH + 1) / 2) * OW * (OC / 8);
+                } else {
+                    s.kernel = "mlvc_depthwise_v8_f16";
+                    work = static_cast<long long>(N) * OH * OW * (OC / 8);
+                }
             } else {
                 std::vector<uint16_t> wp(static_cast<size_t>(OC) * KH * KW * ICG);
                 for (int o = 0; o < OC; ++o)
@@ -1073,33 +1151,9 @@ void Backend::plan()
     // ---- output boundary
     for (size_t k = 0; k < ext_outputs_.size(); ++k) {
         const uint32_t id = graph_.outputs[ext_outputs_[k]];
-        const Value& v = values_[id];
-        const auto d = dims4(v.shape);
-        if (v.nhwc && d[1] > 1 && d[2] * d[3] > 1) {
-            Step s;
-            s.kernel = "mlvc_transpose_f16";
-            s.info.kernel = s.kernel;
-            s.info.nodes = "output:" + graph_.tensors[id].name;
-            s.info.bytes = 2.0 * v.bytes;
-            s.reads = {id};
-            const size_t kk = k;
-            s.build = [this, id, d, kk](Step& st) {
-                CopyParams p{};
-                p.src = reinterpret_cast<const mlvc_half*>(values_[id].addr);
-                p.dst = reinterpret_cast<mlvc_half*>(output_stage_dev_.at(kk).get());
-                p.dims[0] = static_cast<int>(d[0]);
-                p.dims[1] = static_cast<int>(d[2] * d[3]);
-                p.dims[2] = static_cast<int>(d[1]);
-                p.ss[0] = p.ds[0] = d[1] * d[2] * d[3];
-                st.set(p);
-                st.grid = static_cast<unsigned>((d[1] + 31) / 32);
-                st.grid_y = static_cast<unsigned>((d[2] * d[3] + 31) / 32);
-                st.grid_z = static_cast<unsigned>(d[0]);
-                st.block = 32;
-                st.block_y = 8;
-            };
-            steps_.push_back(std::move(s));
-        }
+        if (!needs_conversion(values_[id]) && output_source[k].second == 1)
+            continue;
+        steps_.push_back(boundary_step(id, output_source[k].first, output_source[k].second, true, k));
     }
     for (const auto& b : bindings_) {
         const uint32_t out_id = graph_.outputs[b.output_index];
@@ -1142,6 +1196,8 @@ void Backend::build_schedule()
     }
     for (auto id : graph_.outputs) {
         Value& v = values_[id];
+        if (std::find(absorbed_outputs_.begin(), absorbed_outputs_.end(), id) != absorbed_outputs_.end())
+            continue;  // produced directly into its host staging buffer
         if (v.kind == Value::kNone)
             throw std::runtime_error("mlvc-b200: graph output is never produced");
         if (v.kind == Value::kArena)
@@ -1215,7 +1271,8 @@ void Backend::build_schedule()
         const uint32_t id = graph_.outputs[ext_outputs_[k]];
         const Value& v = values_[id];
         const auto d = dims4(v.shape);
-        const bool convert = v.nhwc && d[1] > 1 && d[2] * d[3] > 1;
+        const bool convert = (v.nhwc && d[1] > 1 && d[2] * d[3] > 1) ||
+                             std::find(absorbed_outputs_.begin(), absorbed_outputs_.end(), id) != absorbed_outputs_.end();
         output_stage_dev_.emplace_back(convert ? align_up(v.bytes, 256) : 0);
     }
     for (size_t id = 1; id < values_.size(); ++id) {
@@ -1225,9 +1282,9 @@ void Backend::build_schedule()
         else if (v.kind == Value::kWeight)
             v.addr = weights_dev_.get() + v.weight_off;
     }
-    // A graph input that is also a graph output is copied through the arena-less path.
     for (auto id : graph_.outputs)
-        if (!values_[id].addr)
+        if (!values_[id].addr &&
+            std::find(absorbed_outputs_.begin(), absorbed_outputs_.end(), id) == absorbed_outputs_.end())
             throw std::runtime_error("mlvc-b200: unresolved graph output address");
 
     // The dynamic shared-memory limit is a property of the function, shared by

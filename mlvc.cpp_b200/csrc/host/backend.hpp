@@ -122,6 +122,7 @@ private:
     std::vector<StateBinding> bindings_;
     std::vector<size_t> ext_inputs_;   // indices into graph_.inputs
     std::vector<size_t> ext_outputs_;  // indices into graph_.outputs
+    std::vector<uint32_t> absorbed_outputs_;  // outputs written straight into host staging
 
     std::vector<Value> values_;
     std::vector<Step> steps_;

@@ -158,6 +158,56 @@ extern "C" __global__ void mlvc_transpose_f16(const __grid_constant__ CopyParams
     }
 }
 
+// NCHW <-> NHWC with pixel (un)shuffle fused, through shared memory.  One
+// block handles one device row band: 32 device pixels of one row of the NHWC
+// tensor and all of its C*r*r channels, i.e. C*r rows x 32*r columns of the
+// NCHW tensor.  Global reads and writes are both contiguous runs.
+extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid_constant__ BoundaryParams p)
+{
+    extern __shared__ __align__(16) uint8_t dyn_smem[];
+    mlvc_half* tile = reinterpret_cast<mlvc_half*>(dyn_smem);  // [c][dy][32*r + 1]
+    const int r = p.r, rr = r * r, span = 32 * r, pitch = span + 1;
+    const int dh = p.h, dw = p.w, dc = p.c;         // device NHWC extents
+    const int hc = dc / rr, hh = dh * r, hw = dw * r; // host NCHW extents
+    const int tiles_x = (dw + 31) / 32;
+    const int band = blockIdx.x;
+    const int tx = band % tiles_x;
+    const int y = (band / tiles_x) % dh;
+    const long long n = band / (tiles_x * dh);
+    const int x0 = tx * 32, nx = min(32, dw - x0);
+    const int hx0 = x0 * r, hspan = nx * r;
+    // host side <-> tile: rows (c, dy), columns 0..hspan
+    const int host_elems = hc * r * hspan;
+    const int dev_elems = nx * dc;
+    if (!p.to_host) {
+        for (int e = threadIdx.x; e < host_elems; e += blockDim.x) {
+            const int col = e % hspan, row = e / hspan;  // row = c*r + dy
+            const int c = row / r, dy = row % r;
+            tile[row * pitch + col] = p.src[((n * hc + c) * hh + y * r + dy) * static_cast<long long>(hw) + hx0 + col];
+        }
+        __syncthreads();
+        mlvc_half* dst = p.dst + ((n * dh + y) * static_cast<long long>(dw) + x0) * dc;
+        for (int e = threadIdx.x; e < dev_elems; e += blockDim.x) {
+            const int k = e % dc, j = e / dc;  // device pixel j, channel k = c*r*r + dy*r + dx
+            const int c = k / rr, dy = (k % rr) / r, dx = k % r;
+            dst[e] = tile[(c * r + dy) * pitch + j * r + dx];
+        }
+    } else {
+        const mlvc_half* src = p.src + ((n * dh + y) * static_cast<long long>(dw) + x0) * dc;
+        for (int e = threadIdx.x; e < dev_elems; e += blockDim.x) {
+            const int k = e % dc, j = e / dc;
+            const int c = k / rr, dy = (k % rr) / r, dx = k % r;
+            tile[(c * r + dy) * pitch + j * r + dx] = src[e];
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < host_elems; e += blockDim.x) {
+            const int col = e % hspan, row = e / hspan;
+            const int c = row / r, dy = row % r;
+            p.dst[((n * hc + c) * hh + y * r + dy) * static_cast<long long>(hw) + hx0 + col] = tile[row * pitch + col];
+        }
+    }
+}
+
 extern "C" __global__ void mlvc_gather_rows_f16(const __grid_constant__ GatherParams p)
 {
     int row = p.index[0];
@@ -281,6 +331,104 @@ extern "C" __global__ void mlvc_depthwise_v8_f16(const __grid_constant__ DirectC
             o[k] = pack_h2(acc[2 * k], acc[2 * k + 1]);
         *reinterpret_cast<uint4*>(p.y + i * 8) = ov;
     }
+}
+
+// Depthwise 3x3 (stride 1 or 2, pad 0 or 1), specialised: each thread owns 8
+// consecutive channels (16 bytes) of kRows vertically adjacent output pixels.
+// All input vectors it needs ((kRows-1)*stride+3 rows x 3 columns) are loaded
+// up front, so the loads are in flight together instead of one tap at a time;
+// a warp covers 32 x 8 channels of one column, so every load is a contiguous
+// 512-byte row segment for C = 256.  Taps outside the image are skipped, and
+// the accumulation starts from the bias and runs in (ky, kx) order with FMA.
+template <int kStride>
+__device__ __forceinline__ void depthwise3x3_body(const DirectConvParams& p)
+{
+    constexpr int kRows = 2;
+    constexpr int kInRows = (kRows - 1) * kStride + 3;
+    const int cv = p.oc / 8;
+    const int strips = (p.oh + kRows - 1) / kRows;
+    const long long total = static_cast<long long>(p.n) * strips * p.ow * cv;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+        long long t = i;
+        const int c8 = static_cast<int>(t % cv) * 8;
+        t /= cv;
+        const int ox = static_cast<int>(t % p.ow);
+        t /= p.ow;
+        const int strip = static_cast<int>(t % strips);
+        const long long n = t / strips;
+        const int oy0 = strip * kRows;
+        const int iy0 = oy0 * kStride - p.ph, ix0 = ox * kStride - p.pw;
+        uint4 x[kInRows][3];
+#pragma unroll
+        for (int r = 0; r < kInRows; ++r)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int iy = iy0 + r, ix = ix0 + c;
+                x[r][c] = (iy >= 0 && iy < p.ih && ix >= 0 && ix < p.iw)
+                              ? *reinterpret_cast<const uint4*>(p.x + ((n * p.ih + iy) * p.iw + ix) * p.ic + c8)
+                              : make_uint4(0, 0, 0, 0);
+            }
+        float bias[8];
+        if (p.bias) {
+            const uint4 bv = *reinterpret_cast<const uint4*>(p.bias + c8);
+            const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                unpack_h2(bw[k], bias[2 * k], bias[2 * k + 1]);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                bias[k] = 0.0f;
+        }
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+            const int oy = oy0 + r;
+            if (oy >= p.oh)
+                break;
+            float acc[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                acc[k] = bias[k];
+#pragma unroll
+            for (int ky = 0; ky < 3; ++ky) {
+                const int iy = iy0 + r * kStride + ky;
+                if (iy < 0 || iy >= p.ih)
+                    continue;
+#pragma unroll
+                for (int kx = 0; kx < 3; ++kx) {
+                    const int ix = ix0 + kx;
+                    if (ix < 0 || ix >= p.iw)
+                        continue;
+                    const uint4 wt = __ldg(reinterpret_cast<const uint4*>(p.w + (ky * 3 + kx) * p.oc + c8));
+                    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&x[r * kStride + ky][kx]);
+                    const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wt);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        float x0, x1, w0, w1;
+                        unpack_h2(xw[k], x0, x1);
+                        unpack_h2(ww[k], w0, w1);
+                        acc[2 * k] = fmaf(x0, w0, acc[2 * k]);
+                        acc[2 * k + 1] = fmaf(x1, w1, acc[2 * k + 1]);
+                    }
+                }
+            }
+            uint4 ov;
+            uint32_t* o = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                o[k] = pack_h2(acc[2 * k], acc[2 * k + 1]);
+            *reinterpret_cast<uint4*>(p.y + ((n * p.oh + oy) * p.ow + ox) * p.oc + c8) = ov;
+        }
+    }
+}
+
+extern "C" __global__ void __launch_bounds__(256, 2) mlvc_depthwise3x3_f16(const __grid_constant__ DirectConvParams p)
+{
+    if (p.sh == 2)
+        depthwise3x3_body<2>(p);
+    else
+        depthwise3x3_body<1>(p);
 }
 
 // Generic grouped direct convolution (fallback for shapes the tensor-core

@@ -61,26 +61,37 @@ __device__ __forceinline__ uint32_t tmem_cols_for(int bn)
 
 // ----------------------------------------------------------- epilogue
 // One thread owns one output pixel (TMEM lane) of the tile and walks its
-// columns 16 at a time.
+// columns 32 at a time (one tcgen05.ld of 32 columns, one wait).  For the
+// residual epilogue the next chunk's residual is loaded from global memory
+// before the current chunk is processed, so its latency overlaps the work.
+__device__ __forceinline__ void load_residual32(const mlvc_half* res, int col, int n_valid, uint4 (&r)[4])
+{
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        r[q] = col + 8 * (q + 1) <= n_valid ? reinterpret_cast<const uint4*>(res)[q] : make_uint4(0, 0, 0, 0);
+}
+
 __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcShared& sh, uint32_t tmem_acc,
-                                              int quadrant, int lane, long long pixel, bool valid, int n_tile)
+                                              int quadrant, long long pixel, bool valid, int n_tile,
+                                              uint4 (&res_next)[4])
 {
     const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16);
     if (p.epilogue == kEpiReglu) {
         const int half = p.BN / 2;
         mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * half;
         for (int c0 = 0; c0 < half; c0 += 16) {
-            float g[16], l[16];
-            tmem_ld16(lane_addr + c0, g);
-            tmem_ld16(lane_addr + half + c0, l);
+            uint32_t gr[16], lr[16];
+            tmem_ld16_nowait(lane_addr + c0, gr);
+            tmem_ld16_nowait(lane_addr + half + c0, lr);
+            tmem_wait_ld();
             uint32_t packed[8];
 #pragma unroll
             for (int i = 0; i < 16; i += 2) {
                 float r2[2];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    const float gv = round_h(g[i + j] + sh.bias[c0 + i + j]);
-                    const float lv = round_h(l[i + j] + sh.bias[half + c0 + i + j]);
+                    const float gv = round_h(__uint_as_float(gr[i + j]) + sh.bias[c0 + i + j]);
+                    const float lv = round_h(__uint_as_float(lr[i + j]) + sh.bias[half + c0 + i + j]);
                     const float cg = round_h(fminf(fmaxf(gv, p.clip_lo), p.clip_hi));
                     r2[j] = cg * lv;
                 }
@@ -96,24 +107,29 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
     }
     mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * p.BN;
     const mlvc_half* res = p.residual ? p.residual + pixel * p.ldr + n_tile * p.BN : nullptr;
-    for (int c0 = 0; c0 < p.BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(lane_addr + c0, v);
+    const bool residual = p.epilogue == kEpiResidual && valid;
+    for (int c0 = 0; c0 < p.BN; c0 += 32) {
+        uint4 rc[4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-            v[i] = round_h(v[i] + sh.bias[c0 + i]);
+        for (int q = 0; q < 4; ++q)
+            rc[q] = res_next[q];
+        if (residual && c0 + 32 < p.BN)
+            load_residual32(res + c0 + 32, n_tile * p.BN + c0 + 32, p.n_valid, res_next);
+        uint32_t a[32];
+        tmem_ld32_nowait(lane_addr + c0, a);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            v[i] = round_h(__uint_as_float(a[i]) + sh.bias[c0 + i]);
         if (p.epilogue == kEpiLeaky) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
+            for (int i = 0; i < 32; ++i)
                 v[i] = v[i] < 0.0f ? round_h(v[i] * p.alpha) : v[i];
-        } else if (p.epilogue == kEpiResidual && valid) {
-            const uint4* r = reinterpret_cast<const uint4*>(res + c0);
-            const int col = n_tile * p.BN + c0;
-            const uint4 zero = make_uint4(0, 0, 0, 0);
-            const uint4 r0 = col + 8 <= p.n_valid ? r[0] : zero, r1 = col + 16 <= p.n_valid ? r[1] : zero;
-            const uint32_t rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+        } else if (residual) {
+            const uint32_t* rr = reinterpret_cast<const uint32_t*>(rc);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 16; ++i) {
                 float ra, rb;
                 unpack_h2(rr[i], ra, rb);
                 v[2 * i] += ra;
@@ -121,16 +137,16 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
             }
         }
         if (valid) {
-            uint32_t packed[8];
+            uint32_t packed[16];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < 16; ++i)
                 packed[i] = pack_h2(v[2 * i], v[2 * i + 1]);
             uint4* d = reinterpret_cast<uint4*>(dst + c0);
             const int col = n_tile * p.BN + c0;  // channels beyond n_valid are padding rows
-            if (col + 8 <= p.n_valid)
-                d[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            if (col + 16 <= p.n_valid)
-                d[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (col + 8 * (q + 1) <= p.n_valid)
+                    d[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
         }
     }
 }
@@ -148,9 +164,6 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
     asm volatile("bar.sync 1, 128;" ::: "memory");
     uint32_t acc = 0, acc_phase = 0;
     for (int t = first_tile; t < total_tiles; t += tile_step) {
-        if (!mbar_wait(&sh.tmem_full[acc], acc_phase, &sh.abort_flag, kErrWaitEpilogue))
-            return;
-        tc_fence_after();
         const int m_tile = t / p.n_tiles;
         const int row = quadrant * 32 + lane;
         long long pixel;
@@ -165,7 +178,15 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
             valid = ox < p.out_w;
             pixel = static_cast<long long>(oy) * p.out_w + ox;
         }
-        epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, lane, pixel, valid, n_tile);
+        // first residual chunk is fetched while the MMAs of this tile run
+        uint4 res_next[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                             make_uint4(0, 0, 0, 0)};
+        if (p.epilogue == kEpiResidual && valid)
+            load_residual32(p.residual + pixel * p.ldr + n_tile * p.BN, n_tile * p.BN, p.n_valid, res_next);
+        if (!mbar_wait(&sh.tmem_full[acc], acc_phase, &sh.abort_flag, kErrWaitEpilogue))
+            return;
+        tc_fence_after();
+        epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, pixel, valid, n_tile, res_next);
         tc_fence_before();
         mbar_arrive(&sh.tmem_empty[acc]);
         acc ^= 1u;
@@ -232,7 +253,7 @@ __device__ __forceinline__ void drain_armed(uint64_t* bars, const uint32_t* arme
 }
 
 // ===================================================== 1x1 conv (GEMM)
-extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_conv1x1_tc(const __grid_constant__ ConvTcParams p)
+extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const __grid_constant__ ConvTcParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
     // 1024-byte alignment for the swizzled operand tiles.

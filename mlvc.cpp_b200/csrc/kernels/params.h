@@ -111,6 +111,20 @@ struct PixelShuffleParams {
     long long count;
 };
 
+// Boundary conversion between the host's NCHW and the device's NHWC, fused
+// with pixel (un)shuffle by `r` (r = 1: plain layout conversion).  (n, h, w, c)
+// are the DEVICE tensor's NHWC extents; the host tensor is NCHW
+// [n][c/(r*r)][h*r][w*r].
+//   to_host = 0: device <- host, i.e. pixel_unshuffle(r) of the host tensor
+//   to_host = 1: host <- device, i.e. pixel_shuffle(r) of the device tensor
+struct BoundaryParams {
+    const mlvc_half* src;
+    mlvc_half* dst;
+    int n, h, w, c;
+    int r;
+    int to_host;
+};
+
 struct RegluParams {
     const mlvc_half* src;  // NHWC [P, 2C]
     mlvc_half* dst;        // NHWC [P, C]

@@ -145,7 +145,7 @@ def test_plan_block_stack_fuses_like_the_reference():
     be = plan(*gb.finish())
     k = _kernels(be)
     assert k.count("mlvc_conv1x1_tc") == 32
-    assert k.count("mlvc_depthwise_v8_f16") == 8
+    assert k.count("mlvc_depthwise3x3_f16") == 8
     assert "mlvc_unary_f16" not in k and "mlvc_binary_same_f16" not in k and "mlvc_reglu_f16" not in k
     nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_conv1x1_tc"]
     assert "6-10" in nodes  # conv + slice + slice + clip + mul
