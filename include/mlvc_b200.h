@@ -120,6 +120,14 @@ int mlvc_b200_step_info(const mlvc_b200_backend* backend, size_t index, const ch
                         double* flops, double* bytes, uint32_t* grid, uint32_t* block, uint32_t* smem);
 int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, size_t flush_bytes, float* ms_per_step);
 int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend);
+
+/* Phase trace of one tensor-core conv step: relaunches it once with
+ * %globaltimer stamps enabled; writes 16 stamps per CTA (CTA start, setup
+ * done, weights issued, weights landed, first activation panel, last MMA
+ * commit, first accumulator seen by the epilogue, epilogue done, exit; 0 =
+ * not reached) and the total count to *count. */
+int mlvc_b200_trace_step(mlvc_b200_backend* backend, size_t index, uint64_t* stamps, size_t capacity,
+                         size_t* count);
 size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend);
 
 /* Debug dump of one named tensor of the last run, NCHW on the host: the

@@ -20,6 +20,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstddef>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <limits>
@@ -550,7 +552,7 @@ void Backend::plan()
             const int smem_cap = max_smem_optin_ - 1024;  // slack for the in-kernel 1024-byte alignment
             if (tc_shape && is1x1) {
                 // ---- tcgen05 GEMM
-                const int K = IC, NN = (OC + 15) / 16 * 16;  // weight rows padded to a multiple of 16
+                const int K = IC, NN = (OC + 31) / 32 * 32;  // weight rows padded to a multiple of 32
                 const int k_panels = (K + 63) / 64;
                 const int m_tiles = (IH * IW + 127) / 128;
                 // Candidate N tiles divide NN and keep the CTA's weight slice resident.
@@ -560,8 +562,8 @@ void Backend::plan()
                 // gives one tile per SM; otherwise fall back to one CTA per SM.
                 constexpr int kTwoCtaSmem = 233472 / 2 - 1024;
                 std::vector<int> cands;
-                for (int bn = std::min(256, NN); bn >= 16; bn -= 16)
-                    if (NN % bn == 0 && (!reglu || bn % 32 == 0) &&
+                for (int bn = std::min(256, NN); bn >= 32; bn -= 32)  // the epilogue walks 32 columns
+                    if (NN % bn == 0 && (!reglu || bn % 64 == 0) &&
                         header + k_panels * bn * 128 + 2 * 16384 <= smem_cap)
                         cands.push_back(bn);
                 auto stages_for = [&](int bn, int cap) { return (cap - header - 1024 - k_panels * bn * 128) / 16384; };
@@ -609,7 +611,7 @@ void Backend::plan()
                     s.kernel = "mlvc_conv1x1_tc";
                     s.info.kernel = s.kernel;
                     s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 + 1024);
-                    s.block = 192;
+                    s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     const int M = IH * IW;
                     s.build = [=, this](Step& st) {
@@ -664,7 +666,7 @@ void Backend::plan()
                     continue;
                 }
             }
-            if (tc_shape && IC % 64 == 0 && OC % 16 == 0 && !is1x1 && !reglu && (SH == 1 || SH == 2) && SH == SW &&
+            if (tc_shape && IC % 64 == 0 && OC % 32 == 0 && !is1x1 && !reglu && (SH == 1 || SH == 2) && SH == SW &&
                 KH <= 8 && KW <= 8 &&
                 PH == PW && PW < KW && OW >= 1) {
                 // ---- tcgen05 implicit GEMM with halo tiles
@@ -684,7 +686,7 @@ void Backend::plan()
                 const int halo_stride = static_cast<int>(align_up(halo_bytes, 1024));
                 const bool halo_ok = halo_px <= 256 && (stride == 1 || IW >= 2);
                 int BN = 0, a_st = 0, b_st = 0, resident = 0;
-                for (int bn = std::min(256, OC); halo_ok && bn >= 16 && !BN; bn -= 16) {
+                for (int bn = std::min(256, OC); halo_ok && bn >= 32 && !BN; bn -= 32) {
                     if (OC % bn)
                         continue;
                     const int bpanel = bn * 128;
@@ -721,7 +723,7 @@ void Backend::plan()
                     s.kernel = "mlvc_convkxk_tc";
                     s.info.kernel = s.kernel;
                     s.smem = static_cast<unsigned>(header + b_slots * BN * 128 + a_st * halo_stride + 1024);
-                    s.block = 192;
+                    s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     s.build = [=, this](Step& st) {
                         ConvTcParams p{};
@@ -824,9 +826,13 @@ void Backend::plan()
                         wp[static_cast<size_t>(k) * OC + c] = w[static_cast<size_t>(c) * KH * KW + k];
                 w_off = prep(wp.data(), wp.size() * 2);
                 const bool dw3 = KH == 3 && KW == 3 && SH == SW && (SH == 1 || SH == 2) && PH == PW && PH <= 1;
-                if (dw3) {
+                if (dw3 && OC / 8 <= 256) {
                     s.kernel = "mlvc_depthwise3x3_f16";
-                    work = static_cast<long long>(N) * ((OH + 1) / 2) * OW * (OC / 8);
+                    work = 0;
+                    const int per_block = 256 / (OC / 8);
+                    s.grid = static_cast<unsigned>((OW + per_block - 1) / per_block);
+                    s.grid_y = static_cast<unsigned>((OH + 1) / 2);
+                    s.grid_z = static_cast<unsigned>(N);
                 } else {
                     s.kernel = "mlvc_depthwise_v8_f16";
                     work = static_cast<long long>(N) * OH * OW * (OC / 8);
@@ -845,7 +851,8 @@ void Backend::plan()
             }
             const size_t b_off = prep(bias_full.data(), bias_full.size() * 2);
             s.info.kernel = s.kernel;
-            s.grid = blocks_for(work, 256, sm_count_);
+            if (work)
+                s.grid = blocks_for(work, 256, sm_count_);
             s.build = [=, this](Step& st) {
                 DirectConvParams p = dp;
                 p.x = reinterpret_cast<const mlvc_half*>(values_[x_id].addr);
@@ -1314,14 +1321,39 @@ void Backend::build_schedule()
 
 void Backend::launch_steps(CUstream s)
 {
+    // Kernels are launched with programmatic stream serialisation: each one
+    // may start its prologue (barriers, TMEM, weight loads) while its
+    // predecessor drains, and waits in-kernel (griddepcontrol.wait) before it
+    // touches activations.  MLVC_B200_PDL=0 turns this off.
+    const char* env = std::getenv("MLVC_B200_PDL");
+    const bool pdl = !(env && env[0] == '0');
     for (auto& st : steps_) {
         if (st.type == Step::kCopy) {
             check(cuMemcpyDtoDAsync(st.dst, st.src, st.bytes, s), "cuMemcpyDtoDAsync");
             continue;
         }
         void* args[] = {st.params.data()};
-        check(cuLaunchKernel(st.f, st.grid, st.grid_y, st.grid_z, st.block, st.block_y, 1, st.smem, s, args, nullptr),
-              st.kernel.c_str());
+        if (!pdl) {
+            check(cuLaunchKernel(st.f, st.grid, st.grid_y, st.grid_z, st.block, st.block_y, 1, st.smem, s, args,
+                                 nullptr),
+                  st.kernel.c_str());
+            continue;
+        }
+        CUlaunchAttribute attr{};
+        attr.id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        attr.value.programmaticStreamSerializationAllowed = 1;
+        CUlaunchConfig cfg{};
+        cfg.gridDimX = st.grid;
+        cfg.gridDimY = st.grid_y;
+        cfg.gridDimZ = st.grid_z;
+        cfg.blockDimX = st.block;
+        cfg.blockDimY = st.block_y;
+        cfg.blockDimZ = 1;
+        cfg.sharedMemBytes = st.smem;
+        cfg.hStream = s;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        check(cuLaunchKernelEx(&cfg, st.f, args, nullptr), st.kernel.c_str());
     }
 }
 
@@ -1356,6 +1388,30 @@ size_t Backend::device_bytes() const
         for (const auto& b : *v)
             t += b.bytes();
     return t;
+}
+
+std::vector<uint64_t> Backend::trace_step(size_t index)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    Step& st = steps_.at(index);
+    if (st.kernel != "mlvc_conv1x1_tc" && st.kernel != "mlvc_convkxk_tc")
+        throw std::runtime_error("mlvc-b200: only tensor-core conv steps carry a phase trace");
+    ContextGuard guard(ctx_);
+    const size_t n = static_cast<size_t>(st.grid) * kTracePoints;
+    DeviceBuffer buf(n * sizeof(uint64_t));
+    check(cuMemsetD8(buf.get(), 0, buf.bytes()), "cuMemsetD8(trace)");
+    std::vector<uint8_t> params = st.params;
+    unsigned long long* ptr = reinterpret_cast<unsigned long long*>(buf.get());
+    std::memcpy(params.data() + offsetof(ConvTcParams, trace), &ptr, sizeof(ptr));
+    void* args[] = {params.data()};
+    check(cuLaunchKernel(st.f, st.grid, st.grid_y, st.grid_z, st.block, st.block_y, 1, st.smem, stream_, args, nullptr),
+          "cuLaunchKernel(trace)");
+    check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
+    std::vector<uint64_t> out(n);
+    check(cuMemcpyDtoH(out.data(), buf.get(), buf.bytes()), "cuMemcpyDtoH(trace)");
+    check_status();
+    return out;
 }
 
 void Backend::set_keep_all_values(bool keep)

@@ -92,6 +92,10 @@ public:
     // fused step are never materialised) to host memory in NCHW order.
     // Returns false when the tensor does not exist on the device.
     bool read_value(const std::string& name, void* dst, size_t bytes);
+    // Launches tensor-core conv step `index` once more with its phase trace
+    // enabled and returns kTracePoints %globaltimer stamps per CTA (0 = not
+    // reached).  Uses the device state of the last run.
+    std::vector<uint64_t> trace_step(size_t index);
     // Before load(): give every materialised tensor its own arena slot so
     // read_value() sees all of them after a run (costs memory; debug only).
     void set_keep_all_values(bool keep);

@@ -264,6 +264,19 @@ int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend)
     return backend && backend->impl ? backend->impl->kernel_launches_per_run() : -1;
 }
 
+int mlvc_b200_trace_step(mlvc_b200_backend* backend, size_t index, uint64_t* stamps, size_t capacity,
+                         size_t* count)
+{
+    return guarded([&] {
+        const auto t = require(backend).trace_step(index);
+        if (count)
+            *count = t.size();
+        if (stamps)
+            for (size_t i = 0; i < t.size() && i < capacity; ++i)
+                stamps[i] = t[i];
+    });
+}
+
 int mlvc_b200_set_debug_tensors(mlvc_b200_backend* backend, int enable)
 {
     return guarded([&] { require(backend).set_keep_all_values(enable != 0); });

@@ -91,6 +91,8 @@ MLVC_FWD(cuLaunchKernel,
           void** kernelParams, void** extra),
          (f, gridDimX, gridDimY, gridDimZ, blockDimX, blockDimY, blockDimZ, sharedMemBytes, hStream, kernelParams,
           extra))
+MLVC_FWD(cuLaunchKernelEx, (const CUlaunchConfig* config, CUfunction f, void** kernelParams, void** extra),
+         (config, f, kernelParams, extra))
 MLVC_FWD(cuStreamBeginCapture, (CUstream hStream, CUstreamCaptureMode mode), (hStream, mode))
 MLVC_FWD(cuStreamEndCapture, (CUstream hStream, CUgraph* phGraph), (hStream, phGraph))
 MLVC_FWD(cuGraphInstantiateWithFlags, (CUgraphExec * phGraphExec, CUgraph hGraph, unsigned long long flags),

@@ -35,6 +35,8 @@ __device__ __forceinline__ float binary_op(float a, float b, int op)
 // ------------------------------------------------------------- unary
 extern "C" __global__ void mlvc_unary_f16(const __grid_constant__ ElementwiseParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long vecs = p.count / 8;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < vecs; i += stride) {
@@ -57,6 +59,8 @@ extern "C" __global__ void mlvc_unary_f16(const __grid_constant__ ElementwisePar
 // Same-shape operands: 16-byte vectors.
 extern "C" __global__ void mlvc_binary_same_f16(const __grid_constant__ ElementwiseParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long vecs = p.count / 8;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < vecs; i += stride) {
@@ -82,6 +86,8 @@ extern "C" __global__ void mlvc_binary_same_f16(const __grid_constant__ Elementw
 // addressed through per-dimension strides (0 on broadcast dimensions).
 extern "C" __global__ void mlvc_binary_bcast_f16(const __grid_constant__ ElementwiseParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
         long long r = i;
@@ -100,6 +106,8 @@ extern "C" __global__ void mlvc_binary_bcast_f16(const __grid_constant__ Element
 // -------------------------------------------------------------- copies
 extern "C" __global__ void mlvc_strided_copy_f16(const __grid_constant__ CopyParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
         long long r = i;
@@ -118,6 +126,8 @@ extern "C" __global__ void mlvc_strided_copy_f16(const __grid_constant__ CopyPar
 // the innermost extent is a multiple of 8 and contiguous on both sides.
 extern "C" __global__ void mlvc_strided_copy_v8_f16(const __grid_constant__ CopyParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     const long long inner = p.dims[3] / 8;
     const long long total = p.count / 8;
@@ -138,6 +148,8 @@ extern "C" __global__ void mlvc_strided_copy_v8_f16(const __grid_constant__ Copy
 // through a 32x33 shared tile, both sides coalesced.
 extern "C" __global__ void mlvc_transpose_f16(const __grid_constant__ CopyParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     // dims: [images, rows, cols]; src is [rows][cols], dst is [cols][rows]
     __shared__ mlvc_half tile[32][33];
     const int rows = p.dims[1], cols = p.dims[2];
@@ -164,6 +176,8 @@ extern "C" __global__ void mlvc_transpose_f16(const __grid_constant__ CopyParams
 // NCHW tensor.  Global reads and writes are both contiguous runs.
 extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid_constant__ BoundaryParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     extern __shared__ __align__(16) uint8_t dyn_smem[];
     mlvc_half* tile = reinterpret_cast<mlvc_half*>(dyn_smem);  // [c][dy][32*r + 1]
     const int r = p.r, rr = r * r, span = 32 * r, pitch = span + 1;
@@ -210,6 +224,8 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid
 
 extern "C" __global__ void mlvc_gather_rows_f16(const __grid_constant__ GatherParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     int row = p.index[0];
     if (row < 0)
         row += p.rows;
@@ -225,6 +241,8 @@ extern "C" __global__ void mlvc_gather_rows_f16(const __grid_constant__ GatherPa
 // channel c reads input pixel (y / r, x / r) channel c*r*r + (y%r)*r + x%r.
 extern "C" __global__ void mlvc_depth_to_space_f16(const __grid_constant__ PixelShuffleParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const int r = p.r, oc = p.c / (r * r), ow = p.w * r, oh = p.h * r;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
@@ -244,6 +262,8 @@ extern "C" __global__ void mlvc_depth_to_space_f16(const __grid_constant__ Pixel
 // c*r*r + dy*r + dx of pixel (y, x) reads input pixel (y*r+dy, x*r+dx) channel c.
 extern "C" __global__ void mlvc_space_to_depth_f16(const __grid_constant__ PixelShuffleParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const int r = p.r, oh = p.h / r, ow = p.w / r, oc = p.c * r * r;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
@@ -262,6 +282,8 @@ extern "C" __global__ void mlvc_space_to_depth_f16(const __grid_constant__ Pixel
 // ------------------------------------------------------------- ReGLU
 extern "C" __global__ void mlvc_reglu_f16(const __grid_constant__ RegluParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long total = p.pixels * p.c;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
@@ -279,6 +301,8 @@ extern "C" __global__ void mlvc_reglu_f16(const __grid_constant__ RegluParams p)
 // loads of input and weights); weights are [kh*kw][C].  Requires C % 8 == 0.
 extern "C" __global__ void mlvc_depthwise_v8_f16(const __grid_constant__ DirectConvParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const int cv = p.oc / 8;
     const long long total = static_cast<long long>(p.n) * p.oh * p.ow * cv;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -335,10 +359,12 @@ extern "C" __global__ void mlvc_depthwise_v8_f16(const __grid_constant__ DirectC
 
 // Depthwise 3x3 (stride 1 or 2, pad 0 or 1), specialised: each thread owns 8
 // consecutive channels (16 bytes) of kRows vertically adjacent output pixels.
-// All input vectors it needs ((kRows-1)*stride+3 rows x 3 columns) are loaded
-// up front, so the loads are in flight together instead of one tap at a time;
-// a warp covers 32 x 8 channels of one column, so every load is a contiguous
-// 512-byte row segment for C = 256.  Taps outside the image are skipped, and
+// A block of 256 threads covers 256 / (C/8) adjacent output columns of one
+// row strip (grid: x = column groups, y = row strips, z = images), so all
+// index math is 32-bit and division-free in the inner loops.  All input
+// vectors a thread needs ((kRows-1)*stride+3 rows x 3 columns) are loaded up
+// front, so the loads are in flight together; a warp reads contiguous
+// channel runs of adjacent pixels.  Taps outside the image are skipped, and
 // the accumulation starts from the bias and runs in (ky, kx) order with FMA.
 template <int kStride>
 __device__ __forceinline__ void depthwise3x3_body(const DirectConvParams& p)
@@ -346,85 +372,82 @@ __device__ __forceinline__ void depthwise3x3_body(const DirectConvParams& p)
     constexpr int kRows = 2;
     constexpr int kInRows = (kRows - 1) * kStride + 3;
     const int cv = p.oc / 8;
-    const int strips = (p.oh + kRows - 1) / kRows;
-    const long long total = static_cast<long long>(p.n) * strips * p.ow * cv;
-    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
-        long long t = i;
-        const int c8 = static_cast<int>(t % cv) * 8;
-        t /= cv;
-        const int ox = static_cast<int>(t % p.ow);
-        t /= p.ow;
-        const int strip = static_cast<int>(t % strips);
-        const long long n = t / strips;
-        const int oy0 = strip * kRows;
-        const int iy0 = oy0 * kStride - p.ph, ix0 = ox * kStride - p.pw;
-        uint4 x[kInRows][3];
+    const int per_block = blockDim.x / cv;
+    const int c8 = (threadIdx.x % cv) * 8;
+    const int ox = blockIdx.x * per_block + threadIdx.x / cv;
+    if (threadIdx.x >= per_block * cv || ox >= p.ow)
+        return;
+    const int oy0 = blockIdx.y * kRows;
+    const int n = blockIdx.z;
+    const int iy0 = oy0 * kStride - p.ph, ix0 = ox * kStride - p.pw;
+    const mlvc_half* xin = p.x + static_cast<size_t>(n) * p.ih * p.iw * p.ic + c8;
+    uint4 x[kInRows][3];
 #pragma unroll
-        for (int r = 0; r < kInRows; ++r)
+    for (int r = 0; r < kInRows; ++r)
 #pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                const int iy = iy0 + r, ix = ix0 + c;
-                x[r][c] = (iy >= 0 && iy < p.ih && ix >= 0 && ix < p.iw)
-                              ? *reinterpret_cast<const uint4*>(p.x + ((n * p.ih + iy) * p.iw + ix) * p.ic + c8)
-                              : make_uint4(0, 0, 0, 0);
-            }
-        float bias[8];
-        if (p.bias) {
-            const uint4 bv = *reinterpret_cast<const uint4*>(p.bias + c8);
-            const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                unpack_h2(bw[k], bias[2 * k], bias[2 * k + 1]);
-        } else {
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-                bias[k] = 0.0f;
+        for (int c = 0; c < 3; ++c) {
+            const int iy = iy0 + r, ix = ix0 + c;
+            x[r][c] = (iy >= 0 && iy < p.ih && ix >= 0 && ix < p.iw)
+                          ? *reinterpret_cast<const uint4*>(xin + (static_cast<size_t>(iy) * p.iw + ix) * p.ic)
+                          : make_uint4(0, 0, 0, 0);
         }
+    float bias[8];
+    if (p.bias) {
+        const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + c8));
+        const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-            const int oy = oy0 + r;
-            if (oy >= p.oh)
-                break;
-            float acc[8];
+        for (int k = 0; k < 4; ++k)
+            unpack_h2(bw[k], bias[2 * k], bias[2 * k + 1]);
+    } else {
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-                acc[k] = bias[k];
+        for (int k = 0; k < 8; ++k)
+            bias[k] = 0.0f;
+    }
 #pragma unroll
-            for (int ky = 0; ky < 3; ++ky) {
-                const int iy = iy0 + r * kStride + ky;
-                if (iy < 0 || iy >= p.ih)
+    for (int r = 0; r < kRows; ++r) {
+        const int oy = oy0 + r;
+        if (oy >= p.oh)
+            break;
+        float acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            acc[k] = bias[k];
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky) {
+            const int iy = iy0 + r * kStride + ky;
+            if (iy < 0 || iy >= p.ih)
+                continue;
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) {
+                const int ix = ix0 + kx;
+                if (ix < 0 || ix >= p.iw)
                     continue;
+                const uint4 wt = __ldg(reinterpret_cast<const uint4*>(p.w + (ky * 3 + kx) * p.oc + c8));
+                const uint32_t* xw = reinterpret_cast<const uint32_t*>(&x[r * kStride + ky][kx]);
+                const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wt);
 #pragma unroll
-                for (int kx = 0; kx < 3; ++kx) {
-                    const int ix = ix0 + kx;
-                    if (ix < 0 || ix >= p.iw)
-                        continue;
-                    const uint4 wt = __ldg(reinterpret_cast<const uint4*>(p.w + (ky * 3 + kx) * p.oc + c8));
-                    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&x[r * kStride + ky][kx]);
-                    const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wt);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        float x0, x1, w0, w1;
-                        unpack_h2(xw[k], x0, x1);
-                        unpack_h2(ww[k], w0, w1);
-                        acc[2 * k] = fmaf(x0, w0, acc[2 * k]);
-                        acc[2 * k + 1] = fmaf(x1, w1, acc[2 * k + 1]);
-                    }
+                for (int k = 0; k < 4; ++k) {
+                    float x0, x1, w0, w1;
+                    unpack_h2(xw[k], x0, x1);
+                    unpack_h2(ww[k], w0, w1);
+                    acc[2 * k] = fmaf(x0, w0, acc[2 * k]);
+                    acc[2 * k + 1] = fmaf(x1, w1, acc[2 * k + 1]);
                 }
             }
-            uint4 ov;
-            uint32_t* o = reinterpret_cast<uint32_t*>(&ov);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                o[k] = pack_h2(acc[2 * k], acc[2 * k + 1]);
-            *reinterpret_cast<uint4*>(p.y + ((n * p.oh + oy) * p.ow + ox) * p.oc + c8) = ov;
         }
+        uint4 ov;
+        uint32_t* o = reinterpret_cast<uint32_t*>(&ov);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            o[k] = pack_h2(acc[2 * k], acc[2 * k + 1]);
+        *reinterpret_cast<uint4*>(p.y + ((static_cast<size_t>(n) * p.oh + oy) * p.ow + ox) * p.oc + c8) = ov;
     }
 }
 
 extern "C" __global__ void __launch_bounds__(256, 2) mlvc_depthwise3x3_f16(const __grid_constant__ DirectConvParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     if (p.sh == 2)
         depthwise3x3_body<2>(p);
     else
@@ -436,6 +459,8 @@ extern "C" __global__ void __launch_bounds__(256, 2) mlvc_depthwise3x3_f16(const
 // LeakyReLU / residual with the graph's double rounding.
 extern "C" __global__ void mlvc_conv_direct_f16(const __grid_constant__ DirectConvParams p)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long total = static_cast<long long>(p.n) * p.oh * p.ow * p.oc;
     const int icg = p.ic / p.groups, ocg = p.oc / p.groups;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;

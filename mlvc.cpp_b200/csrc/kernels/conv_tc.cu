@@ -19,8 +19,9 @@
 //    start address by whole pixels.  Weight panels (64 channels of one tap)
 //    stream through their own ring or stay resident when they fit.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2..5 = epilogue (one TMEM lane quadrant each).  Persistent:
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer, warps 2..9 = epilogue: two warpgroups, each warp reading its TMEM
+// lane quadrant (warp % 4) and the warpgroup's share of the column chunks.  Persistent:
 // each CTA walks tiles t = blockIdx.x + i * gridDim.x, and gridDim.x is a
 // multiple of n_tiles so a CTA keeps one N tile.  Accumulators are double
 // buffered in TMEM so the epilogue of tile i overlaps the MMAs of tile i+1.
@@ -28,7 +29,8 @@
 
 namespace mlvc_b200 {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;          // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpilogueThreads = 256;  // two warpgroups, one per half of the 32-column chunks
 constexpr int kBM = 128;
 constexpr int kMaxStages = 8;
 constexpr unsigned int kErrWaitProducer = 0x1u;
@@ -49,6 +51,12 @@ struct TcShared {
     float bias[256];
 };
 static_assert(sizeof(TcShared) <= kTcHeaderBytes, "TcShared must fit the header reserved by the host");
+
+__device__ __forceinline__ void trace(const ConvTcParams& p, int point)
+{
+    if (p.trace)
+        p.trace[blockIdx.x * kTracePoints + point] = globaltimer_ns();
+}
 
 __device__ __forceinline__ uint32_t tmem_cols_for(int bn)
 {
@@ -72,14 +80,14 @@ __device__ __forceinline__ void load_residual32(const mlvc_half* res, int col, i
 }
 
 __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcShared& sh, uint32_t tmem_acc,
-                                              int quadrant, long long pixel, bool valid, int n_tile,
+                                              int quadrant, int group, long long pixel, bool valid, int n_tile,
                                               uint4 (&res_next)[4])
 {
     const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16);
     if (p.epilogue == kEpiReglu) {
         const int half = p.BN / 2;
         mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * half;
-        for (int c0 = 0; c0 < half; c0 += 16) {
+        for (int c0 = group * 16; c0 < half; c0 += 32) {
             uint32_t gr[16], lr[16];
             tmem_ld16_nowait(lane_addr + c0, gr);
             tmem_ld16_nowait(lane_addr + half + c0, lr);
@@ -108,13 +116,13 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
     mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * p.BN;
     const mlvc_half* res = p.residual ? p.residual + pixel * p.ldr + n_tile * p.BN : nullptr;
     const bool residual = p.epilogue == kEpiResidual && valid;
-    for (int c0 = 0; c0 < p.BN; c0 += 32) {
+    for (int c0 = group * 32; c0 < p.BN; c0 += 64) {
         uint4 rc[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q)
             rc[q] = res_next[q];
-        if (residual && c0 + 32 < p.BN)
-            load_residual32(res + c0 + 32, n_tile * p.BN + c0 + 32, p.n_valid, res_next);
+        if (residual && c0 + 64 < p.BN)
+            load_residual32(res + c0 + 64, n_tile * p.BN + c0 + 64, p.n_valid, res_next);
         uint32_t a[32];
         tmem_ld32_nowait(lane_addr + c0, a);
         tmem_wait_ld();
@@ -156,12 +164,15 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
                                               bool kxk)
 {
     const int quadrant = warp & 3;
-    const int et = (warp - 2) * 32 + lane;  // 0..127
-    for (int i = et; i < p.BN; i += 128) {
+    const int group = (warp - 2) / 4;       // column-chunk warpgroup
+    const int et = (warp - 2) * 32 + lane;  // 0..255
+    for (int i = et; i < p.BN; i += kEpilogueThreads) {
         const int col = n_tile * p.BN + i;
         sh.bias[i] = (p.bias && col < p.N) ? __half2float(p.bias[col]) : 0.0f;
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads + 32) : "memory");  // bias loaded + TMEM allocated
+    tc_fence_after();
+    pdl_wait();  // residual reads and output writes follow the previous kernel
     uint32_t acc = 0, acc_phase = 0;
     for (int t = first_tile; t < total_tiles; t += tile_step) {
         const int m_tile = t / p.n_tiles;
@@ -181,23 +192,30 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
         // first residual chunk is fetched while the MMAs of this tile run
         uint4 res_next[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
                              make_uint4(0, 0, 0, 0)};
-        if (p.epilogue == kEpiResidual && valid)
-            load_residual32(p.residual + pixel * p.ldr + n_tile * p.BN, n_tile * p.BN, p.n_valid, res_next);
+        if (p.epilogue == kEpiResidual && valid && group * 32 < p.BN)
+            load_residual32(p.residual + pixel * p.ldr + n_tile * p.BN + group * 32, n_tile * p.BN + group * 32,
+                            p.n_valid, res_next);
         if (!mbar_wait(&sh.tmem_full[acc], acc_phase, &sh.abort_flag, kErrWaitEpilogue))
             return;
         tc_fence_after();
-        epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, pixel, valid, n_tile, res_next);
+        if (t == first_tile && et == 0)
+            trace(p, kTrFirstAcc);
+        epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, group, pixel, valid, n_tile, res_next);
         tc_fence_before();
         mbar_arrive(&sh.tmem_empty[acc]);
         acc ^= 1u;
         acc_phase ^= (acc == 0) ? 1u : 0u;
     }
+    if (et == 0)
+        trace(p, kTrEpilogueDone);
 }
 
 // --------------------------------------------------------------- setup
 __device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvTcParams& p, int warp)
 {
     TcShared* sh = reinterpret_cast<TcShared*>(smem_raw);
+    if (threadIdx.x == 0)
+        trace(p, kTrEntry);
     if (threadIdx.x == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
             mbar_init(&sh->a_full[s], 1);
@@ -207,7 +225,7 @@ __device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvT
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sh->tmem_full[s], 1);
-            mbar_init(&sh->tmem_empty[s], 128);
+            mbar_init(&sh->tmem_empty[s], kEpilogueThreads);
         }
         mbar_init(&sh->drain, 1);
         sh->abort_flag = 0;
@@ -217,12 +235,25 @@ __device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvT
         tma_prefetch_desc(&p.map_a0);
         tma_prefetch_desc(&p.map_b);
     }
-    if (warp == 1)
-        tmem_alloc(&sh->tmem_base, tmem_cols_for(p.BN));
-    tc_fence_before();
+    // Only the barriers must be visible before the producer starts; TMEM is
+    // allocated by warp 1 afterwards and handed to the epilogue warps through
+    // named barrier 1 (see alloc_tmem_and_publish / epilogue_role).
     __syncthreads();
-    tc_fence_after();
+    if (threadIdx.x == 0)
+        trace(p, kTrSetup);
+    pdl_launch_dependents();
     return sh;
+}
+
+// Warp 1: allocate the accumulators and publish their address to the
+// epilogue warpgroups (named barrier 1: 256 epilogue threads + this warp).
+__device__ __forceinline__ void alloc_tmem_and_publish(TcShared* sh, const ConvTcParams& p)
+{
+    tmem_alloc(&sh->tmem_base, tmem_cols_for(p.BN));
+    tc_fence_before();
+    asm volatile("bar.arrive 1, %0;" ::"n"(kEpilogueThreads + 32) : "memory");
+    __syncwarp();
+    tc_fence_after();
 }
 
 __device__ __forceinline__ void teardown(const ConvTcParams& p, TcShared* sh, int warp, bool mma_thread,
@@ -240,6 +271,8 @@ __device__ __forceinline__ void teardown(const ConvTcParams& p, TcShared* sh, in
         tc_fence_after();
         tmem_dealloc(sh->tmem_base, tmem_cols_for(p.BN));
     }
+    if (threadIdx.x == 0)
+        trace(p, kTrExit);
 }
 
 // Producer-side drain: wait (bounded) for every TMA this thread armed, so no
@@ -280,6 +313,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
             mbar_arrive_expect_tx(&sh->b_full[0], static_cast<uint32_t>(b_panel_bytes * k_panels));
             for (int kp = 0; kp < k_panels; ++kp)
                 tma_load_2d(b_smem + kp * b_panel_bytes, &p.map_b, &sh->b_full[0], kp * 64, n_tile * p.BN);
+            trace(p, kTrWeightsIssued);
+            pdl_wait();  // activations are written by the previous kernel
             int stage = 0;
             uint32_t phase = 0;
             for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {
@@ -305,11 +340,13 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
         }
         __syncwarp();
     } else if (warp == 1) {
+        alloc_tmem_and_publish(sh, p);
         if (elect_one()) {
             mma_thread = true;
             const uint32_t idesc = idesc_f16_f32(kBM, static_cast<uint32_t>(p.BN));
             if (mbar_wait(&sh->b_full[0], 0, &sh->abort_flag, kErrWaitMma)) {
                 tc_fence_after();
+                trace(p, kTrWeightsLanded);
                 int stage = 0;
                 uint32_t phase = 0, acc = 0, acc_phase = 0;
                 const uint32_t b_addr = smem_u32(b_smem), a_addr = smem_u32(a_smem);
@@ -325,6 +362,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                             break;
                         }
                         tc_fence_after();
+                        if (issued == 0)
+                            trace(p, kTrFirstA);
                         const uint32_t a_st = a_addr + stage * kAPanelBytes;
                         const uint32_t b_st = b_addr + static_cast<uint32_t>(kp * b_panel_bytes);
 #pragma unroll
@@ -346,6 +385,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                     acc ^= 1u;
                     acc_phase ^= (acc == 0) ? 1u : 0u;
                 }
+                trace(p, kTrLastCommit);
             }
         }
         __syncwarp();
@@ -405,6 +445,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
                                     &sh->b_full[0], tap * p.in_c + kp * 64, n_tile * p.BN);
                 b_armed[0] = true;
             }
+            pdl_wait();  // activations are written by the previous kernel
             int as = 0, bs = 0;
             uint32_t aph = 0, bph = 0;
             for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {
@@ -458,6 +499,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
         }
         __syncwarp();
     } else if (warp == 1) {
+        alloc_tmem_and_publish(sh, p);
         if (elect_one()) {
             mma_thread = true;
             const uint32_t idesc = idesc_f16_f32(kBM, static_cast<uint32_t>(p.BN));

@@ -56,6 +56,23 @@ struct ConvTcParams {
     int kh, kw, stride, pad;
     int halo_px;                // pixels (or pixel pairs) per halo row
     int px_min;                 // leftmost halo offset relative to the tile start (<= 0)
+    // Optional phase trace (null in normal runs): kTracePoints %globaltimer
+    // stamps per CTA, written by the role that reaches each point.
+    unsigned long long* trace;
+};
+
+// Phase trace points of the tensor-core conv kernels.
+enum TracePoint : int {
+    kTrEntry = 0,          // CTA start
+    kTrSetup = 1,          // barriers initialised, TMEM allocated
+    kTrWeightsIssued = 2,  // producer issued the weight loads
+    kTrWeightsLanded = 3,  // MMA issuer saw the weights arrive
+    kTrFirstA = 4,         // MMA issuer saw the first activation panel
+    kTrLastCommit = 5,     // MMA issuer committed its last tile
+    kTrFirstAcc = 6,       // epilogue saw the first accumulator
+    kTrEpilogueDone = 7,   // epilogue finished its last tile
+    kTrExit = 8,           // CTA teardown done
+    kTracePoints = 16
 };
 
 struct ElementwiseParams {

@@ -45,6 +45,15 @@ __device__ __forceinline__ bool elect_one()
     return pred != 0;
 }
 
+// ------------------------------------------------- programmatic launch
+// With programmatic stream serialisation the next kernel in the stream may
+// start while this one runs; it must call pdl_wait() before touching memory
+// that earlier kernels read or write (it returns once they have completed and
+// their writes are visible).  Without a programmatic dependency both are
+// no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
 {

@@ -71,6 +71,8 @@ EXPORTS = {
                              ctypes.c_int),
     "mlvc_b200_kernel_launches": ([ctypes.c_void_p], ctypes.c_int),
     "mlvc_b200_device_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
+    "mlvc_b200_trace_step": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t,
+                              ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "mlvc_b200_set_debug_tensors": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
     "mlvc_b200_read_tensor": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_size_t,
                                ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
@@ -247,6 +249,15 @@ class Backend:
         buf = (ctypes.c_float * max(1, n))()
         _check(lib().mlvc_b200_time_steps(self._h, iterations, flush_bytes, buf))
         return list(buf[:n])
+
+    def trace_step(self, index):
+        """[CTAs, 16] %globaltimer stamps of one tensor-core conv step (see
+        include/mlvc_b200.h); requires a previous run()."""
+        n = ctypes.c_size_t()
+        _check(lib().mlvc_b200_trace_step(self._h, index, None, 0, ctypes.byref(n)))
+        buf = (ctypes.c_uint64 * n.value)()
+        _check(lib().mlvc_b200_trace_step(self._h, index, buf, n.value, ctypes.byref(n)))
+        return np.frombuffer(buf, np.uint64).reshape(-1, 16).copy()
 
     @property
     def kernel_launches(self):
