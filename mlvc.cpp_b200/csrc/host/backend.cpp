@@ -564,9 +564,11 @@ void Backend::plan()
                 std::vector<int> cands;
                 for (int bn = std::min(256, NN); bn >= 32; bn -= 32)  // the epilogue walks 32 columns
                     if (NN % bn == 0 && (!reglu || bn % 64 == 0) &&
-                        header + k_panels * bn * 128 + 2 * 16384 <= smem_cap)
+                        header + k_panels * bn * 128 + 2 * 16384 + kTcStageBytes <= smem_cap)
                         cands.push_back(bn);
-                auto stages_for = [&](int bn, int cap) { return (cap - header - 1024 - k_panels * bn * 128) / 16384; };
+                auto stages_for = [&](int bn, int cap) {
+                    return (cap - header - 1024 - kTcStageBytes - k_panels * bn * 128) / 16384;
+                };
                 int best = 0, ctas_per_sm = 1;
                 for (int bn : cands)
                     if (bn <= 128 && stages_for(bn, kTwoCtaSmem) >= 2 && m_tiles * (NN / bn) >= sm_count_) {
@@ -604,13 +606,12 @@ void Backend::plan()
                     const size_t w_off = prep(wp.data(), wp.size() * 2);
                     const size_t b_off = prep(bp.data(), bp.size() * 2);
                     const int a_stages =
-                        std::min(8, ctas_per_sm == 2 ? stages_for(BN, kTwoCtaSmem)
-                                                     : (smem_cap - header - k_panels * BN * 128) / 16384);
+                        std::min(8, ctas_per_sm == 2 ? stages_for(BN, kTwoCtaSmem) : stages_for(BN, smem_cap + 1024));
                     const int slots = sm_count_ * ctas_per_sm;
                     const int grid = n_tiles * std::max(1, std::min(m_tiles, slots / n_tiles));
                     s.kernel = "mlvc_conv1x1_tc";
                     s.info.kernel = s.kernel;
-                    s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 + 1024);
+                    s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 + kTcStageBytes + 1024);
                     s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     const int M = IH * IW;
@@ -641,6 +642,18 @@ void Backend::plan()
                                   "cuTensorMapEncodeTiled(conv1x1 B)");
                         }
                         p.map_a1 = p.map_a0;
+                        {
+                            const cuuint64_t ncols = static_cast<cuuint64_t>(reglu ? OC / 2 : OC);
+                            const cuuint64_t dims[2] = {ncols, static_cast<cuuint64_t>(M)};
+                            const cuuint64_t strides[1] = {ncols * 2};
+                            const cuuint32_t box[2] = {32, 32};
+                            check(cuTensorMapEncodeTiled(&p.map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                                         reinterpret_cast<void*>(values_[out_id].addr), dims, strides,
+                                                         box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                         CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  "cuTensorMapEncodeTiled(conv1x1 out)");
+                        }
                         p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b_off);
                         p.residual = res_id ? reinterpret_cast<const mlvc_half*>(values_[res_id].addr) : nullptr;
                         p.out = reinterpret_cast<mlvc_half*>(values_[out_id].addr);
@@ -691,15 +704,16 @@ void Backend::plan()
                         continue;
                     const int bpanel = bn * 128;
                     const int res_bytes = taps * k_panels * bpanel;
-                    if (header + res_bytes + 2 * halo_stride <= smem_cap) {
+                    const int fixed = header + kTcStageBytes;
+                    if (fixed + res_bytes + 2 * halo_stride <= smem_cap) {
                         BN = bn;
                         resident = 1;
-                        a_st = std::min(4, (smem_cap - header - res_bytes) / halo_stride);
+                        a_st = std::min(4, (smem_cap - fixed - res_bytes) / halo_stride);
                         b_st = 1;
                     } else {
                         for (int as = 2; as >= 1 && !BN; --as)
                             for (int bs = 4; bs >= 2 && !BN; --bs)
-                                if (header + bs * bpanel + as * halo_stride <= smem_cap) {
+                                if (fixed + bs * bpanel + as * halo_stride <= smem_cap) {
                                     BN = bn;
                                     a_st = as;
                                     b_st = bs;
@@ -722,7 +736,8 @@ void Backend::plan()
                     const int b_slots = resident ? taps * k_panels : b_st;
                     s.kernel = "mlvc_convkxk_tc";
                     s.info.kernel = s.kernel;
-                    s.smem = static_cast<unsigned>(header + b_slots * BN * 128 + a_st * halo_stride + 1024);
+                    s.smem =
+                        static_cast<unsigned>(header + b_slots * BN * 128 + a_st * halo_stride + kTcStageBytes + 1024);
                     s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     s.build = [=, this](Step& st) {
@@ -744,6 +759,19 @@ void Backend::plan()
                         }
                         if (parities == 1)
                             p.map_a1 = p.map_a0;
+                        {
+                            const cuuint64_t dims[3] = {static_cast<cuuint64_t>(OC), static_cast<cuuint64_t>(OW),
+                                                        static_cast<cuuint64_t>(OH)};
+                            const cuuint64_t strides[2] = {static_cast<cuuint64_t>(OC) * 2,
+                                                           static_cast<cuuint64_t>(OW) * OC * 2};
+                            const cuuint32_t box[3] = {32, 32, 1};
+                            check(cuTensorMapEncodeTiled(&p.map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                                                         reinterpret_cast<void*>(values_[out_id].addr), dims, strides,
+                                                         box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                         CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  "cuTensorMapEncodeTiled(convkxk out)");
+                        }
                         {
                             const cuuint64_t Kt = static_cast<cuuint64_t>(taps) * IC;
                             const cuuint64_t dims[2] = {Kt, static_cast<cuuint64_t>(OC)};

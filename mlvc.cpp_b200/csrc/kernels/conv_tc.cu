@@ -68,61 +68,104 @@ __device__ __forceinline__ uint32_t tmem_cols_for(int bn)
 }
 
 // ----------------------------------------------------------- epilogue
-// One thread owns one output pixel (TMEM lane) of the tile and walks its
-// columns 32 at a time (one tcgen05.ld of 32 columns, one wait).  For the
-// residual epilogue the next chunk's residual is loaded from global memory
-// before the current chunk is processed, so its latency overlaps the work.
-__device__ __forceinline__ void load_residual32(const mlvc_half* res, int col, int n_valid, uint4 (&r)[4])
+// Each epilogue warp owns one TMEM lane quadrant (32 output pixels) and, with
+// the other warpgroup, alternate 32-column chunks.  Per chunk a thread reads
+// its pixel's 32 accumulators (one tcgen05.ld), applies bias / activation /
+// residual with the graph's rounding, and writes the 64-byte row into a warp
+// staging buffer (64-byte swizzle, bank-conflict free); one lane then stores
+// the 32x32 block with a TMA bulk store (full-line writes, clipped at the
+// tensor edges).  The residual block is read coalesced into the same buffer
+// first.  Two buffers per warp let a store drain while the next chunk runs.
+__device__ __forceinline__ uint32_t swz64(int row, int chunk)
 {
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-        r[q] = col + 8 * (q + 1) <= n_valid ? reinterpret_cast<const uint4*>(res)[q] : make_uint4(0, 0, 0, 0);
+    return static_cast<uint32_t>(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
+}
+
+struct EpiTile {
+    long long pixel0;  // first pixel of the warp's 32 rows (1x1) / row start (kxk)
+    int rows_valid;    // rows of the warp block inside the output
+    int oy, ox0;       // kxk: output row and first column of the warp block
+};
+
+__device__ __forceinline__ void store_block(const ConvTcParams& p, const uint8_t* buf, const EpiTile& et, int col,
+                                            bool kxk)
+{
+    if (kxk)
+        tma_store_3d(&p.map_out, buf, col, et.ox0, et.oy);
+    else
+        tma_store_2d(&p.map_out, buf, col, static_cast<int>(et.pixel0));
+    bulk_commit();
 }
 
 __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcShared& sh, uint32_t tmem_acc,
-                                              int quadrant, int group, long long pixel, bool valid, int n_tile,
-                                              uint4 (&res_next)[4])
+                                              int quadrant, int group, int lane, const EpiTile& et, int n_tile,
+                                              uint8_t* stage, int& nbuf, bool kxk)
 {
     const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16);
     if (p.epilogue == kEpiReglu) {
         const int half = p.BN / 2;
-        mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * half;
-        for (int c0 = group * 16; c0 < half; c0 += 32) {
-            uint32_t gr[16], lr[16];
-            tmem_ld16_nowait(lane_addr + c0, gr);
-            tmem_ld16_nowait(lane_addr + half + c0, lr);
-            tmem_wait_ld();
-            uint32_t packed[8];
+        for (int c0 = group * 32; c0 < half; c0 += 64) {
+            uint8_t* buf = stage + (nbuf & 1) * 2048;
+            if (nbuf >= 2) {
+                if (lane == 0)
+                    bulk_wait_read<1>();
+                __syncwarp();
+            }
 #pragma unroll
-            for (int i = 0; i < 16; i += 2) {
-                float r2[2];
+            for (int h = 0; h < 2; ++h) {
+                uint32_t gr[16], lr[16];
+                tmem_ld16_nowait(lane_addr + c0 + 16 * h, gr);
+                tmem_ld16_nowait(lane_addr + half + c0 + 16 * h, lr);
+                tmem_wait_ld();
+                uint32_t packed[8];
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const float gv = round_h(__uint_as_float(gr[i + j]) + sh.bias[c0 + i + j]);
-                    const float lv = round_h(__uint_as_float(lr[i + j]) + sh.bias[half + c0 + i + j]);
-                    const float cg = round_h(fminf(fmaxf(gv, p.clip_lo), p.clip_hi));
-                    r2[j] = cg * lv;
+                for (int i = 0; i < 16; i += 2) {
+                    float r2[2];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const float gv = round_h(__uint_as_float(gr[i + j]) + sh.bias[c0 + 16 * h + i + j]);
+                        const float lv = round_h(__uint_as_float(lr[i + j]) + sh.bias[half + c0 + 16 * h + i + j]);
+                        const float cg = round_h(fminf(fmaxf(gv, p.clip_lo), p.clip_hi));
+                        r2[j] = cg * lv;
+                    }
+                    packed[i / 2] = pack_h2(r2[0], r2[1]);
                 }
-                packed[i / 2] = pack_h2(r2[0], r2[1]);
+                *reinterpret_cast<uint4*>(buf + swz64(lane, 2 * h)) =
+                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                *reinterpret_cast<uint4*>(buf + swz64(lane, 2 * h + 1)) =
+                    make_uint4(packed[4], packed[5], packed[6], packed[7]);
             }
-            if (valid) {
-                uint4* d = reinterpret_cast<uint4*>(dst + c0);
-                d[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                d[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0)
+                store_block(p, buf, et, p.out_col0 + n_tile * half + c0, kxk);
+            ++nbuf;
         }
         return;
     }
-    mlvc_half* dst = p.out + pixel * p.ldo + p.out_col0 + n_tile * p.BN;
-    const mlvc_half* res = p.residual ? p.residual + pixel * p.ldr + n_tile * p.BN : nullptr;
-    const bool residual = p.epilogue == kEpiResidual && valid;
+    const bool residual = p.epilogue == kEpiResidual;
     for (int c0 = group * 32; c0 < p.BN; c0 += 64) {
-        uint4 rc[4];
+        uint8_t* buf = stage + (nbuf & 1) * 2048;
+        if (nbuf >= 2) {
+            if (lane == 0)
+                bulk_wait_read<1>();
+            __syncwarp();
+        }
+        const int col = n_tile * p.BN + c0;
+        if (residual) {
+            // 32 rows x 64 bytes, 8 rows per instruction, contiguous 64-byte segments
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-            rc[q] = res_next[q];
-        if (residual && c0 + 64 < p.BN)
-            load_residual32(res + c0 + 64, n_tile * p.BN + c0 + 64, p.n_valid, res_next);
+            for (int j = 0; j < 4; ++j) {
+                const int piece = lane + 32 * j, r = piece >> 2, ch = piece & 3;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (r < et.rows_valid && col + 8 * (ch + 1) <= p.n_valid) {
+                    const long long px = kxk ? static_cast<long long>(et.oy) * p.out_w + et.ox0 + r : et.pixel0 + r;
+                    v = *reinterpret_cast<const uint4*>(p.residual + px * p.ldr + col + ch * 8);
+                }
+                *reinterpret_cast<uint4*>(buf + swz64(r, ch)) = v;
+            }
+            __syncwarp();
+        }
         uint32_t a[32];
         tmem_ld32_nowait(lane_addr + c0, a);
         tmem_wait_ld();
@@ -135,38 +178,42 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
             for (int i = 0; i < 32; ++i)
                 v[i] = v[i] < 0.0f ? round_h(v[i] * p.alpha) : v[i];
         } else if (residual) {
-            const uint32_t* rr = reinterpret_cast<const uint32_t*>(rc);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                float ra, rb;
-                unpack_h2(rr[i], ra, rb);
-                v[2 * i] += ra;
-                v[2 * i + 1] += rb;
+            for (int q = 0; q < 4; ++q) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(buf + swz64(lane, q));
+                const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float ra, rb;
+                    unpack_h2(rr[i], ra, rb);
+                    v[8 * q + 2 * i] += ra;
+                    v[8 * q + 2 * i + 1] += rb;
+                }
             }
         }
-        if (valid) {
-            uint32_t packed[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-                packed[i] = pack_h2(v[2 * i], v[2 * i + 1]);
-            uint4* d = reinterpret_cast<uint4*>(dst + c0);
-            const int col = n_tile * p.BN + c0;  // channels beyond n_valid are padding rows
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (col + 8 * (q + 1) <= p.n_valid)
-                    d[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-        }
+        for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(buf + swz64(lane, q)) =
+                make_uint4(pack_h2(v[8 * q], v[8 * q + 1]), pack_h2(v[8 * q + 2], v[8 * q + 3]),
+                           pack_h2(v[8 * q + 4], v[8 * q + 5]), pack_h2(v[8 * q + 6], v[8 * q + 7]));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0)
+            store_block(p, buf, et, p.out_col0 + col, kxk);
+        ++nbuf;
     }
 }
 
-__device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& sh, int warp, int lane,
-                                              int n_tile, int first_tile, int tile_step, int total_tiles,
+__device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& sh, uint8_t* stage_base, int warp,
+                                              int lane, int n_tile, int first_tile, int tile_step, int total_tiles,
                                               bool kxk)
 {
     const int quadrant = warp & 3;
     const int group = (warp - 2) / 4;       // column-chunk warpgroup
-    const int et = (warp - 2) * 32 + lane;  // 0..255
-    for (int i = et; i < p.BN; i += kEpilogueThreads) {
+    const int et_id = (warp - 2) * 32 + lane;  // 0..255
+    uint8_t* stage = stage_base + (warp - 2) * 4096;
+    int nbuf = 0;
+    for (int i = et_id; i < p.BN; i += kEpilogueThreads) {
         const int col = n_tile * p.BN + i;
         sh.bias[i] = (p.bias && col < p.N) ? __half2float(p.bias[col]) : 0.0f;
     }
@@ -176,37 +223,34 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
     uint32_t acc = 0, acc_phase = 0;
     for (int t = first_tile; t < total_tiles; t += tile_step) {
         const int m_tile = t / p.n_tiles;
-        const int row = quadrant * 32 + lane;
-        long long pixel;
-        bool valid;
+        EpiTile et;
         if (!kxk) {
-            pixel = static_cast<long long>(m_tile) * kBM + row;
-            valid = pixel < p.M;
+            et.pixel0 = static_cast<long long>(m_tile) * kBM + quadrant * 32;
+            et.rows_valid = static_cast<int>(min(32LL, max(0LL, p.M - et.pixel0)));
+            et.oy = et.ox0 = 0;
         } else {
             const int tiles_per_row = (p.out_w + kBM - 1) / kBM;
-            const int oy = m_tile / tiles_per_row;
-            const int ox = (m_tile % tiles_per_row) * kBM + row;
-            valid = ox < p.out_w;
-            pixel = static_cast<long long>(oy) * p.out_w + ox;
+            et.oy = m_tile / tiles_per_row;
+            et.ox0 = (m_tile % tiles_per_row) * kBM + quadrant * 32;
+            et.rows_valid = max(0, min(32, p.out_w - et.ox0));
+            et.pixel0 = static_cast<long long>(et.oy) * p.out_w + et.ox0;
         }
-        // first residual chunk is fetched while the MMAs of this tile run
-        uint4 res_next[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                             make_uint4(0, 0, 0, 0)};
-        if (p.epilogue == kEpiResidual && valid && group * 32 < p.BN)
-            load_residual32(p.residual + pixel * p.ldr + n_tile * p.BN + group * 32, n_tile * p.BN + group * 32,
-                            p.n_valid, res_next);
         if (!mbar_wait(&sh.tmem_full[acc], acc_phase, &sh.abort_flag, kErrWaitEpilogue))
-            return;
+            break;
         tc_fence_after();
-        if (t == first_tile && et == 0)
+        if (t == first_tile && et_id == 0)
             trace(p, kTrFirstAcc);
-        epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, group, pixel, valid, n_tile, res_next);
+        if (et.rows_valid > 0)
+            epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, group, lane, et, n_tile, stage, nbuf, kxk);
         tc_fence_before();
         mbar_arrive(&sh.tmem_empty[acc]);
         acc ^= 1u;
         acc_phase ^= (acc == 0) ? 1u : 0u;
     }
-    if (et == 0)
+    if (lane == 0)
+        bulk_wait_all();  // stores complete before the CTA (and its shared memory) retires
+    __syncwarp();
+    if (et_id == 0)
         trace(p, kTrEpilogueDone);
 }
 
@@ -234,6 +278,7 @@ __device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvT
     if (warp == 0 && elect_one()) {
         tma_prefetch_desc(&p.map_a0);
         tma_prefetch_desc(&p.map_b);
+        tma_prefetch_desc(&p.map_out);
     }
     // Only the barriers must be visible before the producer starts; TMEM is
     // allocated by warp 1 afterwards and handed to the epilogue warps through
@@ -298,6 +343,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
     const size_t b_panel_bytes = static_cast<size_t>(p.BN) * 128;
     uint8_t* a_smem = b_smem + b_panel_bytes * k_panels;
     constexpr uint32_t kAPanelBytes = kBM * 128;
+    uint8_t* stage_smem = a_smem + static_cast<size_t>(p.a_stages) * kAPanelBytes;  // 1024-aligned
 
     const int total_tiles = p.m_tiles * p.n_tiles;
     const int n_tile = blockIdx.x % p.n_tiles;
@@ -390,7 +436,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
         }
         __syncwarp();
     } else {
-        epilogue_role(p, *sh, warp, lane, n_tile, first, step, total_tiles, false);
+        epilogue_role(p, *sh, stage_smem, warp, lane, n_tile, first, step, total_tiles, false);
     }
     teardown(p, sh, warp, mma_thread, issued);
 }
@@ -425,6 +471,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
     uint8_t* b_smem = base + ((sizeof(TcShared) + 1023) & ~size_t(1023));
     const int b_slots = p.b_resident ? taps * k_panels : p.b_stages;
     uint8_t* a_smem = b_smem + static_cast<size_t>(b_slots) * b_panel_bytes;
+    uint8_t* stage_smem = a_smem + static_cast<size_t>(p.a_stages) * halo_stride;  // 1024-aligned
 
     const int tiles_per_row = (p.out_w + kBM - 1) / kBM;
     const int total_tiles = p.m_tiles * p.n_tiles;
@@ -579,7 +626,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
         }
         __syncwarp();
     } else {
-        epilogue_role(p, *sh, warp, lane, n_tile, first, step, total_tiles, true);
+        epilogue_role(p, *sh, stage_smem, warp, lane, n_tile, first, step, total_tiles, true);
     }
     teardown(p, sh, warp, mma_thread, issued);
 }

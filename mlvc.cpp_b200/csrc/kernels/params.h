@@ -21,6 +21,10 @@ namespace mlvc_b200 {
 // 1024-byte aligned).
 constexpr int kTcHeaderBytes = 2048;
 
+// Epilogue staging per tensor-core conv CTA: 8 epilogue warps x 2 buffers of
+// 32 rows x 32 FP16 columns (64-byte swizzled rows) for the TMA output stores.
+constexpr int kTcStageBytes = 8 * 2 * 2048;
+
 // Epilogue kinds of the tensor-core conv kernels.  Rounding follows the graph:
 // the conv result is rounded to FP16 first, then the fused operator is applied
 // and rounded again.
@@ -36,6 +40,7 @@ struct ConvTcParams {
     CUtensorMap map_a0;  // activations (1x1: [M rows, K]; kxk: parity 0 view)
     CUtensorMap map_a1;  // kxk stride-2: parity 1 view (unused otherwise)
     CUtensorMap map_b;   // prepared weights [N rows, K = taps * IC] (K-major)
+    CUtensorMap map_out; // output store view: 1x1 {channels, pixels}, kxk {channels, W, H}; 32x32 boxes, 64B swizzle
     const mlvc_half* bias;      // [N] in prepared column order, may be null
     const mlvc_half* residual;  // NHWC [M, ldr] or null
     mlvc_half* out;             // NHWC [M, ldo]
