@@ -44,7 +44,33 @@ UNIT = "frames/s"
 FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
 
+def single_op(name):
+    """Single-operator graphs at 544x960 (inputs larger than L2) for kernel
+    tuning and ncu captures: dw3x3 (256 ch), conv1x1 (128->256 + LeakyReLU)."""
+    from mlvc_b200.graph import GraphBuilder, kaiming_normal, small_bias
+    rng = np.random.default_rng(0)
+    gb = GraphBuilder()
+    if name == "op_dw3x3":
+        x = gb.input("x", [1, 256, 544, 960])
+        w = gb.weight("w", kaiming_normal(rng, (256, 1, 3, 3), 1.0))
+        b = gb.weight("b", small_bias(rng, 256))
+        gb.output(gb.conv(x, w, b, (1, 1), (1, 1), groups=256), "y")
+        inputs = [rng.standard_normal((1, 256, 544, 960), dtype=np.float32).astype(np.float16)]
+        desc = "single op: depthwise 3x3 s1 p1, 256 ch @544x960 (NCHW boundary conversion included)"
+    else:
+        x = gb.input("x", [1, 128, 544, 960])
+        w = gb.weight("w", kaiming_normal(rng, (256, 128, 1, 1)))
+        b = gb.weight("b", small_bias(rng, 256))
+        gb.output(gb.leaky_relu(gb.conv(x, w, b), 0.01), "y")
+        inputs = [rng.standard_normal((1, 128, 544, 960), dtype=np.float32).astype(np.float16)]
+        desc = "single op: 1x1 conv 128->256 + LeakyReLU @544x960 (NCHW boundary conversion included)"
+    graph, weights = gb.finish()
+    return graph, weights, inputs, desc, METRIC.replace("config 2 block stack", desc)
+
+
 def workload(name):
+    if name.startswith("op_"):
+        return single_op(name)
     if name == "conv3x3":
         gb, inputs = build_conv3x3(0)
         desc = ("config1-conv3x3: one FP16 3x3 s1 p1 conv 64->64 @184x320, W~N(0,sqrt(2/576)), b~U(-0.1,0.1), "
@@ -331,7 +357,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["block_stack", "conv3x3"], default="block_stack")
+    ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1"], default="block_stack")
     ap.add_argument("--cpu-frames", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
