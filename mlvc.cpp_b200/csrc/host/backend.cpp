@@ -375,7 +375,8 @@ void Backend::plan()
         const int tiles_x = static_cast<int>((dd[3] + 31) / 32);
         s.grid = static_cast<unsigned>(dd[0] * dd[2] * tiles_x);
         s.block = 256;
-        s.smem = static_cast<unsigned>((dd[1] / (r * r)) * r * (32 * r + 1) * 2);
+        // tile of host rows: scalar path pitch 32r+1, vector path 32r+8 halfs
+        s.smem = static_cast<unsigned>((dd[1] / (r * r)) * r * (32 * r + 8) * 2);
         s.build = [this, dev_id, dd, r, to_host, k](Step& st) {
             BoundaryParams p{};
             const CUdeviceptr stage = to_host ? output_stage_dev_.at(k).get() : input_stage_dev_.at(k).get();
@@ -859,7 +860,7 @@ void Backend::plan()
                     work = 0;
                     const int per_block = 256 / (OC / 8);
                     s.grid = static_cast<unsigned>((OW + per_block - 1) / per_block);
-                    s.grid_y = static_cast<unsigned>((OH + 1) / 2);
+                    s.grid_y = static_cast<unsigned>((OH + 3) / 4);  // four output rows per thread
                     s.grid_z = static_cast<unsigned>(N);
                 } else {
                     s.kernel = "mlvc_depthwise_v8_f16";

@@ -173,16 +173,89 @@ extern "C" __global__ void mlvc_transpose_f16(const __grid_constant__ CopyParams
 // NCHW <-> NHWC with pixel (un)shuffle fused, through shared memory.  One
 // block handles one device row band: 32 device pixels of one row of the NHWC
 // tensor and all of its C*r*r channels, i.e. C*r rows x 32*r columns of the
-// NCHW tensor.  Global reads and writes are both contiguous runs.
-extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid_constant__ BoundaryParams p)
+// NCHW tensor.  Both global sides move 16-byte vectors in contiguous runs;
+// the tile keeps host rows at a 16-byte aligned pitch.  Vector path for
+// r in {1, 2}; any other r (or unaligned widths) takes the scalar path.
+template <int R>
+__device__ __forceinline__ void boundary_vec(const BoundaryParams& p, mlvc_half* tile)
 {
-    pdl_launch_dependents();
-    pdl_wait();
-    extern __shared__ __align__(16) uint8_t dyn_smem[];
-    mlvc_half* tile = reinterpret_cast<mlvc_half*>(dyn_smem);  // [c][dy][32*r + 1]
+    constexpr int RR = R * R;
+    constexpr int kSpan = 32 * R;
+    constexpr int kPitch = kSpan + 8;
+    const int dh = p.h, dw = p.w, dc = p.c;
+    const int hc = dc / RR, hh = dh * R, hw = dw * R;
+    const int tiles_x = (dw + 31) / 32;
+    const int tx = blockIdx.x % tiles_x;
+    const int y = (blockIdx.x / tiles_x) % dh;
+    const size_t n = blockIdx.x / (tiles_x * dh);
+    const int x0 = tx * 32, nx = min(32, dw - x0);
+    const int hx0 = x0 * R, hspan = nx * R;
+    const int rows = hc * R;
+    const int vpr = (hspan + 7) / 8;  // vectors per host row (last one may be partial)
+    const int dcv = dc / 8;
+    const size_t dev_base = ((n * dh + y) * static_cast<size_t>(dw) + x0) * dc;
+    if (!p.to_host) {
+        for (int e = threadIdx.x; e < rows * vpr; e += blockDim.x) {
+            const int row = e / vpr, v = e - (e / vpr) * vpr;
+            const int c = row / R, dy = row % R;
+            const mlvc_half* src = p.src + ((n * hc + c) * hh + y * R + dy) * static_cast<size_t>(hw) + hx0 + v * 8;
+            mlvc_half* dst = tile + row * kPitch + v * 8;
+            if (v * 8 + 8 <= hspan)
+                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+            else
+                for (int i = 0; v * 8 + i < hspan; ++i)
+                    dst[i] = src[i];
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < nx * dcv; e += blockDim.x) {
+            const int j = e / dcv, kv = e - (e / dcv) * dcv;
+            uint16_t h[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int k = kv * 8 + i;  // device channel c*R*R + dy*R + dx
+                const int c = k / RR, dy = (k % RR) / R, dx = k % R;
+                h[i] = reinterpret_cast<const uint16_t*>(tile)[(c * R + dy) * kPitch + j * R + dx];
+            }
+            uint4 o;
+            o.x = h[0] | (static_cast<uint32_t>(h[1]) << 16);
+            o.y = h[2] | (static_cast<uint32_t>(h[3]) << 16);
+            o.z = h[4] | (static_cast<uint32_t>(h[5]) << 16);
+            o.w = h[6] | (static_cast<uint32_t>(h[7]) << 16);
+            *reinterpret_cast<uint4*>(p.dst + dev_base + static_cast<size_t>(e) * 8) = o;
+        }
+    } else {
+        for (int e = threadIdx.x; e < nx * dcv; e += blockDim.x) {
+            const int j = e / dcv, kv = e - (e / dcv) * dcv;
+            const uint4 v = *reinterpret_cast<const uint4*>(p.src + dev_base + static_cast<size_t>(e) * 8);
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int k = kv * 8 + i;
+                const int c = k / RR, dy = (k % RR) / R, dx = k % R;
+                reinterpret_cast<uint16_t*>(tile)[(c * R + dy) * kPitch + j * R + dx] =
+                    static_cast<uint16_t>(w4[i / 2] >> (16 * (i % 2)));
+            }
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < rows * vpr; e += blockDim.x) {
+            const int row = e / vpr, v = e - (e / vpr) * vpr;
+            const int c = row / R, dy = row % R;
+            mlvc_half* dst = p.dst + ((n * hc + c) * hh + y * R + dy) * static_cast<size_t>(hw) + hx0 + v * 8;
+            const mlvc_half* src = tile + row * kPitch + v * 8;
+            if (v * 8 + 8 <= hspan)
+                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+            else
+                for (int i = 0; v * 8 + i < hspan; ++i)
+                    dst[i] = src[i];
+        }
+    }
+}
+
+__device__ __forceinline__ void boundary_scalar(const BoundaryParams& p, mlvc_half* tile)
+{
     const int r = p.r, rr = r * r, span = 32 * r, pitch = span + 1;
-    const int dh = p.h, dw = p.w, dc = p.c;         // device NHWC extents
-    const int hc = dc / rr, hh = dh * r, hw = dw * r; // host NCHW extents
+    const int dh = p.h, dw = p.w, dc = p.c;           // device NHWC extents
+    const int hc = dc / rr, hh = dh * r, hw = dw * r;  // host NCHW extents
     const int tiles_x = (dw + 31) / 32;
     const int band = blockIdx.x;
     const int tx = band % tiles_x;
@@ -190,7 +263,6 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid
     const long long n = band / (tiles_x * dh);
     const int x0 = tx * 32, nx = min(32, dw - x0);
     const int hx0 = x0 * r, hspan = nx * r;
-    // host side <-> tile: rows (c, dy), columns 0..hspan
     const int host_elems = hc * r * hspan;
     const int dev_elems = nx * dc;
     if (!p.to_host) {
@@ -220,6 +292,21 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid
             p.dst[((n * hc + c) * hh + y * r + dy) * static_cast<long long>(hw) + hx0 + col] = tile[row * pitch + col];
         }
     }
+}
+
+extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid_constant__ BoundaryParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ __align__(16) uint8_t dyn_smem[];
+    mlvc_half* tile = reinterpret_cast<mlvc_half*>(dyn_smem);
+    const bool vec = (p.w * p.r) % 8 == 0 && p.c % 8 == 0;
+    if (vec && p.r == 1)
+        boundary_vec<1>(p, tile);
+    else if (vec && p.r == 2)
+        boundary_vec<2>(p, tile);
+    else
+        boundary_scalar(p, tile);
 }
 
 extern "C" __global__ void mlvc_gather_rows_f16(const __grid_constant__ GatherParams p)
@@ -360,16 +447,17 @@ extern "C" __global__ void mlvc_depthwise_v8_f16(const __grid_constant__ DirectC
 // Depthwise 3x3 (stride 1 or 2, pad 0 or 1), specialised: each thread owns 8
 // consecutive channels (16 bytes) of kRows vertically adjacent output pixels.
 // A block of 256 threads covers 256 / (C/8) adjacent output columns of one
-// row strip (grid: x = column groups, y = row strips, z = images), so all
-// index math is 32-bit and division-free in the inner loops.  All input
-// vectors a thread needs ((kRows-1)*stride+3 rows x 3 columns) are loaded up
-// front, so the loads are in flight together; a warp reads contiguous
-// channel runs of adjacent pixels.  Taps outside the image are skipped, and
-// the accumulation starts from the bias and runs in (ky, kx) order with FMA.
+// row strip (grid: x = column groups, y = row strips, z = images), so the
+// index math is 32-bit and division-free.  The thread walks the three kernel
+// columns; per column it loads the (kRows-1)*stride+3 input vectors it needs
+// (all in flight together), converts each input and each weight to FP32
+// exactly once and feeds every output row that uses it, so conversions stay
+// well below the FMA count.  The accumulation starts from the bias with FP32
+// FMA; taps that fall outside the image contribute nothing.
 template <int kStride>
 __device__ __forceinline__ void depthwise3x3_body(const DirectConvParams& p)
 {
-    constexpr int kRows = 2;
+    constexpr int kRows = 4;
     constexpr int kInRows = (kRows - 1) * kStride + 3;
     const int cv = p.oc / 8;
     const int per_block = blockDim.x / cv;
@@ -381,65 +469,76 @@ __device__ __forceinline__ void depthwise3x3_body(const DirectConvParams& p)
     const int n = blockIdx.z;
     const int iy0 = oy0 * kStride - p.ph, ix0 = ox * kStride - p.pw;
     const mlvc_half* xin = p.x + static_cast<size_t>(n) * p.ih * p.iw * p.ic + c8;
-    uint4 x[kInRows][3];
+    float acc[kRows][8];
+    {
+        float bias[8];
+        if (p.bias) {
+            const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + c8));
+            const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
 #pragma unroll
-    for (int r = 0; r < kInRows; ++r)
+            for (int k = 0; k < 4; ++k)
+                unpack_h2(bw[k], bias[2 * k], bias[2 * k + 1]);
+        } else {
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const int iy = iy0 + r, ix = ix0 + c;
-            x[r][c] = (iy >= 0 && iy < p.ih && ix >= 0 && ix < p.iw)
-                          ? *reinterpret_cast<const uint4*>(xin + (static_cast<size_t>(iy) * p.iw + ix) * p.ic)
-                          : make_uint4(0, 0, 0, 0);
+            for (int k = 0; k < 8; ++k)
+                bias[k] = 0.0f;
         }
-    float bias[8];
-    if (p.bias) {
-        const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + c8));
-        const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            unpack_h2(bw[k], bias[2 * k], bias[2 * k + 1]);
-    } else {
+        for (int r = 0; r < kRows; ++r)
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-            bias[k] = 0.0f;
+            for (int k = 0; k < 8; ++k)
+                acc[r][k] = bias[k];
+    }
+#pragma unroll
+    for (int kx = 0; kx < 3; ++kx) {
+        const int ix = ix0 + kx;
+        if (ix < 0 || ix >= p.iw)
+            continue;
+        uint4 col[kInRows];
+#pragma unroll
+        for (int j = 0; j < kInRows; ++j) {
+            const int iy = iy0 + j;
+            col[j] = (iy >= 0 && iy < p.ih)
+                         ? *reinterpret_cast<const uint4*>(xin + (static_cast<size_t>(iy) * p.iw + ix) * p.ic)
+                         : make_uint4(0, 0, 0, 0);
+        }
+        float w[3][8];
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky) {
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(p.w + (ky * 3 + kx) * p.oc + c8));
+            const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                unpack_h2(ww[k], w[ky][2 * k], w[ky][2 * k + 1]);
+        }
+#pragma unroll
+        for (int j = 0; j < kInRows; ++j) {
+            float xf[8];
+            const uint32_t* xw = reinterpret_cast<const uint32_t*>(&col[j]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                unpack_h2(xw[k], xf[2 * k], xf[2 * k + 1]);
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                const int ky = j - r * kStride;
+                if (ky < 0 || ky > 2)
+                    continue;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    acc[r][k] = fmaf(xf[k], w[ky][k], acc[r][k]);
+            }
+        }
     }
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
         const int oy = oy0 + r;
         if (oy >= p.oh)
             break;
-        float acc[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-            acc[k] = bias[k];
-#pragma unroll
-        for (int ky = 0; ky < 3; ++ky) {
-            const int iy = iy0 + r * kStride + ky;
-            if (iy < 0 || iy >= p.ih)
-                continue;
-#pragma unroll
-            for (int kx = 0; kx < 3; ++kx) {
-                const int ix = ix0 + kx;
-                if (ix < 0 || ix >= p.iw)
-                    continue;
-                const uint4 wt = __ldg(reinterpret_cast<const uint4*>(p.w + (ky * 3 + kx) * p.oc + c8));
-                const uint32_t* xw = reinterpret_cast<const uint32_t*>(&x[r * kStride + ky][kx]);
-                const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wt);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    float x0, x1, w0, w1;
-                    unpack_h2(xw[k], x0, x1);
-                    unpack_h2(ww[k], w0, w1);
-                    acc[2 * k] = fmaf(x0, w0, acc[2 * k]);
-                    acc[2 * k + 1] = fmaf(x1, w1, acc[2 * k + 1]);
-                }
-            }
-        }
         uint4 ov;
         uint32_t* o = reinterpret_cast<uint32_t*>(&ov);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-            o[k] = pack_h2(acc[2 * k], acc[2 * k + 1]);
+            o[k] = pack_h2(acc[r][2 * k], acc[r][2 * k + 1]);
         *reinterpret_cast<uint4*>(p.y + ((static_cast<size_t>(n) * p.oh + oy) * p.ow + ox) * p.oc + c8) = ov;
     }
 }
