@@ -117,18 +117,20 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
                 tmem_ld16_nowait(lane_addr + c0 + 16 * h, gr);
                 tmem_ld16_nowait(lane_addr + half + c0 + 16 * h, lr);
                 tmem_wait_ld();
+                // gate/linear: FP32 bias add, one rounding each; clip and product
+                // in packed FP16 (both exact on FP16 operands: the min/max select
+                // and the single rounding of an exact FP16 x FP16 product equal
+                // the reference's FP32 clip / multiply followed by a rounding)
                 uint32_t packed[8];
+                const __half2 lo2 = __float2half2_rn(p.clip_lo), hi2 = __float2half2_rn(p.clip_hi);
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                    float r2[2];
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const float gv = round_h(__uint_as_float(gr[i + j]) + sh.bias[c0 + 16 * h + i + j]);
-                        const float lv = round_h(__uint_as_float(lr[i + j]) + sh.bias[half + c0 + 16 * h + i + j]);
-                        const float cg = round_h(fminf(fmaxf(gv, p.clip_lo), p.clip_hi));
-                        r2[j] = cg * lv;
-                    }
-                    packed[i / 2] = pack_h2(r2[0], r2[1]);
+                    const float* bg = &sh.bias[c0 + 16 * h + i];
+                    const float* bl = &sh.bias[half + c0 + 16 * h + i];
+                    const __half2 g2 = __floats2half2_rn(__uint_as_float(gr[i]) + bg[0], __uint_as_float(gr[i + 1]) + bg[1]);
+                    const __half2 l2 = __floats2half2_rn(__uint_as_float(lr[i]) + bl[0], __uint_as_float(lr[i + 1]) + bl[1]);
+                    const __half2 r2 = __hmul2(__hmin2(__hmax2(g2, lo2), hi2), l2);
+                    packed[i / 2] = *reinterpret_cast<const uint32_t*>(&r2);
                 }
                 *reinterpret_cast<uint4*>(buf + swz64(lane, 2 * h)) =
                     make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -169,33 +171,40 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
         uint32_t a[32];
         tmem_ld32_nowait(lane_addr + c0, a);
         tmem_wait_ld();
-        float v[32];
+        // conv result: FP32 bias add and one rounding, packed two per register
+        uint32_t h[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            v[i] = round_h(__uint_as_float(a[i]) + sh.bias[c0 + i]);
+        for (int i = 0; i < 16; ++i) {
+            const float2 b2 = *reinterpret_cast<const float2*>(&sh.bias[c0 + 2 * i]);
+            h[i] = pack_h2(__uint_as_float(a[2 * i]) + b2.x, __uint_as_float(a[2 * i + 1]) + b2.y);
+        }
         if (p.epilogue == kEpiLeaky) {
+            // negative halves become fp16(fp32(x) * alpha) (alpha is an FP32 constant)
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                v[i] = v[i] < 0.0f ? round_h(v[i] * p.alpha) : v[i];
+            for (int i = 0; i < 16; ++i) {
+                float x0, x1;
+                unpack_h2(h[i], x0, x1);
+                const uint32_t m = pack_h2(x0 * p.alpha, x1 * p.alpha);
+                const uint32_t neg = ((h[i] >> 15) & 0x00010001u) * 0xFFFFu;  // sign bit -> 16-bit mask
+                h[i] = (m & neg) | (h[i] & ~neg);
+            }
         } else if (residual) {
+            // fp16 + fp16 with one rounding equals the FP32 add + rounding of the reference
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const uint4 rv = *reinterpret_cast<const uint4*>(buf + swz64(lane, q));
                 const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    float ra, rb;
-                    unpack_h2(rr[i], ra, rb);
-                    v[8 * q + 2 * i] += ra;
-                    v[8 * q + 2 * i + 1] += rb;
+                    const __half2 s2 = __hadd2(*reinterpret_cast<const __half2*>(&h[4 * q + i]),
+                                               *reinterpret_cast<const __half2*>(&rr[i]));
+                    h[4 * q + i] = *reinterpret_cast<const uint32_t*>(&s2);
                 }
             }
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(buf + swz64(lane, q)) =
-                make_uint4(pack_h2(v[8 * q], v[8 * q + 1]), pack_h2(v[8 * q + 2], v[8 * q + 3]),
-                           pack_h2(v[8 * q + 4], v[8 * q + 5]), pack_h2(v[8 * q + 6], v[8 * q + 7]));
+            *reinterpret_cast<uint4*>(buf + swz64(lane, q)) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0)
