@@ -121,11 +121,12 @@ int mlvc_b200_step_info(const mlvc_b200_backend* backend, size_t index, const ch
 int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, size_t flush_bytes, float* ms_per_step);
 int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend);
 
-/* Phase trace of one tensor-core conv step: relaunches it once with
- * %globaltimer stamps enabled; writes 16 stamps per CTA (CTA start, setup
- * done, weights issued, weights landed, first activation panel, last MMA
- * commit, first accumulator seen by the epilogue, epilogue done, exit; 0 =
- * not reached) and the total count to *count. */
+/* Phase trace of one tensor-core conv or fused FFN step: relaunches it once
+ * with %globaltimer stamps enabled; writes 24 stamps per CTA (CTA start,
+ * setup done, weights issued, weights landed, first activation panel, last
+ * MMA commit, first accumulator seen by the epilogue, epilogue done, exit,
+ * then fused-FFN chunk events; 0 = not reached) and the total count to
+ * *count.  Debug facility: no counterpart in the reference. */
 int mlvc_b200_trace_step(mlvc_b200_backend* backend, size_t index, uint64_t* stamps, size_t capacity,
                          size_t* count);
 size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend);

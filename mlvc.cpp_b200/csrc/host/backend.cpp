@@ -292,6 +292,10 @@ void Backend::load_bytes(const uint8_t* graph, size_t graph_size, const uint8_t*
 // ---------------------------------------------------------------- planning
 void Backend::plan()
 {
+    {
+        const char* env = std::getenv("MLVC_B200_FFN_FUSION");
+        ffn_fusion_ = !(env && env[0] == '0');
+    }
     const size_t nt = graph_.tensors.size();
     values_.assign(nt, Value{});
     for (size_t id = 1; id < nt; ++id) {
@@ -471,6 +475,35 @@ void Backend::plan()
         return values_[mu.output].shape == values_[s1.output].shape;
     };
 
+    // Conv at node ci followed by LeakyRelu or Add of a same-shape NHWC tensor:
+    // sets the fused epilogue and returns the number of nodes the step covers.
+    auto conv_epilogue = [&](size_t ci, int& epi, float& alpha, uint32_t& out_id, uint32_t& res_id) -> size_t {
+        const NodeDesc& n = nodes[ci];
+        const auto& oshape = values_[n.output].shape;
+        epi = kEpiBias;
+        out_id = n.output;
+        res_id = 0;
+        if (!only_consumer(n.output) || ci + 1 >= nodes.size())
+            return 1;
+        const NodeDesc& e = nodes[ci + 1];
+        if (e.op == Op::kLeakyRelu && e.inputs[0] == n.output) {
+            epi = kEpiLeaky;
+            alpha = e.alpha;
+            out_id = e.output;
+            return 2;
+        }
+        if (e.op == Op::kAdd && (e.inputs[0] == n.output || e.inputs[1] == n.output)) {
+            const uint32_t r = e.inputs[0] == n.output ? e.inputs[1] : e.inputs[0];
+            if (r != n.output && values_[r].nhwc && values_[r].shape == oshape && values_[e.output].shape == oshape) {
+                epi = kEpiResidual;
+                res_id = r;
+                out_id = e.output;
+                return 2;
+            }
+        }
+        return 1;
+    };
+
     for (size_t i = 0; i < nodes.size();) {
         const NodeDesc& n = nodes[i];
         if (absorbed[i]) {
@@ -497,26 +530,7 @@ void Backend::plan()
             int epi = kEpiBias;
             float alpha = 0.0f, lo = 0.0f, hi = 0.0f;
             uint32_t out_id = n.output, res_id = 0;
-            size_t consumed = 1;
-            const bool conv_private = only_consumer(n.output);
-            if (conv_private && i + 1 < nodes.size()) {
-                const NodeDesc& e = nodes[i + 1];
-                if (e.op == Op::kLeakyRelu && e.inputs[0] == n.output) {
-                    epi = kEpiLeaky;
-                    alpha = e.alpha;
-                    out_id = e.output;
-                    consumed = 2;
-                } else if (e.op == Op::kAdd && (e.inputs[0] == n.output || e.inputs[1] == n.output)) {
-                    const uint32_t r = e.inputs[0] == n.output ? e.inputs[1] : e.inputs[0];
-                    if (r != n.output && values_[r].nhwc && values_[r].shape == oshape &&
-                        values_[e.output].shape == oshape) {
-                        epi = kEpiResidual;
-                        res_id = r;
-                        out_id = e.output;
-                        consumed = 2;
-                    }
-                }
-            }
+            size_t consumed = conv_epilogue(i, epi, alpha, out_id, res_id);
             const bool is1x1 = G == 1 && KH == 1 && KW == 1 && SH == 1 && SW == 1 && PH == 0 && PW == 0;
             bool reglu = false;
             if (epi == kEpiBias && is1x1 && match_reglu_tail(i + 1, n.output, lo, hi)) {
@@ -551,6 +565,134 @@ void Backend::plan()
             const bool tc_shape = G == 1 && N == 1 && IC % 8 == 0 && OC % 8 == 0 && (!reglu || OC % 64 == 0);
             const int header = kTcHeaderBytes;
             const int smem_cap = max_smem_optin_ - 1024;  // slack for the in-kernel 1024-byte alignment
+            if (reglu && tc_shape && is1x1 && ffn_fusion_ && i + 5 < nodes.size() && IC % 64 == 0 && IC <= 256 &&
+                (OC / 2) % kFfnChunk == 0 && OC / 2 <= kFfnMaxHidden) {
+                // ---- fused feed-forward block: this ReGLU conv and the 1x1 conv that
+                // consumes its output, with the hidden tensor kept on chip
+                const NodeDesc& n2 = nodes[i + 5];
+                const int H = OC / 2;
+                const uint32_t hid_id = out_id;
+                bool ok = n2.op == Op::kConv && n2.inputs[0] == hid_id && only_consumer(hid_id) && n2.groups == 1 &&
+                          n2.strides[0] == 1 && n2.strides[1] == 1 && n2.pads[0] == 0 && n2.pads[1] == 0;
+                const uint32_t w2_id = ok ? n2.inputs[1] : 0;
+                const uint32_t b2_id = ok && n2.inputs.size() > 2 ? n2.inputs[2] : 0;
+                int OC2 = 0;
+                if (ok) {
+                    const Value& w2v = values_[w2_id];
+                    ok = w2v.kind == Value::kWeight && w2v.dtype == DType::kFp16 && w2v.shape.size() == 4 &&
+                         w2v.shape[1] == H && w2v.shape[2] == 1 && w2v.shape[3] == 1 &&
+                         (!b2_id || values_[b2_id].kind == Value::kWeight);
+                    OC2 = ok ? static_cast<int>(w2v.shape[0]) : 0;
+                    ok = ok && OC2 % 32 == 0 && OC2 <= 256;
+                }
+                const int kpan = IC / 64, M = IH * IW;
+                const int slot = std::max(16384, OC2 * 128);
+                const int m_tiles = (M + 127) / 128;
+                const int grid = std::min(m_tiles, sm_count_);
+                const int per_cta = (m_tiles + grid - 1) / grid;
+                // Fixed part: alignment slack, header, two hidden panels (which are
+                // also the output staging buffers).
+                const int fixed = 1024 + kFfnHeaderBytes + 2 * 16384;
+                auto ws_for = [&](int xs) { return (max_smem_optin_ - fixed - xs * kpan * 16384) / slot; };
+                int xs = per_cta > 1 && ws_for(2) >= 6 ? 2 : 1;
+                const int ws = std::min(kFfnMaxWStages, ws_for(xs));
+                // One CTA per SM (above half of the SM's shared memory): its 512 TMEM
+                // columns never wait for another CTA's.
+                const int ffn_smem = fixed + xs * kpan * 16384 + ws * slot;
+                if (ok && ws >= 2 && ffn_smem > 233472 / 2) {
+                    int epi2 = kEpiBias;
+                    float alpha2 = 0.0f;
+                    uint32_t out2 = 0, res2 = 0;
+                    const size_t consumed2 = conv_epilogue(i + 5, epi2, alpha2, out2, res2);
+                    // W1 rows in chunk order: per 64 hidden channels, 64 gate rows then 64 linear rows.
+                    std::vector<uint16_t> w1p(static_cast<size_t>(OC) * IC), b1p(OC);
+                    for (int r = 0; r < OC; ++r) {
+                        const int j = r / 128, k = r % 128;
+                        const int src = k < 64 ? j * 64 + k : H + j * 64 + (k - 64);
+                        std::memcpy(&w1p[static_cast<size_t>(r) * IC], w + static_cast<size_t>(src) * IC, IC * 2);
+                        b1p[r] = bias_full[src];
+                    }
+                    std::vector<uint16_t> b2p(OC2, 0);
+                    if (b2_id)
+                        std::copy(wdata(b2_id), wdata(b2_id) + OC2, b2p.begin());
+                    const size_t w1_off = prep(w1p.data(), w1p.size() * 2);
+                    const size_t b1_off = prep(b1p.data(), b1p.size() * 2);
+                    const size_t w2_off = prep(wdata(w2_id), static_cast<size_t>(OC2) * H * 2);
+                    const size_t b2_off = prep(b2p.data(), b2p.size() * 2);
+                    Step f;
+                    f.reads = {x_id};
+                    if (res2)
+                        f.reads.push_back(res2);
+                    f.writes = {out2};
+                    {
+                        std::ostringstream os;
+                        os << i << "-" << (i + 5 + consumed2 - 1);
+                        f.info.nodes = os.str();
+                    }
+                    f.info.flops = 2.0 * M * (static_cast<double>(OC) * IC + static_cast<double>(OC2) * H);
+                    f.info.bytes = 2.0 * (static_cast<double>(M) * IC + static_cast<double>(OC) * IC + OC +
+                                          static_cast<double>(OC2) * H + OC2 + static_cast<double>(M) * OC2 * (res2 ? 2 : 1));
+                    f.kernel = "mlvc_ffn_tc";
+                    f.info.kernel = f.kernel;
+                    f.smem = static_cast<unsigned>(ffn_smem);
+                    f.block = 320;
+                    f.grid = static_cast<unsigned>(grid);
+                    const float clip_lo = lo, clip_hi = hi;
+                    f.build = [=, this](Step& st) {
+                        FfnTcParams fp{};
+                        ConvTcParams& p = fp.c;
+                        const cuuint32_t elem1[2] = {1, 1};
+                        auto encode = [&](CUtensorMap* map, CUdeviceptr addr, cuuint64_t cols, cuuint64_t rows,
+                                          cuuint32_t box_cols, cuuint32_t box_rows, CUtensorMapSwizzle swz,
+                                          const char* what) {
+                            const cuuint64_t dims[2] = {cols, rows};
+                            const cuuint64_t strides[1] = {cols * 2};
+                            const cuuint32_t box[2] = {box_cols, box_rows};
+                            check(cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                                         reinterpret_cast<void*>(addr), dims, strides, box, elem1,
+                                                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  what);
+                        };
+                        encode(&p.map_a0, values_[x_id].addr, IC, M, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B,
+                               "cuTensorMapEncodeTiled(ffn X)");
+                        encode(&p.map_b, prepped_dev_.get() + w1_off, IC, OC, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B,
+                               "cuTensorMapEncodeTiled(ffn W1)");
+                        encode(&fp.map_w2, prepped_dev_.get() + w2_off, H, OC2, 64, static_cast<cuuint32_t>(OC2),
+                               CU_TENSOR_MAP_SWIZZLE_128B, "cuTensorMapEncodeTiled(ffn W2)");
+                        encode(&p.map_out, values_[out2].addr, OC2, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
+                               "cuTensorMapEncodeTiled(ffn out)");
+                        p.map_a1 = p.map_a0;
+                        p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b2_off);
+                        p.residual = res2 ? reinterpret_cast<const mlvc_half*>(values_[res2].addr) : nullptr;
+                        p.out = reinterpret_cast<mlvc_half*>(values_[out2].addr);
+                        p.M = M;
+                        p.N = OC2;
+                        p.n_valid = OC2;
+                        p.K = IC;
+                        p.BN = OC2;
+                        p.n_tiles = 1;
+                        p.m_tiles = m_tiles;
+                        p.ldo = OC2;
+                        p.out_col0 = 0;
+                        p.ldr = OC2;
+                        p.epilogue = epi2;
+                        p.alpha = alpha2;
+                        p.clip_lo = clip_lo;
+                        p.clip_hi = clip_hi;
+                        p.a_stages = xs;
+                        p.b_stages = ws;
+                        fp.bias1 = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b1_off);
+                        fp.hidden = H;
+                        fp.w_slot_bytes = slot;
+                        st.set(fp);
+                    };
+                    steps_.push_back(std::move(f));
+                    i += 5 + consumed2;
+                    continue;
+                }
+            }
             if (tc_shape && is1x1) {
                 // ---- tcgen05 GEMM
                 const int K = IC, NN = (OC + 31) / 32 * 32;  // weight rows padded to a multiple of 32
@@ -1424,7 +1566,7 @@ std::vector<uint64_t> Backend::trace_step(size_t index)
     if (offline_)
         throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
     Step& st = steps_.at(index);
-    if (st.kernel != "mlvc_conv1x1_tc" && st.kernel != "mlvc_convkxk_tc")
+    if (st.kernel != "mlvc_conv1x1_tc" && st.kernel != "mlvc_convkxk_tc" && st.kernel != "mlvc_ffn_tc")
         throw std::runtime_error("mlvc-b200: only tensor-core conv steps carry a phase trace");
     ContextGuard guard(ctx_);
     const size_t n = static_cast<size_t>(st.grid) * kTracePoints;

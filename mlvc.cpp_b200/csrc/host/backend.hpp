@@ -142,6 +142,9 @@ private:
     bool state_ready_ = false;
     bool loaded_ = false;
     bool offline_ = false;
+    // FFN fusion (ReGLU conv + following 1x1 conv in one kernel); MLVC_B200_FFN_FUSION=0 plans
+    // the two convs as separate steps (same results, for comparison).
+    bool ffn_fusion_ = true;
     bool keep_all_values_ = false;
 };
 

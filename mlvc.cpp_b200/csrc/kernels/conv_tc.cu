@@ -48,9 +48,10 @@ struct TcShared {
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
-    float bias[256];
+    alignas(16) float bias[256];  // read as float2
 };
 static_assert(sizeof(TcShared) <= kTcHeaderBytes, "TcShared must fit the header reserved by the host");
+static_assert(offsetof(TcShared, bias) % 16 == 0, "vector bias reads");
 
 __device__ __forceinline__ void trace(const ConvTcParams& p, int point)
 {
@@ -97,9 +98,61 @@ __device__ __forceinline__ void store_block(const ConvTcParams& p, const uint8_t
     bulk_commit();
 }
 
-__device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcShared& sh, uint32_t tmem_acc,
+// Residual block of one 32-column chunk (32 rows x 64 bytes) as 4 coalesced
+// 16-byte pieces per lane: piece lane + 32 j holds row (piece / 4), 8-channel
+// group (piece % 4).
+__device__ __forceinline__ void residual_fetch(const ConvTcParams& p, const EpiTile& et, int col, int lane, bool kxk,
+                                               uint4 (&v)[4])
+{
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int piece = lane + 32 * j, r = piece >> 2, ch = piece & 3;
+        v[j] = make_uint4(0, 0, 0, 0);
+        if (r < et.rows_valid && col + 8 * (ch + 1) <= p.n_valid) {
+            const long long px = kxk ? static_cast<long long>(et.oy) * p.out_w + et.ox0 + r : et.pixel0 + r;
+            v[j] = __ldg(reinterpret_cast<const uint4*>(p.residual + px * p.ldr + col + ch * 8));
+        }
+    }
+}
+
+// Writes fetched residual pieces into a staging block (one row per lane later).
+__device__ __forceinline__ void residual_put(uint8_t* buf, int lane, const uint4 (&v)[4])
+{
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int piece = lane + 32 * j;
+        *reinterpret_cast<uint4*>(buf + swz64(piece >> 2, piece & 3)) = v[j];
+    }
+}
+
+// Residual of the warp's first two chunks, loaded into its two staging buffers
+// before the accumulator is ready (the load latency overlaps the MMAs).  The
+// warp's earlier TMA stores must have finished reading the buffers; `nbuf`
+// restarts at 0 so chunk k of the tile uses buffer k % 2.
+__device__ __forceinline__ void residual_prestage(const ConvTcParams& p, const EpiTile& et, int n_tile, int c0, int lane,
+                                                  bool kxk, uint8_t* stage, int& nbuf)
+{
+    uint4 r0[4], r1[4];
+    const bool two = c0 + 64 < p.BN;
+    const int col0 = n_tile * p.BN + c0;
+    residual_fetch(p, et, col0, lane, kxk, r0);
+    if (two)
+        residual_fetch(p, et, col0 + 64, lane, kxk, r1);
+    if (lane == 0)
+        bulk_wait_read<0>();
+    __syncwarp();
+    residual_put(stage, lane, r0);
+    if (two)
+        residual_put(stage + 2048, lane, r1);
+    __syncwarp();
+    nbuf = 0;
+}
+
+// Chunks [0, staged) of the warp find their residual block already in the
+// staging buffer (residual_prestage); later chunks load it here.
+__device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const float* bias, uint32_t tmem_acc,
                                               int quadrant, int group, int lane, const EpiTile& et, int n_tile,
-                                              uint8_t* stage, int& nbuf, bool kxk)
+                                              uint8_t* stage, int& nbuf, bool kxk, int staged)
 {
     const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16);
     if (p.epilogue == kEpiReglu) {
@@ -125,8 +178,8 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
                 const __half2 lo2 = __float2half2_rn(p.clip_lo), hi2 = __float2half2_rn(p.clip_hi);
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                    const float* bg = &sh.bias[c0 + 16 * h + i];
-                    const float* bl = &sh.bias[half + c0 + 16 * h + i];
+                    const float* bg = &bias[c0 + 16 * h + i];
+                    const float* bl = &bias[half + c0 + 16 * h + i];
                     const __half2 g2 = __floats2half2_rn(__uint_as_float(gr[i]) + bg[0], __uint_as_float(gr[i + 1]) + bg[1]);
                     const __half2 l2 = __floats2half2_rn(__uint_as_float(lr[i]) + bl[0], __uint_as_float(lr[i + 1]) + bl[1]);
                     const __half2 r2 = __hmul2(__hmin2(__hmax2(g2, lo2), hi2), l2);
@@ -146,7 +199,7 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
         return;
     }
     const bool residual = p.epilogue == kEpiResidual;
-    for (int c0 = group * 32; c0 < p.BN; c0 += 64) {
+    for (int c0 = group * 32, k = 0; c0 < p.BN; c0 += 64, ++k) {
         uint8_t* buf = stage + (nbuf & 1) * 2048;
         if (nbuf >= 2) {
             if (lane == 0)
@@ -154,18 +207,10 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
             __syncwarp();
         }
         const int col = n_tile * p.BN + c0;
-        if (residual) {
-            // 32 rows x 64 bytes, 8 rows per instruction, contiguous 64-byte segments
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int piece = lane + 32 * j, r = piece >> 2, ch = piece & 3;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (r < et.rows_valid && col + 8 * (ch + 1) <= p.n_valid) {
-                    const long long px = kxk ? static_cast<long long>(et.oy) * p.out_w + et.ox0 + r : et.pixel0 + r;
-                    v = *reinterpret_cast<const uint4*>(p.residual + px * p.ldr + col + ch * 8);
-                }
-                *reinterpret_cast<uint4*>(buf + swz64(r, ch)) = v;
-            }
+        if (residual && k >= staged) {
+            uint4 v[4];
+            residual_fetch(p, et, col, lane, kxk, v);
+            residual_put(buf, lane, v);
             __syncwarp();
         }
         uint32_t a[32];
@@ -175,7 +220,7 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const TcSha
         uint32_t h[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const float2 b2 = *reinterpret_cast<const float2*>(&sh.bias[c0 + 2 * i]);
+            const float2 b2 = *reinterpret_cast<const float2*>(&bias[c0 + 2 * i]);
             h[i] = pack_h2(__uint_as_float(a[2 * i]) + b2.x, __uint_as_float(a[2 * i + 1]) + b2.y);
         }
         if (p.epilogue == kEpiLeaky) {
@@ -244,13 +289,19 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
             et.rows_valid = max(0, min(32, p.out_w - et.ox0));
             et.pixel0 = static_cast<long long>(et.oy) * p.out_w + et.ox0;
         }
+        int staged = 0;
+        if (p.epilogue == kEpiResidual && et.rows_valid > 0 && group * 32 < p.BN) {
+            residual_prestage(p, et, n_tile, group * 32, lane, kxk, stage, nbuf);
+            staged = 2;
+        }
         if (!mbar_wait(&sh.tmem_full[acc], acc_phase, &sh.abort_flag, kErrWaitEpilogue))
             break;
         tc_fence_after();
         if (t == first_tile && et_id == 0)
             trace(p, kTrFirstAcc);
         if (et.rows_valid > 0)
-            epilogue_tile(p, sh, sh.tmem_base + acc * p.BN, quadrant, group, lane, et, n_tile, stage, nbuf, kxk);
+            epilogue_tile(p, sh.bias, sh.tmem_base + acc * p.BN, quadrant, group, lane, et, n_tile, stage, nbuf, kxk,
+                          staged);
         tc_fence_before();
         mbar_arrive(&sh.tmem_empty[acc]);
         acc ^= 1u;
@@ -329,14 +380,26 @@ __device__ __forceinline__ void teardown(const ConvTcParams& p, TcShared* sh, in
         trace(p, kTrExit);
 }
 
+// Register-resident record of the TMA loads a producer armed: bit s of
+// `armed` = slot s was armed, bit s of `parity` = the phase it was armed for
+// (bit masks rather than arrays, so nothing of it lives in local memory).
+struct ArmedSlots {
+    uint32_t armed = 0, parity = 0;
+    __device__ __forceinline__ void arm(int s, uint32_t phase)
+    {
+        armed |= 1u << s;
+        parity = (parity & ~(1u << s)) | (phase << s);
+    }
+};
+
 // Producer-side drain: wait (bounded) for every TMA this thread armed, so no
 // bulk copy is still writing shared memory when an aborted CTA exits.
-__device__ __forceinline__ void drain_armed(uint64_t* bars, const uint32_t* armed_parity, const bool* armed, int n)
+__device__ __forceinline__ void drain_armed(uint64_t* bars, const ArmedSlots& a, int n)
 {
     volatile int never = 0;
     for (int s = 0; s < n; ++s)
-        if (armed[s])
-            mbar_wait(&bars[s], armed_parity[s], &never, kErrWaitProducer);
+        if ((a.armed >> s) & 1u)
+            mbar_wait(&bars[s], (a.parity >> s) & 1u, &never, kErrWaitProducer);
 }
 
 // ===================================================== 1x1 conv (GEMM)
@@ -344,7 +407,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
 {
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
     // 1024-byte alignment for the swizzled operand tiles.
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = align_smem_1024(smem_dyn);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     TcShared* sh = setup_shared(base, p, warp);
     uint8_t* b_smem = base + ((sizeof(TcShared) + 1023) & ~size_t(1023));
@@ -362,9 +425,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
 
     if (warp == 0) {
         if (elect_one()) {
-            bool armed[kMaxStages] = {};
-            uint32_t armed_parity[kMaxStages] = {};
-            bool b_armed = true;
+            ArmedSlots a_armed, b_armed;
+            b_armed.arm(0, 0);
             mbar_arrive_expect_tx(&sh->b_full[0], static_cast<uint32_t>(b_panel_bytes * k_panels));
             for (int kp = 0; kp < k_panels; ++kp)
                 tma_load_2d(b_smem + kp * b_panel_bytes, &p.map_b, &sh->b_full[0], kp * 64, n_tile * p.BN);
@@ -379,8 +441,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                         break;
                     mbar_arrive_expect_tx(&sh->a_full[stage], kAPanelBytes);
                     tma_load_2d(a_smem + stage * kAPanelBytes, &p.map_a0, &sh->a_full[stage], kp * 64, m_tile * kBM);
-                    armed[stage] = true;
-                    armed_parity[stage] = phase;
+                    a_armed.arm(stage, phase);
                     if (++stage == p.a_stages) {
                         stage = 0;
                         phase ^= 1u;
@@ -388,9 +449,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                 }
             }
             if (sh->abort_flag) {
-                drain_armed(sh->a_full, armed_parity, armed, p.a_stages);
-                const uint32_t zero = 0;
-                drain_armed(sh->b_full, &zero, &b_armed, 1);
+                drain_armed(sh->a_full, a_armed, p.a_stages);
+                drain_armed(sh->b_full, b_armed, 1);
             }
         }
         __syncwarp();
@@ -459,7 +519,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
 extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const __grid_constant__ ConvTcParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = align_smem_1024(smem_dyn);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     TcShared* sh = setup_shared(base, p, warp);
     if (warp == 0 && elect_one() && p.stride == 2)
@@ -491,15 +551,14 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
 
     if (warp == 0) {
         if (elect_one()) {
-            bool a_armed[kMaxStages] = {}, b_armed[kMaxStages] = {};
-            uint32_t a_par[kMaxStages] = {}, b_par[kMaxStages] = {};
+            ArmedSlots a_armed, b_armed;
             if (p.b_resident) {
                 mbar_arrive_expect_tx(&sh->b_full[0], b_panel_bytes * taps * k_panels);
                 for (int kp = 0; kp < k_panels; ++kp)
                     for (int tap = 0; tap < taps; ++tap)
                         tma_load_2d(b_smem + static_cast<size_t>(kp * taps + tap) * b_panel_bytes, &p.map_b,
                                     &sh->b_full[0], tap * p.in_c + kp * 64, n_tile * p.BN);
-                b_armed[0] = true;
+                b_armed.arm(0, 0);
             }
             pdl_wait();  // activations are written by the previous kernel
             int as = 0, bs = 0;
@@ -525,8 +584,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
                         for (int j = 0; j < 8; ++j)
                             tma_load_3d(dst + (q * 8 + j) * chunk_bytes, q ? &p.map_a1 : &p.map_a0, &sh->a_full[as],
                                         kp * 64 + j * 8, x0, iy0);
-                    a_armed[as] = true;
-                    a_par[as] = aph;
+                    a_armed.arm(as, aph);
                     if (++as == p.a_stages) {
                         as = 0;
                         aph ^= 1u;
@@ -538,8 +596,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
                             mbar_arrive_expect_tx(&sh->b_full[bs], b_panel_bytes);
                             tma_load_2d(b_smem + static_cast<size_t>(bs) * b_panel_bytes, &p.map_b, &sh->b_full[bs],
                                         tap * p.in_c + kp * 64, n_tile * p.BN);
-                            b_armed[bs] = true;
-                            b_par[bs] = bph;
+                            b_armed.arm(bs, bph);
                             if (++bs == p.b_stages) {
                                 bs = 0;
                                 bph ^= 1u;
@@ -549,8 +606,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
                 }
             }
             if (sh->abort_flag) {
-                drain_armed(sh->a_full, a_par, a_armed, p.a_stages);
-                drain_armed(sh->b_full, b_par, b_armed, p.b_resident ? 1 : p.b_stages);
+                drain_armed(sh->a_full, a_armed, p.a_stages);
+                drain_armed(sh->b_full, b_armed, p.b_resident ? 1 : p.b_stages);
             }
         }
         __syncwarp();

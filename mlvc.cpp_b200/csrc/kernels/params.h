@@ -77,7 +77,42 @@ enum TracePoint : int {
     kTrFirstAcc = 6,       // epilogue saw the first accumulator
     kTrEpilogueDone = 7,   // epilogue finished its last tile
     kTrExit = 8,           // CTA teardown done
-    kTracePoints = 16
+    kTrFfnHidden0 = 9,     // fused FFN: epilogue wrote the first hidden chunk
+    kTrFfnHiddenLast = 10, // fused FFN: epilogue wrote the first tile's last hidden chunk
+    kTrFfnAcc2 = 11,       // fused FFN: epilogue saw the first tile's output accumulator
+    kTrFfnXIssued = 12,    // fused FFN: producer issued the first X tile
+    kTrFfnChunkWaited = 13,  // fused FFN: epilogue passed both waits of hidden chunk 1
+    kTrFfnChunkLoaded = 14,  // fused FFN: chunk 1 accumulators in registers
+    kTrFfnChunkStored = 15,  // fused FFN: chunk 1 written to shared memory
+    kTrFfnG1First = 16,      // fused FFN: MMA issuer committed GEMM1 of chunk 0
+    kTrFfnG1Second = 17,     // fused FFN: MMA issuer committed GEMM1 of chunk 1
+    kTrFfnG2First = 18,      // fused FFN: MMA issuer passed the waits of GEMM2 chunk 0
+    kTrFfnChunk1Done = 19,   // fused FFN: epilogue released hidden chunk 1
+    kTracePoints = 24
+};
+
+// Fused feed-forward block (mlvc_ffn_tc):
+//     hidden = clip(fp16(X W1g^T + b1g), lo, hi) * fp16(X W1l^T + b1l)   (ReGLU, FP16 rounding per op)
+//     out    = epilogue(fp16(hidden W2^T + b2))                           (bias / LeakyReLU / + residual)
+// The hidden tensor stays in shared memory, 64 channels at a time.
+constexpr int kFfnHeaderBytes = 4096;  // barriers, TMEM address, both bias vectors
+constexpr int kFfnChunk = 64;          // hidden channels per chunk
+constexpr int kFfnMaxHidden = 256;     // bias1 capacity in the header (2 x hidden floats)
+constexpr int kFfnMaxWStages = 12;     // weight ring slots (barrier pairs in the header)
+
+struct FfnTcParams {
+    // map_a0 = X [M, C] (128 x 64 boxes), map_b = W1 in chunk order
+    // [hidden/64 x (64 gate + 64 linear) rows, C] (128 x 64 boxes), map_out /
+    // bias (b2) / residual / out / epilogue describe the second conv's output;
+    // K = C, BN = N = n_valid = output channels, a_stages = X tiles in flight,
+    // b_stages = weight ring slots, clip_lo/clip_hi = ReGLU clip.
+    ConvTcParams c;
+    CUtensorMap map_w2;      // W2 [C_out rows, hidden] (C_out x 64 boxes)
+    const mlvc_half* bias1;  // [2 x hidden] in W1's chunk order
+    int hidden;              // hidden channels (multiple of 64, <= kFfnMaxHidden)
+    int w_slot_bytes;        // bytes per weight ring slot (max of a W1 and a W2 panel)
+    // Shared memory: header, X tiles (a_stages), two hidden panels (also the
+    // output epilogue's staging buffers), weight ring (b_stages slots).
 };
 
 struct ElementwiseParams {

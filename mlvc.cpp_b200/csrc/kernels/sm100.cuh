@@ -55,6 +55,15 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // ---------------------------------------------------------------- mbarrier
+// Rounds a pointer into dynamic shared memory up to 1024 bytes by pointer
+// arithmetic on the shared array itself, so that the compiler keeps knowing
+// the address space of everything derived from it (shared-memory loads and
+// stores instead of generic ones).
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* smem)
+{
+    return smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
 {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

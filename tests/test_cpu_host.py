@@ -138,19 +138,44 @@ def _kernels(be):
     return [s["kernel"] for s in be.steps()]
 
 
-def test_plan_block_stack_fuses_like_the_reference():
+def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
     """Conv+LeakyReLU, Conv+Add and Conv+Slice+Slice+Clip+Mul collapse into the
-    tensor-core conv epilogue (fusion_registry.cpp:711-1036)."""
+    tensor-core conv epilogue (fusion_registry.cpp:711-1036); with FFN fusion
+    the ReGLU conv and the conv after it (+ residual Add) become one step."""
     gb, _ = build_block_stack(seed=0)
     be = plan(*gb.finish())
     k = _kernels(be)
-    assert k.count("mlvc_conv1x1_tc") == 32
+    assert k.count("mlvc_conv1x1_tc") == 16 and k.count("mlvc_ffn_tc") == 8
     assert k.count("mlvc_depthwise3x3_f16") == 8
     assert "mlvc_unary_f16" not in k and "mlvc_binary_same_f16" not in k and "mlvc_reglu_f16" not in k
-    nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_conv1x1_tc"]
-    assert "6-10" in nodes  # conv + slice + slice + clip + mul
+    nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_ffn_tc"]
+    assert "6-12" in nodes  # conv + slice + slice + clip + mul + conv + add
     flops = sum(s["flops"] for s in be.steps())
     assert abs(flops - 39.13e9) / 39.13e9 < 0.01  # config-2 algorithmic FLOPs
+    assert all(s["smem"] > 233472 // 2 for s in be.steps() if s["kernel"] == "mlvc_ffn_tc")  # one CTA per SM
+
+    monkeypatch.setenv("MLVC_B200_FFN_FUSION", "0")
+    split = _kernels(plan(*gb.finish()))
+    assert split.count("mlvc_conv1x1_tc") == 32 and "mlvc_ffn_tc" not in split
+    nodes = [s["nodes"] for s in plan(*gb.finish()).steps() if s["kernel"] == "mlvc_conv1x1_tc"]
+    assert "6-10" in nodes  # conv + slice + slice + clip + mul
+
+
+@pytest.mark.parametrize("c,hidden,c_out,fused", [
+    (128, 256, 128, True), (64, 64, 32, True), (256, 128, 256, True), (64, 192, 96, True),
+    (48, 64, 32, False),   # C not a multiple of 64
+    (128, 512, 128, False),  # hidden above the kernel's bias capacity
+    (128, 256, 136, False),  # C_out not a multiple of 32
+])
+def test_plan_ffn_fusion_predicates(c, hidden, c_out, fused):
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, 9, 21])
+    t = gb.conv(x, gb.weight("w1", np.zeros((2 * hidden, c, 1, 1), np.float16)))
+    gate, lin = gb.slice(t, 1, 0, hidden), gb.slice(t, 1, hidden, 2 * hidden)
+    y = gb.conv(gb.mul(gb.clip(gate, 0.0, 1.0), lin), gb.weight("w2", np.zeros((c_out, hidden, 1, 1), np.float16)))
+    gb.output(y, "y")
+    k = _kernels(plan(*gb.finish()))
+    assert ("mlvc_ffn_tc" in k) == fused, k
 
 
 def test_plan_conv3x3_uses_halo_kernel():

@@ -72,6 +72,60 @@ def test_conv1x1_reglu(c, h, w):
     assert len([s for s in steps if s["kernel"] != "mlvc_boundary_f16"]) == 1, steps
 
 
+FFN_CASES = [  # (C, hidden, C_out, H, W, epilogue of the second conv)
+    (128, 256, 128, 92, 160, "residual"),  # block-stack FFN (residual = FFN input)
+    (64, 64, 32, 13, 17, None),            # one hidden chunk, ragged last tile
+    (256, 128, 256, 8, 20, "leaky"),       # four input panels, one accumulator buffer
+    (128, 256, 128, 160, 160, "residual"), # 200 tiles: two tiles per CTA, two X buffers
+    (64, 192, 96, 20, 30, "residual_other"),
+]
+
+
+def _ffn_graph(c, hidden, c_out, h, w, epilogue, seed=21):
+    rng = np.random.default_rng(seed)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, h, w])
+    w1 = gb.weight("w1", (rng.standard_normal((2 * hidden, c, 1, 1), dtype=np.float32) * np.sqrt(2.0 / c)).astype(np.float16))
+    b1 = gb.weight("b1", rng.uniform(-0.1, 0.1, 2 * hidden).astype(np.float16))
+    w2 = gb.weight("w2", (rng.standard_normal((c_out, hidden, 1, 1), dtype=np.float32) * np.sqrt(1.0 / hidden)).astype(np.float16))
+    b2 = gb.weight("b2", rng.uniform(-0.1, 0.1, c_out).astype(np.float16))
+    t = gb.conv(x, w1, b1)
+    gate = gb.slice(t, 1, 0, hidden)
+    lin = gb.slice(t, 1, hidden, 2 * hidden)
+    hid = gb.mul(gb.clip(gate, 0.0, 1.0), lin)  # node order of the exported ReGLU tail
+    y = gb.conv(hid, w2, b2)
+    inputs = [rng.standard_normal((1, c, h, w), dtype=np.float32).astype(np.float16)]
+    if epilogue == "residual":
+        y = gb.add(y, x)
+    elif epilogue == "residual_other":
+        r = gb.input("r", [1, c_out, h, w])
+        y = gb.add(r, y)
+        inputs.append(rng.standard_normal((1, c_out, h, w), dtype=np.float32).astype(np.float16))
+    elif epilogue == "leaky":
+        y = gb.leaky_relu(y, 0.01)
+    gb.output(y, "y")
+    return gb, inputs
+
+
+@pytest.mark.parametrize("c,hidden,c_out,h,w,epilogue", FFN_CASES)
+def test_ffn_fused(c, hidden, c_out, h, w, epilogue, monkeypatch):
+    """Conv1x1 -> ReGLU -> Conv1x1 (+ residual / LeakyReLU) as one kernel with
+    the hidden tensor on chip: parity with the oracle, and bit-identical to the
+    same graph planned as separate tensor-core convs (same accumulation order,
+    same FP16 roundings)."""
+    gb, inputs = _ffn_graph(c, hidden, c_out, h, w, epilogue)
+    got, want, be = run_both(gb, inputs)
+    compare(got[0], want[0])
+    kernels = [s["kernel"] for s in be.steps() if s["kernel"] != "mlvc_boundary_f16"]
+    assert kernels == ["mlvc_ffn_tc"], kernels
+    graph, weights = gb.finish()
+    monkeypatch.setenv("MLVC_B200_FFN_FUSION", "0")
+    split = Backend(0)
+    split.load_memory(graph, weights)
+    assert "mlvc_ffn_tc" not in {s["kernel"] for s in split.steps()}
+    bits_equal(split.run(inputs)[0], got[0])
+
+
 SPATIAL = [  # (IC, OC, stride, kernel, pad, H, W)
     (24, 24, 1, 3, 1, 13, 17), (40, 264, 2, 3, 1, 13, 17), (8, 8, 2, 2, 0, 13, 17), (128, 256, 2, 2, 0, 13, 17),
     (64, 64, 1, 3, 1, 13, 17), (64, 128, 2, 3, 1, 13, 17), (64, 64, 1, 3, 1, 46, 300), (128, 64, 1, 3, 1, 9, 140),
