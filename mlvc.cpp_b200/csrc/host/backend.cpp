@@ -91,6 +91,33 @@ float half_bits_to_float(uint16_t h)
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Output / residual tile view of a tensor-core epilogue on an NHWC tensor:
+// 1x1 (w == 0): {channels, pixels} with {64, 128} boxes; k x k: {channels,
+// w, h} with {64, 128, 1} boxes; 128-byte swizzle.  Boxes are clipped (stores)
+// or zero-filled (loads) at the tensor edges.
+void encode_tile_map(CUtensorMap* map, CUdeviceptr addr, int channels, int pixels, int w, int h, const char* what)
+{
+    const cuuint32_t elem[3] = {1, 1, 1};
+    const cuuint64_t c = static_cast<cuuint64_t>(channels);
+    if (w == 0) {
+        const cuuint64_t dims[2] = {c, static_cast<cuuint64_t>(pixels)};
+        const cuuint64_t strides[1] = {c * 2};
+        const cuuint32_t box[2] = {64, 128};
+        check(cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, reinterpret_cast<void*>(addr), dims,
+                                     strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+              what);
+    } else {
+        const cuuint64_t dims[3] = {c, static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h)};
+        const cuuint64_t strides[2] = {c * 2, static_cast<cuuint64_t>(w) * c * 2};
+        const cuuint32_t box[3] = {64, 128, 1};
+        check(cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, reinterpret_cast<void*>(addr), dims,
+                                     strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+              what);
+    }
+}
+
 std::vector<int64_t> dims4(const std::vector<int64_t>& s)
 {
     std::vector<int64_t> d(4 - std::min<size_t>(4, s.size()), 1);
@@ -152,10 +179,30 @@ struct Backend::Step {
     }
 };
 
+// One buffered frame of the slot pipeline (reference: the two codec slots of
+// backends/driver_cubin/src/cuda_graph_executor.cpp:205-290).  Pinned host
+// buffers for the caller, device staging of its own, and a CUDA graph that
+// moves the staged inputs into the schedule's input buffers, runs the
+// schedule and copies the outputs out to the staging: the host->device copy
+// of one slot and the device->host copy of another overlap the schedule of a
+// third on separate copy streams.
 struct Backend::Slot {
     std::vector<PinnedBuffer> in, out;
-    Event done;
+    std::vector<DeviceBuffer> din, dout;
+    Event in_done{CU_EVENT_DISABLE_TIMING}, computed{CU_EVENT_DISABLE_TIMING}, done{CU_EVENT_DISABLE_TIMING};
+    CUgraph graph = nullptr;
+    CUgraphExec exec = nullptr;
     bool pending = false;
+    Slot() = default;
+    Slot(const Slot&) = delete;
+    Slot& operator=(const Slot&) = delete;
+    ~Slot()
+    {
+        if (exec)
+            cuGraphExecDestroy(exec);
+        if (graph)
+            cuGraphDestroy(graph);
+    }
 };
 
 // ------------------------------------------------------------ lifecycle
@@ -195,6 +242,9 @@ Backend::~Backend()
     cuCtxSetCurrent(ctx_);
     if (stream_)
         cuStreamSynchronize(stream_);
+    for (CUstream s : {copy_in_, copy_out_})
+        if (s)
+            cuStreamSynchronize(s);
     if (graph_exec_)
         cuGraphExecDestroy(graph_exec_);
     if (graph_handle_)
@@ -210,6 +260,11 @@ Backend::~Backend()
     state_dev_.clear();
     if (module_)
         cuModuleUnload(module_);
+    for (CUstream s : {copy_in_, copy_out_})
+        if (s) {
+            cuStreamSynchronize(s);
+            cuStreamDestroy(s);
+        }
     if (stream_)
         cuStreamDestroy(stream_);
     cuDevicePrimaryCtxRelease(dev_);
@@ -583,7 +638,8 @@ void Backend::plan()
                          w2v.shape[1] == H && w2v.shape[2] == 1 && w2v.shape[3] == 1 &&
                          (!b2_id || values_[b2_id].kind == Value::kWeight);
                     OC2 = ok ? static_cast<int>(w2v.shape[0]) : 0;
-                    ok = ok && OC2 % 32 == 0 && OC2 <= 256;
+                    // output tile staged in the two hidden panels: at most 128 columns
+                    ok = ok && OC2 % 64 == 0 && OC2 <= 128;
                 }
                 const int kpan = IC / 64, M = IH * IW;
                 const int slot = std::max(16384, OC2 * 128);
@@ -599,11 +655,14 @@ void Backend::plan()
                 // One CTA per SM (above half of the SM's shared memory): its 512 TMEM
                 // columns never wait for another CTA's.
                 const int ffn_smem = fixed + xs * kpan * 16384 + ws * slot;
+                int epi2 = kEpiBias;
+                float alpha2 = 0.0f;
+                uint32_t out2 = 0, res2 = 0;
+                const size_t consumed2 = ok ? conv_epilogue(i + 5, epi2, alpha2, out2, res2) : 0;
+                // The residual is read from the X tile in shared memory: only the
+                // FFN input itself can be the residual.
+                ok = ok && (res2 == 0 || res2 == x_id);
                 if (ok && ws >= 2 && ffn_smem > 233472 / 2) {
-                    int epi2 = kEpiBias;
-                    float alpha2 = 0.0f;
-                    uint32_t out2 = 0, res2 = 0;
-                    const size_t consumed2 = conv_epilogue(i + 5, epi2, alpha2, out2, res2);
                     // W1 rows in chunk order: per 64 hidden channels, 64 gate rows then 64 linear rows.
                     std::vector<uint16_t> w1p(static_cast<size_t>(OC) * IC), b1p(OC);
                     for (int r = 0; r < OC; ++r) {
@@ -661,11 +720,10 @@ void Backend::plan()
                                "cuTensorMapEncodeTiled(ffn W1)");
                         encode(&fp.map_w2, prepped_dev_.get() + w2_off, H, OC2, 64, static_cast<cuuint32_t>(OC2),
                                CU_TENSOR_MAP_SWIZZLE_128B, "cuTensorMapEncodeTiled(ffn W2)");
-                        encode(&p.map_out, values_[out2].addr, OC2, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
-                               "cuTensorMapEncodeTiled(ffn out)");
+                        encode_tile_map(&p.map_out, values_[out2].addr, OC2, M, 0, 0, "cuTensorMapEncodeTiled(ffn out)");
+                        p.map_res = p.map_out;  // unused: the residual comes from the X tile
                         p.map_a1 = p.map_a0;
                         p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b2_off);
-                        p.residual = res2 ? reinterpret_cast<const mlvc_half*>(values_[res2].addr) : nullptr;
                         p.out = reinterpret_cast<mlvc_half*>(values_[out2].addr);
                         p.M = M;
                         p.N = OC2;
@@ -674,9 +732,6 @@ void Backend::plan()
                         p.BN = OC2;
                         p.n_tiles = 1;
                         p.m_tiles = m_tiles;
-                        p.ldo = OC2;
-                        p.out_col0 = 0;
-                        p.ldr = OC2;
                         p.epilogue = epi2;
                         p.alpha = alpha2;
                         p.clip_lo = clip_lo;
@@ -695,7 +750,9 @@ void Backend::plan()
             }
             if (tc_shape && is1x1) {
                 // ---- tcgen05 GEMM
-                const int K = IC, NN = (OC + 31) / 32 * 32;  // weight rows padded to a multiple of 32
+                // Weight rows padded to a multiple of 64: the epilogue stages and
+                // stores 64-column panels (ReGLU: 64 output columns = 128 weight rows).
+                const int K = IC, NN = (OC + 63) / 64 * 64;
                 const int k_panels = (K + 63) / 64;
                 const int m_tiles = (IH * IW + 127) / 128;
                 // Candidate N tiles divide NN and keep the CTA's weight slice resident.
@@ -704,13 +761,14 @@ void Backend::plan()
                 // other's loads and MMAs.  Among those, the largest BN that still
                 // gives one tile per SM; otherwise fall back to one CTA per SM.
                 constexpr int kTwoCtaSmem = 233472 / 2 - 1024;
+                auto stage_for = [&](int bn) { return (reglu ? bn / 2 : bn) / 64 * kTcStagePanelBytes; };
                 std::vector<int> cands;
-                for (int bn = std::min(256, NN); bn >= 32; bn -= 32)  // the epilogue walks 32 columns
-                    if (NN % bn == 0 && (!reglu || bn % 64 == 0) &&
-                        header + k_panels * bn * 128 + 2 * 16384 + kTcStageBytes <= smem_cap)
+                for (int bn = std::min(256, NN); bn >= 64; bn -= 64)
+                    if (NN % bn == 0 && (!reglu || bn % 128 == 0) &&
+                        header + k_panels * bn * 128 + 2 * 16384 + stage_for(bn) <= smem_cap)
                         cands.push_back(bn);
                 auto stages_for = [&](int bn, int cap) {
-                    return (cap - header - 1024 - kTcStageBytes - k_panels * bn * 128) / 16384;
+                    return (cap - header - 1024 - stage_for(bn) - k_panels * bn * 128) / 16384;
                 };
                 int best = 0, ctas_per_sm = 1;
                 for (int bn : cands)
@@ -754,7 +812,7 @@ void Backend::plan()
                     const int grid = n_tiles * std::max(1, std::min(m_tiles, slots / n_tiles));
                     s.kernel = "mlvc_conv1x1_tc";
                     s.info.kernel = s.kernel;
-                    s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 + kTcStageBytes + 1024);
+                    s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 + stage_for(BN) + 1024);
                     s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     const int M = IH * IW;
@@ -785,20 +843,14 @@ void Backend::plan()
                                   "cuTensorMapEncodeTiled(conv1x1 B)");
                         }
                         p.map_a1 = p.map_a0;
-                        {
-                            const cuuint64_t ncols = static_cast<cuuint64_t>(reglu ? OC / 2 : OC);
-                            const cuuint64_t dims[2] = {ncols, static_cast<cuuint64_t>(M)};
-                            const cuuint64_t strides[1] = {ncols * 2};
-                            const cuuint32_t box[2] = {32, 32};
-                            check(cuTensorMapEncodeTiled(&p.map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                                                         reinterpret_cast<void*>(values_[out_id].addr), dims, strides,
-                                                         box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                                         CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                                  "cuTensorMapEncodeTiled(conv1x1 out)");
-                        }
+                        encode_tile_map(&p.map_out, values_[out_id].addr, reglu ? OC / 2 : OC, M, 0, 0,
+                                        "cuTensorMapEncodeTiled(conv1x1 out)");
+                        if (res_id)
+                            encode_tile_map(&p.map_res, values_[res_id].addr, OC, M, 0, 0,
+                                            "cuTensorMapEncodeTiled(conv1x1 residual)");
+                        else
+                            p.map_res = p.map_out;
                         p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b_off);
-                        p.residual = res_id ? reinterpret_cast<const mlvc_half*>(values_[res_id].addr) : nullptr;
                         p.out = reinterpret_cast<mlvc_half*>(values_[out_id].addr);
                         p.M = M;
                         p.N = NN;
@@ -807,9 +859,6 @@ void Backend::plan()
                         p.BN = BN;
                         p.n_tiles = n_tiles;
                         p.m_tiles = m_tiles;
-                        p.ldo = reglu ? OC / 2 : OC;
-                        p.out_col0 = 0;
-                        p.ldr = OC;
                         p.epilogue = epi;
                         p.alpha = alpha;
                         p.clip_lo = lo;
@@ -822,7 +871,7 @@ void Backend::plan()
                     continue;
                 }
             }
-            if (tc_shape && IC % 64 == 0 && OC % 32 == 0 && !is1x1 && !reglu && (SH == 1 || SH == 2) && SH == SW &&
+            if (tc_shape && IC % 64 == 0 && !is1x1 && !reglu && (SH == 1 || SH == 2) && SH == SW &&
                 KH <= 8 && KW <= 8 &&
                 PH == PW && PW < KW && OW >= 1) {
                 // ---- tcgen05 implicit GEMM with halo tiles
@@ -841,13 +890,15 @@ void Backend::plan()
                 const int halo_bytes = parities * 8 * chunk_bytes;
                 const int halo_stride = static_cast<int>(align_up(halo_bytes, 1024));
                 const bool halo_ok = halo_px <= 256 && (stride == 1 || IW >= 2);
+                // Weight rows padded to a multiple of 64 (64-column output panels).
+                const int NN = (OC + 63) / 64 * 64;
                 int BN = 0, a_st = 0, b_st = 0, resident = 0;
-                for (int bn = std::min(256, OC); halo_ok && bn >= 32 && !BN; bn -= 32) {
-                    if (OC % bn)
+                for (int bn = std::min(256, NN); halo_ok && bn >= 64 && !BN; bn -= 64) {
+                    if (NN % bn)
                         continue;
                     const int bpanel = bn * 128;
                     const int res_bytes = taps * k_panels * bpanel;
-                    const int fixed = header + kTcStageBytes;
+                    const int fixed = header + bn / 64 * kTcStagePanelBytes;
                     if (fixed + res_bytes + 2 * halo_stride <= smem_cap) {
                         BN = bn;
                         resident = 1;
@@ -864,8 +915,10 @@ void Backend::plan()
                     }
                 }
                 if (BN) {
-                    // weights OIHW -> [OC][KH][KW][IC]
-                    std::vector<uint16_t> wp(static_cast<size_t>(OC) * taps * IC);
+                    // weights OIHW -> [NN][KH][KW][IC] (rows past OC stay zero)
+                    std::vector<uint16_t> wp(static_cast<size_t>(NN) * taps * IC, 0);
+                    std::vector<uint16_t> bp(NN, 0);
+                    std::copy(bias_full.begin(), bias_full.end(), bp.begin());
                     for (int o = 0; o < OC; ++o)
                         for (int ky = 0; ky < KH; ++ky)
                             for (int kx = 0; kx < KW; ++kx)
@@ -873,14 +926,15 @@ void Backend::plan()
                                     wp[((static_cast<size_t>(o) * KH + ky) * KW + kx) * IC + c] =
                                         w[((static_cast<size_t>(o) * IC + c) * KH + ky) * KW + kx];
                     const size_t w_off = prep(wp.data(), wp.size() * 2);
-                    const size_t b_off = prep(bias_full.data(), bias_full.size() * 2);
-                    const int n_tiles = OC / BN, tiles_per_row = (OW + 127) / 128, m_tiles = OH * tiles_per_row;
+                    const size_t b_off = prep(bp.data(), bp.size() * 2);
+                    const int n_tiles = NN / BN, tiles_per_row = (OW + 127) / 128, m_tiles = OH * tiles_per_row;
                     const int grid = n_tiles * std::max(1, std::min(m_tiles, sm_count_ / n_tiles));
                     const int b_slots = resident ? taps * k_panels : b_st;
                     s.kernel = "mlvc_convkxk_tc";
                     s.info.kernel = s.kernel;
                     s.smem =
-                        static_cast<unsigned>(header + b_slots * BN * 128 + a_st * halo_stride + kTcStageBytes + 1024);
+                        static_cast<unsigned>(header + b_slots * BN * 128 + a_st * halo_stride +
+                                              BN / 64 * kTcStagePanelBytes + 1024);
                     s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     s.build = [=, this](Step& st) {
@@ -902,22 +956,16 @@ void Backend::plan()
                         }
                         if (parities == 1)
                             p.map_a1 = p.map_a0;
-                        {
-                            const cuuint64_t dims[3] = {static_cast<cuuint64_t>(OC), static_cast<cuuint64_t>(OW),
-                                                        static_cast<cuuint64_t>(OH)};
-                            const cuuint64_t strides[2] = {static_cast<cuuint64_t>(OC) * 2,
-                                                           static_cast<cuuint64_t>(OW) * OC * 2};
-                            const cuuint32_t box[3] = {32, 32, 1};
-                            check(cuTensorMapEncodeTiled(&p.map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                                                         reinterpret_cast<void*>(values_[out_id].addr), dims, strides,
-                                                         box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                                         CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                                  "cuTensorMapEncodeTiled(convkxk out)");
-                        }
+                        encode_tile_map(&p.map_out, values_[out_id].addr, OC, 0, OW, OH,
+                                        "cuTensorMapEncodeTiled(convkxk out)");
+                        if (res_id)
+                            encode_tile_map(&p.map_res, values_[res_id].addr, OC, 0, OW, OH,
+                                            "cuTensorMapEncodeTiled(convkxk residual)");
+                        else
+                            p.map_res = p.map_out;
                         {
                             const cuuint64_t Kt = static_cast<cuuint64_t>(taps) * IC;
-                            const cuuint64_t dims[2] = {Kt, static_cast<cuuint64_t>(OC)};
+                            const cuuint64_t dims[2] = {Kt, static_cast<cuuint64_t>(NN)};
                             const cuuint64_t strides[1] = {Kt * 2};
                             const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(BN)};
                             check(cuTensorMapEncodeTiled(&p.map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
@@ -928,18 +976,14 @@ void Backend::plan()
                                   "cuTensorMapEncodeTiled(convkxk B)");
                         }
                         p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b_off);
-                        p.residual = res_id ? reinterpret_cast<const mlvc_half*>(values_[res_id].addr) : nullptr;
                         p.out = reinterpret_cast<mlvc_half*>(values_[out_id].addr);
                         p.M = OH * OW;
-                        p.N = OC;
+                        p.N = NN;
                         p.n_valid = OC;
                         p.K = taps * IC;
                         p.BN = BN;
                         p.n_tiles = n_tiles;
                         p.m_tiles = m_tiles;
-                        p.ldo = OC;
-                        p.out_col0 = 0;
-                        p.ldr = OC;
                         p.epilogue = epi;
                         p.alpha = alpha;
                         p.a_stages = a_st;
@@ -1714,17 +1758,48 @@ void Backend::configure_slots(size_t count)
     for (auto& s : slots_)
         if (s.pending)
             check(cuEventSynchronize(s.done.get()), "cuEventSynchronize");
+    check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
     slots_.clear();
-    slots_.resize(count);
+    if (!copy_in_)
+        check(cuStreamCreate(&copy_in_, CU_STREAM_NON_BLOCKING), "cuStreamCreate(copy in)");
+    if (!copy_out_)
+        check(cuStreamCreate(&copy_out_, CU_STREAM_NON_BLOCKING), "cuStreamCreate(copy out)");
+    slots_ = std::vector<Slot>(count);
     for (auto& s : slots_) {
         for (size_t k = 0; k < ext_inputs_.size(); ++k) {
             const auto& d = input_desc(k);
-            s.in.emplace_back(static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype));
+            const size_t bytes = static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype);
+            s.in.emplace_back(bytes);
+            s.din.emplace_back(align_up(bytes, 256));
         }
         for (size_t k = 0; k < ext_outputs_.size(); ++k) {
             const auto& d = output_desc(k);
-            s.out.emplace_back(static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype));
+            const size_t bytes = static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype);
+            s.out.emplace_back(bytes);
+            s.dout.emplace_back(align_up(bytes, 256));
         }
+        // graph: staged inputs -> schedule inputs, schedule, outputs -> staging
+        check(cuStreamBeginCapture(stream_, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL), "cuStreamBeginCapture(slot)");
+        try {
+            for (size_t k = 0; k < ext_inputs_.size(); ++k) {
+                const CUdeviceptr dst = input_stage_dev_[k] ? input_stage_dev_[k].get() : input_dev_[k].get();
+                check(cuMemcpyDtoDAsync(dst, s.din[k].get(), s.in[k].bytes(), stream_), "cuMemcpyDtoDAsync(slot in)");
+            }
+            launch_steps(stream_);
+            for (size_t k = 0; k < ext_outputs_.size(); ++k) {
+                const uint32_t id = graph_.outputs[ext_outputs_[k]];
+                const CUdeviceptr src = output_stage_dev_[k] ? output_stage_dev_[k].get() : values_[id].addr;
+                check(cuMemcpyDtoDAsync(s.dout[k].get(), src, s.out[k].bytes(), stream_), "cuMemcpyDtoDAsync(slot out)");
+            }
+        } catch (...) {
+            CUgraph g = nullptr;
+            cuStreamEndCapture(stream_, &g);
+            if (g)
+                cuGraphDestroy(g);
+            throw;
+        }
+        check(cuStreamEndCapture(stream_, &s.graph), "cuStreamEndCapture(slot)");
+        check(cuGraphInstantiateWithFlags(&s.exec, s.graph, 0), "cuGraphInstantiate(slot)");
     }
 }
 
@@ -1743,17 +1818,22 @@ void Backend::submit(size_t slot)
     Slot& s = slots_.at(slot);
     if (s.pending)
         throw std::runtime_error("mlvc-b200: slot resubmitted before wait_slot()");
-    for (size_t k = 0; k < ext_inputs_.size(); ++k) {
-        const CUdeviceptr dst = input_stage_dev_[k] ? input_stage_dev_[k].get() : input_dev_[k].get();
-        check(cuMemcpyHtoDAsync(dst, s.in[k].get(), s.in[k].bytes(), stream_), "cuMemcpyHtoDAsync(slot)");
-    }
-    check(cuGraphLaunch(graph_exec_, stream_), "cuGraphLaunch");
-    for (size_t k = 0; k < ext_outputs_.size(); ++k) {
-        const uint32_t id = graph_.outputs[ext_outputs_[k]];
-        const CUdeviceptr src = output_stage_dev_[k] ? output_stage_dev_[k].get() : values_[id].addr;
-        check(cuMemcpyDtoHAsync(s.out[k].get(), src, s.out[k].bytes(), stream_), "cuMemcpyDtoHAsync(slot)");
-    }
-    check(cuEventRecord(s.done.get(), stream_), "cuEventRecord");
+    // host -> device on the input copy stream, once the slot's previous graph
+    // has read its device staging
+    check(cuStreamWaitEvent(copy_in_, s.computed.get(), 0), "cuStreamWaitEvent(copy in)");
+    for (size_t k = 0; k < ext_inputs_.size(); ++k)
+        check(cuMemcpyHtoDAsync(s.din[k].get(), s.in[k].get(), s.in[k].bytes(), copy_in_), "cuMemcpyHtoDAsync(slot)");
+    check(cuEventRecord(s.in_done.get(), copy_in_), "cuEventRecord(in)");
+    // the schedule, in submission order on the compute stream (recurrent state
+    // passes from frame to frame there)
+    check(cuStreamWaitEvent(stream_, s.in_done.get(), 0), "cuStreamWaitEvent(compute)");
+    check(cuGraphLaunch(s.exec, stream_), "cuGraphLaunch(slot)");
+    check(cuEventRecord(s.computed.get(), stream_), "cuEventRecord(computed)");
+    // device -> host on the output copy stream
+    check(cuStreamWaitEvent(copy_out_, s.computed.get(), 0), "cuStreamWaitEvent(copy out)");
+    for (size_t k = 0; k < ext_outputs_.size(); ++k)
+        check(cuMemcpyDtoHAsync(s.out[k].get(), s.dout[k].get(), s.out[k].bytes(), copy_out_), "cuMemcpyDtoHAsync(slot)");
+    check(cuEventRecord(s.done.get(), copy_out_), "cuEventRecord(done)");
     s.pending = true;
 }
 

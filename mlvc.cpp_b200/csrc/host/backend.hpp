@@ -115,7 +115,8 @@ private:
     int device_ = 0;
     CUdevice dev_ = 0;
     CUcontext ctx_ = nullptr;
-    CUstream stream_ = nullptr;
+    CUstream stream_ = nullptr;                             // compute: every schedule launch
+    CUstream copy_in_ = nullptr, copy_out_ = nullptr;       // slot pipeline copies
     CUmodule module_ = nullptr;
     CUdeviceptr status_ptr_ = 0;
     int sm_count_ = 148;

@@ -84,6 +84,7 @@ MLVC_FWD(cuEventCreate, (CUevent * phEvent, unsigned int Flags), (phEvent, Flags
 MLVC_FWD(cuEventDestroy, (CUevent hEvent), (hEvent))
 MLVC_FWD(cuEventRecord, (CUevent hEvent, CUstream hStream), (hEvent, hStream))
 MLVC_FWD(cuEventSynchronize, (CUevent hEvent), (hEvent))
+MLVC_FWD(cuStreamWaitEvent, (CUstream hStream, CUevent hEvent, unsigned int Flags), (hStream, hEvent, Flags))
 MLVC_FWD(cuEventElapsedTime, (float* pMilliseconds, CUevent hStart, CUevent hEnd), (pMilliseconds, hStart, hEnd))
 MLVC_FWD(cuLaunchKernel,
          (CUfunction f, unsigned int gridDimX, unsigned int gridDimY, unsigned int gridDimZ, unsigned int blockDimX,

@@ -127,7 +127,7 @@ private:
 
 class Event {
 public:
-    Event() { check(cuEventCreate(&ev_, CU_EVENT_DEFAULT), "cuEventCreate"); }
+    explicit Event(unsigned int flags = CU_EVENT_DEFAULT) { check(cuEventCreate(&ev_, flags), "cuEventCreate"); }
     ~Event()
     {
         if (ev_)

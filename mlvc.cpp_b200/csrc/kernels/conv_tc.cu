@@ -45,6 +45,7 @@ struct TcShared {
     uint64_t b_empty[kMaxStages];
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
+    uint64_t stg_ready, stg_full;  // output staging hand-over (see StageSync)
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -69,101 +70,71 @@ __device__ __forceinline__ uint32_t tmem_cols_for(int bn)
 }
 
 // ----------------------------------------------------------- epilogue
-// Each epilogue warp owns one TMEM lane quadrant (32 output pixels) and, with
-// the other warpgroup, alternate 32-column chunks.  Per chunk a thread reads
-// its pixel's 32 accumulators (one tcgen05.ld), applies bias / activation /
-// residual with the graph's rounding, and writes the 64-byte row into a warp
-// staging buffer (64-byte swizzle, bank-conflict free); one lane then stores
-// the 32x32 block with a TMA bulk store (full-line writes, clipped at the
-// tensor edges).  The residual block is read coalesced into the same buffer
-// first.  Two buffers per warp let a store drain while the next chunk runs.
-__device__ __forceinline__ uint32_t swz64(int row, int chunk)
+// The epilogue writes the whole output tile (128 rows x the tile's output
+// columns) into a shared staging buffer laid out as 64-column panels of 128
+// rows x 128 bytes with the 128-byte swizzle (16-byte chunk q of row r at
+// chunk q ^ (r % 8)), which is exactly the shared-memory image of a {64, 128}
+// SWIZZLE_128B TMA box; one thread then stores the tile with one TMA
+// instruction per panel, clipped at the tensor edges.  A residual operand is
+// TMA-loaded into the same buffer beforehand (or read from an operand tile
+// already in shared memory in this layout).  Few TMA instructions per tile
+// matter: each one occupies the SM's copy engine for tens of nanoseconds
+// whatever its size.  Each epilogue warp owns one TMEM lane quadrant (32
+// rows); the two warpgroups take alternate 32-column chunks.  The 32 lanes of
+// a warp are 32 consecutive rows, so the 16-byte staging accesses are free of
+// bank conflicts.
+__device__ __forceinline__ uint32_t stage_off(int row, int col)  // col: multiple of 8 within the tile
 {
-    return static_cast<uint32_t>(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
+    return static_cast<uint32_t>((col >> 6) * 16384 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4));
 }
 
-struct EpiTile {
-    long long pixel0;  // first pixel of the warp's 32 rows (1x1) / row start (kxk)
-    int rows_valid;    // rows of the warp block inside the output
-    int oy, ox0;       // kxk: output row and first column of the warp block
+// TMA coordinates of an output tile: 1x1 / FFN maps are {channels, pixels},
+// k x k maps are {channels, W, H}.
+struct TileCoord {
+    int pixel0;   // 1x1: first pixel of the tile
+    int ox0, oy;  // k x k: first output column and the output row of the tile
 };
 
-__device__ __forceinline__ void store_block(const ConvTcParams& p, const uint8_t* buf, const EpiTile& et, int col,
-                                            bool kxk)
+__device__ __forceinline__ void tile_copy(const CUtensorMap* map, bool load, uint8_t* stage, int panels, int col0,
+                                          const TileCoord& tc, bool kxk, uint64_t* bar)
 {
-    if (kxk)
-        tma_store_3d(&p.map_out, buf, col, et.ox0, et.oy);
-    else
-        tma_store_2d(&p.map_out, buf, col, static_cast<int>(et.pixel0));
-    bulk_commit();
-}
-
-// Residual block of one 32-column chunk (32 rows x 64 bytes) as 4 coalesced
-// 16-byte pieces per lane: piece lane + 32 j holds row (piece / 4), 8-channel
-// group (piece % 4).
-__device__ __forceinline__ void residual_fetch(const ConvTcParams& p, const EpiTile& et, int col, int lane, bool kxk,
-                                               uint4 (&v)[4])
-{
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int piece = lane + 32 * j, r = piece >> 2, ch = piece & 3;
-        v[j] = make_uint4(0, 0, 0, 0);
-        if (r < et.rows_valid && col + 8 * (ch + 1) <= p.n_valid) {
-            const long long px = kxk ? static_cast<long long>(et.oy) * p.out_w + et.ox0 + r : et.pixel0 + r;
-            v[j] = __ldg(reinterpret_cast<const uint4*>(p.residual + px * p.ldr + col + ch * 8));
+    for (int i = 0; i < panels; ++i) {
+        uint8_t* s = stage + i * 16384;
+        const int x = col0 + 64 * i;
+        if (load) {
+            if (kxk)
+                tma_load_3d(s, map, bar, x, tc.ox0, tc.oy);
+            else
+                tma_load_2d(s, map, bar, x, tc.pixel0);
+        } else {
+            if (kxk)
+                tma_store_3d(map, s, x, tc.ox0, tc.oy);
+            else
+                tma_store_2d(map, s, x, tc.pixel0);
         }
     }
 }
 
-// Writes fetched residual pieces into a staging block (one row per lane later).
-__device__ __forceinline__ void residual_put(uint8_t* buf, int lane, const uint4 (&v)[4])
-{
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int piece = lane + 32 * j;
-        *reinterpret_cast<uint4*>(buf + swz64(piece >> 2, piece & 3)) = v[j];
-    }
-}
+// Staging hand-over between tiles (both in shared memory):
+//   ready: the leader thread found the previous tile's stores done reading the
+//          buffer and, for a staged residual, the residual tile has landed;
+//   full:  all epilogue threads wrote their rows (count kEpilogueThreads).
+struct StageSync {
+    uint64_t* ready;
+    uint64_t* full;
+};
 
-// Residual of the warp's first two chunks, loaded into its two staging buffers
-// before the accumulator is ready (the load latency overlaps the MMAs).  The
-// warp's earlier TMA stores must have finished reading the buffers; `nbuf`
-// restarts at 0 so chunk k of the tile uses buffer k % 2.
-__device__ __forceinline__ void residual_prestage(const ConvTcParams& p, const EpiTile& et, int n_tile, int c0, int lane,
-                                                  bool kxk, uint8_t* stage, int& nbuf)
+// One thread's row of the tile: for the 32-column chunks c0 = 32 group + 64 k
+// it reads 32 accumulators, applies bias and the fused operator with the
+// graph's rounding and writes the row into the staging panels.  `res` is the
+// residual tile (same layout), read before the row is overwritten.
+__device__ __forceinline__ void epilogue_rows(const ConvTcParams& p, const float* bias, uint32_t lane_addr, int group,
+                                              int row, uint8_t* stage, const uint8_t* res)
 {
-    uint4 r0[4], r1[4];
-    const bool two = c0 + 64 < p.BN;
-    const int col0 = n_tile * p.BN + c0;
-    residual_fetch(p, et, col0, lane, kxk, r0);
-    if (two)
-        residual_fetch(p, et, col0 + 64, lane, kxk, r1);
-    if (lane == 0)
-        bulk_wait_read<0>();
-    __syncwarp();
-    residual_put(stage, lane, r0);
-    if (two)
-        residual_put(stage + 2048, lane, r1);
-    __syncwarp();
-    nbuf = 0;
-}
-
-// Chunks [0, staged) of the warp find their residual block already in the
-// staging buffer (residual_prestage); later chunks load it here.
-__device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const float* bias, uint32_t tmem_acc,
-                                              int quadrant, int group, int lane, const EpiTile& et, int n_tile,
-                                              uint8_t* stage, int& nbuf, bool kxk, int staged)
-{
-    const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16);
     if (p.epilogue == kEpiReglu) {
         const int half = p.BN / 2;
+        const __half2 lo2 = __float2half2_rn(p.clip_lo), hi2 = __float2half2_rn(p.clip_hi);
         for (int c0 = group * 32; c0 < half; c0 += 64) {
-            uint8_t* buf = stage + (nbuf & 1) * 2048;
-            if (nbuf >= 2) {
-                if (lane == 0)
-                    bulk_wait_read<1>();
-                __syncwarp();
-            }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 uint32_t gr[16], lr[16];
@@ -175,44 +146,24 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const float
                 // and the single rounding of an exact FP16 x FP16 product equal
                 // the reference's FP32 clip / multiply followed by a rounding)
                 uint32_t packed[8];
-                const __half2 lo2 = __float2half2_rn(p.clip_lo), hi2 = __float2half2_rn(p.clip_hi);
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                    const float* bg = &bias[c0 + 16 * h + i];
-                    const float* bl = &bias[half + c0 + 16 * h + i];
-                    const __half2 g2 = __floats2half2_rn(__uint_as_float(gr[i]) + bg[0], __uint_as_float(gr[i + 1]) + bg[1]);
-                    const __half2 l2 = __floats2half2_rn(__uint_as_float(lr[i]) + bl[0], __uint_as_float(lr[i + 1]) + bl[1]);
+                    const float2 bg = *reinterpret_cast<const float2*>(&bias[c0 + 16 * h + i]);
+                    const float2 bl = *reinterpret_cast<const float2*>(&bias[half + c0 + 16 * h + i]);
+                    const __half2 g2 = __floats2half2_rn(__uint_as_float(gr[i]) + bg.x, __uint_as_float(gr[i + 1]) + bg.y);
+                    const __half2 l2 = __floats2half2_rn(__uint_as_float(lr[i]) + bl.x, __uint_as_float(lr[i + 1]) + bl.y);
                     const __half2 r2 = __hmul2(__hmin2(__hmax2(g2, lo2), hi2), l2);
                     packed[i / 2] = *reinterpret_cast<const uint32_t*>(&r2);
                 }
-                *reinterpret_cast<uint4*>(buf + swz64(lane, 2 * h)) =
+                *reinterpret_cast<uint4*>(stage + stage_off(row, c0 + 16 * h)) =
                     make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                *reinterpret_cast<uint4*>(buf + swz64(lane, 2 * h + 1)) =
+                *reinterpret_cast<uint4*>(stage + stage_off(row, c0 + 16 * h + 8)) =
                     make_uint4(packed[4], packed[5], packed[6], packed[7]);
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0)
-                store_block(p, buf, et, p.out_col0 + n_tile * half + c0, kxk);
-            ++nbuf;
         }
         return;
     }
-    const bool residual = p.epilogue == kEpiResidual;
-    for (int c0 = group * 32, k = 0; c0 < p.BN; c0 += 64, ++k) {
-        uint8_t* buf = stage + (nbuf & 1) * 2048;
-        if (nbuf >= 2) {
-            if (lane == 0)
-                bulk_wait_read<1>();
-            __syncwarp();
-        }
-        const int col = n_tile * p.BN + c0;
-        if (residual && k >= staged) {
-            uint4 v[4];
-            residual_fetch(p, et, col, lane, kxk, v);
-            residual_put(buf, lane, v);
-            __syncwarp();
-        }
+    for (int c0 = group * 32; c0 < p.BN; c0 += 64) {
         uint32_t a[32];
         tmem_ld32_nowait(lane_addr + c0, a);
         tmem_wait_ld();
@@ -233,11 +184,11 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const float
                 const uint32_t neg = ((h[i] >> 15) & 0x00010001u) * 0xFFFFu;  // sign bit -> 16-bit mask
                 h[i] = (m & neg) | (h[i] & ~neg);
             }
-        } else if (residual) {
+        } else if (p.epilogue == kEpiResidual) {
             // fp16 + fp16 with one rounding equals the FP32 add + rounding of the reference
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const uint4 rv = *reinterpret_cast<const uint4*>(buf + swz64(lane, q));
+                const uint4 rv = *reinterpret_cast<const uint4*>(res + stage_off(row, c0 + 8 * q));
                 const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -249,24 +200,62 @@ __device__ __forceinline__ void epilogue_tile(const ConvTcParams& p, const float
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(buf + swz64(lane, q)) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0)
-            store_block(p, buf, et, p.out_col0 + col, kxk);
-        ++nbuf;
+            *reinterpret_cast<uint4*>(stage + stage_off(row, c0 + 8 * q)) =
+                make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
     }
 }
 
-__device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& sh, uint8_t* stage_base, int warp,
-                                              int lane, int n_tile, int first_tile, int tile_step, int total_tiles,
-                                              bool kxk)
+// Leader thread, before a tile's rows are written: the previous tile's stores
+// must have read the staging buffer; then the residual tile is loaded into it
+// (load_residual) or the buffer is simply released.
+__device__ __forceinline__ void stage_prepare(const ConvTcParams& p, uint8_t* stage, int panels, int col0,
+                                              const TileCoord& tc, bool kxk, bool load_residual, uint64_t* ready)
+{
+    bulk_wait_read<0>();
+    if (load_residual) {
+        mbar_arrive_expect_tx(ready, static_cast<uint32_t>(panels) * 16384u);
+        tile_copy(&p.map_res, true, stage, panels, col0, tc, kxk, ready);
+    } else {
+        mbar_arrive(ready);
+    }
+}
+
+// All epilogue threads, one tile: wait for the accumulator and the staging
+// buffer, convert, release the accumulator, and let the leader store the tile.
+// `it` counts the CTA's tiles (barrier parities).  Returns false on abort.
+__device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float* bias, uint32_t tmem_acc,
+                                              uint64_t* acc_full, uint32_t acc_parity, uint64_t* acc_empty,
+                                              const StageSync& ss, uint32_t it, uint8_t* stage, const uint8_t* res,
+                                              int panels, int col0, const TileCoord& tc, bool kxk, int quadrant,
+                                              int group, int lane, bool leader, volatile int* abort_flag)
+{
+    if (!mbar_wait(acc_full, acc_parity, abort_flag, kErrWaitEpilogue))
+        return false;
+    tc_fence_after();
+    if (!mbar_wait(ss.ready, it & 1u, abort_flag, kErrWaitEpilogue))
+        return false;
+    epilogue_rows(p, bias, tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16), group, quadrant * 32 + lane, stage,
+                  res ? res : stage);
+    tc_fence_before();
+    mbar_arrive(acc_empty);
+    fence_proxy_async_smem();  // staging rows become visible to the TMA store (async proxy)
+    mbar_arrive(ss.full);
+    if (leader) {
+        if (!mbar_wait(ss.full, it & 1u, abort_flag, kErrWaitEpilogue))
+            return false;
+        tile_copy(&p.map_out, false, stage, panels, col0, tc, kxk, nullptr);
+        bulk_commit();
+    }
+    return true;
+}
+
+__device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& sh, uint8_t* stage, int warp, int lane,
+                                              int n_tile, int first_tile, int tile_step, int total_tiles, bool kxk)
 {
     const int quadrant = warp & 3;
-    const int group = (warp - 2) / 4;       // column-chunk warpgroup
+    const int group = (warp - 2) / 4;          // column-chunk warpgroup
     const int et_id = (warp - 2) * 32 + lane;  // 0..255
-    uint8_t* stage = stage_base + (warp - 2) * 4096;
-    int nbuf = 0;
+    const bool leader = et_id == 0;
     for (int i = et_id; i < p.BN; i += kEpilogueThreads) {
         const int col = n_tile * p.BN + i;
         sh.bias[i] = (p.bias && col < p.N) ? __half2float(p.bias[col]) : 0.0f;
@@ -274,44 +263,32 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
     asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads + 32) : "memory");  // bias loaded + TMEM allocated
     tc_fence_after();
     pdl_wait();  // residual reads and output writes follow the previous kernel
-    uint32_t acc = 0, acc_phase = 0;
-    for (int t = first_tile; t < total_tiles; t += tile_step) {
+    const int out_cols = p.epilogue == kEpiReglu ? p.BN / 2 : p.BN;
+    const int panels = out_cols / 64;
+    const StageSync ss{&sh.stg_ready, &sh.stg_full};
+    const int tiles_per_row = kxk ? (p.out_w + kBM - 1) / kBM : 1;
+    uint32_t acc = 0, acc_phase = 0, it = 0;
+    for (int t = first_tile; t < total_tiles; t += tile_step, ++it) {
         const int m_tile = t / p.n_tiles;
-        EpiTile et;
-        if (!kxk) {
-            et.pixel0 = static_cast<long long>(m_tile) * kBM + quadrant * 32;
-            et.rows_valid = static_cast<int>(min(32LL, max(0LL, p.M - et.pixel0)));
-            et.oy = et.ox0 = 0;
-        } else {
-            const int tiles_per_row = (p.out_w + kBM - 1) / kBM;
-            et.oy = m_tile / tiles_per_row;
-            et.ox0 = (m_tile % tiles_per_row) * kBM + quadrant * 32;
-            et.rows_valid = max(0, min(32, p.out_w - et.ox0));
-            et.pixel0 = static_cast<long long>(et.oy) * p.out_w + et.ox0;
-        }
-        int staged = 0;
-        if (p.epilogue == kEpiResidual && et.rows_valid > 0 && group * 32 < p.BN) {
-            residual_prestage(p, et, n_tile, group * 32, lane, kxk, stage, nbuf);
-            staged = 2;
-        }
-        if (!mbar_wait(&sh.tmem_full[acc], acc_phase, &sh.abort_flag, kErrWaitEpilogue))
+        TileCoord tc;
+        tc.pixel0 = m_tile * kBM;
+        tc.oy = m_tile / tiles_per_row;
+        tc.ox0 = (m_tile % tiles_per_row) * kBM;
+        if (leader)
+            stage_prepare(p, stage, panels, n_tile * out_cols, tc, kxk, p.epilogue == kEpiResidual, ss.ready);
+        if (!epilogue_tile(p, sh.bias, sh.tmem_base + acc * p.BN, &sh.tmem_full[acc], acc_phase, &sh.tmem_empty[acc],
+                           ss, it, stage, nullptr, panels, n_tile * out_cols, tc, kxk, quadrant, group, lane, leader,
+                           &sh.abort_flag))
             break;
-        tc_fence_after();
-        if (t == first_tile && et_id == 0)
+        if (t == first_tile && leader)
             trace(p, kTrFirstAcc);
-        if (et.rows_valid > 0)
-            epilogue_tile(p, sh.bias, sh.tmem_base + acc * p.BN, quadrant, group, lane, et, n_tile, stage, nbuf, kxk,
-                          staged);
-        tc_fence_before();
-        mbar_arrive(&sh.tmem_empty[acc]);
         acc ^= 1u;
         acc_phase ^= (acc == 0) ? 1u : 0u;
     }
-    if (lane == 0)
+    if (leader) {
         bulk_wait_all();  // stores complete before the CTA (and its shared memory) retires
-    __syncwarp();
-    if (et_id == 0)
         trace(p, kTrEpilogueDone);
+    }
 }
 
 // --------------------------------------------------------------- setup
@@ -331,6 +308,8 @@ __device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvT
             mbar_init(&sh->tmem_full[s], 1);
             mbar_init(&sh->tmem_empty[s], kEpilogueThreads);
         }
+        mbar_init(&sh->stg_ready, 1);
+        mbar_init(&sh->stg_full, kEpilogueThreads);
         mbar_init(&sh->drain, 1);
         sh->abort_flag = 0;
         fence_barrier_init();
@@ -339,6 +318,8 @@ __device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvT
         tma_prefetch_desc(&p.map_a0);
         tma_prefetch_desc(&p.map_b);
         tma_prefetch_desc(&p.map_out);
+        if (p.epilogue == kEpiResidual)
+            tma_prefetch_desc(&p.map_res);
     }
     // Only the barriers must be visible before the producer starts; TMEM is
     // allocated by warp 1 afterwards and handed to the epilogue warps through

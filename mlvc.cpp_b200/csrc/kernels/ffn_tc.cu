@@ -34,7 +34,7 @@ struct FfnShared {
     uint64_t acc1_full[2], acc1_empty[2];
     uint64_t hid_full[2], hid_empty[2];
     uint64_t acc2_full[2], acc2_empty[2];
-    uint64_t stage_free;  // all epilogue threads: the tile's stores have read the staging panels
+    uint64_t stg_ready, stg_full;  // hidden/staging panel hand-over (see StageSync)
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -97,9 +97,11 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_ffn_tc(const __gr
     uint8_t* x_smem = base + kFfnHeaderBytes;
     uint8_t* hid_smem = x_smem + static_cast<size_t>(p.a_stages) * x_tile_bytes;
     uint8_t* w_smem = hid_smem + 2 * kFfnPanelBytes;
-    // The output epilogue stages its TMA stores in the hidden panels: they are
-    // free once the tile's last GEMM2 completed (acc2 full) and are handed back
-    // to the next tile's ReGLU epilogue after the stores have read them.
+    // The output epilogue stages the output tile in the hidden panels: they
+    // are free once the tile's last GEMM2 completed (acc2 full) and go back to
+    // the next tile's ReGLU epilogue once the TMA stores have read them.  The
+    // residual (when the graph adds the FFN input) is read from the X tile,
+    // which therefore stays resident until the output epilogue is done.
     uint8_t* stage_smem = hid_smem;
 
     if (threadIdx.x == 0) {
@@ -107,7 +109,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_ffn_tc(const __gr
             p.trace[blockIdx.x * kTracePoints + kTrEntry] = globaltimer_ns();
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sh->x_full[s], 1);
-            mbar_init(&sh->x_empty[s], 1);
+            mbar_init(&sh->x_empty[s], 1 + kEpilogueThreads);  // last GEMM1 + the output epilogue's residual reads
             mbar_init(&sh->acc1_full[s], 1);
             mbar_init(&sh->acc1_empty[s], kEpilogueThreads);
             mbar_init(&sh->hid_full[s], kEpilogueThreads);
@@ -119,7 +121,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_ffn_tc(const __gr
             mbar_init(&sh->w_full[s], 1);
             mbar_init(&sh->w_empty[s], 1);
         }
-        mbar_init(&sh->stage_free, kEpilogueThreads);
+        mbar_init(&sh->stg_ready, 1);
+        mbar_init(&sh->stg_full, kEpilogueThreads);
         mbar_init(&sh->drain, 1);
         sh->abort_flag = 0;
         fence_barrier_init();
@@ -320,33 +323,28 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_ffn_tc(const __gr
         const int group = (warp - 2) / 4;
         const int et_id = (warp - 2) * 32 + lane;
         const int row = quadrant * 32 + lane;  // TMEM lane = pixel row of the tile
-        uint8_t* stage = stage_smem + (warp - 2) * 4096;
-        int nbuf = 0;
+        const bool leader = et_id == 0;
         for (int i = et_id; i < 2 * fp.hidden; i += kEpilogueThreads)
             sh->bias1[i] = fp.bias1 ? __half2float(fp.bias1[i]) : 0.0f;
         for (int i = et_id; i < p.BN; i += kEpilogueThreads)
             sh->bias2[i] = (p.bias && i < p.N) ? __half2float(p.bias[i]) : 0.0f;
         asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads + 32) : "memory");  // biases + TMEM address
         tc_fence_after();
-        pdl_wait();  // residual reads and output writes follow the previous kernel
+        pdl_wait();  // output writes follow the previous kernel
         const uint32_t lane_base = sh->tmem_base + (static_cast<uint32_t>(quadrant * 32) << 16);
         const __half2 lo2 = __float2half2_rn(p.clip_lo), hi2 = __float2half2_rn(p.clip_hi);
-        uint32_t c1 = 0, a2ph = 0, tiles_done = 0;
-        int a2 = 0;
+        const StageSync ss{&sh->stg_ready, &sh->stg_full};
+        uint32_t c1 = 0, a2ph = 0, it = 0;
+        int a2 = 0, xs = 0;
         bool ok = true;
-        for (int t = first; ok && t < tiles; t += step) {
-            EpiTile et;
-            et.pixel0 = static_cast<long long>(t) * kBM + quadrant * 32;
-            et.rows_valid = static_cast<int>(min(32LL, max(0LL, p.M - et.pixel0)));
-            et.oy = et.ox0 = 0;
-            // residual of the warp's first two output chunks, in flight while the hidden chunks run
-            const bool pre = p.epilogue == kEpiResidual && et.rows_valid > 0 && group * 32 < p.BN;
-            const bool pre2 = pre && group * 32 + 64 < p.BN;
-            uint4 r0[4], r1[4];
-            if (pre)
-                residual_fetch(p, et, group * 32, lane, false, r0);
-            if (pre2)
-                residual_fetch(p, et, group * 32 + 64, lane, false, r1);
+        for (int t = first; ok && t < tiles; t += step, ++it) {
+            // the previous tile's output stores must have read the panels
+            if (leader) {
+                bulk_wait_read<0>();
+                mbar_arrive(ss.ready);
+            }
+            if (!mbar_wait(ss.ready, it & 1u, &sh->abort_flag, kErrWaitEpilogue))
+                break;
             for (int j = 0; j < nch; ++j, ++c1) {
                 const uint32_t b = c1 & 1u, ph = (c1 >> 1) & 1u;
                 if (!mbar_wait(&sh->acc1_full[b], ph, &sh->abort_flag, kErrWaitEpilogue) ||
@@ -406,42 +404,28 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_ffn_tc(const __gr
             }
             if (!ok)
                 break;
-            if (!mbar_wait(&sh->acc2_full[a2], a2ph, &sh->abort_flag, kErrWaitEpilogue))
+            TileCoord tc;
+            tc.pixel0 = t * kBM;
+            tc.ox0 = tc.oy = 0;
+            const uint8_t* x_tile = x_smem + static_cast<size_t>(xs) * x_tile_bytes;
+            if (!epilogue_tile(p, sh->bias2, sh->tmem_base + 256u + static_cast<uint32_t>(a2 * p.BN), &sh->acc2_full[a2],
+                               a2ph, &sh->acc2_empty[a2], ss, it, stage_smem, x_tile, p.BN / 64, 0, tc, false, quadrant,
+                               group, lane, leader, &sh->abort_flag))
                 break;
-            tc_fence_after();
-            if (et_id == 0 && t == first)
+            if (leader && t == first)
                 trace(p, kTrFfnAcc2);
-            nbuf = 0;
-            if (pre) {  // every GEMM2 of the tile is done: the hidden panels become staging
-                residual_put(stage, lane, r0);
-                if (pre2)
-                    residual_put(stage + 2048, lane, r1);
-                __syncwarp();
-            }
-            if (et.rows_valid > 0)
-                epilogue_tile(p, sh->bias2, sh->tmem_base + 256u + static_cast<uint32_t>(a2 * p.BN), quadrant, group,
-                              lane, et, 0, stage, nbuf, false, pre ? 2 : 0);
-            // Hand the panels back to the ReGLU epilogue once every warp's
-            // stores have read their staging block (bounded wait).
-            if (lane == 0)
-                bulk_wait_read<0>();
-            __syncwarp();
-            mbar_arrive(&sh->stage_free);
-            if (!mbar_wait(&sh->stage_free, tiles_done & 1u, &sh->abort_flag, kErrWaitEpilogue))
-                break;
-            ++tiles_done;
-            tc_fence_before();
-            mbar_arrive(&sh->acc2_empty[a2]);
+            mbar_arrive(&sh->x_empty[xs]);  // residual reads of this X tile are done
+            if (++xs == p.a_stages)
+                xs = 0;
             if (++a2 == acc2_bufs) {
                 a2 = 0;
                 a2ph ^= 1u;
             }
         }
-        if (lane == 0)
+        if (leader) {
             bulk_wait_all();
-        __syncwarp();
-        if (et_id == 0)
             trace(p, kTrEpilogueDone);
+        }
     }
 
     if (mma_thread && sh->abort_flag && issued) {

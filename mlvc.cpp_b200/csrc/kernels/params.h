@@ -21,9 +21,9 @@ namespace mlvc_b200 {
 // 1024-byte aligned).
 constexpr int kTcHeaderBytes = 2048;
 
-// Epilogue staging per tensor-core conv CTA: 8 epilogue warps x 2 buffers of
-// 32 rows x 32 FP16 columns (64-byte swizzled rows) for the TMA output stores.
-constexpr int kTcStageBytes = 8 * 2 * 2048;
+// Epilogue staging of a tensor-core conv CTA: the whole output tile, 128 rows
+// x 128 bytes per 64 output columns (128-byte swizzle), stored by TMA.
+constexpr int kTcStagePanelBytes = 128 * 128;
 
 // Epilogue kinds of the tensor-core conv kernels.  Rounding follows the graph:
 // the conv result is rounded to FP16 first, then the fused operator is applied
@@ -40,16 +40,18 @@ struct ConvTcParams {
     CUtensorMap map_a0;  // activations (1x1: [M rows, K]; kxk: parity 0 view)
     CUtensorMap map_a1;  // kxk stride-2: parity 1 view (unused otherwise)
     CUtensorMap map_b;   // prepared weights [N rows, K = taps * IC] (K-major)
-    CUtensorMap map_out; // output store view: 1x1 {channels, pixels}, kxk {channels, W, H}; 32x32 boxes, 64B swizzle
+    // Output store view and residual load view (same geometry): 1x1 {channels,
+    // pixels} with {64, 128} boxes, kxk {channels, W, H} with {64, 128, 1}
+    // boxes, 128-byte swizzle; stores and loads are clipped / zero-filled at the
+    // tensor edges, so partial tiles need no special case.
+    CUtensorMap map_out;
+    CUtensorMap map_res;
     const mlvc_half* bias;      // [N] in prepared column order, may be null
-    const mlvc_half* residual;  // NHWC [M, ldr] or null
-    mlvc_half* out;             // NHWC [M, ldo]
+    mlvc_half* out;             // NHWC output (written through map_out; kept for debugging)
     int M, N, K;                // GEMM extents (K = taps * IC); N counts prepared (padded) weight rows
-    int n_valid;                // output channels actually stored (<= N, multiple of 8)
-    int BN;                     // columns per N tile (multiple of 16, <= 256)
+    int n_valid;                // output channels actually stored (<= N)
+    int BN;                     // columns per N tile (multiple of 64, <= 256; ReGLU: multiple of 128)
     int n_tiles, m_tiles;       // tile counts
-    int ldo, out_col0;          // output row stride / first channel written
-    int ldr;                    // residual row stride
     int epilogue;               // Epilogue
     float alpha, clip_lo, clip_hi;
     int a_stages;               // A ring depth (1x1: 16 KB panels; kxk: halo blocks)

@@ -162,10 +162,11 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
 
 
 @pytest.mark.parametrize("c,hidden,c_out,fused", [
-    (128, 256, 128, True), (64, 64, 32, True), (256, 128, 256, True), (64, 192, 96, True),
-    (48, 64, 32, False),   # C not a multiple of 64
+    (128, 256, 128, True), (64, 64, 64, True), (256, 128, 128, True), (64, 192, 64, True),
+    (48, 64, 64, False),     # C not a multiple of 64
     (128, 512, 128, False),  # hidden above the kernel's bias capacity
-    (128, 256, 136, False),  # C_out not a multiple of 32
+    (128, 256, 96, False),   # C_out not a multiple of 64 (64-column output panels)
+    (128, 256, 256, False),  # output tile larger than the two hidden panels it is staged in
 ])
 def test_plan_ffn_fusion_predicates(c, hidden, c_out, fused):
     gb = GraphBuilder()

@@ -74,10 +74,11 @@ def test_conv1x1_reglu(c, h, w):
 
 FFN_CASES = [  # (C, hidden, C_out, H, W, epilogue of the second conv)
     (128, 256, 128, 92, 160, "residual"),  # block-stack FFN (residual = FFN input)
-    (64, 64, 32, 13, 17, None),            # one hidden chunk, ragged last tile
-    (256, 128, 256, 8, 20, "leaky"),       # four input panels, one accumulator buffer
+    (64, 64, 64, 13, 17, None),            # one hidden chunk, ragged last tile
+    (256, 128, 128, 8, 20, "leaky"),       # four input panels
     (128, 256, 128, 160, 160, "residual"), # 200 tiles: two tiles per CTA, two X buffers
-    (64, 192, 96, 20, 30, "residual_other"),
+    (64, 192, 64, 20, 30, "residual"),     # three hidden chunks
+    (64, 128, 64, 20, 30, "residual_other"),  # residual is not the FFN input: two separate convs
 ]
 
 
@@ -117,6 +118,9 @@ def test_ffn_fused(c, hidden, c_out, h, w, epilogue, monkeypatch):
     got, want, be = run_both(gb, inputs)
     compare(got[0], want[0])
     kernels = [s["kernel"] for s in be.steps() if s["kernel"] != "mlvc_boundary_f16"]
+    if epilogue == "residual_other":
+        assert kernels == ["mlvc_conv1x1_tc", "mlvc_conv1x1_tc"], kernels
+        return
     assert kernels == ["mlvc_ffn_tc"], kernels
     graph, weights = gb.finish()
     monkeypatch.setenv("MLVC_B200_FFN_FUSION", "0")
@@ -319,6 +323,42 @@ def test_state_binding_and_slots():
         be.submit(slot)
         be.wait_slot(slot)
         bits_equal(be.slot_output(slot, 0), outs[i])
+
+
+def test_slot_pipeline_overlapped_frames():
+    """Two slots in flight (host->device of one frame, the schedule of the
+    previous one and its device->host copy overlap on separate streams):
+    frames still run in submission order, the recurrent state passes from
+    frame to frame, and every slot returns the bits run() gives."""
+    rng = np.random.default_rng(9)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 32, 64, 96])
+    ref = gb.input("ref", [1, 64, 32, 48])
+    w = gb.weight("w", (rng.standard_normal((64, 128, 1, 1), dtype=np.float32) * 0.1).astype(np.float16))
+    feat = gb.add(gb.conv(gb.space_to_depth(x, 2), w), ref)
+    gb.output(gb.depth_to_space(gb.leaky_relu(feat, 0.1), 2), "y")
+    gb.output(feat, "feature")
+    graph, weights = gb.finish()
+    be = Backend(0)
+    be.load_memory(graph, weights, [(1, 1)])
+    frames = [_rand((1, 32, 64, 96), 20 + i) for i in range(7)]
+    be.reset_state()
+    want = [be.run([f])[0].copy() for f in frames]
+    be.reset_state()
+    be.configure_slots(2)
+    got = [None] * len(frames)
+    for i, f in enumerate(frames):
+        slot = i % 2
+        if i >= 2:
+            be.wait_slot(slot)
+            got[i - 2] = be.slot_output(slot, 0).copy()
+        be.slot_input(slot, 0)[...] = f
+        be.submit(slot)
+    for i in range(len(frames) - 2, len(frames)):
+        be.wait_slot(i % 2)
+        got[i] = be.slot_output(i % 2, 0).copy()
+    for g, w_ in zip(got, want):
+        bits_equal(g, w_)
 
 
 def test_rejects_bad_input_shape():
