@@ -350,6 +350,8 @@ void Backend::plan()
     {
         const char* env = std::getenv("MLVC_B200_FFN_FUSION");
         ffn_fusion_ = !(env && env[0] == '0');
+        env = std::getenv("MLVC_B200_DW_FUSION");
+        dw_fusion_ = !(env && env[0] == '0');
     }
     const size_t nt = graph_.tensors.size();
     values_.assign(nt, Value{});
@@ -1015,6 +1017,123 @@ void Backend::plan()
                 s.info.nodes = std::to_string(i);
             }
             const bool depthwise = G == IC && OC == IC && ICG == 1 && IC % 8 == 0 && epi == kEpiBias;
+            if (depthwise && dw_fusion_ && N == 1 && KH == 3 && KW == 3 && SH == 1 && SW == 1 && PH == 1 && PW == 1 &&
+                IC % 64 == 0 && OW % 4 == 0 && i + 1 < nodes.size()) {
+                // ---- fused depthwise 3x3 + the 1x1 conv that consumes it: the
+                // depthwise result is the GEMM's A operand in shared memory
+                const NodeDesc& n2 = nodes[i + 1];
+                bool ok = n2.op == Op::kConv && n2.inputs[0] == n.output && only_consumer(n.output) && n2.groups == 1 &&
+                          n2.strides[0] == 1 && n2.strides[1] == 1 && n2.pads[0] == 0 && n2.pads[1] == 0;
+                const uint32_t w2_id = ok ? n2.inputs[1] : 0;
+                const uint32_t b2_id = ok && n2.inputs.size() > 2 ? n2.inputs[2] : 0;
+                int OC2 = 0;
+                if (ok) {
+                    const Value& w2v = values_[w2_id];
+                    ok = w2v.kind == Value::kWeight && w2v.dtype == DType::kFp16 && w2v.shape.size() == 4 &&
+                         w2v.shape[1] == IC && w2v.shape[2] == 1 && w2v.shape[3] == 1 &&
+                         (!b2_id || values_[b2_id].kind == Value::kWeight);
+                    OC2 = ok ? static_cast<int>(w2v.shape[0]) : 0;
+                    ok = ok && OC2 % 64 == 0 && OC2 <= 256;
+                }
+                const int M = OH * OW, halo_px = 128 + 2 * OW + 2;
+                const int halo_boxes = (halo_px + 255) / 256, halo_box = (halo_px + halo_boxes - 1) / halo_boxes;
+                const int halo_stride = static_cast<int>(align_up(static_cast<size_t>(halo_boxes) * halo_box * 128, 1024));
+                const int fixed = 1024 + kDwHeaderBytes + 2 * 16384 + 2 * OC2 * 128 + OC2 / 64 * kTcStagePanelBytes;
+                int h_stages = 0;
+                if (ok && halo_boxes <= 3)
+                    h_stages = fixed + 2 * halo_stride <= max_smem_optin_ ? 2 : (fixed + halo_stride <= max_smem_optin_ ? 1 : 0);
+                if (h_stages) {
+                    int epi2 = kEpiBias;
+                    float alpha2 = 0.0f;
+                    uint32_t out2 = 0, res2 = 0;
+                    const size_t consumed2 = conv_epilogue(i + 1, epi2, alpha2, out2, res2);
+                    std::vector<uint16_t> dwp(static_cast<size_t>(9) * IC);
+                    for (int c = 0; c < IC; ++c)
+                        for (int k = 0; k < 9; ++k)
+                            dwp[static_cast<size_t>(k) * IC + c] = w[static_cast<size_t>(c) * 9 + k];
+                    std::vector<uint16_t> b2p(OC2, 0);
+                    if (b2_id)
+                        std::copy(wdata(b2_id), wdata(b2_id) + OC2, b2p.begin());
+                    const size_t dww_off = prep(dwp.data(), dwp.size() * 2);
+                    const size_t dwb_off = bias ? prep(bias_full.data(), bias_full.size() * 2) : 0;
+                    const size_t w2_off = prep(wdata(w2_id), static_cast<size_t>(OC2) * IC * 2);
+                    const size_t b2_off = prep(b2p.data(), b2p.size() * 2);
+                    const bool has_dw_bias = bias != nullptr;
+                    const int m_tiles = (M + 127) / 128;
+                    Step f;
+                    f.reads = {x_id};
+                    if (res2)
+                        f.reads.push_back(res2);
+                    f.writes = {out2};
+                    f.info.nodes = std::to_string(i) + "-" + std::to_string(i + consumed2);
+                    f.info.flops = 2.0 * M * IC * 9 + 2.0 * M * static_cast<double>(IC) * OC2;
+                    f.info.bytes = 2.0 * (static_cast<double>(M) * IC + 9.0 * IC + IC + static_cast<double>(OC2) * IC +
+                                          OC2 + static_cast<double>(M) * OC2 * (res2 ? 2 : 1));
+                    f.kernel = "mlvc_dwconv_tc";
+                    f.info.kernel = f.kernel;
+                    f.smem = static_cast<unsigned>(fixed + h_stages * halo_stride);
+                    f.block = 320;
+                    f.grid = static_cast<unsigned>(std::min(m_tiles, sm_count_));
+                    f.build = [=, this](Step& st) {
+                        DwConvTcParams dwp_{};
+                        ConvTcParams& p = dwp_.c;
+                        const cuuint32_t elem1[2] = {1, 1};
+                        {
+                            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(IC), static_cast<cuuint64_t>(M)};
+                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(IC) * 2};
+                            const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(halo_box)};
+                            check(cuTensorMapEncodeTiled(&dwp_.map_halo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                                         reinterpret_cast<void*>(values_[x_id].addr), dims, strides, box,
+                                                         elem1, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  "cuTensorMapEncodeTiled(dwconv halo)");
+                        }
+                        {
+                            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(IC), static_cast<cuuint64_t>(OC2)};
+                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(IC) * 2};
+                            const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(OC2)};
+                            check(cuTensorMapEncodeTiled(&p.map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                                         reinterpret_cast<void*>(prepped_dev_.get() + w2_off), dims,
+                                                         strides, box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  "cuTensorMapEncodeTiled(dwconv W)");
+                        }
+                        encode_tile_map(&p.map_out, values_[out2].addr, OC2, M, 0, 0, "cuTensorMapEncodeTiled(dwconv out)");
+                        if (res2)
+                            encode_tile_map(&p.map_res, values_[res2].addr, OC2, M, 0, 0,
+                                            "cuTensorMapEncodeTiled(dwconv residual)");
+                        else
+                            p.map_res = p.map_out;
+                        p.map_a0 = p.map_a1 = dwp_.map_halo;
+                        p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b2_off);
+                        p.out = reinterpret_cast<mlvc_half*>(values_[out2].addr);
+                        p.M = M;
+                        p.N = OC2;
+                        p.n_valid = OC2;
+                        p.K = IC;
+                        p.BN = OC2;
+                        p.n_tiles = 1;
+                        p.m_tiles = m_tiles;
+                        p.epilogue = epi2;
+                        p.alpha = alpha2;
+                        p.a_stages = 2;
+                        p.b_stages = 2;
+                        dwp_.dw_w = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + dww_off);
+                        dwp_.dw_b = has_dw_bias ? reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + dwb_off) : nullptr;
+                        dwp_.width = OW;
+                        dwp_.halo_px = halo_px;
+                        dwp_.halo_box = halo_box;
+                        dwp_.halo_boxes = halo_boxes;
+                        dwp_.h_stages = h_stages;
+                        st.set(dwp_);
+                    };
+                    steps_.push_back(std::move(f));
+                    i += 1 + consumed2;
+                    continue;
+                }
+            }
             DirectConvParams dp{};
             dp.n = N;
             dp.ih = IH;
@@ -1610,7 +1729,8 @@ std::vector<uint64_t> Backend::trace_step(size_t index)
     if (offline_)
         throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
     Step& st = steps_.at(index);
-    if (st.kernel != "mlvc_conv1x1_tc" && st.kernel != "mlvc_convkxk_tc" && st.kernel != "mlvc_ffn_tc")
+    if (st.kernel != "mlvc_conv1x1_tc" && st.kernel != "mlvc_convkxk_tc" && st.kernel != "mlvc_ffn_tc" &&
+        st.kernel != "mlvc_dwconv_tc")
         throw std::runtime_error("mlvc-b200: only tensor-core conv steps carry a phase trace");
     ContextGuard guard(ctx_);
     const size_t n = static_cast<size_t>(st.grid) * kTracePoints;

@@ -146,6 +146,9 @@ private:
     // FFN fusion (ReGLU conv + following 1x1 conv in one kernel); MLVC_B200_FFN_FUSION=0 plans
     // the two convs as separate steps (same results, for comparison).
     bool ffn_fusion_ = true;
+    // Depthwise 3x3 + following 1x1 conv in one kernel; MLVC_B200_DW_FUSION=0
+    // plans them as separate steps (same results, for comparison).
+    bool dw_fusion_ = true;
     bool keep_all_values_ = false;
 };
 

@@ -90,6 +90,7 @@ enum TracePoint : int {
     kTrFfnG1Second = 17,     // fused FFN: MMA issuer committed GEMM1 of chunk 1
     kTrFfnG2First = 18,      // fused FFN: MMA issuer passed the waits of GEMM2 chunk 0
     kTrFfnChunk1Done = 19,   // fused FFN: epilogue released hidden chunk 1
+    kTrDwFirstSlice = 20,    // fused depthwise + 1x1: first depthwise slice written as an A panel
     kTracePoints = 24
 };
 
@@ -115,6 +116,29 @@ struct FfnTcParams {
     int w_slot_bytes;        // bytes per weight ring slot (max of a W1 and a W2 panel)
     // Shared memory: header, X tiles (a_stages), two hidden panels (also the
     // output epilogue's staging buffers), weight ring (b_stages slots).
+};
+
+// Fused depthwise 3x3 (stride 1, pad 1) + 1x1 conv (mlvc_dwconv_tc):
+//     d   = fp16(dw3x3(x) + b_dw)               CUDA cores, FP32 FMA from the bias
+//     out = epilogue(fp16(d W^T + b))           tcgen05; bias / LeakyReLU / + residual
+// The depthwise result of each 128-pixel tile is written straight into the
+// GEMM's A operand in shared memory, 64 channels at a time.
+constexpr int kDwHeaderBytes = 2048;
+
+struct DwConvTcParams {
+    // map_b = W [C_out rows, C] (C_out x 64 boxes, 128-byte swizzle);
+    // map_out / map_res / bias / epilogue / alpha describe the 1x1 conv's
+    // output; K = C, BN = N = n_valid = C_out, a_stages = A panels in flight,
+    // b_stages = W ring slots.
+    ConvTcParams c;
+    CUtensorMap map_halo;    // x [M pixels, C] in {64, halo_box} boxes, no swizzle (128-byte pixel rows)
+    const mlvc_half* dw_w;   // [9][C], tap (ky * 3 + kx) major
+    const mlvc_half* dw_b;   // [C] or null
+    int width;               // image width (multiple of 4)
+    int halo_px;             // 128 + 2 * width + 2 pixels per 64-channel slice
+    int halo_box;            // pixels per halo TMA box (<= 256)
+    int halo_boxes;          // boxes per slice
+    int h_stages;            // halo slices in flight (1 or 2)
 };
 
 struct ElementwiseParams {

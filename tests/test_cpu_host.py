@@ -145,20 +145,41 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
     gb, _ = build_block_stack(seed=0)
     be = plan(*gb.finish())
     k = _kernels(be)
-    assert k.count("mlvc_conv1x1_tc") == 16 and k.count("mlvc_ffn_tc") == 8
-    assert k.count("mlvc_depthwise3x3_f16") == 8
+    assert k.count("mlvc_conv1x1_tc") == 8 and k.count("mlvc_ffn_tc") == 8 and k.count("mlvc_dwconv_tc") == 8
+    assert "mlvc_depthwise3x3_f16" not in k and len(k) == 26
     assert "mlvc_unary_f16" not in k and "mlvc_binary_same_f16" not in k and "mlvc_reglu_f16" not in k
     nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_ffn_tc"]
     assert "6-12" in nodes  # conv + slice + slice + clip + mul + conv + add
+    nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_dwconv_tc"]
+    assert "3-5" in nodes  # depthwise conv + 1x1 conv + add
     flops = sum(s["flops"] for s in be.steps())
     assert abs(flops - 39.13e9) / 39.13e9 < 0.01  # config-2 algorithmic FLOPs
     assert all(s["smem"] > 233472 // 2 for s in be.steps() if s["kernel"] == "mlvc_ffn_tc")  # one CTA per SM
 
     monkeypatch.setenv("MLVC_B200_FFN_FUSION", "0")
+    monkeypatch.setenv("MLVC_B200_DW_FUSION", "0")
     split = _kernels(plan(*gb.finish()))
-    assert split.count("mlvc_conv1x1_tc") == 32 and "mlvc_ffn_tc" not in split
+    assert split.count("mlvc_conv1x1_tc") == 32 and split.count("mlvc_depthwise3x3_f16") == 8
+    assert "mlvc_ffn_tc" not in split and "mlvc_dwconv_tc" not in split
     nodes = [s["nodes"] for s in plan(*gb.finish()).steps() if s["kernel"] == "mlvc_conv1x1_tc"]
     assert "6-10" in nodes  # conv + slice + slice + clip + mul
+
+
+@pytest.mark.parametrize("c,c_out,h,w,fused", [
+    (256, 128, 92, 160, True), (64, 64, 13, 20, True), (128, 128, 9, 300, True), (64, 256, 8, 8, True),
+    (64, 64, 13, 17, False),    # width not a multiple of 4
+    (48, 64, 8, 8, False),      # channels not a multiple of 64
+    (64, 96, 8, 8, False),      # output channels not a multiple of 64
+    (64, 64, 4, 2000, False),   # halo rows beyond three TMA boxes
+])
+def test_plan_depthwise_fusion_predicates(c, c_out, h, w, fused):
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, h, w])
+    d = gb.conv(x, gb.weight("dw", np.zeros((c, 1, 3, 3), np.float16)), gb.weight("db", np.zeros(c, np.float16)),
+                (1, 1), (1, 1), groups=c)
+    gb.output(gb.conv(d, gb.weight("w", np.zeros((c_out, c, 1, 1), np.float16))), "y")
+    k = _kernels(plan(*gb.finish()))
+    assert ("mlvc_dwconv_tc" in k) == fused, k
 
 
 @pytest.mark.parametrize("c,hidden,c_out,fused", [

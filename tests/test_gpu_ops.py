@@ -130,6 +130,49 @@ def test_ffn_fused(c, hidden, c_out, h, w, epilogue, monkeypatch):
     bits_equal(split.run(inputs)[0], got[0])
 
 
+DW_CASES = [  # (C, C_out, H, W, epilogue of the 1x1 conv)
+    (256, 128, 92, 160, "residual"),  # block-stack shape: two halo boxes, two halo stages
+    (64, 64, 13, 20, None),           # one halo box, ragged last tile
+    (128, 128, 9, 300, "leaky"),      # three halo boxes, one halo stage
+    (64, 64, 160, 160, "residual"),   # 200 tiles: two tiles per CTA
+    (64, 256, 8, 8, None),            # 256 output columns (four staging panels)
+]
+
+
+@pytest.mark.parametrize("c,c_out,h,w,epilogue", DW_CASES)
+def test_dwconv_fused(c, c_out, h, w, epilogue, monkeypatch):
+    """Depthwise 3x3 -> 1x1 conv (+ residual / LeakyReLU) as one kernel, the
+    depthwise result written straight into the tensor-core A operand: parity
+    with the oracle, and bit-identical to the two stand-alone kernels."""
+    rng = np.random.default_rng(31)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, h, w])
+    dw = gb.weight("dw", (rng.standard_normal((c, 1, 3, 3), dtype=np.float32) / 3.0).astype(np.float16))
+    db = gb.weight("db", rng.uniform(-0.1, 0.1, c).astype(np.float16))
+    d = gb.conv(x, dw, db, (1, 1), (1, 1), groups=c)
+    wt = gb.weight("w", (rng.standard_normal((c_out, c, 1, 1), dtype=np.float32) * np.sqrt(1.0 / c)).astype(np.float16))
+    b = gb.weight("b", rng.uniform(-0.1, 0.1, c_out).astype(np.float16))
+    y = gb.conv(d, wt, b)
+    inputs = [rng.standard_normal((1, c, h, w), dtype=np.float32).astype(np.float16)]
+    if epilogue == "residual":
+        r = gb.input("r", [1, c_out, h, w])
+        y = gb.add(y, r)
+        inputs.append(rng.standard_normal((1, c_out, h, w), dtype=np.float32).astype(np.float16))
+    elif epilogue == "leaky":
+        y = gb.leaky_relu(y, 0.01)
+    gb.output(y, "y")
+    got, want, be = run_both(gb, inputs)
+    compare(got[0], want[0])
+    kernels = [s["kernel"] for s in be.steps() if s["kernel"] != "mlvc_boundary_f16"]
+    assert kernels == ["mlvc_dwconv_tc"], kernels
+    graph, weights = gb.finish()
+    monkeypatch.setenv("MLVC_B200_DW_FUSION", "0")
+    split = Backend(0)
+    split.load_memory(graph, weights)
+    assert "mlvc_dwconv_tc" not in {s["kernel"] for s in split.steps()}
+    bits_equal(split.run(inputs)[0], got[0])
+
+
 SPATIAL = [  # (IC, OC, stride, kernel, pad, H, W)
     (24, 24, 1, 3, 1, 13, 17), (40, 264, 2, 3, 1, 13, 17), (8, 8, 2, 2, 0, 13, 17), (128, 256, 2, 2, 0, 13, 17),
     (64, 64, 1, 3, 1, 13, 17), (64, 128, 2, 3, 1, 13, 17), (64, 64, 1, 3, 1, 46, 300), (128, 64, 1, 3, 1, 9, 140),
