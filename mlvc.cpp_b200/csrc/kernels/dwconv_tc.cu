@@ -272,14 +272,15 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                         for (int k = 0; k < 8; ++k)
                             acc4[i][k] = b8[k];
                 }
-                float wf[9][8];
+                // taps as packed FP16 pairs: the mixed-precision FMA needs no conversion
+                uint32_t wv[9][4];
 #pragma unroll
                 for (int tap = 0; tap < 9; ++tap) {
-                    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(dp.dw_w + tap * p.K + ch));
-                    const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        unpack_h2(ww[k], wf[tap][2 * k], wf[tap][2 * k + 1]);
+                    const uint4 q = __ldg(reinterpret_cast<const uint4*>(dp.dw_w + tap * p.K + ch));
+                    wv[tap][0] = q.x;
+                    wv[tap][1] = q.y;
+                    wv[tap][2] = q.z;
+                    wv[tap][3] = q.w;
                 }
                 const uint8_t* halo = h_smem + static_cast<size_t>(hs) * halo_stride + cq * 16;
                 // input columns x0 - 1 .. x0 + 4; output pixel i takes column cc with kx = cc - i
@@ -288,15 +289,15 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                     const int ix = x0 - 1 + cc;
                     if (ix < 0 || ix >= W)
                         continue;  // outside the image: the tap is skipped (no padding term)
-                    float xf[3][8];
+                    uint32_t xv[3][4];
 #pragma unroll
                     for (int ky = 0; ky < 3; ++ky) {
                         const uint4 v =
                             *reinterpret_cast<const uint4*>(halo + static_cast<size_t>(h0 + (ky - 1) * W + cc - 1) * 128);
-                        const uint32_t* vw = reinterpret_cast<const uint32_t*>(&v);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            unpack_h2(vw[k], xf[ky][2 * k], xf[ky][2 * k + 1]);
+                        xv[ky][0] = v.x;
+                        xv[ky][1] = v.y;
+                        xv[ky][2] = v.z;
+                        xv[ky][3] = v.w;
                     }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -306,8 +307,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
 #pragma unroll
                         for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
-                            for (int k = 0; k < 8; ++k)
-                                acc4[i][k] = fmaf(xf[ky][k], wf[ky * 3 + kx][k], acc4[i][k]);
+                            for (int k = 0; k < 4; ++k)
+                                fma_h2(acc4[i][2 * k], acc4[i][2 * k + 1], xv[ky][k], wv[ky * 3 + kx][k]);
                     }
                 }
                 mbar_arrive(&sh->h_empty[hs]);  // halo slice read

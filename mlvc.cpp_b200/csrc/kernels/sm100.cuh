@@ -286,6 +286,22 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b)
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// a_lo = fma(x_lo, w_lo, a_lo), a_hi = fma(x_hi, w_hi, a_hi) on the two FP16
+// halves of x2 and w2 with FP32 accumulators (sm_100 mixed-precision
+// fma.rn.f32.f16).  A product of two FP16 values is exact in FP32, so each
+// result equals fmaf(float(x), float(w), a) bit for bit, without the two
+// FP16 -> FP32 conversions (a slow pipe) that fmaf would need.
+__device__ __forceinline__ void fma_h2(float& a_lo, float& a_hi, uint32_t x2, uint32_t w2)
+{
+    asm("{\n\t.reg .b16 xl, xh, wl, wh;\n\t"
+        "mov.b32 {xl, xh}, %2;\n\t"
+        "mov.b32 {wl, wh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, xl, wl, %0;\n\t"
+        "fma.rn.f32.f16 %1, xh, wh, %1;\n\t}"
+        : "+f"(a_lo), "+f"(a_hi)
+        : "r"(x2), "r"(w2));
+}
+
 __device__ __forceinline__ void unpack_h2(uint32_t u, float& a, float& b)
 {
     __half2 h = *reinterpret_cast<__half2*>(&u);
