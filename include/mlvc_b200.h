@@ -105,6 +105,24 @@ const void* mlvc_b200_slot_output(const mlvc_b200_backend* backend, size_t slot,
 int mlvc_b200_submit(mlvc_b200_backend* backend, size_t slot);
 int mlvc_b200_wait_slot(mlvc_b200_backend* backend, size_t slot);
 
+/* BufferedCodecBackend codec I/O (backend.hpp:69-93): CodecIoConfig {width,
+ * height, model_width, model_height, pixel_range, slots} with the frame
+ * placement of frame_padding (core/src/yuv.cpp:324-337: top-left, transposed
+ * when it only fits rotated).  Graph input `input_index` then takes a YUV420
+ * frame per slot, converted on the GPU like prepare_model_input
+ * (yuv.cpp:339-400), and output `output_index` returns one, converted like
+ * prepare_model_output_into (yuv.cpp:410-525); pass MLVC_B200_NO_CODEC_TENSOR
+ * to keep either side a tensor.  Configures `slots` slots. */
+#define MLVC_B200_NO_CODEC_TENSOR ((size_t)-1)
+int mlvc_b200_configure_codec_io(mlvc_b200_backend* backend, int width, int height, int model_width,
+                                 int model_height, float pixel_range, size_t slots, size_t input_index,
+                                 size_t output_index);
+/* encoder_input_yuv(slot) / decoder_output_yuv(slot) (backend.hpp:86, 93):
+ * the slot's pinned Y, U, V planes (width x height, then two quarter planes). */
+int mlvc_b200_slot_input_yuv(mlvc_b200_backend* backend, size_t slot, uint8_t** y, uint8_t** u, uint8_t** v);
+int mlvc_b200_slot_output_yuv(const mlvc_b200_backend* backend, size_t slot, const uint8_t** y, const uint8_t** u,
+                              const uint8_t** v);
+
 /* Measurement hooks (no reference counterpart; the reference times whole
  * runs with steady_clock, codec/src/pipeline.cpp:341-415).  enqueue replays
  * the captured schedule on the backend's stream with the device-resident

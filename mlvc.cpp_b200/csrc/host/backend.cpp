@@ -1885,31 +1885,68 @@ void Backend::configure_slots(size_t count)
     if (!copy_out_)
         check(cuStreamCreate(&copy_out_, CU_STREAM_NON_BLOCKING), "cuStreamCreate(copy out)");
     slots_ = std::vector<Slot>(count);
+    const size_t yuv_bytes = static_cast<size_t>(codec_.width) * codec_.height * 3 / 2;
+    auto yuv_launch = [&](const char* kernel, YuvParams yp, long long work) {
+        void* args[] = {&yp};
+        const unsigned grid = blocks_for(work, 256, sm_count_);
+        check(cuLaunchKernel(fn(kernel), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr), kernel);
+    };
+    auto yuv_params = [&]() {
+        YuvParams yp{};
+        yp.width = codec_.width;
+        yp.height = codec_.height;
+        yp.model_width = codec_.model_width;
+        yp.model_height = codec_.model_height;
+        yp.pad_left = codec_.pad_left;
+        yp.pad_top = codec_.pad_top;
+        yp.rotated = codec_.rotated ? 1 : 0;
+        yp.pixel_range = codec_.pixel_range;
+        return yp;
+    };
     for (auto& s : slots_) {
         for (size_t k = 0; k < ext_inputs_.size(); ++k) {
             const auto& d = input_desc(k);
-            const size_t bytes = static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype);
+            const size_t bytes = k == codec_.input ? yuv_bytes
+                                                   : static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype);
             s.in.emplace_back(bytes);
             s.din.emplace_back(align_up(bytes, 256));
         }
         for (size_t k = 0; k < ext_outputs_.size(); ++k) {
             const auto& d = output_desc(k);
-            const size_t bytes = static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype);
+            const size_t bytes = k == codec_.output ? yuv_bytes
+                                                    : static_cast<size_t>(element_count(d.shape)) * dtype_size(d.dtype);
             s.out.emplace_back(bytes);
             s.dout.emplace_back(align_up(bytes, 256));
         }
-        // graph: staged inputs -> schedule inputs, schedule, outputs -> staging
+        // graph: staged inputs -> schedule inputs (a YUV frame through the
+        // YUV -> tensor kernel), schedule, outputs -> staging (the decoded
+        // frame through the tensor -> YUV kernel)
         check(cuStreamBeginCapture(stream_, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL), "cuStreamBeginCapture(slot)");
         try {
             for (size_t k = 0; k < ext_inputs_.size(); ++k) {
                 const CUdeviceptr dst = input_stage_dev_[k] ? input_stage_dev_[k].get() : input_dev_[k].get();
-                check(cuMemcpyDtoDAsync(dst, s.din[k].get(), s.in[k].bytes(), stream_), "cuMemcpyDtoDAsync(slot in)");
+                if (k == codec_.input) {
+                    YuvParams yp = yuv_params();
+                    yp.yuv_in = reinterpret_cast<const uint8_t*>(s.din[k].get());
+                    yp.t_out = reinterpret_cast<mlvc_half*>(dst);
+                    yuv_launch("mlvc_yuv420_to_tensor_f16", yp,
+                               3LL * codec_.model_width * static_cast<long long>(codec_.model_height));
+                } else {
+                    check(cuMemcpyDtoDAsync(dst, s.din[k].get(), s.in[k].bytes(), stream_), "cuMemcpyDtoDAsync(slot in)");
+                }
             }
             launch_steps(stream_);
             for (size_t k = 0; k < ext_outputs_.size(); ++k) {
                 const uint32_t id = graph_.outputs[ext_outputs_[k]];
                 const CUdeviceptr src = output_stage_dev_[k] ? output_stage_dev_[k].get() : values_[id].addr;
-                check(cuMemcpyDtoDAsync(s.dout[k].get(), src, s.out[k].bytes(), stream_), "cuMemcpyDtoDAsync(slot out)");
+                if (k == codec_.output) {
+                    YuvParams yp = yuv_params();
+                    yp.t_in = reinterpret_cast<const mlvc_half*>(src);
+                    yp.yuv_out = reinterpret_cast<uint8_t*>(s.dout[k].get());
+                    yuv_launch("mlvc_tensor_to_yuv420", yp, static_cast<long long>(codec_.width) * codec_.height);
+                } else {
+                    check(cuMemcpyDtoDAsync(s.dout[k].get(), src, s.out[k].bytes(), stream_), "cuMemcpyDtoDAsync(slot out)");
+                }
             }
         } catch (...) {
             CUgraph g = nullptr;
@@ -1927,6 +1964,75 @@ size_t Backend::slot_count() const { return slots_.size(); }
 
 void* Backend::slot_input(size_t slot, size_t i) { return slots_.at(slot).in.at(i).get(); }
 const void* Backend::slot_output(size_t slot, size_t i) const { return slots_.at(slot).out.at(i).get(); }
+
+// Reference: BufferedCodecBackend::configure_codec_io with CodecIoConfig
+// (runtime/include/mlvc/runtime/backend.hpp:69-83) and the frame placement of
+// frame_padding (core/src/yuv.cpp:324-337).
+void Backend::configure_codec_io(int width, int height, int model_width, int model_height, float pixel_range,
+                                 size_t slots, size_t input_index, size_t output_index)
+{
+    if (!loaded_)
+        throw std::runtime_error("mlvc-b200: load() must be called before configure_codec_io()");
+    auto even = [](int w, int h) { return w > 0 && h > 0 && w % 2 == 0 && h % 2 == 0; };
+    if (!even(width, height) || !even(model_width, model_height))
+        throw std::runtime_error("mlvc-b200: YUV420 dimensions must be positive and even");
+    if (!std::isfinite(pixel_range) || pixel_range <= 0.0f)
+        throw std::runtime_error("mlvc-b200: pixel range must be finite and positive");
+    const bool native = width <= model_width && height <= model_height;
+    const bool rotated = height <= model_width && width <= model_height;
+    if (!native && !rotated)
+        throw std::runtime_error("mlvc-b200: input frame is larger than the model dimensions");
+    auto check_tensor = [&](const TensorDesc& d, const char* what) {
+        const std::vector<int64_t> want{1, 3, model_height, model_width};
+        if (d.dtype != DType::kFp16 || d.shape != want)
+            throw std::runtime_error(std::string("mlvc-b200: codec ") + what + " must be FP16 [1, 3, model_height, model_width]");
+    };
+    if (input_index != kNoCodecTensor) {
+        if (input_index >= ext_inputs_.size())
+            throw std::runtime_error("mlvc-b200: codec input index out of range");
+        check_tensor(input_desc(input_index), "input");
+    }
+    if (output_index != kNoCodecTensor) {
+        if (output_index >= ext_outputs_.size())
+            throw std::runtime_error("mlvc-b200: codec output index out of range");
+        check_tensor(output_desc(output_index), "output");
+    }
+    CodecIo c;
+    c.width = width;
+    c.height = height;
+    c.model_width = model_width;
+    c.model_height = model_height;
+    c.pixel_range = pixel_range;
+    c.rotated = !native;
+    c.pad_left = 0;
+    c.pad_top = 0;
+    c.input = input_index;
+    c.output = output_index;
+    codec_ = c;
+    configure_slots(slots);
+}
+
+void Backend::slot_input_yuv(size_t slot, uint8_t** y, uint8_t** u, uint8_t** v)
+{
+    if (codec_.input == kNoCodecTensor)
+        throw std::runtime_error("mlvc-b200: no codec input configured");
+    auto* base = static_cast<uint8_t*>(slot_input(slot, codec_.input));
+    const size_t ys = static_cast<size_t>(codec_.width) * codec_.height;
+    *y = base;
+    *u = base + ys;
+    *v = base + ys + ys / 4;
+}
+
+void Backend::slot_output_yuv(size_t slot, const uint8_t** y, const uint8_t** u, const uint8_t** v) const
+{
+    if (codec_.output == kNoCodecTensor)
+        throw std::runtime_error("mlvc-b200: no codec output configured");
+    const auto* base = static_cast<const uint8_t*>(slot_output(slot, codec_.output));
+    const size_t ys = static_cast<size_t>(codec_.width) * codec_.height;
+    *y = base;
+    *u = base + ys;
+    *v = base + ys + ys / 4;
+}
 
 void Backend::submit(size_t slot)
 {

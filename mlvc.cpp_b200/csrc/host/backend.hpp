@@ -77,6 +77,15 @@ public:
     void submit(size_t slot);
     void wait_slot(size_t slot);
 
+    // Codec I/O on the slot path: the graph input `input_index` takes a YUV420
+    // frame (converted on the GPU) and the output `output_index` returns one
+    // (kNoCodecTensor: that side stays a tensor).  Calls configure_slots(slots).
+    static constexpr size_t kNoCodecTensor = static_cast<size_t>(-1);
+    void configure_codec_io(int width, int height, int model_width, int model_height, float pixel_range,
+                            size_t slots, size_t input_index, size_t output_index);
+    void slot_input_yuv(size_t slot, uint8_t** y, uint8_t** u, uint8_t** v);
+    void slot_output_yuv(size_t slot, const uint8_t** y, const uint8_t** u, const uint8_t** v) const;
+
     // Device-resident replay of the whole schedule (no host copies) for
     // timing; optional per-step event timing.
     void enqueue();
@@ -133,6 +142,13 @@ private:
     std::vector<Step> steps_;
     std::vector<StepInfo> step_info_;
     std::vector<Slot> slots_;
+    struct CodecIo {
+        int width = 0, height = 0, model_width = 0, model_height = 0;
+        float pixel_range = 1.0f;
+        int pad_left = 0, pad_top = 0;
+        bool rotated = false;
+        size_t input = kNoCodecTensor, output = kNoCodecTensor;
+    } codec_;
 
     DeviceBuffer weights_dev_, prepped_dev_, arena_dev_, flush_dev_;
     std::vector<DeviceBuffer> input_dev_, input_stage_dev_, output_stage_dev_, state_dev_;

@@ -198,6 +198,35 @@ const void* mlvc_b200_slot_output(const mlvc_b200_backend* backend, size_t slot,
     return p;
 }
 
+int mlvc_b200_configure_codec_io(mlvc_b200_backend* backend, int width, int height, int model_width,
+                                 int model_height, float pixel_range, size_t slots, size_t input_index,
+                                 size_t output_index)
+{
+    return guarded([&] {
+        require(backend).configure_codec_io(width, height, model_width, model_height, pixel_range, slots, input_index,
+                                            output_index);
+    });
+}
+
+int mlvc_b200_slot_input_yuv(mlvc_b200_backend* backend, size_t slot, uint8_t** y, uint8_t** u, uint8_t** v)
+{
+    return guarded([&] {
+        if (!y || !u || !v)
+            throw std::runtime_error("mlvc-b200: null plane pointer");
+        require(backend).slot_input_yuv(slot, y, u, v);
+    });
+}
+
+int mlvc_b200_slot_output_yuv(const mlvc_b200_backend* backend, size_t slot, const uint8_t** y, const uint8_t** u,
+                              const uint8_t** v)
+{
+    return guarded([&] {
+        if (!y || !u || !v)
+            throw std::runtime_error("mlvc-b200: null plane pointer");
+        require(backend).slot_output_yuv(slot, y, u, v);
+    });
+}
+
 int mlvc_b200_submit(mlvc_b200_backend* backend, size_t slot)
 {
     return guarded([&] { require(backend).submit(slot); });

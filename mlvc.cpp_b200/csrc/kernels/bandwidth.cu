@@ -294,6 +294,79 @@ __device__ __forceinline__ void boundary_scalar(const BoundaryParams& p, mlvc_ha
     }
 }
 
+// ------------------------------------------------------------ codec I/O
+// YUV420 frame -> model input tensor (reference: prepare_model_input,
+// core/src/yuv.cpp:339-400).  One thread per tensor element; the 256-entry
+// byte -> FP16 table is built per block in shared memory with the
+// reference's arithmetic ((s / 255) * pixel_range in FP32, one rounding).
+extern "C" __global__ void __launch_bounds__(256) mlvc_yuv420_to_tensor_f16(const __grid_constant__ YuvParams p)
+{
+    __shared__ mlvc_half lut[256];
+    pdl_launch_dependents();
+    lut[threadIdx.x] = __float2half_rn(__fmul_rn(__fdiv_rn(static_cast<float>(threadIdx.x), 255.0f), p.pixel_range));
+    __syncthreads();
+    pdl_wait();
+    const long long plane = static_cast<long long>(p.model_width) * p.model_height;
+    const long long total = plane * 3;
+    const size_t y_size = static_cast<size_t>(p.width) * p.height;
+    const int uv_width = p.width / 2;
+    // canvas extent covered by the (possibly transposed) frame
+    const int active_w = p.rotated ? p.height : p.width;
+    const int active_h = p.rotated ? p.width : p.height;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int ch = static_cast<int>(i / plane);
+        const long long s = i - ch * plane;
+        const int y = static_cast<int>(s / p.model_width), x = static_cast<int>(s % p.model_width);
+        const int cy = min(y, active_h - 1), cx = min(x, active_w - 1);  // edge replication
+        const int sy = p.rotated ? cx : cy, sx = p.rotated ? cy : cx;    // frame coordinates
+        uint8_t v;
+        if (ch == 0)
+            v = p.yuv_in[static_cast<size_t>(sy) * p.width + sx];
+        else
+            v = p.yuv_in[y_size + static_cast<size_t>(ch - 1) * (y_size / 4) + static_cast<size_t>(sy / 2) * uv_width +
+                         sx / 2];
+        p.t_out[i] = lut[v];
+    }
+}
+
+__device__ __forceinline__ uint8_t quantize_byte(float v)
+{
+    v = fminf(fmaxf(v, 0.0f), 1.0f);
+    return static_cast<uint8_t>(__float2int_rn(__fmul_rn(v, 255.0f)));
+}
+
+// Model output tensor -> YUV420 frame (reference: prepare_model_output_into,
+// core/src/yuv.cpp:410-525; values divided by pixel_range in FP32 as there).
+// One thread per luma byte; threads of the first quarter also write one U and
+// one V byte.
+extern "C" __global__ void __launch_bounds__(256) mlvc_tensor_to_yuv420(const __grid_constant__ YuvParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const long long plane = static_cast<long long>(p.model_width) * p.model_height;
+    const int y_count = p.width * p.height;
+    const int uv_width = p.width / 2, uv_count = y_count / 4;
+    auto sample = [&](int ch, int y, int x) {
+        const int my = (p.rotated ? x : y) + p.pad_top, mx = (p.rotated ? y : x) + p.pad_left;
+        return __fdiv_rn(__half2float(p.t_in[ch * plane + static_cast<long long>(my) * p.model_width + mx]),
+                         p.pixel_range);
+    };
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < y_count; i += gridDim.x * blockDim.x) {
+        const int y = i / p.width, x = i - (i / p.width) * p.width;
+        p.yuv_out[i] = quantize_byte(sample(0, y, x));
+        if (i < uv_count) {
+            const int uy = i / uv_width, ux = i - uy * uv_width;
+            float u = __fadd_rn(sample(1, 2 * uy, 2 * ux), sample(1, 2 * uy, 2 * ux + 1));
+            float v = __fadd_rn(sample(2, 2 * uy, 2 * ux), sample(2, 2 * uy, 2 * ux + 1));
+            u = __fadd_rn(__fadd_rn(u, sample(1, 2 * uy + 1, 2 * ux)), sample(1, 2 * uy + 1, 2 * ux + 1));
+            v = __fadd_rn(__fadd_rn(v, sample(2, 2 * uy + 1, 2 * ux)), sample(2, 2 * uy + 1, 2 * ux + 1));
+            p.yuv_out[y_count + i] = quantize_byte(__fmul_rn(u, 0.25f));
+            p.yuv_out[y_count + uv_count + i] = quantize_byte(__fmul_rn(v, 0.25f));
+        }
+    }
+}
+
 extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid_constant__ BoundaryParams p)
 {
     pdl_launch_dependents();

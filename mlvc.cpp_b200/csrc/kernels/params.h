@@ -216,4 +216,24 @@ struct RegluParams {
     float lo, hi;
 };
 
+// Codec I/O between a YUV420 frame (planar Y, U, V bytes, width x height,
+// both even) and the model's [1, 3, model_height, model_width] FP16 NCHW
+// tensor, with the reference's conventions (core/src/yuv.cpp:324-525): the
+// frame sits at the top-left of the model canvas, transposed when it only
+// fits rotated; input pixels are byte * pixel_range / 255 rounded to FP16 and
+// replicate the last row / column into the padding; output bytes are
+// round(clamp(value / pixel_range, 0, 1) * 255), chroma from the mean of a
+// 2x2 block summed in raster order.
+struct YuvParams {
+    const uint8_t* yuv_in;    // to tensor: Y | U | V planes
+    uint8_t* yuv_out;         // from tensor
+    const mlvc_half* t_in;    // from tensor: NCHW [3, model_height, model_width]
+    mlvc_half* t_out;         // to tensor
+    int width, height;        // frame
+    int model_width, model_height;
+    int pad_left, pad_top;    // position of the frame on the canvas (output side)
+    int rotated;              // 1: the canvas holds the transposed frame
+    float pixel_range;
+};
+
 }  // namespace mlvc_b200

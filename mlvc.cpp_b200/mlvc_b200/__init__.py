@@ -57,6 +57,13 @@ EXPORTS = {
     "mlvc_b200_slot_count": ([ctypes.c_void_p], ctypes.c_size_t),
     "mlvc_b200_slot_input": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t], ctypes.c_void_p),
     "mlvc_b200_slot_output": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t], ctypes.c_void_p),
+    "mlvc_b200_configure_codec_io": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_float, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t],
+                                     ctypes.c_int),
+    "mlvc_b200_slot_input_yuv": ([ctypes.c_void_p, ctypes.c_size_t] + [ctypes.POINTER(ctypes.c_void_p)] * 3,
+                                 ctypes.c_int),
+    "mlvc_b200_slot_output_yuv": ([ctypes.c_void_p, ctypes.c_size_t] + [ctypes.POINTER(ctypes.c_void_p)] * 3,
+                                  ctypes.c_int),
     "mlvc_b200_submit": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_wait_slot": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_enqueue": ([ctypes.c_void_p], ctypes.c_int),
@@ -211,6 +218,36 @@ class Backend:
         _, dt, shape = self._out[i]
         n = int(np.prod(shape)) * np.dtype(dt).itemsize
         return np.frombuffer((ctypes.c_char * n).from_address(ptr), dt).reshape(shape)
+
+    NO_CODEC_TENSOR = ctypes.c_size_t(-1).value
+
+    def configure_codec_io(self, width, height, model_width, model_height, pixel_range=1.0, slots=2,
+                           input_index=None, output_index=None):
+        """BufferedCodecBackend::configure_codec_io: graph input `input_index`
+        takes a YUV420 frame per slot, output `output_index` returns one (None:
+        that side stays a tensor)."""
+        none = self.NO_CODEC_TENSOR
+        _check(lib().mlvc_b200_configure_codec_io(
+            self._h, width, height, model_width, model_height, pixel_range, slots,
+            none if input_index is None else input_index, none if output_index is None else output_index))
+        self._yuv = (width, height)
+
+    def _planes(self, fn, slot):
+        ptrs = [ctypes.c_void_p() for _ in range(3)]
+        _check(fn(self._h, slot, *[ctypes.byref(q) for q in ptrs]))
+        w, h = self._yuv
+        sizes = (w * h, w * h // 4, w * h // 4)
+        shapes = ((h, w), (h // 2, w // 2), (h // 2, w // 2))
+        return tuple(np.frombuffer((ctypes.c_char * n).from_address(q.value), np.uint8).reshape(s)
+                     for q, n, s in zip(ptrs, sizes, shapes))
+
+    def slot_input_yuv(self, slot):
+        """(Y, U, V) numpy views of the slot's pinned YUV420 input frame."""
+        return self._planes(lib().mlvc_b200_slot_input_yuv, slot)
+
+    def slot_output_yuv(self, slot):
+        """(Y, U, V) numpy views of the slot's decoded YUV420 frame."""
+        return self._planes(lib().mlvc_b200_slot_output_yuv, slot)
 
     def submit(self, slot):
         _check(lib().mlvc_b200_submit(self._h, slot))

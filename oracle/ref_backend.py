@@ -35,6 +35,10 @@ def lib():
         L.mlvc_ref_output_info.argtypes = [vp, ctypes.c_int, vp, vp, vp]
         L.mlvc_ref_output_copy.argtypes = [vp, ctypes.c_int, vp, sz]
         L.mlvc_ref_destroy.argtypes = [vp]
+        L.mlvc_ref_yuv_to_tensor.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_float, vp, vp, cp, sz]
+        L.mlvc_ref_tensor_to_yuv.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_float, vp, cp, sz]
         _lib = L
     return _lib
 
@@ -86,3 +90,30 @@ class RefCpuBackend:
             self.close()
         except Exception:
             pass
+
+
+def ref_yuv_to_tensor(yuv, width, height, model_width, model_height, pixel_range=1.0):
+    """The reference's prepare_model_input (core/src/yuv.cpp:339-400) on a
+    planar YUV420 byte frame: returns ([1, 3, mh, mw] float16, rotated)."""
+    import numpy as np
+    yuv = np.ascontiguousarray(yuv, np.uint8)
+    out = np.empty((1, 3, model_height, model_width), np.float16)
+    rot = ctypes.c_int(0)
+    err = ctypes.create_string_buffer(512)
+    if lib().mlvc_ref_yuv_to_tensor(yuv.ctypes.data, width, height, model_width, model_height, pixel_range,
+                                    out.ctypes.data, ctypes.byref(rot), err, 512):
+        raise RuntimeError(err.value.decode())
+    return out, bool(rot.value)
+
+
+def ref_tensor_to_yuv(tensor, width, height, pixel_range=1.0):
+    """The reference's prepare_model_output_into (core/src/yuv.cpp:410-525):
+    [1, 3, mh, mw] float16 -> planar YUV420 bytes of a width x height frame."""
+    import numpy as np
+    t = np.ascontiguousarray(tensor, np.float16)
+    mh, mw = t.shape[2], t.shape[3]
+    out = np.empty(width * height * 3 // 2, np.uint8)
+    err = ctypes.create_string_buffer(512)
+    if lib().mlvc_ref_tensor_to_yuv(t.ctypes.data, mw, mh, width, height, pixel_range, out.ctypes.data, err, 512):
+        raise RuntimeError(err.value.decode())
+    return out

@@ -8,6 +8,7 @@
 // run(inputs) -> outputs.  Errors are reported as a non-zero return plus a
 // message, the same convention as the reference C ABI (codec/src/c_api.cpp:60-88).
 #include "mlvc/core/assets.hpp"
+#include "mlvc/core/yuv.hpp"
 #include "mlvc/runtime/backend.hpp"
 
 #include <algorithm>
@@ -158,6 +159,44 @@ int mlvc_ref_output_copy(void* h, int i, void* dst, std::size_t capacity)
 void mlvc_ref_destroy(void* h)
 {
     delete static_cast<RefHandle*>(h);
+}
+
+// The reference's codec I/O conversions (core/src/yuv.cpp, compiled
+// unchanged): prepare_model_input (frame -> [1, 3, mh, mw] FP16 tensor,
+// placement from frame_padding) and prepare_model_output_into (tensor ->
+// frame).  Planes are Y (w x h) then U, V (w/2 x h/2).
+int mlvc_ref_yuv_to_tensor(const std::uint8_t* yuv, int w, int h, int mw, int mh, float pixel_range,
+                           std::uint16_t* out, int* rotated, char* err, std::size_t err_len)
+{
+    try {
+        const std::size_t ys = static_cast<std::size_t>(w) * h;
+        mlvc::Yuv420FrameView frame(w, h, {yuv, ys}, {yuv + ys, ys / 4}, {yuv + ys + ys / 4, ys / 4});
+        mlvc::FramePadding padding;
+        const mlvc::Tensor t = mlvc::prepare_model_input(frame, mw, mh, pixel_range, padding);
+        std::memcpy(out, t.raw_data(), t.byte_size());
+        *rotated = padding.rotated ? 1 : 0;
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, err_len, e.what());
+        return -1;
+    }
+}
+
+int mlvc_ref_tensor_to_yuv(const std::uint16_t* tensor, int mw, int mh, int w, int h, float pixel_range,
+                           std::uint8_t* yuv, char* err, std::size_t err_len)
+{
+    try {
+        const std::size_t ys = static_cast<std::size_t>(w) * h;
+        mlvc::Tensor t{"x_hat", {1, 3, mh, mw},
+                       std::vector<mlvc::Float16Storage>(tensor, tensor + static_cast<std::size_t>(3) * mw * mh)};
+        const mlvc::FramePadding padding = mlvc::frame_padding(w, h, mw, mh);
+        mlvc::MutableYuv420FrameView frame(w, h, {yuv, ys}, {yuv + ys, ys / 4}, {yuv + ys + ys / 4, ys / 4});
+        mlvc::prepare_model_output_into(t, frame, pixel_range, padding);
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, err_len, e.what());
+        return -1;
+    }
 }
 
 }  // extern "C"
