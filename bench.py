@@ -47,7 +47,7 @@ FLUSH_BYTES = 256 << 20  # > 126 MB L2
 def single_op(name):
     """Single-operator graphs at 544x960 (inputs larger than L2) for kernel
     tuning and ncu captures: dw3x3 (256 ch), conv1x1 (128->256 + LeakyReLU),
-    ffn (the block's feed-forward half)."""
+    ffn (the block's feed-forward half), dwconv (depthwise + 1x1 + residual)."""
     from mlvc_b200.graph import GraphBuilder, kaiming_normal, small_bias
     rng = np.random.default_rng(0)
     gb = GraphBuilder()
@@ -58,6 +58,17 @@ def single_op(name):
         gb.output(gb.conv(x, w, b, (1, 1), (1, 1), groups=256), "y")
         inputs = [rng.standard_normal((1, 256, 544, 960), dtype=np.float32).astype(np.float16)]
         desc = "single op: depthwise 3x3 s1 p1, 256 ch @544x960 (NCHW boundary conversion included)"
+    elif name == "op_dwconv":
+        x = gb.input("x", [1, 256, 1024, 316])
+        d = gb.conv(x, gb.weight("dw", kaiming_normal(rng, (256, 1, 3, 3), 1.0)), gb.weight("db", small_bias(rng, 256)),
+                    (1, 1), (1, 1), groups=256)
+        y = gb.conv(d, gb.weight("w", kaiming_normal(rng, (128, 256, 1, 1), 1.0)), gb.weight("b", small_bias(rng, 128)))
+        r = gb.input("r", [1, 128, 1024, 316])
+        gb.output(gb.add(y, r), "y")
+        inputs = [rng.standard_normal((1, 256, 1024, 316), dtype=np.float32).astype(np.float16),
+                  rng.standard_normal((1, 128, 1024, 316), dtype=np.float32).astype(np.float16)]
+        desc = ("single op: depthwise 3x3 256 -> 1x1 256->128 + residual @1024x316 (widest image the fused "
+                "kernel takes; NCHW boundary conversion included)")
     elif name == "op_ffn":
         x = gb.input("x", [1, 128, 544, 960])
         t = gb.conv(x, gb.weight("w1", kaiming_normal(rng, (512, 128, 1, 1))), gb.weight("b1", small_bias(rng, 512)))
@@ -380,7 +391,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn"], default="block_stack")
+    ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv"], default="block_stack")
     ap.add_argument("--cpu-frames", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -1018,7 +1018,7 @@ void Backend::plan()
             }
             const bool depthwise = G == IC && OC == IC && ICG == 1 && IC % 8 == 0 && epi == kEpiBias;
             if (depthwise && dw_fusion_ && N == 1 && KH == 3 && KW == 3 && SH == 1 && SW == 1 && PH == 1 && PW == 1 &&
-                IC % 64 == 0 && OW % 4 == 0 && i + 1 < nodes.size()) {
+                IC % 64 == 0 && IC <= 256 && OW % 4 == 0 && i + 1 < nodes.size()) {
                 // ---- fused depthwise 3x3 + the 1x1 conv that consumes it: the
                 // depthwise result is the GEMM's A operand in shared memory
                 const NodeDesc& n2 = nodes[i + 1];
@@ -1038,7 +1038,9 @@ void Backend::plan()
                 const int M = OH * OW, halo_px = 128 + 2 * OW + 2;
                 const int halo_boxes = (halo_px + 255) / 256, halo_box = (halo_px + halo_boxes - 1) / halo_boxes;
                 const int halo_stride = static_cast<int>(align_up(static_cast<size_t>(halo_boxes) * halo_box * 128, 1024));
-                const int fixed = 1024 + kDwHeaderBytes + 2 * 16384 + 2 * OC2 * 128 + OC2 / 64 * kTcStagePanelBytes;
+                // + the depthwise taps and bias ([10][C] FP16, one TMA box: C <= 256)
+                const int fixed = 1024 + kDwHeaderBytes + 2 * 16384 + 2 * OC2 * 128 + OC2 / 64 * kTcStagePanelBytes +
+                                  static_cast<int>(align_up(static_cast<size_t>(10) * IC * 2, 1024));
                 int h_stages = 0;
                 if (ok && halo_boxes <= 3)
                     h_stages = fixed + 2 * halo_stride <= max_smem_optin_ ? 2 : (fixed + halo_stride <= max_smem_optin_ ? 1 : 0);
@@ -1047,18 +1049,18 @@ void Backend::plan()
                     float alpha2 = 0.0f;
                     uint32_t out2 = 0, res2 = 0;
                     const size_t consumed2 = conv_epilogue(i + 1, epi2, alpha2, out2, res2);
-                    std::vector<uint16_t> dwp(static_cast<size_t>(9) * IC);
+                    std::vector<uint16_t> dwp(static_cast<size_t>(10) * IC, 0);  // taps, then the bias row
                     for (int c = 0; c < IC; ++c)
                         for (int k = 0; k < 9; ++k)
                             dwp[static_cast<size_t>(k) * IC + c] = w[static_cast<size_t>(c) * 9 + k];
+                    if (bias)
+                        std::copy(bias, bias + IC, dwp.begin() + static_cast<size_t>(9) * IC);
                     std::vector<uint16_t> b2p(OC2, 0);
                     if (b2_id)
                         std::copy(wdata(b2_id), wdata(b2_id) + OC2, b2p.begin());
                     const size_t dww_off = prep(dwp.data(), dwp.size() * 2);
-                    const size_t dwb_off = bias ? prep(bias_full.data(), bias_full.size() * 2) : 0;
                     const size_t w2_off = prep(wdata(w2_id), static_cast<size_t>(OC2) * IC * 2);
                     const size_t b2_off = prep(b2p.data(), b2p.size() * 2);
-                    const bool has_dw_bias = bias != nullptr;
                     const int m_tiles = (M + 127) / 128;
                     Step f;
                     f.reads = {x_id};
@@ -1106,6 +1108,17 @@ void Backend::plan()
                                             "cuTensorMapEncodeTiled(dwconv residual)");
                         else
                             p.map_res = p.map_out;
+                        {
+                            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(IC), 10};
+                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(IC) * 2};
+                            const cuuint32_t box[2] = {static_cast<cuuint32_t>(IC), 10};
+                            check(cuTensorMapEncodeTiled(&dwp_.map_dw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                                         reinterpret_cast<void*>(prepped_dev_.get() + dww_off), dims,
+                                                         strides, box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  "cuTensorMapEncodeTiled(dwconv taps)");
+                        }
                         p.map_a0 = p.map_a1 = dwp_.map_halo;
                         p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b2_off);
                         p.out = reinterpret_cast<mlvc_half*>(values_[out2].addr);
@@ -1120,8 +1133,6 @@ void Backend::plan()
                         p.alpha = alpha2;
                         p.a_stages = 2;
                         p.b_stages = 2;
-                        dwp_.dw_w = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + dww_off);
-                        dwp_.dw_b = has_dw_bias ? reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + dwb_off) : nullptr;
                         dwp_.width = OW;
                         dwp_.halo_px = halo_px;
                         dwp_.halo_box = halo_box;

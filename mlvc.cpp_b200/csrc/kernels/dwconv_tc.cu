@@ -40,6 +40,7 @@ struct DwShared {
     uint64_t w_full[2], w_empty[2];  // 1x1 weight panels
     uint64_t acc_full[2], acc_empty[2];
     uint64_t stg_ready, stg_full;    // output staging hand-over (see StageSync)
+    uint64_t dw_full;                // depthwise taps + bias landed
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -66,6 +67,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
     uint8_t* w_smem = a_smem + static_cast<size_t>(p.a_stages) * kDwPanelBytes;
     uint8_t* h_smem = w_smem + static_cast<size_t>(p.b_stages) * w_bytes;
     uint8_t* stage_smem = h_smem + static_cast<size_t>(dp.h_stages) * halo_stride;  // 1024-aligned
+    // depthwise taps [9][C] and bias [C], FP16, loaded once per CTA by TMA
+    const uint8_t* dw_smem = stage_smem + static_cast<size_t>(p.BN / 64) * kTcStagePanelBytes;
 
     if (threadIdx.x == 0) {
         if (p.trace)
@@ -82,12 +85,14 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
         }
         mbar_init(&sh->stg_ready, 1);
         mbar_init(&sh->stg_full, kEpilogueThreads);
+        mbar_init(&sh->dw_full, 1);
         mbar_init(&sh->drain, 1);
         sh->abort_flag = 0;
         fence_barrier_init();
     }
     if (warp == 0 && elect_one()) {
         tma_prefetch_desc(&dp.map_halo);
+        tma_prefetch_desc(&dp.map_dw);
         tma_prefetch_desc(&p.map_b);
         tma_prefetch_desc(&p.map_out);
         if (p.epilogue == kEpiResidual)
@@ -122,6 +127,10 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 return true;
             };
             // The weights do not depend on the previous kernel.
+            ArmedSlots dw_armed;
+            mbar_arrive_expect_tx(&sh->dw_full, static_cast<uint32_t>(10 * p.K * 2));
+            tma_load_2d(const_cast<uint8_t*>(dw_smem), &dp.map_dw, &sh->dw_full, 0, 0);
+            dw_armed.arm(0, 0);
             int w_issued = 0;
             if (first < tiles)
                 for (; w_issued < min(kpan, p.b_stages); ++w_issued)
@@ -155,6 +164,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
             if (sh->abort_flag) {
                 drain_armed(sh->h_full, h_armed, dp.h_stages);
                 drain_armed(sh->w_full, w_armed, p.b_stages);
+                drain_armed(&sh->dw_full, dw_armed, 1);
             }
         }
         __syncwarp();
@@ -232,9 +242,9 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
         const StageSync ss{&sh->stg_ready, &sh->stg_full};
         const int panels = p.BN / 64;
         const int W = dp.width;
+        bool ok = mbar_wait(&sh->dw_full, 0, &sh->abort_flag, kErrWaitEpilogue);
         int hs = 0, as = 0;
         uint32_t hph = 0, aph = 0, acc = 0, acc_phase = 0, it = 0;
-        bool ok = true;
         for (int t = first; ok && t < tiles; t += step, ++it) {
             TileCoord tc;
             tc.pixel0 = t * kBM;
@@ -255,17 +265,11 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 float acc4[4][8];
                 {
                     float b8[8];
-                    if (dp.dw_b) {
-                        const uint4 bv = __ldg(reinterpret_cast<const uint4*>(dp.dw_b + ch));
-                        const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+                    const uint4 bv = *reinterpret_cast<const uint4*>(dw_smem + (9 * p.K + ch) * 2);
+                    const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            unpack_h2(bw[k], b8[2 * k], b8[2 * k + 1]);
-                    } else {
-#pragma unroll
-                        for (int k = 0; k < 8; ++k)
-                            b8[k] = 0.0f;
-                    }
+                    for (int k = 0; k < 4; ++k)
+                        unpack_h2(bw[k], b8[2 * k], b8[2 * k + 1]);
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -276,7 +280,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 uint32_t wv[9][4];
 #pragma unroll
                 for (int tap = 0; tap < 9; ++tap) {
-                    const uint4 q = __ldg(reinterpret_cast<const uint4*>(dp.dw_w + tap * p.K + ch));
+                    const uint4 q = *reinterpret_cast<const uint4*>(dw_smem + (tap * p.K + ch) * 2);
                     wv[tap][0] = q.x;
                     wv[tap][1] = q.y;
                     wv[tap][2] = q.z;

@@ -132,8 +132,7 @@ struct DwConvTcParams {
     // b_stages = W ring slots.
     ConvTcParams c;
     CUtensorMap map_halo;    // x [M pixels, C] in {64, halo_box} boxes, no swizzle (128-byte pixel rows)
-    const mlvc_half* dw_w;   // [9][C], tap (ky * 3 + kx) major
-    const mlvc_half* dw_b;   // [C] or null
+    CUtensorMap map_dw;      // depthwise taps and bias [10][C] (rows 0..8: tap ky * 3 + kx, row 9: bias), one {C, 10} box
     int width;               // image width (multiple of 4)
     int halo_px;             // 128 + 2 * width + 2 pixels per 64-channel slice
     int halo_box;            // pixels per halo TMA box (<= 256)

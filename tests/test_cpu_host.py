@@ -171,6 +171,7 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
     (48, 64, 8, 8, False),      # channels not a multiple of 64
     (64, 96, 8, 8, False),      # output channels not a multiple of 64
     (64, 64, 4, 2000, False),   # halo rows beyond three TMA boxes
+    (320, 128, 8, 8, False),    # depthwise taps beyond one TMA box row (C > 256)
 ])
 def test_plan_depthwise_fusion_predicates(c, c_out, h, w, fused):
     gb = GraphBuilder()
