@@ -92,10 +92,12 @@ float half_bits_to_float(uint16_t h)
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Output / residual tile view of a tensor-core epilogue on an NHWC tensor:
-// 1x1 (w == 0): {channels, pixels} with {64, 128} boxes; k x k: {channels,
-// w, h} with {64, 128, 1} boxes; 128-byte swizzle.  Boxes are clipped (stores)
+// 1x1 (w == 0): {channels, pixels} with {64, 128} boxes; otherwise {channels,
+// w, h} with {64, box_w, box_h} boxes (k x k: one 128-pixel row segment,
+// fused depthwise: 16 x 8 pixels); 128-byte swizzle.  Boxes are clipped (stores)
 // or zero-filled (loads) at the tensor edges.
-void encode_tile_map(CUtensorMap* map, CUdeviceptr addr, int channels, int pixels, int w, int h, const char* what)
+void encode_tile_map(CUtensorMap* map, CUdeviceptr addr, int channels, int pixels, int w, int h, const char* what,
+                     int box_w = 128, int box_h = 1)
 {
     const cuuint32_t elem[3] = {1, 1, 1};
     const cuuint64_t c = static_cast<cuuint64_t>(channels);
@@ -110,7 +112,7 @@ void encode_tile_map(CUtensorMap* map, CUdeviceptr addr, int channels, int pixel
     } else {
         const cuuint64_t dims[3] = {c, static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h)};
         const cuuint64_t strides[2] = {c * 2, static_cast<cuuint64_t>(w) * c * 2};
-        const cuuint32_t box[3] = {64, 128, 1};
+        const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_w), static_cast<cuuint32_t>(box_h)};
         check(cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, reinterpret_cast<void*>(addr), dims,
                                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
@@ -1018,7 +1020,7 @@ void Backend::plan()
             }
             const bool depthwise = G == IC && OC == IC && ICG == 1 && IC % 8 == 0 && epi == kEpiBias;
             if (depthwise && dw_fusion_ && N == 1 && KH == 3 && KW == 3 && SH == 1 && SW == 1 && PH == 1 && PW == 1 &&
-                IC % 64 == 0 && IC <= 256 && OW % 4 == 0 && i + 1 < nodes.size()) {
+                IC % 64 == 0 && IC <= 256 && i + 1 < nodes.size()) {
                 // ---- fused depthwise 3x3 + the 1x1 conv that consumes it: the
                 // depthwise result is the GEMM's A operand in shared memory
                 const NodeDesc& n2 = nodes[i + 1];
@@ -1035,14 +1037,13 @@ void Backend::plan()
                     OC2 = ok ? static_cast<int>(w2v.shape[0]) : 0;
                     ok = ok && OC2 % 64 == 0 && OC2 <= 256;
                 }
-                const int M = OH * OW, halo_px = 128 + 2 * OW + 2;
-                const int halo_boxes = (halo_px + 255) / 256, halo_box = (halo_px + halo_boxes - 1) / halo_boxes;
-                const int halo_stride = static_cast<int>(align_up(static_cast<size_t>(halo_boxes) * halo_box * 128, 1024));
+                const int M = OH * OW, halo_stride = kDwHaloBytes;
+                const int tiles_x = (OW + kDwTileW - 1) / kDwTileW, tiles_y = (OH + kDwTileH - 1) / kDwTileH;
                 // + the depthwise taps and bias ([10][C] FP16, one TMA box: C <= 256)
                 const int fixed = 1024 + kDwHeaderBytes + 2 * 16384 + 2 * OC2 * 128 + OC2 / 64 * kTcStagePanelBytes +
                                   static_cast<int>(align_up(static_cast<size_t>(10) * IC * 2, 1024));
                 int h_stages = 0;
-                if (ok && halo_boxes <= 3)
+                if (ok)
                     h_stages = fixed + 2 * halo_stride <= max_smem_optin_ ? 2 : (fixed + halo_stride <= max_smem_optin_ ? 1 : 0);
                 if (h_stages) {
                     int epi2 = kEpiBias;
@@ -1061,7 +1062,7 @@ void Backend::plan()
                     const size_t dww_off = prep(dwp.data(), dwp.size() * 2);
                     const size_t w2_off = prep(wdata(w2_id), static_cast<size_t>(OC2) * IC * 2);
                     const size_t b2_off = prep(b2p.data(), b2p.size() * 2);
-                    const int m_tiles = (M + 127) / 128;
+                    const int m_tiles = tiles_x * tiles_y;
                     Step f;
                     f.reads = {x_id};
                     if (res2)
@@ -1081,12 +1082,15 @@ void Backend::plan()
                         ConvTcParams& p = dwp_.c;
                         const cuuint32_t elem1[2] = {1, 1};
                         {
-                            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(IC), static_cast<cuuint64_t>(M)};
-                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(IC) * 2};
-                            const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(halo_box)};
-                            check(cuTensorMapEncodeTiled(&dwp_.map_halo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                            const cuuint32_t elem3[3] = {1, 1, 1};
+                            const cuuint64_t dims[3] = {static_cast<cuuint64_t>(IC), static_cast<cuuint64_t>(OW),
+                                                        static_cast<cuuint64_t>(OH)};
+                            const cuuint64_t strides[2] = {static_cast<cuuint64_t>(IC) * 2,
+                                                           static_cast<cuuint64_t>(OW) * IC * 2};
+                            const cuuint32_t box[3] = {64, kDwTileW + 2, kDwTileH + 2};
+                            check(cuTensorMapEncodeTiled(&dwp_.map_halo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                                                          reinterpret_cast<void*>(values_[x_id].addr), dims, strides, box,
-                                                         elem1, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                                         elem3, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
                                   "cuTensorMapEncodeTiled(dwconv halo)");
@@ -1102,10 +1106,11 @@ void Backend::plan()
                                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
                                   "cuTensorMapEncodeTiled(dwconv W)");
                         }
-                        encode_tile_map(&p.map_out, values_[out2].addr, OC2, M, 0, 0, "cuTensorMapEncodeTiled(dwconv out)");
+                        encode_tile_map(&p.map_out, values_[out2].addr, OC2, 0, OW, OH, "cuTensorMapEncodeTiled(dwconv out)",
+                                        kDwTileW, kDwTileH);
                         if (res2)
-                            encode_tile_map(&p.map_res, values_[res2].addr, OC2, M, 0, 0,
-                                            "cuTensorMapEncodeTiled(dwconv residual)");
+                            encode_tile_map(&p.map_res, values_[res2].addr, OC2, 0, OW, OH,
+                                            "cuTensorMapEncodeTiled(dwconv residual)", kDwTileW, kDwTileH);
                         else
                             p.map_res = p.map_out;
                         {
@@ -1134,9 +1139,8 @@ void Backend::plan()
                         p.a_stages = 2;
                         p.b_stages = 2;
                         dwp_.width = OW;
-                        dwp_.halo_px = halo_px;
-                        dwp_.halo_box = halo_box;
-                        dwp_.halo_boxes = halo_boxes;
+                        dwp_.height = OH;
+                        dwp_.tiles_x = tiles_x;
                         dwp_.h_stages = h_stages;
                         st.set(dwp_);
                     };

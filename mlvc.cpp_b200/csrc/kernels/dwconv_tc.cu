@@ -8,13 +8,13 @@
 // writing the C-channel tensor to memory and a GEMM reading it back
 // (backends/driver_cubin/src/execution_plan.cpp:438-457, then the pointwise
 // path of :134-269 with the epilogue fusion of fusion_registry.cpp:711-800).
-// Here the depthwise result never leaves the SM: per 128-pixel tile (raster
-// order) and per 64-channel slice,
+// Here the depthwise result never leaves the SM: per 16 x 8-pixel tile
+// (128 pixels, the MMA's M; row r of the tile = pixel (r % 16, r / 16)) and
+// per 64-channel slice,
 //
-//   producer   TMA loads the slice's halo: the 128 + 2 W + 2 consecutive pixels
-//              [p0 - W - 1, p0 + 128 + W] (rows above and below included; the
+//   producer   TMA loads the slice's 18 x 10-pixel halo as one 3-D box (the
 //              TMA zero fill outside the image is the padding of the top and
-//              bottom rows)
+//              bottom rows; columns outside the image are skipped below)
 //   CUDA cores 256 threads compute the depthwise conv of the 128 pixels x 64
 //              channels (8 channels x 4 horizontally adjacent pixels each,
 //              every input column loaded once) and write it, rounded to FP16,
@@ -61,8 +61,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
 
     const int kpan = p.K / 64;  // 64-channel slices per tile
     const uint32_t w_bytes = static_cast<uint32_t>(p.BN) * 128u;
-    const uint32_t box_bytes = static_cast<uint32_t>(dp.halo_box) * 128u;
-    const uint32_t halo_stride = (static_cast<uint32_t>(dp.halo_boxes) * box_bytes + 1023u) & ~1023u;
+    const uint32_t halo_stride = kDwHaloBytes;
     uint8_t* a_smem = base + kDwHeaderBytes;
     uint8_t* w_smem = a_smem + static_cast<size_t>(p.a_stages) * kDwPanelBytes;
     uint8_t* h_smem = w_smem + static_cast<size_t>(p.b_stages) * w_bytes;
@@ -140,16 +139,15 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
             int local = 0;
             bool ok = true;
             for (int t = first; ok && t < tiles && !sh->abort_flag; t += step, ++local) {
-                const int hbase = t * kBM - dp.width - 1;  // first halo pixel (may be negative: zero fill)
+                const int hx = (t % dp.tiles_x) * kDwTileW - 1, hy = (t / dp.tiles_x) * kDwTileH - 1;  // may be -1
                 for (int kp = 0; kp < kpan; ++kp) {
                     if (!mbar_wait(&sh->h_empty[hs], hph ^ 1u, &sh->abort_flag, kErrWaitProducer)) {
                         ok = false;
                         break;
                     }
                     uint8_t* dst = h_smem + static_cast<size_t>(hs) * halo_stride;
-                    mbar_arrive_expect_tx(&sh->h_full[hs], static_cast<uint32_t>(dp.halo_boxes) * box_bytes);
-                    for (int b = 0; b < dp.halo_boxes; ++b)
-                        tma_load_2d(dst + b * box_bytes, &dp.map_halo, &sh->h_full[hs], kp * 64, hbase + b * dp.halo_box);
+                    mbar_arrive_expect_tx(&sh->h_full[hs], static_cast<uint32_t>(kDwHaloPx) * 128u);
+                    tma_load_3d(dst, &dp.map_halo, &sh->h_full[hs], kp * 64, hx, hy);
                     h_armed.arm(hs, hph);
                     if (++hs == dp.h_stages) {
                         hs = 0;
@@ -247,13 +245,14 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
         uint32_t hph = 0, aph = 0, acc = 0, acc_phase = 0, it = 0;
         for (int t = first; ok && t < tiles; t += step, ++it) {
             TileCoord tc;
-            tc.pixel0 = t * kBM;
-            tc.ox0 = tc.oy = 0;
+            tc.pixel0 = 0;
+            tc.ox0 = (t % dp.tiles_x) * kDwTileW;
+            tc.oy = (t / dp.tiles_x) * kDwTileH;
             if (leader)  // residual tile into the staging buffer while the depthwise runs
-                stage_prepare(p, stage_smem, panels, 0, tc, false, p.epilogue == kEpiResidual, ss.ready);
-            const int P0 = t * kBM + 4 * pg;   // first of the thread's 4 pixels (same image row: W % 4 == 0)
-            const int x0 = P0 % W;
-            const int h0 = 4 * pg + W + 1;     // halo row of pixel P0
+                stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
+            const int ty = pg >> 2, tx = (pg & 3) * 4;  // the thread's 4 pixels: tile row ty, columns tx .. tx + 3
+            const int x0 = tc.ox0 + tx;
+            const int h0 = (ty + 1) * (kDwTileW + 2) + tx + 1;  // halo pixel of the first one
             for (int kp = 0; kp < kpan; ++kp) {
                 if (!mbar_wait(&sh->h_full[hs], hph, &sh->abort_flag, kErrWaitEpilogue) ||
                     !mbar_wait(&sh->a_empty[as], aph ^ 1u, &sh->abort_flag, kErrWaitEpilogue)) {
@@ -297,7 +296,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
 #pragma unroll
                     for (int ky = 0; ky < 3; ++ky) {
                         const uint4 v =
-                            *reinterpret_cast<const uint4*>(halo + static_cast<size_t>(h0 + (ky - 1) * W + cc - 1) * 128);
+                            *reinterpret_cast<const uint4*>(halo + static_cast<size_t>(h0 + (ky - 1) * (kDwTileW + 2) + cc - 1) * 128);
                         xv[ky][0] = v.x;
                         xv[ky][1] = v.y;
                         xv[ky][2] = v.z;
@@ -344,7 +343,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
             if (!ok)
                 break;
             if (!epilogue_tile(p, sh->bias, sh->tmem_base + acc * p.BN, &sh->acc_full[acc], acc_phase, &sh->acc_empty[acc],
-                               ss, it, stage_smem, nullptr, panels, 0, tc, false, quadrant, group, lane, leader,
+                               ss, it, stage_smem, nullptr, panels, 0, tc, true, quadrant, group, lane, leader,
                                &sh->abort_flag))
                 break;
             if (leader && it == 0)

@@ -121,9 +121,12 @@ struct FfnTcParams {
 // Fused depthwise 3x3 (stride 1, pad 1) + 1x1 conv (mlvc_dwconv_tc):
 //     d   = fp16(dw3x3(x) + b_dw)               CUDA cores, FP32 FMA from the bias
 //     out = epilogue(fp16(d W^T + b))           tcgen05; bias / LeakyReLU / + residual
-// The depthwise result of each 128-pixel tile is written straight into the
+// The depthwise result of each 16 x 8-pixel tile is written straight into the
 // GEMM's A operand in shared memory, 64 channels at a time.
 constexpr int kDwHeaderBytes = 2048;
+constexpr int kDwTileW = 16, kDwTileH = 8;                        // output tile (pixels)
+constexpr int kDwHaloPx = (kDwTileW + 2) * (kDwTileH + 2);        // 180 halo pixels per slice
+constexpr int kDwHaloBytes = (kDwHaloPx * 128 + 1023) / 1024 * 1024;  // one 64-channel halo slice in smem
 
 struct DwConvTcParams {
     // map_b = W [C_out rows, C] (C_out x 64 boxes, 128-byte swizzle);
@@ -131,12 +134,12 @@ struct DwConvTcParams {
     // output; K = C, BN = N = n_valid = C_out, a_stages = A panels in flight,
     // b_stages = W ring slots.
     ConvTcParams c;
-    CUtensorMap map_halo;    // x [M pixels, C] in {64, halo_box} boxes, no swizzle (128-byte pixel rows)
+    // Tiles are kDwTileW x kDwTileH pixels (128 = one MMA tile); map_out /
+    // map_res use {64, kDwTileW, kDwTileH} boxes over {C_out, W, H}.
+    CUtensorMap map_halo;    // x {C, W, H} in {64, kDwTileW + 2, kDwTileH + 2} boxes, no swizzle (128-byte pixel rows)
     CUtensorMap map_dw;      // depthwise taps and bias [10][C] (rows 0..8: tap ky * 3 + kx, row 9: bias), one {C, 10} box
-    int width;               // image width (multiple of 4)
-    int halo_px;             // 128 + 2 * width + 2 pixels per 64-channel slice
-    int halo_box;            // pixels per halo TMA box (<= 256)
-    int halo_boxes;          // boxes per slice
+    int width, height;       // image
+    int tiles_x;             // tiles per image row
     int h_stages;            // halo slices in flight (1 or 2)
 };
 

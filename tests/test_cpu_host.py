@@ -167,10 +167,10 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
 
 @pytest.mark.parametrize("c,c_out,h,w,fused", [
     (256, 128, 92, 160, True), (64, 64, 13, 20, True), (128, 128, 9, 300, True), (64, 256, 8, 8, True),
-    (64, 64, 13, 17, False),    # width not a multiple of 4
+    (64, 64, 13, 17, True),     # ragged 16 x 8 tiles
+    (64, 64, 4, 2000, True),    # wide image (2-D tiles: any width)
     (48, 64, 8, 8, False),      # channels not a multiple of 64
     (64, 96, 8, 8, False),      # output channels not a multiple of 64
-    (64, 64, 4, 2000, False),   # halo rows beyond three TMA boxes
     (320, 128, 8, 8, False),    # depthwise taps beyond one TMA box row (C > 256)
 ])
 def test_plan_depthwise_fusion_predicates(c, c_out, h, w, fused):

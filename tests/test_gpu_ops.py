@@ -131,9 +131,9 @@ def test_ffn_fused(c, hidden, c_out, h, w, epilogue, monkeypatch):
 
 
 DW_CASES = [  # (C, C_out, H, W, epilogue of the 1x1 conv)
-    (256, 128, 92, 160, "residual"),  # block-stack shape: two halo boxes, two halo stages
-    (64, 64, 13, 20, None),           # one halo box, ragged last tile
-    (128, 128, 9, 300, "leaky"),      # three halo boxes, one halo stage
+    (256, 128, 92, 160, "residual"),  # block-stack shape (bottom tile row half inside the image)
+    (64, 64, 13, 21, None),           # ragged tiles on both edges, odd width
+    (128, 128, 9, 300, "leaky"),      # wide image
     (64, 64, 160, 160, "residual"),   # 200 tiles: two tiles per CTA
     (64, 256, 8, 8, None),            # 256 output columns (four staging panels)
 ]
