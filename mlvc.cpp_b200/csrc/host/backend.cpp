@@ -354,6 +354,8 @@ void Backend::plan()
         ffn_fusion_ = !(env && env[0] == '0');
         env = std::getenv("MLVC_B200_DW_FUSION");
         dw_fusion_ = !(env && env[0] == '0');
+        env = std::getenv("MLVC_B200_TAIL_FUSION");
+        tail_fusion_ = !(env && env[0] == '0');
     }
     const size_t nt = graph_.tensors.size();
     values_.assign(nt, Value{});
@@ -1214,6 +1216,107 @@ void Backend::plan()
             steps_.push_back(std::move(s));
             i += consumed;
             continue;
+        }
+
+        // ---- recurrent-feature update: Slice x3, Sigmoid x2, Mul, Sub, Mul, Add,
+        // Mul, Mul (+ a later Concat of the last Mul and the Add on channels),
+        // the reference's fusion patterns of fusion_registry.cpp:405-709
+        if (n.op == Op::kSlice && tail_fusion_ && i + 10 < nodes.size()) {
+            static constexpr Op kPattern[11] = {Op::kSlice, Op::kSlice, Op::kSlice, Op::kSigmoid, Op::kSigmoid,
+                                                Op::kMul,   Op::kSub,   Op::kMul,   Op::kAdd,     Op::kMul,
+                                                Op::kMul};
+            bool ok = true;
+            for (int k = 0; ok && k < 11; ++k)
+                ok = nodes[i + k].op == kPattern[k] && !absorbed[i + k];
+            const uint32_t src_id = n.inputs[0];
+            auto out = [&](int k) { return nodes[i + k].output; };
+            auto in = [&](int k) -> const std::vector<uint32_t>& { return nodes[i + k].inputs; };
+            const Value& sv = values_[src_id];
+            int C = 0;
+            if (ok && sv.nhwc && sv.dtype == DType::kFp16 && sv.shape.size() == 4 && sv.shape[1] % 3 == 0) {
+                C = static_cast<int>(sv.shape[1] / 3);
+                ok = C % 8 == 0 && in(1)[0] == src_id && in(2)[0] == src_id && is_channel_slice(nodes[i], src_id, 0, C) &&
+                     is_channel_slice(nodes[i + 1], src_id, C, 2 * C) &&
+                     is_channel_slice(nodes[i + 2], src_id, 2 * C, 3 * C);
+            } else {
+                ok = false;
+            }
+            uint32_t hist_id = 0, one_id = 0, scale_id = 0;
+            if (ok) {
+                ok = in(3) == std::vector<uint32_t>{out(1)} && in(4) == std::vector<uint32_t>{out(2)} &&
+                     in(5).size() == 2 && in(5)[0] == out(3) && in(6).size() == 2 && in(6)[1] == out(3) &&
+                     in(7) == std::vector<uint32_t>{out(6), out(0)} && in(8) == std::vector<uint32_t>{out(5), out(7)} &&
+                     in(9) == std::vector<uint32_t>{out(4), out(8)} && in(10).size() == 2 && in(10)[0] == out(9);
+            }
+            if (ok) {
+                hist_id = in(5)[1];
+                one_id = in(6)[0];
+                scale_id = in(10)[1];
+                const auto& fs = values_[out(0)].shape;
+                const Value &hv = values_[hist_id], &ov = values_[one_id], &scv = values_[scale_id];
+                ok = hv.nhwc && hv.dtype == DType::kFp16 && hv.shape == fs && ov.kind == Value::kWeight &&
+                     ov.dtype == DType::kFp16 && element_count(ov.shape) == 1 && scv.kind == Value::kWeight &&
+                     scv.dtype == DType::kFp16 && scv.shape == std::vector<int64_t>{1, C, 1, 1};
+                for (int k = 3; ok && k <= 10; ++k)
+                    ok = values_[out(k)].nhwc && values_[out(k)].shape == fs && values_[out(k)].dtype == DType::kFp16;
+                // chain-internal values: read only inside the chain
+                const int internal[] = {0, 1, 2, 4, 5, 6, 7, 9};
+                for (int k : internal)
+                    ok = ok && only_consumer(out(k));
+                ok = ok && values_[out(3)].consumers == 2 && !values_[out(3)].graph_output;
+            }
+            if (ok) {
+                const uint32_t scaled_id = out(10), blended_id = out(8);
+                // a later Concat(scaled, blended) on channels is produced here too
+                size_t concat_j = 0;
+                for (size_t j = i + 11; j < nodes.size() && !concat_j; ++j)
+                    if (nodes[j].op == Op::kConcat && !absorbed[j] &&
+                        nodes[j].inputs == std::vector<uint32_t>{scaled_id, blended_id} &&
+                        (nodes[j].axis == 1 || nodes[j].axis == -3) && values_[nodes[j].output].nhwc)
+                        concat_j = j;
+                const uint32_t concat_id = concat_j ? nodes[concat_j].output : 0;
+                // scaled / blended on their own when anything but the concat (and, for
+                // blended, the gated Mul of the chain) reads them
+                const int in_chain_blended = 1 + (concat_j ? 1 : 0);
+                const bool keep_scaled = !concat_j || values_[scaled_id].consumers > 1 || values_[scaled_id].graph_output;
+                const bool keep_blended =
+                    values_[blended_id].consumers > in_chain_blended || values_[blended_id].graph_output;
+                if (concat_j)
+                    absorbed[concat_j] = true;
+                const float one_value = half_bits_to_float(wdata(one_id)[0]);
+                const long long pixels = element_count(values_[out(0)].shape) / C;
+                Step s;
+                s.kernel = "mlvc_feature_update_f16";
+                s.info.kernel = s.kernel;
+                s.info.nodes = std::to_string(i) + "-" + std::to_string(i + 10) +
+                               (concat_j ? "+" + std::to_string(concat_j) : std::string());
+                s.reads = {src_id, hist_id};
+                if (concat_id)
+                    s.writes.push_back(concat_id);
+                if (keep_scaled)
+                    s.writes.push_back(scaled_id);
+                if (keep_blended)
+                    s.writes.push_back(blended_id);
+                s.info.bytes = 2.0 * pixels * C * (3 + 1 + (concat_id ? 2 : 0) + (keep_scaled ? 1 : 0) + (keep_blended ? 1 : 0));
+                s.grid = blocks_for(pixels * (C / 8), 256, sm_count_);
+                s.block = 256;
+                s.build = [=, this](Step& st) {
+                    FeatureUpdateParams p{};
+                    p.src = reinterpret_cast<const mlvc_half*>(values_[src_id].addr);
+                    p.history = reinterpret_cast<const mlvc_half*>(values_[hist_id].addr);
+                    p.scale = reinterpret_cast<const mlvc_half*>(values_[scale_id].addr);
+                    p.concat = concat_id ? reinterpret_cast<mlvc_half*>(values_[concat_id].addr) : nullptr;
+                    p.scaled = keep_scaled ? reinterpret_cast<mlvc_half*>(values_[scaled_id].addr) : nullptr;
+                    p.blended = keep_blended ? reinterpret_cast<mlvc_half*>(values_[blended_id].addr) : nullptr;
+                    p.pixels = pixels;
+                    p.c = C;
+                    p.one = one_value;
+                    st.set(p);
+                };
+                steps_.push_back(std::move(s));
+                i += 11;
+                continue;
+            }
         }
 
         // ---- stand-alone ReGLU: Slice, Slice, Clip, Mul on one tensor

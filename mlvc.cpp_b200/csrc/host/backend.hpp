@@ -165,6 +165,9 @@ private:
     // Depthwise 3x3 + following 1x1 conv in one kernel; MLVC_B200_DW_FUSION=0
     // plans them as separate steps (same results, for comparison).
     bool dw_fusion_ = true;
+    // Recurrent-feature update chain in one kernel; MLVC_B200_TAIL_FUSION=0
+    // runs its operators one by one (same results, for comparison).
+    bool tail_fusion_ = true;
     bool keep_all_values_ = false;
 };
 

@@ -294,6 +294,72 @@ __device__ __forceinline__ void boundary_scalar(const BoundaryParams& p, mlvc_ha
     }
 }
 
+// -------------------------------------------------- recurrent feature update
+// The eleven operators of the recurrent-feature update (three channel slices,
+// two sigmoids, six binary operators) plus the concat of their two results,
+// one thread per 8 channels of a pixel.  Every operator rounds to FP16 as the
+// stand-alone kernels do (same unary_op / binary_op), so the result is
+// bit-identical to running them one by one (reference fused form:
+// backends/driver_cubin/kernels/recurrent_feature.cu:5-107).
+extern "C" __global__ void __launch_bounds__(256) mlvc_feature_update_f16(const __grid_constant__ FeatureUpdateParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int cv = p.c / 8;
+    const long long total = p.pixels * cv;
+    auto rnd = [](float v) { return __half2float(__float2half_rn(v)); };
+    const float one = rnd(p.one);
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long px = i / cv;
+        const int c8 = static_cast<int>(i - px * cv) * 8;
+        const mlvc_half* s = p.src + px * 3 * p.c + c8;
+        const uint4 av = *reinterpret_cast<const uint4*>(s);
+        const uint4 bv = *reinterpret_cast<const uint4*>(s + p.c);
+        const uint4 cv4 = *reinterpret_cast<const uint4*>(s + 2 * p.c);
+        const uint4 hv = *reinterpret_cast<const uint4*>(p.history + px * p.c + c8);
+        const uint4 sv = *reinterpret_cast<const uint4*>(p.scale + c8);
+        const uint32_t* aw = reinterpret_cast<const uint32_t*>(&av);
+        const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
+        const uint32_t* cw = reinterpret_cast<const uint32_t*>(&cv4);
+        const uint32_t* hw = reinterpret_cast<const uint32_t*>(&hv);
+        const uint32_t* sw = reinterpret_cast<const uint32_t*>(&sv);
+        uint4 scaled_v, blended_v;
+        uint32_t* so = reinterpret_cast<uint32_t*>(&scaled_v);
+        uint32_t* bo = reinterpret_cast<uint32_t*>(&blended_v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float a[2], b[2], c[2], h[2], sc[2], sv2[2], bl[2];
+            unpack_h2(aw[k], a[0], a[1]);
+            unpack_h2(bw[k], b[0], b[1]);
+            unpack_h2(cw[k], c[0], c[1]);
+            unpack_h2(hw[k], h[0], h[1]);
+            unpack_h2(sw[k], sv2[0], sv2[1]);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float sig_b = rnd(unary_op(b[j], 2, 0.0f, 0.0f, 0.0f));
+                const float sig_c = rnd(unary_op(c[j], 2, 0.0f, 0.0f, 0.0f));
+                const float weighted_b = rnd(binary_op(sig_b, h[j], 1));
+                const float inverse_gate = rnd(binary_op(one, sig_b, 2));
+                const float weighted_a = rnd(binary_op(inverse_gate, a[j], 1));
+                bl[j] = rnd(binary_op(weighted_b, weighted_a, 0));
+                const float gated = rnd(binary_op(sig_c, bl[j], 1));
+                sc[j] = binary_op(gated, sv2[j], 1);
+            }
+            so[k] = pack_h2(sc[0], sc[1]);
+            bo[k] = pack_h2(bl[0], bl[1]);
+        }
+        if (p.concat) {
+            *reinterpret_cast<uint4*>(p.concat + px * 2 * p.c + c8) = scaled_v;
+            *reinterpret_cast<uint4*>(p.concat + px * 2 * p.c + p.c + c8) = blended_v;
+        }
+        if (p.scaled)
+            *reinterpret_cast<uint4*>(p.scaled + px * p.c + c8) = scaled_v;
+        if (p.blended)
+            *reinterpret_cast<uint4*>(p.blended + px * p.c + c8) = blended_v;
+    }
+}
+
 // ------------------------------------------------------------ codec I/O
 // YUV420 frame -> model input tensor (reference: prepare_model_input,
 // core/src/yuv.cpp:339-400).  One thread per tensor element; the 256-entry

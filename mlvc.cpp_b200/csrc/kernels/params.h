@@ -218,6 +218,25 @@ struct RegluParams {
     float lo, hi;
 };
 
+// Fused recurrent-feature update (mlvc_feature_update_f16), per element with
+// the graph's FP16 rounding after every operator:
+//   sb = sigmoid(b), sc = sigmoid(c), blended = sb * history + (one - sb) * a,
+//   scaled = (sc * blended) * scale[channel]
+// where a, b, c are the three channel thirds of src.  Writes the channel
+// concat [scaled, blended] and, where the graph reads them elsewhere, scaled
+// and blended on their own (each pointer may be null).
+struct FeatureUpdateParams {
+    const mlvc_half* src;      // NHWC [P, 3C]
+    const mlvc_half* history;  // NHWC [P, C]
+    const mlvc_half* scale;    // [C]
+    mlvc_half* concat;         // NHWC [P, 2C]
+    mlvc_half* scaled;         // NHWC [P, C]
+    mlvc_half* blended;        // NHWC [P, C]
+    long long pixels;
+    int c;                     // channels (multiple of 8)
+    float one;                 // the scalar the gate is subtracted from (1 in exported graphs)
+};
+
 // Codec I/O between a YUV420 frame (planar Y, U, V bytes, width x height,
 // both even) and the model's [1, 3, model_height, model_width] FP16 NCHW
 // tensor, with the reference's conventions (core/src/yuv.cpp:324-525): the

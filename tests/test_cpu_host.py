@@ -264,3 +264,21 @@ def test_replica_throughput_gloo_two_ranks():
     for _, value, ms_max in res:
         assert ms_max == 20.0  # max over ranks
         assert value == pytest.approx(2 * 50 / 0.020)
+
+
+@pytest.mark.parametrize("decoder", [False, True])
+def test_plan_feature_update_fusion(decoder, monkeypatch):
+    """The recurrent-feature update (3 slices, 2 sigmoids, 6 binary operators,
+    concat) becomes one step, as in the reference's matchers
+    (fusion_registry.cpp:405-709); in the decoder form the separately consumed
+    halves are materialised as well."""
+    from feature_graphs import feature_update_graph
+    gb, _ = feature_update_graph(16, 6, 10, decoder)
+    k = _kernels(plan(*gb.finish()))
+    assert "mlvc_feature_update_f16" in k, k
+    # no sigmoid or binary operator left (the decoder graph's own LeakyReLU stays)
+    assert k.count("mlvc_unary_f16") == (1 if decoder else 0) and "mlvc_binary_same_f16" not in k, k
+    monkeypatch.setenv("MLVC_B200_TAIL_FUSION", "0")
+    split = _kernels(plan(*gb.finish()))
+    assert "mlvc_feature_update_f16" not in split
+    assert split.count("mlvc_unary_f16") == (3 if decoder else 2), split

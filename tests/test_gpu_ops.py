@@ -413,3 +413,23 @@ def test_rejects_bad_input_shape():
     be.load_memory(graph, weights)
     with pytest.raises(RuntimeError, match="shape"):
         be.run([np.zeros((1, 8, 4, 5), np.float16)])
+
+
+@pytest.mark.parametrize("c,h,w,decoder", [(64, 23, 40, False), (128, 46, 80, True), (16, 7, 9, False)])
+def test_feature_update_fused(c, h, w, decoder, monkeypatch):
+    """Recurrent-feature update as one kernel (reference
+    recurrent_feature.cu:5-107): parity with the oracle (sigmoid within its
+    tolerance), and bit-identical to the same graph run operator by operator."""
+    from feature_graphs import feature_update_graph
+    gb, inputs = feature_update_graph(c, h, w, decoder)
+    got, want, be = run_both(gb, inputs)
+    for g, wnt in zip(got, want):
+        compare(g, wnt)
+    assert "mlvc_feature_update_f16" in {s["kernel"] for s in be.steps()}
+    graph, weights = gb.finish()
+    monkeypatch.setenv("MLVC_B200_TAIL_FUSION", "0")
+    split = Backend(0)
+    split.load_memory(graph, weights)
+    assert "mlvc_feature_update_f16" not in {s["kernel"] for s in split.steps()}
+    for g, s in zip(got, split.run(inputs)):
+        bits_equal(s, g)
