@@ -1218,6 +1218,145 @@ void Backend::plan()
             continue;
         }
 
+        // ---- latent quantisation tails (reference matchers:
+        // fusion_registry.cpp:14-225 for y0, :226-404 for y1)
+        if (tail_fusion_ && (n.op == Op::kSlice || n.op == Op::kSub)) {
+            const bool y0 = n.op == Op::kSlice;
+            static constexpr Op kY0[19] = {Op::kSlice, Op::kSlice, Op::kClip,   Op::kReciprocal, Op::kMul,
+                                           Op::kSub,   Op::kMul,   Op::kSlice,  Op::kSlice,      Op::kAdd,
+                                           Op::kRound, Op::kSlice, Op::kSlice,  Op::kAdd,        Op::kMul,
+                                           Op::kAdd,   Op::kMul,   Op::kConcat, Op::kConcat};
+            static constexpr Op kY1[15] = {Op::kSub, Op::kMul,   Op::kSlice, Op::kSlice, Op::kAdd,
+                                           Op::kRound, Op::kSlice, Op::kSlice, Op::kAdd,   Op::kMul,
+                                           Op::kAdd, Op::kMul,   Op::kConcat, Op::kAdd,  Op::kMul};
+            const Op* pat = y0 ? kY0 : kY1;
+            const size_t len = y0 ? 19 : 15;
+            bool ok = i + len <= nodes.size();
+            for (size_t k = 0; ok && k < len; ++k)
+                ok = nodes[i + k].op == pat[k] && !absorbed[i + k];
+            auto out = [&](size_t k) { return nodes[i + k].output; };
+            auto in = [&](size_t k) -> const std::vector<uint32_t>& { return nodes[i + k].inputs; };
+            auto vec = [](std::initializer_list<uint32_t> l) { return std::vector<uint32_t>(l); };
+            auto rt = [&](uint32_t id) {  // runtime NHWC FP16 rank-4 value
+                const Value& v = values_[id];
+                return v.present && v.nhwc && v.dtype == DType::kFp16 && v.shape.size() == 4;
+            };
+            auto cons = [&](uint32_t id, int c) { return values_[id].consumers == c && !values_[id].graph_output; };
+            // chain offsets of: scaled, y_raw, prior slices, updates (y0 numbering minus 5 for y1)
+            const size_t d = y0 ? 0 : 5;
+            uint32_t prior_id = 0, latent_id = 0, norm_id = 0, qs_id = 0, us0_id = 0, us1_id = 0, c2_id = 0, cl_id = 0;
+            int Q = 0;
+            if (ok) {
+                const uint32_t scaled = out(6 - d), y_raw = out(10 - d);
+                ok = in(7 - d).size() >= 1 && in(7 - d)[0] == scaled && in(8 - d).size() >= 1 && in(8 - d)[0] == scaled &&
+                     in(9 - d) == vec({out(7 - d), out(8 - d)}) && in(10 - d) == vec({out(9 - d)}) &&
+                     in(13 - d) == vec({y_raw, out(11 - d)}) && in(14 - d).size() == 2 && in(14 - d)[0] == out(13 - d) &&
+                     in(15 - d) == vec({y_raw, out(12 - d)}) && in(16 - d).size() == 2 && in(16 - d)[0] == out(15 - d) &&
+                     in(17 - d) == vec({out(14 - d), out(16 - d)}) && rt(y_raw);
+                if (ok) {
+                    Q = static_cast<int>(values_[y_raw].shape[1]);
+                    qs_id = in(6 - d)[1];
+                    us0_id = in(14 - d)[1];
+                    us1_id = in(16 - d)[1];
+                    ok = Q % 8 == 0 && in(6 - d).size() == 2 && in(6 - d)[0] == out(5 - d) && rt(qs_id) && rt(us0_id) &&
+                         rt(us1_id) && cons(out(5 - d), 1) && cons(scaled, 2) && cons(out(7 - d), 1) &&
+                         cons(out(8 - d), 1) && cons(out(9 - d), 1) && values_[y_raw].consumers == 2 &&
+                         cons(out(11 - d), 1) && cons(out(12 - d), 1) && cons(out(13 - d), 1) && cons(out(14 - d), 1) &&
+                         cons(out(15 - d), 1) && cons(out(16 - d), 1) &&
+                         (nodes[i + 17 - d].axis == 1 || nodes[i + 17 - d].axis == -3);
+                }
+            }
+            if (ok && y0) {
+                prior_id = n.inputs[0];
+                latent_id = in(4).size() == 2 ? in(4)[0] : 0;
+                ok = in(1)[0] == prior_id && rt(prior_id) && values_[prior_id].shape[1] == 4 * Q &&
+                     is_channel_slice(nodes[i], prior_id, 0, 2 * Q) && is_channel_slice(nodes[i + 1], prior_id, 2 * Q, 4 * Q) &&
+                     in(2).size() >= 2 && in(2)[0] == out(0) && in(3) == vec({out(2)}) && in(4).size() == 2 &&
+                     in(4)[1] == out(3) && rt(latent_id) && in(5) == vec({out(4), out(1)}) &&
+                     in(11)[0] == out(1) && in(12)[0] == out(1) && is_channel_slice(nodes[i + 7], out(6), 0, Q) &&
+                     is_channel_slice(nodes[i + 8], out(6), Q, 2 * Q) && is_channel_slice(nodes[i + 11], out(1), 0, Q) &&
+                     is_channel_slice(nodes[i + 12], out(1), Q, 2 * Q) && in(18) == vec({out(17), prior_id}) &&
+                     (nodes[i + 18].axis == 1 || nodes[i + 18].axis == -3) && cons(out(0), 1) && cons(out(1), 3) &&
+                     cons(out(3), 1) && values_[prior_id].consumers == 3 && rt(out(18)) &&
+                     (in(2).size() < 3 || in(2)[2] == 0);
+            } else if (ok) {
+                norm_id = n.inputs[0];
+                prior_id = n.inputs.size() == 2 ? n.inputs[1] : 0;
+                c2_id = in(13).size() == 2 ? in(13)[0] : 0;
+                cl_id = in(14).size() == 2 ? in(14)[1] : 0;
+                ok = rt(norm_id) && rt(prior_id) && rt(c2_id) && rt(cl_id) && in(13).size() == 2 && in(13)[1] == out(12) &&
+                     in(14).size() == 2 && in(14)[0] == out(13) && in(6)[0] == prior_id && in(7)[0] == prior_id &&
+                     is_channel_slice(nodes[i + 2], out(1), 0, Q) && is_channel_slice(nodes[i + 3], out(1), Q, 2 * Q) &&
+                     is_channel_slice(nodes[i + 6], prior_id, 0, Q) && is_channel_slice(nodes[i + 7], prior_id, Q, 2 * Q) &&
+                     values_[prior_id].consumers == 3 && cons(out(12), 1) && cons(out(13), 1) && rt(out(14));
+            }
+            if (ok) {
+                const std::vector<int64_t> raw = values_[out(10 - d)].shape;
+                const std::vector<int64_t> two{raw[0], 2 * raw[1], raw[2], raw[3]};
+                ok = values_[qs_id].shape == two && values_[us0_id].shape == raw && values_[us1_id].shape == raw;
+                if (y0)
+                    ok = ok && values_[latent_id].shape == two && values_[prior_id].shape ==
+                                   std::vector<int64_t>{raw[0], 4 * raw[1], raw[2], raw[3]};
+                else
+                    ok = ok && values_[norm_id].shape == two && values_[prior_id].shape == two &&
+                         values_[c2_id].shape == two && values_[cl_id].shape == two;
+            }
+            if (ok) {
+                const uint32_t y_raw = out(10 - d);
+                const long long pixels = element_count(values_[y_raw].shape) / Q;
+                float clip_lo = 0.0f;
+                uint32_t norm_out = 0, clip_out = 0, c2_out = 0, c3_out = 0, result = 0;
+                if (y0) {
+                    clip_lo = scalar(in(2)[1], -INFINITY);
+                    norm_out = values_[out(4)].consumers > 1 || values_[out(4)].graph_output ? out(4) : 0;
+                    clip_out = values_[out(2)].consumers > 1 || values_[out(2)].graph_output ? out(2) : 0;
+                    c2_out = values_[out(17)].consumers > 1 || values_[out(17)].graph_output ? out(17) : 0;
+                    c3_out = out(18);
+                } else {
+                    result = out(14);
+                }
+                Step s;
+                s.kernel = y0 ? "mlvc_y0_tail_f16" : "mlvc_y1_tail_f16";
+                s.info.kernel = s.kernel;
+                s.info.nodes = std::to_string(i) + "-" + std::to_string(i + len - 1);
+                s.reads = y0 ? std::vector<uint32_t>{prior_id, latent_id, qs_id, us0_id, us1_id}
+                             : std::vector<uint32_t>{norm_id, prior_id, qs_id, us0_id, us1_id, c2_id, cl_id};
+                s.writes = {y_raw};
+                for (uint32_t w : {norm_out, clip_out, c2_out, c3_out, result})
+                    if (w)
+                        s.writes.push_back(w);
+                s.info.bytes = 2.0 * pixels * Q * (y0 ? 4 + 2 + 2 + 2 + 1 + 6 : 2 + 2 + 2 + 2 + 2 + 2 + 1 + 2);
+                s.grid = blocks_for(pixels * (Q / 8), 256, sm_count_);
+                s.block = 256;
+                const bool is_y0 = y0;
+                s.build = [=, this](Step& st) {
+                    auto ptr = [&](uint32_t id) { return id ? reinterpret_cast<mlvc_half*>(values_[id].addr) : nullptr; };
+                    QuantTailParams p{};
+                    p.latent = ptr(latent_id);
+                    p.normalized = ptr(norm_id);
+                    p.prior = ptr(prior_id);
+                    p.qscale = ptr(qs_id);
+                    p.uscale0 = ptr(us0_id);
+                    p.uscale1 = ptr(us1_id);
+                    p.concat2_in = ptr(c2_id);
+                    p.clipped_in = ptr(cl_id);
+                    p.normalized_out = ptr(norm_out);
+                    p.clipped_out = ptr(clip_out);
+                    p.y_raw = ptr(y_raw);
+                    p.concat2_out = ptr(c2_out);
+                    p.concat3 = ptr(c3_out);
+                    p.result = ptr(result);
+                    p.pixels = pixels;
+                    p.q = Q;
+                    p.clip_lo = is_y0 ? clip_lo : 0.0f;
+                    st.set(p);
+                };
+                steps_.push_back(std::move(s));
+                i += len;
+                continue;
+            }
+        }
+
         // ---- recurrent-feature update: Slice x3, Sigmoid x2, Mul, Sub, Mul, Add,
         // Mul, Mul (+ a later Concat of the last Mul and the Add on channels),
         // the reference's fusion patterns of fusion_registry.cpp:405-709

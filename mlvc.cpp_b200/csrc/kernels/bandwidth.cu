@@ -360,6 +360,137 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_feature_update_f16(const 
     }
 }
 
+// ------------------------------------------------- latent quantisation tails
+// The two quantisation tails of the MLVC encoder (nineteen and fifteen graph
+// operators), one thread per 8 channels q of a pixel; every operator rounds to
+// FP16 through the stand-alone kernels' unary_op / binary_op, so the results
+// are bit-identical to running the operators one by one.
+namespace {
+
+struct Vec8 {
+    float v[8];
+};
+
+__device__ __forceinline__ Vec8 load8(const mlvc_half* p)
+{
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&u);
+    Vec8 r;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        unpack_h2(w[k], r.v[2 * k], r.v[2 * k + 1]);
+    return r;
+}
+
+__device__ __forceinline__ void store8(mlvc_half* p, const Vec8& x)
+{
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        w[k] = pack_h2(x.v[2 * k], x.v[2 * k + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ float rnd16(float v) { return __half2float(__float2half_rn(v)); }
+
+}  // namespace
+
+extern "C" __global__ void __launch_bounds__(256) mlvc_y0_tail_f16(const __grid_constant__ QuantTailParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int Q = p.q, qv = Q / 8;
+    const long long total = p.pixels * qv;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long px = i / qv;
+        const int q = static_cast<int>(i - px * qv) * 8;
+        const mlvc_half* prior = p.prior + px * 4 * Q;
+        Vec8 clip[2], norm[2], s[2], u[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const Vec8 pr = load8(prior + j * Q + q), lat = load8(p.latent + px * 2 * Q + j * Q + q);
+            const Vec8 tail = load8(prior + 2 * Q + j * Q + q), qs = load8(p.qscale + px * 2 * Q + j * Q + q);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                clip[j].v[k] = rnd16(unary_op(pr.v[k], 1, 0.0f, p.clip_lo, INFINITY));
+                const float rec = rnd16(unary_op(clip[j].v[k], 3, 0.0f, 0.0f, 0.0f));
+                norm[j].v[k] = rnd16(binary_op(lat.v[k], rec, 1));
+                s[j].v[k] = rnd16(binary_op(rnd16(binary_op(norm[j].v[k], tail.v[k], 2)), qs.v[k], 1));
+            }
+        }
+        Vec8 y;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            y.v[k] = rnd16(unary_op(rnd16(binary_op(s[0].v[k], s[1].v[k], 0)), 4, 0.0f, 0.0f, 0.0f));
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const Vec8 tail = load8(prior + 2 * Q + j * Q + q);
+            const Vec8 us = load8((j ? p.uscale1 : p.uscale0) + px * Q + q);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                u[j].v[k] = binary_op(rnd16(binary_op(y.v[k], tail.v[k], 0)), us.v[k], 1);
+        }
+        store8(p.y_raw + px * Q + q, y);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            if (p.normalized_out)
+                store8(p.normalized_out + px * 2 * Q + j * Q + q, norm[j]);
+            if (p.clipped_out)
+                store8(p.clipped_out + px * 2 * Q + j * Q + q, clip[j]);
+            if (p.concat2_out)
+                store8(p.concat2_out + px * 2 * Q + j * Q + q, u[j]);
+            store8(p.concat3 + px * 6 * Q + j * Q + q, u[j]);
+        }
+        // concat3's prior part: channels 2Q .. 6Q
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(p.concat3 + px * 6 * Q + 2 * Q + j * Q + q) =
+                *reinterpret_cast<const uint4*>(prior + j * Q + q);
+    }
+}
+
+extern "C" __global__ void __launch_bounds__(256) mlvc_y1_tail_f16(const __grid_constant__ QuantTailParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int Q = p.q, qv = Q / 8;
+    const long long total = p.pixels * qv;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long px = i / qv;
+        const int q = static_cast<int>(i - px * qv) * 8;
+        const long long b2 = px * 2 * Q;
+        Vec8 s[2], pr[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const Vec8 n = load8(p.normalized + b2 + j * Q + q), qs = load8(p.qscale + b2 + j * Q + q);
+            pr[j] = load8(p.prior + b2 + j * Q + q);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                s[j].v[k] = rnd16(binary_op(rnd16(binary_op(n.v[k], pr[j].v[k], 2)), qs.v[k], 1));
+        }
+        Vec8 y;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            y.v[k] = rnd16(unary_op(rnd16(binary_op(s[0].v[k], s[1].v[k], 0)), 4, 0.0f, 0.0f, 0.0f));
+        store8(p.y_raw + px * Q + q, y);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const Vec8 us = load8((j ? p.uscale1 : p.uscale0) + px * Q + q);
+            const Vec8 c2 = load8(p.concat2_in + b2 + j * Q + q), cl = load8(p.clipped_in + b2 + j * Q + q);
+            Vec8 r;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float upd = rnd16(binary_op(rnd16(binary_op(y.v[k], pr[j].v[k], 0)), us.v[k], 1));
+                r.v[k] = binary_op(rnd16(binary_op(c2.v[k], upd, 0)), cl.v[k], 1);
+            }
+            store8(p.result + b2 + j * Q + q, r);
+        }
+    }
+}
+
 // ------------------------------------------------------------ codec I/O
 // YUV420 frame -> model input tensor (reference: prepare_model_input,
 // core/src/yuv.cpp:339-400).  One thread per tensor element; the 256-entry

@@ -237,6 +237,38 @@ struct FeatureUpdateParams {
     float one;                 // the scalar the gate is subtracted from (1 in exported graphs)
 };
 
+// Fused latent quantisation tails (mlvc_y0_tail_f16 / mlvc_y1_tail_f16),
+// per pixel and channel q < Q with the graph's FP16 rounding after every
+// operator (reference: backends/driver_cubin/kernels/quantization_tail.cu and
+// the matchers of fusion_registry.cpp:14-404).  Halves j = 0, 1 are channels
+// j * Q + q of the 2Q-channel tensors.
+//   y0: clipped_j = max(prior[j], lo), normalized_j = latent_j * (1 / clipped_j),
+//       s_j = (normalized_j - prior[2Q + j]) * qscale_j, y = round(s_0 + s_1),
+//       u_j = (y + prior[2Q + j]) * uscale_j; concat2 = [u_0, u_1],
+//       concat3 = [u_0, u_1, prior (4Q)]
+//   y1: s_j = (normalized_j - prior_j) * qscale_j, y = round(s_0 + s_1),
+//       u_j = (y + prior_j) * uscale_j, result_j = (concat2_j + u_j) * clipped_j
+// Side outputs the graph reads elsewhere are written when non-null.
+struct QuantTailParams {
+    const mlvc_half* latent;      // y0: [P, 2Q]
+    const mlvc_half* normalized;  // y1: [P, 2Q]
+    const mlvc_half* prior;       // y0: [P, 4Q]; y1: [P, 2Q]
+    const mlvc_half* qscale;      // [P, 2Q]
+    const mlvc_half* uscale0;     // [P, Q]
+    const mlvc_half* uscale1;     // [P, Q]
+    const mlvc_half* concat2_in;  // y1: [P, 2Q]
+    const mlvc_half* clipped_in;  // y1: [P, 2Q]
+    mlvc_half* normalized_out;    // y0 side output [P, 2Q] or null
+    mlvc_half* clipped_out;       // y0 side output [P, 2Q] or null
+    mlvc_half* y_raw;             // [P, Q]
+    mlvc_half* concat2_out;       // y0 side output [P, 2Q] or null
+    mlvc_half* concat3;           // y0: [P, 6Q]
+    mlvc_half* result;            // y1: [P, 2Q]
+    long long pixels;
+    int q;                        // Q (multiple of 8)
+    float clip_lo;                // y0 clip lower bound
+};
+
 // Codec I/O between a YUV420 frame (planar Y, U, V bytes, width x height,
 // both even) and the model's [1, 3, model_height, model_width] FP16 NCHW
 // tensor, with the reference's conventions (core/src/yuv.cpp:324-525): the

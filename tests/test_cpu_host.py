@@ -282,3 +282,19 @@ def test_plan_feature_update_fusion(decoder, monkeypatch):
     split = _kernels(plan(*gb.finish()))
     assert "mlvc_feature_update_f16" not in split
     assert split.count("mlvc_unary_f16") == (3 if decoder else 2), split
+
+
+def test_plan_quantisation_tails_fused(monkeypatch):
+    """The y0 (19 operators) and y1 (15 operators) quantisation tails become
+    one step each, as in the reference's matchers (fusion_registry.cpp:14-404)."""
+    from quant_graphs import quant_tails_graph
+    gb, _ = quant_tails_graph(16, 5, 7)
+    steps = plan(*gb.finish()).steps()
+    k = [s["kernel"] for s in steps]
+    assert k.count("mlvc_y0_tail_f16") == 1 and k.count("mlvc_y1_tail_f16") == 1, k
+    assert "mlvc_unary_f16" not in k and "mlvc_binary_same_f16" not in k, k
+    assert [s["nodes"] for s in steps if s["kernel"] == "mlvc_y0_tail_f16"] == ["0-18"]
+    assert [s["nodes"] for s in steps if s["kernel"] == "mlvc_y1_tail_f16"] == ["19-33"]
+    monkeypatch.setenv("MLVC_B200_TAIL_FUSION", "0")
+    split = _kernels(plan(*gb.finish()))
+    assert "mlvc_y0_tail_f16" not in split and split.count("mlvc_unary_f16") == 4  # clip, reciprocal, 2 rounds

@@ -433,3 +433,23 @@ def test_feature_update_fused(c, h, w, decoder, monkeypatch):
     assert "mlvc_feature_update_f16" not in {s["kernel"] for s in split.steps()}
     for g, s in zip(got, split.run(inputs)):
         bits_equal(s, g)
+
+
+@pytest.mark.parametrize("q,h,w", [(64, 23, 40), (16, 5, 7), (128, 12, 20)])
+def test_quantisation_tails_fused(q, h, w, monkeypatch):
+    """y0 and y1 quantisation tails as one kernel each (reference
+    quantization_tail.cu): every output bit-identical to the oracle and to the
+    operator-by-operator schedule (all operators are elementwise)."""
+    from quant_graphs import quant_tails_graph
+    gb, inputs = quant_tails_graph(q, h, w)
+    got, want, be = run_both(gb, inputs)
+    for g, wnt in zip(got, want):
+        bits_equal(g, wnt)
+    kernels = {s["kernel"] for s in be.steps()}
+    assert {"mlvc_y0_tail_f16", "mlvc_y1_tail_f16"} <= kernels, kernels
+    graph, weights = gb.finish()
+    monkeypatch.setenv("MLVC_B200_TAIL_FUSION", "0")
+    split = Backend(0)
+    split.load_memory(graph, weights)
+    for g, s in zip(got, split.run(inputs)):
+        bits_equal(s, g)
