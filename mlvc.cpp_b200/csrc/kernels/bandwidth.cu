@@ -144,32 +144,6 @@ extern "C" __global__ void mlvc_strided_copy_v8_f16(const __grid_constant__ Copy
     }
 }
 
-// NCHW (plane-major) <-> NHWC transpose of one [C, HW] matrix per image
-// through a 32x33 shared tile, both sides coalesced.
-extern "C" __global__ void mlvc_transpose_f16(const __grid_constant__ CopyParams p)
-{
-    pdl_launch_dependents();
-    pdl_wait();
-    // dims: [images, rows, cols]; src is [rows][cols], dst is [cols][rows]
-    __shared__ mlvc_half tile[32][33];
-    const int rows = p.dims[1], cols = p.dims[2];
-    const long long img = blockIdx.z;
-    const mlvc_half* src = p.src + img * p.ss[0];
-    mlvc_half* dst = p.dst + img * p.ds[0];
-    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-    for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
-        const int r = r0 + dy, c = c0 + threadIdx.x;
-        if (r < rows && c < cols)
-            tile[dy][threadIdx.x] = src[static_cast<long long>(r) * cols + c];
-    }
-    __syncthreads();
-    for (int dy = threadIdx.y; dy < 32; dy += blockDim.y) {
-        const int c = c0 + dy, r = r0 + threadIdx.x;
-        if (r < rows && c < cols)
-            dst[static_cast<long long>(c) * rows + r] = tile[threadIdx.x][dy];
-    }
-}
-
 // NCHW <-> NHWC with pixel (un)shuffle fused, through shared memory.  One
 // block handles one device row band: 32 device pixels of one row of the NHWC
 // tensor and all of its C*r*r channels, i.e. C*r rows x 32*r columns of the
