@@ -47,7 +47,8 @@ FLUSH_BYTES = 256 << 20  # > 126 MB L2
 def single_op(name):
     """Single-operator graphs at 544x960 (inputs larger than L2) for kernel
     tuning and ncu captures: dw3x3 (256 ch), conv1x1 (128->256 + LeakyReLU),
-    ffn (the block's feed-forward half), dwconv (depthwise + 1x1 + residual)."""
+    ffn (the block's feed-forward half), dwconv (depthwise + 1x1 + residual),
+    mbconv (the block's first half: expand, depthwise, projection + residual)."""
     from mlvc_b200.graph import GraphBuilder, kaiming_normal, small_bias
     rng = np.random.default_rng(0)
     gb = GraphBuilder()
@@ -69,6 +70,17 @@ def single_op(name):
                   rng.standard_normal((1, 128, 1024, 316), dtype=np.float32).astype(np.float16)]
         desc = ("single op: depthwise 3x3 256 -> 1x1 256->128 + residual @1024x316 (widest image the fused "
                 "kernel takes; NCHW boundary conversion included)")
+    elif name == "op_mbconv":
+        x = gb.input("x", [1, 128, 544, 960])
+        t = gb.leaky_relu(gb.conv(x, gb.weight("w1", kaiming_normal(rng, (256, 128, 1, 1))),
+                                  gb.weight("b1", small_bias(rng, 256))), 0.01)
+        d = gb.conv(t, gb.weight("dw", kaiming_normal(rng, (256, 1, 3, 3), 1.0)), gb.weight("db", small_bias(rng, 256)),
+                    (1, 1), (1, 1), groups=256)
+        y = gb.conv(d, gb.weight("w2", kaiming_normal(rng, (128, 256, 1, 1), 1.0)), gb.weight("b2", small_bias(rng, 128)))
+        gb.output(gb.add(y, x), "y")
+        inputs = [rng.standard_normal((1, 128, 544, 960), dtype=np.float32).astype(np.float16)]
+        desc = ("single op: inverted residual 1x1 128->256 + LeakyReLU -> depthwise 3x3 -> 1x1 256->128 + residual "
+                "@544x960 (the block stack's first half; NCHW boundary conversion included)")
     elif name == "op_ffn":
         x = gb.input("x", [1, 128, 544, 960])
         t = gb.conv(x, gb.weight("w1", kaiming_normal(rng, (512, 128, 1, 1))), gb.weight("b1", small_bias(rng, 512)))
@@ -391,7 +403,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv"], default="block_stack")
+    ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv",
+                                                   "op_mbconv"], default="block_stack")
     ap.add_argument("--cpu-frames", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -140,10 +140,11 @@ int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, size_t flus
 int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend);
 
 /* Phase trace of one tensor-core conv or fused FFN step: relaunches it once
- * with %globaltimer stamps enabled; writes 24 stamps per CTA (CTA start,
+ * with %globaltimer stamps enabled; writes 48 stamps per CTA (CTA start,
  * setup done, weights issued, weights landed, first activation panel, last
  * MMA commit, first accumulator seen by the epilogue, epilogue done, exit,
- * then fused-FFN chunk events; 0 = not reached) and the total count to
+ * then fused-FFN, fused-depthwise and fused-block chunk events; 0 = not
+ * reached) and the total count to
  * *count.  Debug facility: no counterpart in the reference. */
 int mlvc_b200_trace_step(mlvc_b200_backend* backend, size_t index, uint64_t* stamps, size_t capacity,
                          size_t* count);

@@ -354,6 +354,8 @@ void Backend::plan()
         ffn_fusion_ = !(env && env[0] == '0');
         env = std::getenv("MLVC_B200_DW_FUSION");
         dw_fusion_ = !(env && env[0] == '0');
+        env = std::getenv("MLVC_B200_MB_FUSION");
+        mb_fusion_ = !(env && env[0] == '0');
         env = std::getenv("MLVC_B200_TAIL_FUSION");
         tail_fusion_ = !(env && env[0] == '0');
     }
@@ -751,6 +753,155 @@ void Backend::plan()
                     };
                     steps_.push_back(std::move(f));
                     i += 5 + consumed2;
+                    continue;
+                }
+            }
+            if (tc_shape && is1x1 && !reglu && mb_fusion_ && (epi == kEpiBias || epi == kEpiLeaky) && IC % 64 == 0 &&
+                IC <= 128 && OC % 64 == 0 && OC <= kMbMaxExpand && i + consumed + 1 < nodes.size()) {
+                // ---- fused inverted-residual block: this expand conv, the depthwise
+                // 3x3 that consumes it and the 1x1 projection of the depthwise
+                // result, with both intermediates kept on chip
+                const uint32_t e_id = out_id;
+                const NodeDesc& nd = nodes[i + consumed];
+                bool ok = nd.op == Op::kConv && nd.inputs[0] == e_id && only_consumer(e_id) && nd.groups == OC &&
+                          nd.strides[0] == 1 && nd.strides[1] == 1 && nd.pads[0] == 1 && nd.pads[1] == 1;
+                const uint32_t wd_id = ok ? nd.inputs[1] : 0;
+                const uint32_t bd_id = ok && nd.inputs.size() > 2 ? nd.inputs[2] : 0;
+                if (ok) {
+                    const Value& wdv = values_[wd_id];
+                    ok = wdv.kind == Value::kWeight && wdv.dtype == DType::kFp16 &&
+                         wdv.shape == std::vector<int64_t>{OC, 1, 3, 3} && (!bd_id || values_[bd_id].kind == Value::kWeight) &&
+                         values_[nd.output].shape == values_[e_id].shape && only_consumer(nd.output);
+                }
+                const size_t pj = i + consumed + 1;
+                const NodeDesc& np = nodes[pj];
+                ok = ok && np.op == Op::kConv && np.inputs[0] == nd.output && np.groups == 1 && np.strides[0] == 1 &&
+                     np.strides[1] == 1 && np.pads[0] == 0 && np.pads[1] == 0;
+                const uint32_t w2_id = ok ? np.inputs[1] : 0;
+                const uint32_t b2_id = ok && np.inputs.size() > 2 ? np.inputs[2] : 0;
+                int OC2 = 0;
+                if (ok) {
+                    const Value& w2v = values_[w2_id];
+                    ok = w2v.kind == Value::kWeight && w2v.dtype == DType::kFp16 && w2v.shape.size() == 4 &&
+                         w2v.shape[1] == OC && w2v.shape[2] == 1 && w2v.shape[3] == 1 &&
+                         (!b2_id || values_[b2_id].kind == Value::kWeight);
+                    OC2 = ok ? static_cast<int>(w2v.shape[0]) : 0;
+                    // one W2 K slice per ring slot, output staged in its own panels
+                    ok = ok && OC2 % 64 == 0 && OC2 <= 128;
+                }
+                const int kpx = IC / 64, panels2 = OC2 / 64;
+                const int mb_smem = 1024 + kMbHeaderBytes + (kpx + 1) * kMbSliceBytes + 2 * 16384 +
+                                    kMbWStages * kMbWSlotBytes + panels2 * kTcStagePanelBytes + 10 * OC * 2;
+                if (ok && mb_smem <= max_smem_optin_) {
+                    int epi2 = kEpiBias;
+                    float alpha2 = 0.0f;
+                    uint32_t out2 = 0, res2 = 0;
+                    const size_t consumed2 = conv_epilogue(pj, epi2, alpha2, out2, res2);
+                    const uint16_t* wd = wdata(wd_id);
+                    std::vector<uint16_t> dwp(static_cast<size_t>(10) * OC, 0);  // taps, then the bias row
+                    for (int c = 0; c < OC; ++c)
+                        for (int k = 0; k < 9; ++k)
+                            dwp[static_cast<size_t>(k) * OC + c] = wd[static_cast<size_t>(c) * 9 + k];
+                    if (bd_id)
+                        std::copy(wdata(bd_id), wdata(bd_id) + OC, dwp.begin() + static_cast<size_t>(9) * OC);
+                    std::vector<uint16_t> b2p(OC2, 0);
+                    if (b2_id)
+                        std::copy(wdata(b2_id), wdata(b2_id) + OC2, b2p.begin());
+                    const size_t w1_off = prep(w, static_cast<size_t>(OC) * IC * 2);
+                    const size_t b1_off = prep(bias_full.data(), bias_full.size() * 2);
+                    const size_t dww_off = prep(dwp.data(), dwp.size() * 2);
+                    const size_t w2_off = prep(wdata(w2_id), static_cast<size_t>(OC2) * OC * 2);
+                    const size_t b2_off = prep(b2p.data(), b2p.size() * 2);
+                    const int M = IH * IW;
+                    const int tiles_x = (IW + kDwTileW - 1) / kDwTileW, tiles_y = (IH + kDwTileH - 1) / kDwTileH;
+                    const int m_tiles = tiles_x * tiles_y;
+                    Step f;
+                    f.reads = {x_id};
+                    if (res2)
+                        f.reads.push_back(res2);
+                    f.writes = {out2};
+                    f.info.nodes = std::to_string(i) + "-" + std::to_string(pj + consumed2 - 1);
+                    f.info.flops = 2.0 * M * static_cast<double>(IC) * OC + 18.0 * M * OC + 2.0 * M * static_cast<double>(OC) * OC2;
+                    f.info.bytes = 2.0 * (static_cast<double>(M) * IC + static_cast<double>(OC) * IC + OC + 10.0 * OC +
+                                          static_cast<double>(OC2) * OC + OC2 + static_cast<double>(M) * OC2 * (res2 ? 2 : 1));
+                    f.kernel = "mlvc_mbconv_tc";
+                    f.info.kernel = f.kernel;
+                    f.smem = static_cast<unsigned>(mb_smem);
+                    f.block = kMbBlockThreads;
+                    f.grid = static_cast<unsigned>(std::min(m_tiles, sm_count_));
+                    const int E = OC, C = IC;
+                    const int epi1 = epi;
+                    const float alpha1 = alpha;
+                    f.build = [=, this](Step& st) {
+                        MbConvTcParams mp{};
+                        ConvTcParams& p = mp.c;
+                        const cuuint32_t elem1[2] = {1, 1};
+                        auto encode2 = [&](CUtensorMap* map, CUdeviceptr addr, cuuint64_t cols, cuuint64_t rows,
+                                           cuuint32_t box_cols, cuuint32_t box_rows, CUtensorMapSwizzle swz,
+                                           const char* what) {
+                            const cuuint64_t dims[2] = {cols, rows};
+                            const cuuint64_t strides[1] = {cols * 2};
+                            const cuuint32_t box[2] = {box_cols, box_rows};
+                            check(cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                                         reinterpret_cast<void*>(addr), dims, strides, box, elem1,
+                                                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  what);
+                        };
+                        {
+                            const cuuint32_t elem3[3] = {1, 1, 1};
+                            const cuuint64_t dims[3] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(IW),
+                                                        static_cast<cuuint64_t>(IH)};
+                            const cuuint64_t strides[2] = {static_cast<cuuint64_t>(C) * 2,
+                                                           static_cast<cuuint64_t>(IW) * C * 2};
+                            const cuuint32_t box[3] = {64, kDwTileW + 2, kDwTileH + 2};
+                            check(cuTensorMapEncodeTiled(&mp.map_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                                                         reinterpret_cast<void*>(values_[x_id].addr), dims, strides, box,
+                                                         elem3, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  "cuTensorMapEncodeTiled(mbconv x halo)");
+                        }
+                        encode2(&mp.map_w1, prepped_dev_.get() + w1_off, C, E, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B,
+                                "cuTensorMapEncodeTiled(mbconv W1)");
+                        encode2(&p.map_b, prepped_dev_.get() + w2_off, E, OC2, 64, static_cast<cuuint32_t>(OC2),
+                                CU_TENSOR_MAP_SWIZZLE_128B, "cuTensorMapEncodeTiled(mbconv W2)");
+                        encode2(&mp.map_dw, prepped_dev_.get() + dww_off, E, 10, static_cast<cuuint32_t>(E), 10,
+                                CU_TENSOR_MAP_SWIZZLE_NONE, "cuTensorMapEncodeTiled(mbconv taps)");
+                        encode_tile_map(&p.map_out, values_[out2].addr, OC2, 0, IW, IH,
+                                        "cuTensorMapEncodeTiled(mbconv out)", kDwTileW, kDwTileH);
+                        if (res2)
+                            encode_tile_map(&p.map_res, values_[res2].addr, OC2, 0, IW, IH,
+                                            "cuTensorMapEncodeTiled(mbconv residual)", kDwTileW, kDwTileH);
+                        else
+                            p.map_res = p.map_out;
+                        p.map_a0 = p.map_a1 = mp.map_x;
+                        p.bias = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b2_off);
+                        p.out = reinterpret_cast<mlvc_half*>(values_[out2].addr);
+                        p.M = M;
+                        p.N = OC2;
+                        p.n_valid = OC2;
+                        p.K = E;
+                        p.BN = OC2;
+                        p.n_tiles = 1;
+                        p.m_tiles = m_tiles;
+                        p.epilogue = epi2;
+                        p.alpha = alpha2;
+                        p.a_stages = 2;
+                        p.b_stages = kMbWStages;
+                        mp.bias1 = reinterpret_cast<const mlvc_half*>(prepped_dev_.get() + b1_off);
+                        mp.alpha1 = alpha1;
+                        mp.epi1 = epi1;
+                        mp.c_in = C;
+                        mp.expand = E;
+                        mp.width = IW;
+                        mp.height = IH;
+                        mp.tiles_x = tiles_x;
+                        st.set(mp);
+                    };
+                    steps_.push_back(std::move(f));
+                    i = pj + consumed2;
                     continue;
                 }
             }
@@ -1987,7 +2138,7 @@ std::vector<uint64_t> Backend::trace_step(size_t index)
         throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
     Step& st = steps_.at(index);
     if (st.kernel != "mlvc_conv1x1_tc" && st.kernel != "mlvc_convkxk_tc" && st.kernel != "mlvc_ffn_tc" &&
-        st.kernel != "mlvc_dwconv_tc")
+        st.kernel != "mlvc_dwconv_tc" && st.kernel != "mlvc_mbconv_tc")
         throw std::runtime_error("mlvc-b200: only tensor-core conv steps carry a phase trace");
     ContextGuard guard(ctx_);
     const size_t n = static_cast<size_t>(st.grid) * kTracePoints;

@@ -165,6 +165,10 @@ private:
     // Depthwise 3x3 + following 1x1 conv in one kernel; MLVC_B200_DW_FUSION=0
     // plans them as separate steps (same results, for comparison).
     bool dw_fusion_ = true;
+    // 1x1 expand conv (+ LeakyReLU) + depthwise 3x3 + 1x1 projection in one kernel;
+    // MLVC_B200_MB_FUSION=0 plans them as the depthwise + 1x1 pair after a 1x1
+    // conv (same results, for comparison).
+    bool mb_fusion_ = true;
     // Recurrent-feature update chain in one kernel; MLVC_B200_TAIL_FUSION=0
     // runs its operators one by one (same results, for comparison).
     bool tail_fusion_ = true;

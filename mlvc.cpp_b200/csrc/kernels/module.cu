@@ -7,4 +7,5 @@ extern "C" __device__ unsigned int mlvc_b200_status = 0;
 #include "conv_tc.cu"
 #include "ffn_tc.cu"
 #include "dwconv_tc.cu"
+#include "mbconv_tc.cu"
 #include "bandwidth.cu"

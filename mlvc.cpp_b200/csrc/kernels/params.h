@@ -90,8 +90,15 @@ enum TracePoint : int {
     kTrFfnG1Second = 17,     // fused FFN: MMA issuer committed GEMM1 of chunk 1
     kTrFfnG2First = 18,      // fused FFN: MMA issuer passed the waits of GEMM2 chunk 0
     kTrFfnChunk1Done = 19,   // fused FFN: epilogue released hidden chunk 1
-    kTrDwFirstSlice = 20,    // fused depthwise + 1x1: first depthwise slice written as an A panel
-    kTracePoints = 24
+    kTrDwFirstSlice = 20,    // fused depthwise (+ expand): first depthwise slice written as an A panel
+    // fused block, first tile, expand chunk c < 4: compute leader saw the expand
+    // accumulator (kTrMbChunk + 3c), the chunk complete in shared memory
+    // (+1), its A panel written (+2); MMA issuer passed the waits of the expand
+    // GEMM (kTrMbExpandMma + c) and of the projection K slice (kTrMbProjMma + c)
+    kTrMbChunk = 24,
+    kTrMbExpandMma = 36,
+    kTrMbProjMma = 40,
+    kTracePoints = 48
 };
 
 // Fused feed-forward block (mlvc_ffn_tc):
@@ -141,6 +148,40 @@ struct DwConvTcParams {
     int width, height;       // image
     int tiles_x;             // tiles per image row
     int h_stages;            // halo slices in flight (1 or 2)
+};
+
+// Fused inverted-residual block (mlvc_mbconv_tc):
+//     e   = epi1(fp16(x W1^T + b1))             tcgen05 over the 18 x 10 halo; bias (+ LeakyReLU),
+//                                               zero outside the image (the depthwise padding)
+//     d   = fp16(dw3x3(e) + b_dw)               CUDA cores, FP32 FMA from the bias
+//     out = epilogue(fp16(d W2^T + b2))         tcgen05; bias / LeakyReLU / + residual
+// Per 16 x 8-pixel tile the expanded tensor e exists only in shared memory,
+// 64 channels at a time.
+constexpr int kMbHeaderBytes = 4096;                              // barriers, TMEM address, both bias vectors
+constexpr int kMbMaxExpand = 256;                                 // expanded channels (bias1 capacity)
+constexpr int kMbHaloRows = 184;                                  // 180 halo pixels, padded to whole 8-row swizzle atoms
+constexpr int kMbSliceBytes = kMbHaloRows * 128;                  // one 64-channel halo slice (x or e) in smem
+constexpr int kMbRow1 = 56;                                       // first halo row of the second GEMM1 M block (rows 56..183)
+constexpr int kMbWSlotBytes = 16384;                              // one weight ring slot
+constexpr int kMbWStages = 4;
+constexpr int kMbBlockThreads = 576;                              // TMA warp, MMA warp, 16 compute warps
+
+struct MbConvTcParams {
+    // c describes the projection conv (as for mlvc_dwconv_tc): map_b = W2
+    // [C_out rows, E] (C_out x 64 boxes, 128-byte swizzle), map_out / map_res
+    // in {64, 16, 8} boxes over {C_out, W, H}, bias = b2, epilogue / alpha =
+    // its fused operator, K = E, BN = N = n_valid = C_out, m_tiles = tiles.
+    ConvTcParams c;
+    CUtensorMap map_x;       // x {C, W, H} in {64, 18, 10} boxes, 128-byte swizzle (GEMM1's A operand)
+    CUtensorMap map_w1;      // W1 [E rows, C] in {64, 64} boxes, 128-byte swizzle
+    CUtensorMap map_dw;      // depthwise taps and bias [10][E] (rows 0..8: tap ky * 3 + kx, row 9: bias), one {E, 10} box
+    const mlvc_half* bias1;  // [E] expand bias
+    float alpha1;            // expand LeakyReLU slope (epi1 == kEpiLeaky)
+    int epi1;                // kEpiBias or kEpiLeaky
+    int c_in;                // C (multiple of 64, <= 128)
+    int expand;              // E (multiple of 64, <= kMbMaxExpand)
+    int width, height;       // image
+    int tiles_x;             // tiles per image row
 };
 
 struct ElementwiseParams {

@@ -288,13 +288,13 @@ class Backend:
         return list(buf[:n])
 
     def trace_step(self, index):
-        """[CTAs, 24] %globaltimer stamps of one tensor-core conv or fused FFN
+        """[CTAs, 48] %globaltimer stamps of one tensor-core conv or fused FFN
         step (see include/mlvc_b200.h); requires a previous run()."""
         n = ctypes.c_size_t()
         _check(lib().mlvc_b200_trace_step(self._h, index, None, 0, ctypes.byref(n)))
         buf = (ctypes.c_uint64 * n.value)()
         _check(lib().mlvc_b200_trace_step(self._h, index, buf, n.value, ctypes.byref(n)))
-        return np.frombuffer(buf, np.uint64).reshape(-1, 24).copy()
+        return np.frombuffer(buf, np.uint64).reshape(-1, 48).copy()
 
     @property
     def kernel_launches(self):

@@ -141,20 +141,28 @@ def _kernels(be):
 def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
     """Conv+LeakyReLU, Conv+Add and Conv+Slice+Slice+Clip+Mul collapse into the
     tensor-core conv epilogue (fusion_registry.cpp:711-1036); with FFN fusion
-    the ReGLU conv and the conv after it (+ residual Add) become one step."""
+    the ReGLU conv and the conv after it (+ residual Add) become one step, and
+    the expand conv, depthwise conv and projection conv (+ Add) another."""
     gb, _ = build_block_stack(seed=0)
     be = plan(*gb.finish())
     k = _kernels(be)
-    assert k.count("mlvc_conv1x1_tc") == 8 and k.count("mlvc_ffn_tc") == 8 and k.count("mlvc_dwconv_tc") == 8
-    assert "mlvc_depthwise3x3_f16" not in k and len(k) == 26
+    assert k.count("mlvc_mbconv_tc") == 8 and k.count("mlvc_ffn_tc") == 8 and len(k) == 18, k
+    assert "mlvc_conv1x1_tc" not in k and "mlvc_dwconv_tc" not in k and "mlvc_depthwise3x3_f16" not in k
     assert "mlvc_unary_f16" not in k and "mlvc_binary_same_f16" not in k and "mlvc_reglu_f16" not in k
     nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_ffn_tc"]
     assert "6-12" in nodes  # conv + slice + slice + clip + mul + conv + add
-    nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_dwconv_tc"]
-    assert "3-5" in nodes  # depthwise conv + 1x1 conv + add
+    nodes = [s["nodes"] for s in be.steps() if s["kernel"] == "mlvc_mbconv_tc"]
+    assert "1-5" in nodes  # conv + leaky + depthwise conv + conv + add
     flops = sum(s["flops"] for s in be.steps())
     assert abs(flops - 39.13e9) / 39.13e9 < 0.01  # config-2 algorithmic FLOPs
-    assert all(s["smem"] > 233472 // 2 for s in be.steps() if s["kernel"] == "mlvc_ffn_tc")  # one CTA per SM
+    assert all(s["smem"] > 233472 // 2 for s in be.steps() if s["kernel"] in ("mlvc_ffn_tc", "mlvc_mbconv_tc"))
+
+    monkeypatch.setenv("MLVC_B200_MB_FUSION", "0")
+    k = _kernels(plan(*gb.finish()))
+    assert k.count("mlvc_conv1x1_tc") == 8 and k.count("mlvc_ffn_tc") == 8 and k.count("mlvc_dwconv_tc") == 8
+    assert "mlvc_mbconv_tc" not in k and len(k) == 26
+    nodes = [s["nodes"] for s in plan(*gb.finish()).steps() if s["kernel"] == "mlvc_dwconv_tc"]
+    assert "3-5" in nodes  # depthwise conv + 1x1 conv + add
 
     monkeypatch.setenv("MLVC_B200_FFN_FUSION", "0")
     monkeypatch.setenv("MLVC_B200_DW_FUSION", "0")
@@ -163,6 +171,41 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
     assert "mlvc_ffn_tc" not in split and "mlvc_dwconv_tc" not in split
     nodes = [s["nodes"] for s in plan(*gb.finish()).steps() if s["kernel"] == "mlvc_conv1x1_tc"]
     assert "6-10" in nodes  # conv + slice + slice + clip + mul
+
+
+@pytest.mark.parametrize("c,e,c_out,leaky,fused", [
+    (128, 256, 128, True, True), (64, 64, 64, False, True), (64, 192, 128, True, True), (128, 128, 64, True, True),
+    (192, 256, 128, True, False),  # input channels above two 64-channel halo slices
+    (48, 128, 64, True, False),    # input channels not a multiple of 64
+    (128, 320, 128, True, False),  # expanded channels above the kernel's bias capacity
+    (128, 256, 192, True, False),  # a W2 slice (C_out x 64) larger than one ring slot
+    (128, 96, 64, True, False),    # expanded channels not a multiple of 64
+])
+def test_plan_mbconv_fusion_predicates(c, e, c_out, leaky, fused):
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, 11, 37])
+    t = gb.conv(x, gb.weight("w1", np.zeros((e, c, 1, 1), np.float16)), gb.weight("b1", np.zeros(e, np.float16)))
+    if leaky:
+        t = gb.leaky_relu(t, 0.01)
+    d = gb.conv(t, gb.weight("dw", np.zeros((e, 1, 3, 3), np.float16)), gb.weight("db", np.zeros(e, np.float16)),
+                (1, 1), (1, 1), groups=e)
+    gb.output(gb.conv(d, gb.weight("w2", np.zeros((c_out, e, 1, 1), np.float16))), "y")
+    k = _kernels(plan(*gb.finish()))
+    assert ("mlvc_mbconv_tc" in k) == fused, k
+    if fused:
+        assert k == ["mlvc_boundary_f16", "mlvc_mbconv_tc", "mlvc_boundary_f16"], k
+
+
+def test_plan_mbconv_needs_single_consumers():
+    """The expanded tensor and the depthwise result must have no other reader."""
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 64, 8, 16])
+    t = gb.leaky_relu(gb.conv(x, gb.weight("w1", np.zeros((128, 64, 1, 1), np.float16))), 0.01)
+    d = gb.conv(t, gb.weight("dw", np.zeros((128, 1, 3, 3), np.float16)), None, (1, 1), (1, 1), groups=128)
+    gb.output(gb.conv(d, gb.weight("w2", np.zeros((64, 128, 1, 1), np.float16))), "y")
+    gb.output(t, "expanded")
+    k = _kernels(plan(*gb.finish()))
+    assert "mlvc_mbconv_tc" not in k and "mlvc_dwconv_tc" in k, k
 
 
 @pytest.mark.parametrize("c,c_out,h,w,fused", [

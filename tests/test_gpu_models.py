@@ -55,7 +55,7 @@ def test_block_stack_small(channels, h, w, blocks, tmp_path):
     gb, inputs = build_block_stack(seed=3, channels=channels, height=h, width=w, blocks=blocks)
     be, graph, weights = _load(gb)
     (y,) = be.run(inputs)
-    assert per_op_parity(be, graph, weights, inputs) >= 3 * blocks
+    assert per_op_parity(be, graph, weights, inputs) >= 2 * blocks
     _stack_check(y, graph, weights, inputs, tmp_path)
 
 
@@ -65,9 +65,8 @@ def test_block_stack_config2_full(tmp_path):
     be, graph, weights = _load(gb)
     (y,) = be.run(inputs)
     kernels = [s["kernel"] for s in be.steps()]
-    assert kernels.count("mlvc_conv1x1_tc") == 8 and kernels.count("mlvc_ffn_tc") == 8, kernels
-    assert kernels.count("mlvc_dwconv_tc") == 8, kernels
-    assert per_op_parity(be, graph, weights, inputs, conv_impl="gemm") >= 24
+    assert kernels.count("mlvc_mbconv_tc") == 8 and kernels.count("mlvc_ffn_tc") == 8, kernels
+    assert per_op_parity(be, graph, weights, inputs, conv_impl="gemm") >= 16
     _stack_check(y, graph, weights, inputs, tmp_path)
     # run-to-run determinism of the captured graph
     (y2,) = be.run(inputs)

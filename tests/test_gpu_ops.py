@@ -173,6 +173,59 @@ def test_dwconv_fused(c, c_out, h, w, epilogue, monkeypatch):
     bits_equal(split.run(inputs)[0], got[0])
 
 
+MB_CASES = [  # (C, E, C_out, H, W, LeakyReLU after the expand conv, epilogue of the projection)
+    (128, 256, 128, 92, 160, True, "residual_x"),  # the block stack's block (residual = block input)
+    (64, 128, 64, 13, 21, False, None),            # ragged tiles on both edges, odd width
+    (128, 256, 128, 9, 300, True, "leaky"),        # wide image
+    (64, 64, 64, 160, 160, True, "residual"),      # one expand chunk; 200 tiles: two tiles per CTA
+    (64, 192, 64, 8, 8, True, "residual_x"),       # three expand chunks (odd), one tile, half outside
+    (128, 128, 64, 23, 40, True, "residual"),      # two chunks, residual from another tensor
+]
+
+
+@pytest.mark.parametrize("c,e,c_out,h,w,leaky,epilogue", MB_CASES)
+def test_mbconv_fused(c, e, c_out, h, w, leaky, epilogue, monkeypatch):
+    """1x1 expand (+ LeakyReLU) -> depthwise 3x3 -> 1x1 projection (+ residual /
+    LeakyReLU) as one kernel, the expanded tensor and the depthwise result kept
+    in shared memory: parity with the oracle, and bit-identical to the
+    expand-conv + fused-depthwise schedule."""
+    rng = np.random.default_rng(37)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, h, w])
+    w1 = gb.weight("w1", (rng.standard_normal((e, c, 1, 1), dtype=np.float32) * np.sqrt(2.0 / c)).astype(np.float16))
+    b1 = gb.weight("b1", rng.uniform(-0.1, 0.1, e).astype(np.float16))
+    t = gb.conv(x, w1, b1)
+    if leaky:
+        t = gb.leaky_relu(t, 0.01)
+    dw = gb.weight("dw", (rng.standard_normal((e, 1, 3, 3), dtype=np.float32) / 3.0).astype(np.float16))
+    db = gb.weight("db", rng.uniform(-0.1, 0.1, e).astype(np.float16))
+    d = gb.conv(t, dw, db, (1, 1), (1, 1), groups=e)
+    w2 = gb.weight("w2", (rng.standard_normal((c_out, e, 1, 1), dtype=np.float32) * np.sqrt(1.0 / e)).astype(np.float16))
+    b2 = gb.weight("b2", rng.uniform(-0.1, 0.1, c_out).astype(np.float16))
+    y = gb.conv(d, w2, b2)
+    inputs = [rng.standard_normal((1, c, h, w), dtype=np.float32).astype(np.float16)]
+    if epilogue == "residual_x":
+        assert c_out == c
+        y = gb.add(x, y)
+    elif epilogue == "residual":
+        r = gb.input("r", [1, c_out, h, w])
+        y = gb.add(y, r)
+        inputs.append(rng.standard_normal((1, c_out, h, w), dtype=np.float32).astype(np.float16))
+    elif epilogue == "leaky":
+        y = gb.leaky_relu(y, 0.01)
+    gb.output(y, "y")
+    got, want, be = run_both(gb, inputs)
+    compare(got[0], want[0])
+    kernels = [s["kernel"] for s in be.steps() if s["kernel"] != "mlvc_boundary_f16"]
+    assert kernels == ["mlvc_mbconv_tc"], kernels
+    graph, weights = gb.finish()
+    monkeypatch.setenv("MLVC_B200_MB_FUSION", "0")
+    split = Backend(0)
+    split.load_memory(graph, weights)
+    assert "mlvc_mbconv_tc" not in {s["kernel"] for s in split.steps()}
+    bits_equal(split.run(inputs)[0], got[0])
+
+
 SPATIAL = [  # (IC, OC, stride, kernel, pad, H, W)
     (24, 24, 1, 3, 1, 13, 17), (40, 264, 2, 3, 1, 13, 17), (8, 8, 2, 2, 0, 13, 17), (128, 256, 2, 2, 0, 13, 17),
     (64, 64, 1, 3, 1, 13, 17), (64, 128, 2, 3, 1, 13, 17), (64, 64, 1, 3, 1, 46, 300), (128, 64, 1, 3, 1, 9, 140),
