@@ -790,7 +790,9 @@ void Backend::plan()
                     ok = ok && OC2 % 64 == 0 && OC2 <= 128;
                 }
                 const int kpx = IC / 64, panels2 = OC2 / 64;
-                const int mb_smem = 1024 + kMbHeaderBytes + (kpx + 1) * kMbSliceBytes + 2 * 16384 +
+                // header, x halo slices, two e chunk buffers (180 rows x 128 bytes),
+                // two A panels, weight ring, output staging, depthwise taps + bias
+                const int mb_smem = 1024 + kMbHeaderBytes + kpx * kMbSliceBytes + 2 * 180 * 128 + 2 * 16384 +
                                     kMbWStages * kMbWSlotBytes + panels2 * kTcStagePanelBytes + 10 * OC * 2;
                 if (ok && mb_smem <= max_smem_optin_) {
                     int epi2 = kEpiBias;

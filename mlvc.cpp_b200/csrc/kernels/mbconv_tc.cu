@@ -24,12 +24,14 @@
 //              into a double-buffered TMEM accumulator, then, once the
 //              depthwise A panel of the chunk is ready, the projection GEMM
 //              (K = 64) into the output accumulator.
-//   compute    512 threads: the chunk's expand accumulators -> bias,
+//   expand     warps 2..9: the chunk's expand accumulators -> bias,
 //              LeakyReLU, FP16, zero for halo pixels outside the image ->
-//              the 180-row chunk of e in shared memory; then the depthwise
-//              conv of the 128 pixels x 64 channels into the SW128 A panel
-//              (the arithmetic of mlvc_dwconv_tc); after the last chunk the
-//              shared tile epilogue of the conv kernels stores the output.
+//              the 180-row chunk of e in one of two shared-memory buffers
+//   depthwise  warps 10..17: the depthwise conv of the previous chunk's 128
+//              pixels x 64 channels into the SW128 A panel (4 channels x a
+//              2 x 4 pixel block per thread), while the expand warps write
+//              the next chunk; after the last chunk these warps run the
+//              shared tile epilogue of the conv kernels for the output.
 //
 // The expand epilogue is the 1x1 conv kernel's (FP32 bias add, one rounding,
 // LeakyReLU as fp16(fp32(h) * alpha) on negative halves), the depthwise and
@@ -39,13 +41,13 @@
 //
 // Roles (576 threads): warp 0 = TMA producer, warp 1 = TMEM owner (512
 // columns: two expand accumulators of 2 x 64 columns, the output
-// accumulator at column 256) + MMA issuer, warps 2..17 = compute (16 warps:
-// the CUDA-core stages are latency-bound, so four compute warps per SM
-// sub-partition), of which warps 2..9 also run the output epilogue.  All waits
-// are bounded (%globaltimer) and abort the CTA with an error bit in
-// mlvc_b200_status; the compute threads hand the e buffer over through
-// mbarriers (not named barriers), so an aborting thread never strands the
-// others.
+// accumulator at column 256) + MMA issuer, warps 2..9 = expand epilogue,
+// warps 10..17 = depthwise + output epilogue: the two CUDA-core stages use
+// different units (TMEM loads and conversions; shared-memory loads and FMAs)
+// and overlap chunk by chunk.  All waits are bounded (%globaltimer) and abort
+// the CTA with an error bit in mlvc_b200_status; the warps hand buffers over
+// through mbarriers (not named barriers), so an aborting thread never strands
+// the others.
 namespace mlvc_b200 {
 
 struct MbShared {
@@ -54,7 +56,7 @@ struct MbShared {
     uint64_t acc1_full[2], acc1_empty[2];            // expand accumulators
     uint64_t a_full[2], a_empty[2];                  // depthwise A panels
     uint64_t acc2_full, acc2_empty;                  // output accumulator
-    uint64_t hid_full, hid_empty;                    // e chunk written / read by all compute threads
+    uint64_t e_full[2], e_empty[2];                  // e chunk buffers: written by the expand warps, read by the depthwise warps
     uint64_t stg_ready, stg_full;                    // output staging hand-over (see StageSync)
     uint64_t dw_full;                                // depthwise taps + bias landed
     uint64_t drain;
@@ -70,11 +72,16 @@ static_assert(kMbRow1 + kBM == kMbHaloRows && kMbRow1 <= kBM, "the two expand M 
 static_assert(kDwHaloPx <= kMbHaloRows, "halo rows");
 
 constexpr uint32_t kMbPanelBytes = kBM * 128;  // one 128-pixel x 64-channel FP16 panel
-constexpr int kMbComputeThreads = 512;         // warps 2..17: expand epilogue + depthwise
-constexpr int kMbComputeWarps = kMbComputeThreads / 32;
+constexpr int kMbComputeThreads = 512;         // warps 2..17
 constexpr int kMbThreads = kMbComputeThreads + 64;
+constexpr int kMbExpandWarps = 8;              // warps 2..9
+constexpr int kMbDwWarps = 8;                  // warps 10..17
+constexpr int kMbDwThreads = kMbDwWarps * 32;
+constexpr uint32_t kMbEBytes = kDwHaloPx * 128;  // one 64-channel FP16 chunk of e over the halo
+static_assert(kMbThreads == kMbBlockThreads, "block size shared with the host");
+static_assert(kMbDwThreads == kEpilogueThreads, "the depthwise warps run the shared output epilogue");
 
-// One arrival per compute warp (the barriers count warps): the lanes' shared
+// One arrival per warp (these barriers count warps): the lanes' shared
 // memory writes are ordered before lane 0's release by __syncwarp.
 __device__ __forceinline__ void mb_warp_arrive(uint64_t* bar, int lane)
 {
@@ -88,23 +95,27 @@ constexpr uint32_t kMbAcc2Col = 256;           // output accumulator column in T
 constexpr uint32_t kMbTmemCols = 512;
 
 // Weight panel j of a tile's sequence (the MMA issuer consumes them in this
-// order): W1(0), then W1(c), W2(c - 1) for c = 1 .. chunks - 1, then
-// W2(chunks - 1).  kind 0 = W1 (expand) chunk, 1 = W2 (projection) K slice.
-__device__ __forceinline__ void mb_panel(int j, int nseq, int& kind, int& c)
+// order): the expand GEMM runs two chunks ahead of the projection, so it
+// never waits behind a projection slice whose depthwise panel is not ready:
+// W1(0), W1(1), then W1(c), W2(c - 2) for c = 2 .. chunks - 1, then the last
+// two W2 slices.  kind 0 = W1 (expand) chunk, 1 = W2 (projection) K slice.
+__device__ __forceinline__ void mb_panel(int j, int nch, int& kind, int& c)
 {
-    if (j == 0) {
+    const int lead = nch < 2 ? nch : 2;
+    if (j < lead) {
         kind = 0;
-        c = 0;
-    } else if (j == nseq - 1) {
-        kind = 1;
-        c = nseq / 2 - 1;
-    } else if (j & 1) {
-        kind = 0;
-        c = (j + 1) / 2;
-    } else {
-        kind = 1;
-        c = j / 2 - 1;
+        c = j;
+        return;
     }
+    j -= lead;
+    const int steady = 2 * (nch - lead);
+    if (j < steady) {
+        kind = j & 1;
+        c = (j & 1) ? j / 2 : lead + j / 2;
+        return;
+    }
+    kind = 1;
+    c = nch - lead + (j - steady);
 }
 
 // One thread, one halo row of one expand chunk: 16 accumulators (columns
@@ -152,8 +163,8 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
     const int nseq = 2 * nch;           // weight panels per tile
     const int panels = p.BN / 64;       // output panels
     uint8_t* x_smem = base + kMbHeaderBytes;
-    uint8_t* e_smem = x_smem + static_cast<size_t>(kpx) * kMbSliceBytes;
-    uint8_t* a_smem = e_smem + kMbSliceBytes;
+    uint8_t* e_smem = x_smem + static_cast<size_t>(kpx) * kMbSliceBytes;  // two e chunk buffers
+    uint8_t* a_smem = e_smem + 2 * kMbEBytes;
     uint8_t* w_smem = a_smem + 2 * kMbPanelBytes;
     uint8_t* stage_smem = w_smem + kMbWStages * kMbWSlotBytes;  // 1024-aligned
     // depthwise taps [9][E] and bias [E], FP16, loaded once per CTA by TMA
@@ -170,14 +181,14 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sh->acc1_full[s], 1);
-            mbar_init(&sh->acc1_empty[s], kMbComputeWarps);
-            mbar_init(&sh->a_full[s], kMbComputeWarps);
+            mbar_init(&sh->acc1_empty[s], kMbExpandWarps);
+            mbar_init(&sh->a_full[s], kMbDwWarps);
             mbar_init(&sh->a_empty[s], 1);
+            mbar_init(&sh->e_full[s], kMbExpandWarps);
+            mbar_init(&sh->e_empty[s], kMbDwWarps);
         }
         mbar_init(&sh->acc2_full, 1);
         mbar_init(&sh->acc2_empty, kEpilogueThreads);
-        mbar_init(&sh->hid_full, kMbComputeWarps);
-        mbar_init(&sh->hid_empty, kMbComputeWarps);
         mbar_init(&sh->stg_ready, 1);
         mbar_init(&sh->stg_full, kEpilogueThreads);
         mbar_init(&sh->dw_full, 1);
@@ -216,7 +227,7 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
                     return false;
                 uint8_t* dst = w_smem + static_cast<size_t>(ws) * kMbWSlotBytes;
                 int kind, c;
-                mb_panel(j, nseq, kind, c);
+                mb_panel(j, nch, kind, c);
                 if (kind == 0) {
                     mbar_arrive_expect_tx(&sh->w_full[ws], w1_bytes);
                     for (int s = 0; s < kpx; ++s)
@@ -282,7 +293,7 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
                     break;
                 for (int j = 0; j < nseq; ++j) {
                     int kind, c;
-                    mb_panel(j, nseq, kind, c);
+                    mb_panel(j, nch, kind, c);
                     const uint32_t b_st = w_addr + static_cast<uint32_t>(ws) * kMbWSlotBytes;
                     if (kind == 0) {
                         // expand chunk c over both M blocks into acc1[k1 & 1]
@@ -352,169 +363,183 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------ expand epilogue + depthwise + output epilogue
-        // 16 warps: warp w reads TMEM lane quadrant w % 4; its column group
-        // (w - 2) / 4 takes 16 of a chunk's 64 expand columns.  Warps 2..9
-        // (column groups 0 and 1) also run the output epilogue while warps
-        // 10..17 move on to the next tile.
+        // ------------------------------------------------ expand epilogue / depthwise + output epilogue
         const int quadrant = warp & 3;
-        const int group = (warp - 2) / 4;
-        const int et_id = (warp - 2) * 32 + lane;
-        const bool leader = et_id == 0;
-        const bool epi_warp = group < 2;
-        const int cq = et_id & 15;  // 4-channel chunk of the slice
-        const int pg = et_id >> 4;  // pixels 4 pg .. 4 pg + 3 of the tile
-        for (int i = et_id; i < p.BN; i += kMbComputeThreads)
+        const bool expand_role = warp < 2 + kMbExpandWarps;
+        const int group = expand_role ? (warp - 2) / 4 : (warp - 2 - kMbExpandWarps) / 4;  // 0 or 1
+        const int rt = (expand_role ? warp - 2 : warp - 2 - kMbExpandWarps) * 32 + lane;    // 0..255 in the role
+        const bool leader = rt == 0;
+        for (int i = (warp - 2) * 32 + lane; i < p.BN; i += kMbComputeThreads)
             sh->bias2[i] = (p.bias && i < p.N) ? __half2float(p.bias[i]) : 0.0f;
-        for (int i = et_id; i < mp.expand; i += kMbComputeThreads)
+        for (int i = (warp - 2) * 32 + lane; i < mp.expand; i += kMbComputeThreads)
             sh->bias1[i] = mp.bias1 ? __half2float(mp.bias1[i]) : 0.0f;
         asm volatile("bar.sync 1, %0;" ::"n"(kMbComputeThreads + 32) : "memory");  // biases + TMEM address
         tc_fence_after();
         pdl_wait();  // residual reads and output writes follow the previous kernel
-        const StageSync ss{&sh->stg_ready, &sh->stg_full};
         const int W = mp.width, H = mp.height;
-        // this thread's expand rows: halo row r0 = its TMEM lane in block 0;
-        // in block 1 lane L holds halo row kMbRow1 + L, new (>= 128, < 180) only
-        // for lanes 72 .. 123, i.e. quadrants 2 and 3
-        const int r0 = quadrant * 32 + lane, r1 = kMbRow1 + r0;
-        const bool block1 = quadrant >= 2;  // warp-uniform
-        const bool r1_new = r1 >= kBM && r1 < kDwHaloPx;
-        const uint32_t lane_addr = static_cast<uint32_t>(quadrant * 32) << 16;
-        const int col0 = group * 16;  // this warp's 16 columns of a chunk
-        // e / A panel byte offset of the thread's 4 channels within a 128-byte row
-        const int cq_chunk = cq >> 1, cq_half = (cq & 1) * 8;
-        bool ok = mbar_wait(&sh->dw_full, 0, &sh->abort_flag, kErrWaitEpilogue);
-        int as = 0;
-        uint32_t aph = 0, kc = 0, it = 0;
-        for (int t = first; ok && t < tiles; t += step, ++it) {
-            TileCoord tc;
-            tc.pixel0 = 0;
-            tc.ox0 = (t % mp.tiles_x) * kDwTileW;
-            tc.oy = (t / mp.tiles_x) * kDwTileH;
-            if (leader)  // residual tile into the staging buffer while the block runs
-                stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
-            auto inside = [&](int hr) {
-                const int ix = tc.ox0 - 1 + hr % (kDwTileW + 2), iy = tc.oy - 1 + hr / (kDwTileW + 2);
-                return ix >= 0 && ix < W && iy >= 0 && iy < H;
-            };
-            const bool in0 = inside(r0), in1 = inside(r1);
-            const int ty = pg >> 2, tx = (pg & 3) * 4;  // the thread's 4 pixels: tile row ty, columns tx .. tx + 3
-            const int x0 = tc.ox0 + tx;
-            for (int c = 0; c < nch; ++c, ++kc) {
-                // ---- expand accumulators of chunk c -> e rows
-                const uint32_t buf = kc & 1u;
-                if (!mbar_wait(&sh->acc1_full[buf], (kc >> 1) & 1u, &sh->abort_flag, kErrWaitEpilogue) ||
-                    (kc > 0 && !mbar_wait(&sh->hid_empty, (kc - 1) & 1u, &sh->abort_flag, kErrWaitEpilogue))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                if (leader && it == 0 && c < 4)
-                    trace(p, kTrMbChunk + 3 * c);
-                {
-                    const uint32_t acc = sh->tmem_base + lane_addr + buf * 128u + static_cast<uint32_t>(col0);
-                    uint32_t a0[16], a1[16];
-                    tmem_ld16_nowait(acc, a0);
-                    if (block1)
-                        tmem_ld16_nowait(acc + 64u, a1);
-                    tmem_wait_ld();
-                    mb_expand_row(mp, sh->bias1, a0, c * 64 + col0, r0, in0, e_smem);
-                    if (block1 && r1_new)
-                        mb_expand_row(mp, sh->bias1, a1, c * 64 + col0, r1, in1, e_smem);
-                }
-                tc_fence_before();
-                mb_warp_arrive(&sh->acc1_empty[buf], lane);
-                mb_warp_arrive(&sh->hid_full, lane);
-                if (!mbar_wait(&sh->hid_full, kc & 1u, &sh->abort_flag, kErrWaitEpilogue) ||
-                    !mbar_wait(&sh->a_empty[as], aph ^ 1u, &sh->abort_flag, kErrWaitEpilogue)) {
-                    ok = false;
-                    break;
-                }
-                if (leader && it == 0 && c < 4)
-                    trace(p, kTrMbChunk + 3 * c + 1);
-                // ---- depthwise 3x3 of chunk c (4 channels x 4 pixels per thread)
-                const int ch = c * 64 + cq * 4;
-                float acc4[4][4];
-                {
-                    float b4[4];
-                    const uint2 bv = *reinterpret_cast<const uint2*>(dw_smem + (9 * mp.expand + ch) * 2);
-                    unpack_h2(bv.x, b4[0], b4[1]);
-                    unpack_h2(bv.y, b4[2], b4[3]);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            acc4[i][k] = b4[k];
-                }
-                uint32_t wv[9][2];
-#pragma unroll
-                for (int tap = 0; tap < 9; ++tap) {
-                    const uint2 q = *reinterpret_cast<const uint2*>(dw_smem + (tap * mp.expand + ch) * 2);
-                    wv[tap][0] = q.x;
-                    wv[tap][1] = q.y;
-                }
-                // e columns x0 - 1 .. x0 + 4; output pixel i takes column cc with kx = cc - i
-#pragma unroll
-                for (int cc = 0; cc < 6; ++cc) {
-                    const int ix = x0 - 1 + cc;
-                    if (ix < 0 || ix >= W)
-                        continue;  // outside the image: the tap is skipped (no padding term)
-                    uint32_t xv[3][2];
-#pragma unroll
-                    for (int ky = 0; ky < 3; ++ky) {
-                        const int hr = (ty + ky) * (kDwTileW + 2) + tx + cc;
-                        const uint2 v =
-                            *reinterpret_cast<const uint2*>(e_smem + hr * 128 + ((cq_chunk ^ (hr & 7)) << 4) + cq_half);
-                        xv[ky][0] = v.x;
-                        xv[ky][1] = v.y;
+        bool ok = true;
+        uint32_t kc = 0, it = 0;
+        if (expand_role) {
+            // this thread's expand rows: halo row r0 = its TMEM lane in block 0;
+            // in block 1 lane L holds halo row kMbRow1 + L, new (>= 128, < 180)
+            // only for lanes 72 .. 123, i.e. quadrants 2 and 3
+            const int r0 = quadrant * 32 + lane, r1 = kMbRow1 + r0;
+            const bool block1 = quadrant >= 2;  // warp-uniform
+            const bool r1_new = r1 >= kBM && r1 < kDwHaloPx;
+            const uint32_t lane_addr = static_cast<uint32_t>(quadrant * 32) << 16;
+            for (int t = first; ok && t < tiles; t += step, ++it) {
+                const int ox0 = (t % mp.tiles_x) * kDwTileW, oy0 = (t / mp.tiles_x) * kDwTileH;
+                auto inside = [&](int hr) {
+                    const int ix = ox0 - 1 + hr % (kDwTileW + 2), iy = oy0 - 1 + hr / (kDwTileW + 2);
+                    return ix >= 0 && ix < W && iy >= 0 && iy < H;
+                };
+                const bool in0 = inside(r0), in1 = inside(r1);
+                for (int c = 0; c < nch; ++c, ++kc) {
+                    const uint32_t buf = kc & 1u, use = kc >> 1;
+                    if (!mbar_wait(&sh->acc1_full[buf], use & 1u, &sh->abort_flag, kErrWaitEpilogue) ||
+                        !mbar_wait(&sh->e_empty[buf], (use & 1u) ^ 1u, &sh->abort_flag, kErrWaitEpilogue)) {
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    if (leader && it == 0 && c < 4)
+                        trace(p, kTrMbChunk + 3 * c);
+                    uint8_t* e_buf = e_smem + buf * kMbEBytes;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int kx = cc - i;
-                        if (kx < 0 || kx > 2)
-                            continue;
-#pragma unroll
-                        for (int ky = 0; ky < 3; ++ky)
-#pragma unroll
-                            for (int k = 0; k < 2; ++k)
-                                fma_h2(acc4[i][2 * k], acc4[i][2 * k + 1], xv[ky][k], wv[ky * 3 + kx][k]);
+                    for (int h = 0; h < 2; ++h) {  // 16 of the warpgroup's 32 columns at a time
+                        const int col = group * 32 + h * 16;
+                        const uint32_t acc = sh->tmem_base + lane_addr + buf * 128u + static_cast<uint32_t>(col);
+                        uint32_t a0[16], a1[16];
+                        tmem_ld16_nowait(acc, a0);
+                        if (block1)
+                            tmem_ld16_nowait(acc + 64u, a1);
+                        tmem_wait_ld();
+                        mb_expand_row(mp, sh->bias1, a0, c * 64 + col, r0, in0, e_buf);
+                        if (block1 && r1_new)
+                            mb_expand_row(mp, sh->bias1, a1, c * 64 + col, r1, in1, e_buf);
                     }
-                }
-                mb_warp_arrive(&sh->hid_empty, lane);  // e chunk read
-                // rounded depthwise output -> A panel row (4 pg + i), 128-byte swizzle
-                uint8_t* apanel = a_smem + static_cast<size_t>(as) * kMbPanelBytes;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int r = 4 * pg + i;
-                    *reinterpret_cast<uint2*>(apanel + r * 128 + ((cq_chunk ^ (r & 7)) << 4) + cq_half) =
-                        make_uint2(pack_h2(acc4[i][0], acc4[i][1]), pack_h2(acc4[i][2], acc4[i][3]));
-                }
-                fence_proxy_async_smem();  // the tensor core reads the panel through the async proxy
-                mb_warp_arrive(&sh->a_full[as], lane);
-                if (leader && it == 0) {
-                    if (c == 0)
-                        trace(p, kTrDwFirstSlice);
-                    if (c < 4)
-                        trace(p, kTrMbChunk + 3 * c + 2);
-                }
-                if (++as == 2) {
-                    as = 0;
-                    aph ^= 1u;
+                    tc_fence_before();
+                    mb_warp_arrive(&sh->acc1_empty[buf], lane);
+                    mb_warp_arrive(&sh->e_full[buf], lane);
+                    if (leader && it == 0 && c < 4)
+                        trace(p, kTrMbChunk + 3 * c + 1);
                 }
             }
-            if (!ok)
-                break;
-            if (epi_warp &&
-                !epilogue_tile(p, sh->bias2, sh->tmem_base + kMbAcc2Col, &sh->acc2_full, it & 1u, &sh->acc2_empty, ss,
-                               it, stage_smem, nullptr, panels, 0, tc, true, quadrant, group, lane, leader,
-                               &sh->abort_flag))
-                break;
-            if (leader && it == 0)
-                trace(p, kTrFirstAcc);
-        }
-        if (leader) {
-            bulk_wait_all();
-            trace(p, kTrEpilogueDone);
+        } else {
+            // depthwise: 4 channels (cq) x a 2 x 4 pixel block (pb) per thread
+            const int cq = rt & 15;
+            const int pb = rt >> 4;                       // 0..15
+            const int by = (pb >> 2) * 2, bx = (pb & 3) * 4;  // block: tile rows by, by + 1, columns bx .. bx + 3
+            const int cq_chunk = cq >> 1, cq_half = (cq & 1) * 8;  // byte offset of the 4 channels in a row
+            const StageSync ss{&sh->stg_ready, &sh->stg_full};
+            ok = mbar_wait(&sh->dw_full, 0, &sh->abort_flag, kErrWaitEpilogue);
+            int as = 0;
+            uint32_t aph = 0;
+            for (int t = first; ok && t < tiles; t += step, ++it) {
+                TileCoord tc;
+                tc.pixel0 = 0;
+                tc.ox0 = (t % mp.tiles_x) * kDwTileW;
+                tc.oy = (t / mp.tiles_x) * kDwTileH;
+                if (leader)  // residual tile into the staging buffer while the block runs
+                    stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
+                const int x0 = tc.ox0 + bx;
+                for (int c = 0; c < nch; ++c, ++kc) {
+                    const uint32_t buf = kc & 1u, use = kc >> 1;
+                    if (!mbar_wait(&sh->e_full[buf], use & 1u, &sh->abort_flag, kErrWaitEpilogue) ||
+                        !mbar_wait(&sh->a_empty[as], aph ^ 1u, &sh->abort_flag, kErrWaitEpilogue)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t* e_buf = e_smem + buf * kMbEBytes;
+                    const int ch = c * 64 + cq * 4;
+                    float acc[2][4][4];  // [row][column][channel]
+                    {
+                        float b4[4];
+                        const uint2 bv = *reinterpret_cast<const uint2*>(dw_smem + (9 * mp.expand + ch) * 2);
+                        unpack_h2(bv.x, b4[0], b4[1]);
+                        unpack_h2(bv.y, b4[2], b4[3]);
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    acc[j][i][k] = b4[k];
+                    }
+                    uint32_t wv[9][2];
+#pragma unroll
+                    for (int tap = 0; tap < 9; ++tap) {
+                        const uint2 q = *reinterpret_cast<const uint2*>(dw_smem + (tap * mp.expand + ch) * 2);
+                        wv[tap][0] = q.x;
+                        wv[tap][1] = q.y;
+                    }
+                    // e columns x0 - 1 .. x0 + 4 over halo rows by .. by + 3; output
+                    // pixel (j, i) takes column cc with kx = cc - i and halo row j + ky
+#pragma unroll
+                    for (int cc = 0; cc < 6; ++cc) {
+                        const int ix = x0 - 1 + cc;
+                        if (ix < 0 || ix >= W)
+                            continue;  // outside the image: the tap is skipped (no padding term)
+                        uint32_t xv[4][2];
+#pragma unroll
+                        for (int rr = 0; rr < 4; ++rr) {
+                            const int hr = (by + rr) * (kDwTileW + 2) + bx + cc;
+                            const uint2 v =
+                                *reinterpret_cast<const uint2*>(e_buf + hr * 128 + ((cq_chunk ^ (hr & 7)) << 4) + cq_half);
+                            xv[rr][0] = v.x;
+                            xv[rr][1] = v.y;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int kx = cc - i;
+                                if (kx < 0 || kx > 2)
+                                    continue;
+#pragma unroll
+                                for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+                                    for (int k = 0; k < 2; ++k)
+                                        fma_h2(acc[j][i][2 * k], acc[j][i][2 * k + 1], xv[j + ky][k], wv[ky * 3 + kx][k]);
+                            }
+                    }
+                    mb_warp_arrive(&sh->e_empty[buf], lane);  // e chunk read
+                    // rounded depthwise output -> A panel row r (tile pixel (bx + i, by + j)), 128-byte swizzle
+                    uint8_t* apanel = a_smem + static_cast<size_t>(as) * kMbPanelBytes;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int r = (by + j) * kDwTileW + bx + i;
+                            *reinterpret_cast<uint2*>(apanel + r * 128 + ((cq_chunk ^ (r & 7)) << 4) + cq_half) =
+                                make_uint2(pack_h2(acc[j][i][0], acc[j][i][1]), pack_h2(acc[j][i][2], acc[j][i][3]));
+                        }
+                    fence_proxy_async_smem();  // the tensor core reads the panel through the async proxy
+                    mb_warp_arrive(&sh->a_full[as], lane);
+                    if (leader && it == 0) {
+                        if (c == 0)
+                            trace(p, kTrDwFirstSlice);
+                        if (c < 4)
+                            trace(p, kTrMbChunk + 3 * c + 2);
+                    }
+                    if (++as == 2) {
+                        as = 0;
+                        aph ^= 1u;
+                    }
+                }
+                if (!ok)
+                    break;
+                if (!epilogue_tile(p, sh->bias2, sh->tmem_base + kMbAcc2Col, &sh->acc2_full, it & 1u, &sh->acc2_empty,
+                                   ss, it, stage_smem, nullptr, panels, 0, tc, true, quadrant, group, lane, leader,
+                                   &sh->abort_flag))
+                    break;
+                if (leader && it == 0)
+                    trace(p, kTrFirstAcc);
+            }
+            if (leader) {
+                bulk_wait_all();
+                trace(p, kTrEpilogueDone);
+            }
         }
     }
 

@@ -163,7 +163,7 @@ constexpr int kMbHaloRows = 184;                                  // 180 halo pi
 constexpr int kMbSliceBytes = kMbHaloRows * 128;                  // one 64-channel halo slice (x or e) in smem
 constexpr int kMbRow1 = 56;                                       // first halo row of the second GEMM1 M block (rows 56..183)
 constexpr int kMbWSlotBytes = 16384;                              // one weight ring slot
-constexpr int kMbWStages = 4;
+constexpr int kMbWStages = 3;
 constexpr int kMbBlockThreads = 576;                              // TMA warp, MMA warp, 16 compute warps
 
 struct MbConvTcParams {
