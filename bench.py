@@ -37,7 +37,7 @@ for p in (ROOT, ROOT / "mlvc.cpp_b200"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
 
-from mlvc_b200.graph import build_block_stack, build_conv3x3  # noqa: E402
+from mlvc_b200.graph import build_block_stack, build_conv3x3, build_mlvc_decoder_standin  # noqa: E402
 
 METRIC = "conv-stack frames/s (config 2 block stack; stand-in for 1080p MLVC decode frames/s)"
 UNIT = "frames/s"
@@ -99,12 +99,25 @@ def single_op(name):
         inputs = [rng.standard_normal((1, 128, 544, 960), dtype=np.float32).astype(np.float16)]
         desc = "single op: 1x1 conv 128->256 + LeakyReLU @544x960 (NCHW boundary conversion included)"
     graph, weights = gb.finish()
-    return graph, weights, inputs, desc, METRIC.replace("config 2 block stack", desc)
+    return graph, weights, inputs, desc, METRIC.replace("config 2 block stack", desc), []
 
 
 def workload(name):
     if name.startswith("op_"):
         return single_op(name)
+    if name.startswith("mlvc_dec_"):
+        width, height = {"mlvc_dec_1080p": (1920, 1088), "mlvc_dec_640": (640, 368)}[name]
+        gb, inputs = build_mlvc_decoder_standin(0, width, height)
+        desc = (f"MLVC-shaped decoder stand-in @{width}x{height} (the upstream MLVC architecture is absent): documented "
+                "decoder I/O (z_raw 1/128, y_raw_0/1 1/16, ref_feature 256ch 1/8, q_index int32 -> x_hat, feature), "
+                "hyperprior x8 pixel-shuffle up-sampling, QP-indexed dequantisation, 2+2+2 depth-conv blocks at 256 ch "
+                "(the profile's block: 1x1 +LeakyReLU, dw3x3, 1x1 +residual, ReGLU FFN +residual), x8 pixel-shuffle "
+                "reconstruction; Kaiming-normal weights, seed 0")
+        desc += ("; ref_feature <- feature bound as recurrent state (as the codec pipeline binds decoder input 3 to "
+                 "output 1), so it stays on the device between frames")
+        metric = f"MLVC-shaped decoder stand-in frames/s @{width}x{height} (stand-in for MLVC decode frames/s)"
+        graph, weights = gb.finish()
+        return graph, weights, inputs, desc, metric, [(3, 1)]
     if name == "conv3x3":
         gb, inputs = build_conv3x3(0)
         desc = ("config1-conv3x3: one FP16 3x3 s1 p1 conv 64->64 @184x320, W~N(0,sqrt(2/576)), b~U(-0.1,0.1), "
@@ -117,7 +130,7 @@ def workload(name):
                 "pixel_shuffle(2); input [1,32,184,320] fp16 ~N(0,1); Kaiming-normal weights, seed 0")
         metric = METRIC
     graph, weights = gb.finish()
-    return graph, weights, inputs, desc, metric
+    return graph, weights, inputs, desc, metric, []
 
 
 def measured_peaks():
@@ -223,7 +236,7 @@ def reference_backend_frames_per_s(graph, weights, inputs, frames, warmup, threa
 
 
 def run_reference_arm(args, rank, world):
-    graph, weights, inputs, desc, metric = workload(args.workload)
+    graph, weights, inputs, desc, metric, _ = workload(args.workload)
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
@@ -248,9 +261,13 @@ def run_b200_arm(args, rank, world, local_rank):
     from mlvc_b200 import Backend
 
     torch.cuda.set_device(local_rank)
-    graph, weights, inputs, desc, metric = workload(args.workload)
+    graph, weights, all_inputs, desc, metric, bindings = workload(args.workload)
     be = Backend(local_rank)
-    be.load_memory(graph, weights)
+    be.load_memory(graph, weights, bindings)
+    if bindings:  # state-bound inputs live on the device; the CPU baseline gets all inputs
+        be.reset_state()
+    bound = {i for i, _ in bindings}
+    inputs = [a for k, a in enumerate(all_inputs) if k not in bound]
     outs = be.run(inputs)  # inputs now resident on the device
     if not all(np.isfinite(o.astype(np.float32)).all() for o in outs):
         raise RuntimeError("non-finite output")
@@ -320,9 +337,19 @@ def run_b200_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e2e_ms = e_st.elapsed_time(e_en)
     e2e_value, _ = replica_throughput(e2e_ms, args.steps, world, f"cuda:{local_rank}")
-    # output still correct after the slot loop
-    first = be.slot_output((args.steps - 1) % 2, 0)
-    if not np.array_equal(first.view(np.uint16), outs[0].view(np.uint16)):
+    # output still correct after the slot loop (with recurrent state: one frame
+    # each way from a reset state)
+    if bindings:
+        be.reset_state()
+        want = be.run(inputs)[0]
+        be.reset_state()
+        be.submit(0)
+        be.wait_slot(0)
+        first = be.slot_output(0, 0)
+    else:
+        want = outs[0]
+        first = be.slot_output((args.steps - 1) % 2, 0)
+    if not np.array_equal(first.view(np.uint16), want.view(np.uint16)):
         raise RuntimeError("slot path output differs from run()")
 
     # ---- per-kernel timings: in-stack (warm) shares and cold-L2 launches
@@ -386,7 +413,7 @@ def run_b200_arm(args, rank, world, local_rank):
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             try:
-                fps, times = reference_backend_frames_per_s(graph, weights, inputs, args.cpu_frames, 1, threads)
+                fps, times = reference_backend_frames_per_s(graph, weights, all_inputs, args.cpu_frames, 1, threads)
                 line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
                                         "sample": f"{args.cpu_frames} frames of the same workload on the reference "
                                                   f"backends/cpu (AVX2, fusion on), {sum(times):.1f} s"}
@@ -404,7 +431,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv",
-                                                   "op_mbconv"], default="block_stack")
+                                                   "op_mbconv", "mlvc_dec_1080p", "mlvc_dec_640"], default="block_stack")
     ap.add_argument("--cpu-frames", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -1875,8 +1875,14 @@ void Backend::plan()
             s.info.bytes += 2.0 * out_count;
             const auto& sh = values_[a].shape;
             const int r = n.block;
-            s.kernel = n.op == Op::kDepthToSpace ? "mlvc_depth_to_space_f16" : "mlvc_space_to_depth_f16";
-            s.grid = blocks_for(out_count, 256, sm_count_);
+            const bool d2s = n.op == Op::kDepthToSpace;
+            // r = 2 with 8-channel output (d2s) / input (s2d) blocks: 16-byte vectors;
+            // one item = one pixel x 8 channels on the narrow side = 32 output elements
+            const bool v8 = r == 2 && (d2s ? sh[1] % 32 == 0 : sh[1] % 8 == 0);
+            const long long items = v8 ? out_count / 32 : out_count;
+            s.kernel = v8 ? (d2s ? "mlvc_depth_to_space_r2_v8_f16" : "mlvc_space_to_depth_r2_v8_f16")
+                          : (d2s ? "mlvc_depth_to_space_f16" : "mlvc_space_to_depth_f16");
+            s.grid = blocks_for(items, 256, sm_count_);
             s.build = [=, this](Step& st) {
                 PixelShuffleParams p{};
                 p.src = reinterpret_cast<const mlvc_half*>(values_[a].addr);
@@ -1886,7 +1892,7 @@ void Backend::plan()
                 p.h = static_cast<int>(sh[2]);
                 p.w = static_cast<int>(sh[3]);
                 p.r = r;
-                p.count = out_count;
+                p.count = items;
                 st.set(p);
             };
             break;

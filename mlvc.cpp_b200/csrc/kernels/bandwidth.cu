@@ -549,6 +549,10 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid
         boundary_vec<1>(p, tile);
     else if (vec && p.r == 2)
         boundary_vec<2>(p, tile);
+    else if (vec && p.r == 4)
+        boundary_vec<4>(p, tile);
+    else if (vec && p.r == 8)
+        boundary_vec<8>(p, tile);
     else
         boundary_scalar(p, tile);
 }
@@ -586,6 +590,89 @@ extern "C" __global__ void mlvc_depth_to_space_f16(const __grid_constant__ Pixel
         const long long n = t / oh;
         const int ic = c * r * r + (y % r) * r + (x % r);
         p.dst[i] = p.src[((n * p.h + y / r) * p.w + x / r) * p.c + ic];
+    }
+}
+
+// DepthToSpace with r = 2, output channels a multiple of 8: one thread per
+// input pixel and 8 output channels (4 x 16-byte loads of 32 input channels,
+// 4 x 16-byte stores, one per output sub-pixel s = dy * 2 + dx, which takes
+// input channels 4 j + s).  `count` = input pixels x output channels / 8.
+extern "C" __global__ void __launch_bounds__(256) mlvc_depth_to_space_r2_v8_f16(const __grid_constant__ PixelShuffleParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int ocv = p.c / 32;  // 8-channel output blocks per pixel
+    const int ow = p.w * 2;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
+        const int m = static_cast<int>(i % ocv);
+        const long long px = i / ocv;  // input pixel (n, y, x)
+        const int x = static_cast<int>(px % p.w);
+        const long long ny = px / p.w;  // n * h + y
+        const uint4* src = reinterpret_cast<const uint4*>(p.src + px * p.c + m * 32);
+        uint32_t w[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 v = src[q];
+            w[4 * q] = v.x;
+            w[4 * q + 1] = v.y;
+            w[4 * q + 2] = v.z;
+            w[4 * q + 3] = v.w;
+        }
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int dy = s >> 1, dx = s & 1;
+            const uint32_t sel = (s & 1) ? 0x7632u : 0x5410u;  // high or low halves
+            uint32_t o[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                o[k] = __byte_perm(w[4 * k + (s >> 1)], w[4 * k + 2 + (s >> 1)], sel);
+            const long long orow = (ny * 2 + dy) * ow + 2 * x + dx;  // output pixel (n, 2y + dy, 2x + dx)
+            *reinterpret_cast<uint4*>(p.dst + orow * (p.c / 4) + m * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+// SpaceToDepth with r = 2, input channels a multiple of 8: one thread per
+// output pixel and 8 input channels (the inverse of the kernel above).
+// `count` = output pixels x input channels / 8.
+extern "C" __global__ void __launch_bounds__(256) mlvc_space_to_depth_r2_v8_f16(const __grid_constant__ PixelShuffleParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int icv = p.c / 8;
+    const int ow = p.w / 2;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
+        const int m = static_cast<int>(i % icv);
+        const long long opx = i / icv;  // output pixel (n, y, x)
+        const int x = static_cast<int>(opx % ow);
+        const long long ny = opx / ow;
+        uint32_t v[4][4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int dy = s >> 1, dx = s & 1;
+            const long long irow = (ny * 2 + dy) * p.w + 2 * x + dx;
+            const uint4 u = *reinterpret_cast<const uint4*>(p.src + irow * p.c + m * 8);
+            v[s][0] = u.x;
+            v[s][1] = u.y;
+            v[s][2] = u.z;
+            v[s][3] = u.w;
+        }
+        // output channel 4 j + s of block m <- input channel j of sub-pixel s
+        uint4* dst = reinterpret_cast<uint4*>(p.dst + opx * (p.c * 4) + m * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // output channels 8 q .. 8 q + 7 of the block: j = 2 q, 2 q + 1
+            uint32_t o[4];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int j = 2 * q + t;
+                const uint32_t sel = (j & 1) ? 0x7632u : 0x5410u;
+                o[2 * t] = __byte_perm(v[0][j >> 1], v[1][j >> 1], sel);
+                o[2 * t + 1] = __byte_perm(v[2][j >> 1], v[3][j >> 1], sel);
+            }
+            dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
     }
 }
 

@@ -366,3 +366,110 @@ def build_block_stack(seed=0, channels=128, height=92, width=160, blocks=8):
     gb.output(gb.depth_to_space(h, 2), "y")
     inputs = [_fp16(rng.standard_normal((1, c // 4, height * 2, width * 2), dtype=np.float32))]
     return gb, inputs
+
+
+def _depth_conv_block(gb, rng, h, c, prefix, branch_gain=1.0):
+    """One block of the profile's depth_conv_block_params (models/profiles/
+    profiles.json: LeakyReLU, gated chunk mode, ReLU1 FFN gate), as in config 2:
+    1x1 C->2C + LeakyReLU(0.01); depthwise 3x3 (2C); 1x1 2C->C + residual; 1x1
+    C->4C -> ReGLU (clip(gate, 0, 1) * linear) -> 1x1 2C->C + residual.
+    branch_gain scales the two residual-branch output convs (the profile's
+    zero_init_residual starts them at zero)."""
+    w1 = gb.weight(prefix + "expand.weight", kaiming_normal(rng, (2 * c, c, 1, 1), np.sqrt(2.0)))
+    b1 = gb.weight(prefix + "expand.bias", small_bias(rng, 2 * c))
+    wd = gb.weight(prefix + "dw.weight", kaiming_normal(rng, (2 * c, 1, 3, 3), 1.0))
+    bd = gb.weight(prefix + "dw.bias", small_bias(rng, 2 * c))
+    w2 = gb.weight(prefix + "project.weight", _fp16(kaiming_normal(rng, (c, 2 * c, 1, 1), 1.0) * branch_gain))
+    b2 = gb.weight(prefix + "project.bias", small_bias(rng, c))
+    w3 = gb.weight(prefix + "ffn_in.weight", kaiming_normal(rng, (4 * c, c, 1, 1), 1.0))
+    b3 = gb.weight(prefix + "ffn_in.bias", small_bias(rng, 4 * c))
+    w4 = gb.weight(prefix + "ffn_out.weight", _fp16(kaiming_normal(rng, (c, 2 * c, 1, 1), 1.0) * branch_gain))
+    b4 = gb.weight(prefix + "ffn_out.bias", small_bias(rng, c))
+    t = gb.leaky_relu(gb.conv(h, w1, b1), 0.01)
+    t = gb.conv(t, wd, bd, (1, 1), (1, 1), groups=2 * c)
+    h = gb.add(h, gb.conv(t, w2, b2))
+    f = gb.conv(h, w3, b3)
+    g = gb.slice(f, 1, 0, 2 * c)
+    lin = gb.slice(f, 1, 2 * c, 4 * c)
+    f = gb.mul(gb.clip(g, 0.0, 1.0), lin)
+    return gb.add(h, gb.conv(f, w4, b4))
+
+
+def build_mlvc_decoder_standin(seed=0, width=1920, height=1088, feature=256, latent=128, hyper=128, qp_num=72,
+                               q_index=21, blocks_y=2, blocks_feature=2, blocks_recon=2):
+    """MLVC-shaped decoder STAND-IN.  The upstream MLVC architecture source is
+    absent from the reference (tools/python/mlvc_tools/source.py imports it from
+    an external package), so this is not the MLVC network; it is assembled from
+    what the reference documents:
+
+    * decoder I/O and plane sizes (docs/design.md, "Fixed graph I/O"):
+      z_raw [1, hyper, ceil(H/128), ceil(W/128)], y_raw_0 / y_raw_1
+      [1, latent/2, ceil(H/16), ceil(W/16)], ref_feature [1, feature, H/8, W/8],
+      q_index_shifted [1] int32 -> x_hat [1, 3, H, W], feature [1, feature, H/8, W/8];
+    * the blocks of the profile's depth_conv_block_params (_depth_conv_block);
+    * native CRD pixel shuffle for up-sampling (graph schema 3) and a QP-indexed
+      Gather of per-QP scale rows (qp_num = 72 tables).
+
+    Layout: hyperprior decoder z -> 1x1 + LeakyReLU -> block -> three
+    [1x1 to 4 x channels, pixel shuffle 2] stages -> crop to the y plane ->
+    prior (means | context); y = concat(y_raw_0, y_raw_1) * qscale[q] + means;
+    contextual decoder concat(y, context) -> 1x1 -> blocks_y blocks at 1/16 ->
+    1x1 + pixel shuffle 2 -> concat(ref_feature) -> 1x1 -> blocks_feature
+    blocks at 1/8 = new feature; reconstruction blocks_recon blocks -> 1x1 to
+    3 x 64 -> pixel shuffle 8 = x_hat.  Weights Kaiming-normal (gain as in
+    build_block_stack), the residual-branch output convs scaled by 0.25 (with
+    full gain the un-normalised 256-channel residual stream grows to std ~100
+    and the two CPU implementations differ by 10 % rel-L2 at the output; at
+    0.25 the outputs have std ~1 and the CPU-vs-CPU spread is ~1e-3), biases
+    U(-0.1, 0.1), seeded; inputs: integer-valued latents, N(0, 1) reference
+    feature."""
+    rng = np.random.default_rng(seed)
+    h8, w8 = -(-height // 8), -(-width // 8)
+    h16, w16 = -(-height // 16), -(-width // 16)
+    hz, wz = -(-height // 128), -(-width // 128)
+    if h8 != 2 * h16 or w8 != 2 * w16 or height != 8 * h8 or width != 8 * w8:
+        raise ValueError("stand-in needs H and W multiples of 16")
+    gb = GraphBuilder()
+    z = gb.input("z_raw", [1, hyper, hz, wz])
+    y0 = gb.input("y_raw_0", [1, latent // 2, h16, w16])
+    y1 = gb.input("y_raw_1", [1, latent // 2, h16, w16])
+    ref = gb.input("ref_feature", [1, feature, h8, w8])
+    q = gb.input("q_index_shifted", [1], "int32")
+
+    def conv1x1(x, cin, cout, name, gain=1.0):
+        w = gb.weight(name + ".weight", kaiming_normal(rng, (cout, cin, 1, 1), gain))
+        return gb.conv(x, w, gb.weight(name + ".bias", small_bias(rng, cout)))
+
+    # hyperprior decoder: 1/128 -> 1/16 (x8), cropped to the y plane
+    t = gb.leaky_relu(conv1x1(z, hyper, feature, "hyper.in", np.sqrt(2.0)), 0.01)
+    t = _depth_conv_block(gb, rng, t, feature, "hyper.block0.", 0.25)
+    for i in range(3):
+        t = gb.depth_to_space(conv1x1(t, feature, 4 * feature, f"hyper.up{i}"), 2)
+    t = gb.slice(gb.slice(t, 2, 0, h16), 3, 0, w16)
+    means = gb.slice(t, 1, 0, latent)
+    context = gb.slice(t, 1, latent, feature)
+    # QP-indexed dequantisation of the latents
+    table = gb.weight("qscale", rng.uniform(0.5, 2.0, (qp_num, latent, 1, 1)).astype(np.float16))
+    y = gb.add(gb.mul(gb.concat([y0, y1], 1), gb.gather(table, q)), means)
+    # contextual decoder: 1/16 -> 1/8, joined with the reference feature
+    t = conv1x1(gb.concat([y, context], 1), latent + feature - latent, feature, "ctx.in")
+    for i in range(blocks_y):
+        t = _depth_conv_block(gb, rng, t, feature, f"ctx.block{i}.", 0.25)
+    t = gb.depth_to_space(conv1x1(t, feature, 4 * feature, "ctx.up"), 2)
+    t = conv1x1(gb.concat([t, ref], 1), 2 * feature, feature, "feat.in")
+    for i in range(blocks_feature):
+        t = _depth_conv_block(gb, rng, t, feature, f"feat.block{i}.", 0.25)
+    new_feature = t
+    # reconstruction: 1/8 -> full resolution
+    r = t
+    for i in range(blocks_recon):
+        r = _depth_conv_block(gb, rng, r, feature, f"recon.block{i}.", 0.25)
+    x_hat = gb.depth_to_space(conv1x1(r, feature, 3 * 64, "recon.out"), 8)
+    gb.output(x_hat, "x_hat")
+    gb.output(new_feature, "feature")
+    inputs = [np.rint(rng.standard_normal((1, hyper, hz, wz)) * 4).astype(np.float16),
+              np.rint(rng.standard_normal((1, latent // 2, h16, w16)) * 3).astype(np.float16),
+              np.rint(rng.standard_normal((1, latent // 2, h16, w16)) * 3).astype(np.float16),
+              _fp16(rng.standard_normal((1, feature, h8, w8), dtype=np.float32)),
+              np.array([q_index], np.int32)]
+    return gb, inputs

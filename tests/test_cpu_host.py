@@ -13,7 +13,7 @@ import pytest
 
 import mlvc_b200
 from mlvc_b200 import Backend
-from mlvc_b200.graph import GraphBuilder, build_block_stack, build_conv3x3
+from mlvc_b200.graph import GraphBuilder, build_block_stack, build_conv3x3, build_mlvc_decoder_standin
 from oracle.graph_oracle import GraphOracle
 from oracle.wire_schema import parse_graph
 
@@ -171,6 +171,22 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
     assert "mlvc_ffn_tc" not in split and "mlvc_dwconv_tc" not in split
     nodes = [s["nodes"] for s in plan(*gb.finish()).steps() if s["kernel"] == "mlvc_conv1x1_tc"]
     assert "6-10" in nodes  # conv + slice + slice + clip + mul
+
+
+def test_plan_mlvc_decoder_standin():
+    """The MLVC-shaped stand-in plans on the tensor-core path: every 1x1 conv
+    (256-channel blocks, up-sampling convs) on tcgen05, LeakyReLU / residual /
+    ReGLU in the conv epilogues, depthwise on the bandwidth kernel; graph I/O as
+    documented for the decoder."""
+    gb, inputs = build_mlvc_decoder_standin(width=640, height=368)
+    graph, weights = gb.finish()
+    be = plan(graph, weights)
+    k = _kernels(be)
+    assert k.count("mlvc_conv1x1_tc") == 36 and k.count("mlvc_depthwise3x3_f16") == 7, k
+    assert "mlvc_conv_direct_f16" not in k and "mlvc_unary_f16" not in k and "mlvc_reglu_f16" not in k
+    assert [tuple(s) for _, _, s in be.inputs] == [(1, 128, 3, 5), (1, 64, 23, 40), (1, 64, 23, 40),
+                                                     (1, 256, 46, 80), (1,)]
+    assert [tuple(s) for _, _, s in be.outputs] == [(1, 3, 368, 640), (1, 256, 46, 80)]
 
 
 @pytest.mark.parametrize("c,e,c_out,leaky,fused", [

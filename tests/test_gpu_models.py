@@ -18,7 +18,7 @@ import pytest
 
 from helpers import compare_scaled, per_op_parity
 from mlvc_b200 import Backend
-from mlvc_b200.graph import build_block_stack, build_conv3x3
+from mlvc_b200.graph import build_block_stack, build_conv3x3, build_mlvc_decoder_standin
 from oracle.graph_oracle import GraphOracle
 from oracle.ref_backend import RefCpuBackend
 
@@ -31,16 +31,23 @@ def _rel(a, b):
 
 
 def _stack_check(y, graph, weights, inputs, tmp_path):
+    """Every graph output (y: one array or a list) against the reference CPU
+    backend, within twice the spread between the two CPU implementations (the
+    reference backend and the oracle) or rel-L2 1e-3, whichever is larger."""
+    ys = y if isinstance(y, (list, tuple)) else [y]
     part = tmp_path / "aot" / "m"
     part.mkdir(parents=True)
     (part / "graph.pb").write_bytes(graph)
     (part / "weights.bin").write_bytes(weights)
-    (ref,) = RefCpuBackend(tmp_path, "m", 0).run(inputs)
-    (alt,) = GraphOracle(graph, weights, "gemm").run(inputs)
-    spread = _rel(alt, ref)
-    got = _rel(y, ref)
-    assert np.isfinite(y.astype(np.float32)).all()
-    assert got <= max(1e-3, 2.0 * spread), f"GPU vs reference CPU rel-L2 {got:.3g}, CPU-vs-CPU spread {spread:.3g}"
+    refs = RefCpuBackend(tmp_path, "m", 0).run(inputs)
+    alts = GraphOracle(graph, weights, "gemm").run(inputs)
+    assert len(refs) == len(ys) == len(alts)
+    for k, (yk, ref, alt) in enumerate(zip(ys, refs, alts)):
+        spread = _rel(alt, ref)
+        got = _rel(yk, ref)
+        assert np.isfinite(yk.astype(np.float32)).all()
+        assert got <= max(1e-3, 2.0 * spread), \
+            f"output {k}: GPU vs reference CPU rel-L2 {got:.3g}, CPU-vs-CPU spread {spread:.3g}"
 
 
 def _load(gb):
@@ -71,6 +78,20 @@ def test_block_stack_config2_full(tmp_path):
     # run-to-run determinism of the captured graph
     (y2,) = be.run(inputs)
     assert np.array_equal(y.view(np.uint16), y2.view(np.uint16))
+
+
+@pytest.mark.parametrize("width,height", [(256, 128), (640, 368)])
+def test_mlvc_decoder_standin(width, height, tmp_path):
+    """The MLVC-shaped decoder stand-in (256-channel blocks on the unfused
+    tensor-core path, pixel shuffle x2 / x8, spatial crops, channel concats,
+    QP-indexed Gather): every materialised step against the oracle, then the
+    whole graph against the reference CPU backend."""
+    gb, inputs = build_mlvc_decoder_standin(seed=5, width=width, height=height)
+    be, graph, weights = _load(gb)
+    x_hat, feature = be.run(inputs)
+    assert x_hat.shape == (1, 3, height, width) and feature.shape == (1, 256, height // 8, width // 8)
+    assert per_op_parity(be, graph, weights, inputs, conv_impl="gemm") >= 30
+    _stack_check([x_hat, feature], graph, weights, inputs, tmp_path)
 
 
 def test_conv3x3_config1_per_op():

@@ -372,6 +372,28 @@ def test_pixel_shuffle_order(factor):
     bits_equal(got[1], inputs[0])
 
 
+@pytest.mark.parametrize("c,h,w", [(64, 6, 10), (32, 4, 14), (24, 4, 6)])
+def test_pixel_shuffle_mid_graph(c, h, w):
+    """Pixel shuffle / unshuffle between two other operators (not folded into
+    the NCHW <-> NHWC boundary): 16-byte vector kernels for r = 2 when the
+    8-channel blocks allow (c % 32 for the shuffle, c % 8 for the unshuffle),
+    element kernels otherwise; CRD order bit-exact against the oracle."""
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, h, w])
+    one = gb.weight("one", np.ones((1, 1, 1, 1), np.float16))
+    shuffled = gb.depth_to_space(gb.mul(x, one), 2)
+    gb.output(gb.mul(shuffled, one), "shuffled")
+    unshuffled = gb.space_to_depth(gb.mul(x, one), 2)
+    gb.output(gb.mul(unshuffled, one), "unshuffled")
+    inputs = [np.arange(c * h * w, dtype=np.float32).reshape(1, c, h, w).astype(np.float16)]
+    got, want, be = run_both(gb, inputs)
+    bits_equal(got[0], want[0])
+    bits_equal(got[1], want[1])
+    kernels = {s["kernel"] for s in be.steps()}
+    assert ("mlvc_depth_to_space_r2_v8_f16" in kernels) == (c % 32 == 0), kernels
+    assert ("mlvc_space_to_depth_r2_v8_f16" in kernels) == (c % 8 == 0), kernels
+
+
 def test_reglu_standalone():
     gb = GraphBuilder()
     x = gb.input("x", [1, 48, 5, 7])
