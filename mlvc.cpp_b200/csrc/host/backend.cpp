@@ -1175,7 +1175,7 @@ void Backend::plan()
             }
             const bool depthwise = G == IC && OC == IC && ICG == 1 && IC % 8 == 0 && epi == kEpiBias;
             if (depthwise && dw_fusion_ && N == 1 && KH == 3 && KW == 3 && SH == 1 && SW == 1 && PH == 1 && PW == 1 &&
-                IC % 64 == 0 && IC <= 256 && i + 1 < nodes.size()) {
+                IC % 64 == 0 && IC <= 512 && i + 1 < nodes.size()) {
                 // ---- fused depthwise 3x3 + the 1x1 conv that consumes it: the
                 // depthwise result is the GEMM's A operand in shared memory
                 const NodeDesc& n2 = nodes[i + 1];
@@ -1269,9 +1269,10 @@ void Backend::plan()
                         else
                             p.map_res = p.map_out;
                         {
+                            // [10][C], loaded as dw_tap_group(C)-channel boxes that tile C exactly
                             const cuuint64_t dims[2] = {static_cast<cuuint64_t>(IC), 10};
                             const cuuint64_t strides[1] = {static_cast<cuuint64_t>(IC) * 2};
-                            const cuuint32_t box[2] = {static_cast<cuuint32_t>(IC), 10};
+                            const cuuint32_t box[2] = {static_cast<cuuint32_t>(dw_tap_group(IC)), 10};
                             check(cuTensorMapEncodeTiled(&dwp_.map_dw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                                                          reinterpret_cast<void*>(prepped_dev_.get() + dww_off), dims,
                                                          strides, box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,

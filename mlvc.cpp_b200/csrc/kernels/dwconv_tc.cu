@@ -66,8 +66,12 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
     uint8_t* w_smem = a_smem + static_cast<size_t>(p.a_stages) * kDwPanelBytes;
     uint8_t* h_smem = w_smem + static_cast<size_t>(p.b_stages) * w_bytes;
     uint8_t* stage_smem = h_smem + static_cast<size_t>(dp.h_stages) * halo_stride;  // 1024-aligned
-    // depthwise taps [9][C] and bias [C], FP16, loaded once per CTA by TMA
+    // depthwise taps and bias, FP16, loaded once per CTA by TMA in groups of
+    // tg = dw_tap_group(C) channels (a TMA box dimension is at most 256; the
+    // groups tile C exactly): group g holds rows [10][tg] (rows 0..8: tap
+    // ky * 3 + kx, row 9: bias) of channels g * tg .. g * tg + tg - 1
     const uint8_t* dw_smem = stage_smem + static_cast<size_t>(p.BN / 64) * kTcStagePanelBytes;
+    const int tg = dw_tap_group(p.K);
 
     if (threadIdx.x == 0) {
         if (p.trace)
@@ -128,7 +132,9 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
             // The weights do not depend on the previous kernel.
             ArmedSlots dw_armed;
             mbar_arrive_expect_tx(&sh->dw_full, static_cast<uint32_t>(10 * p.K * 2));
-            tma_load_2d(const_cast<uint8_t*>(dw_smem), &dp.map_dw, &sh->dw_full, 0, 0);
+            for (int g = 0; g * tg < p.K; ++g)
+                tma_load_2d(const_cast<uint8_t*>(dw_smem) + static_cast<size_t>(g) * 10 * tg * 2, &dp.map_dw,
+                            &sh->dw_full, g * tg, 0);
             dw_armed.arm(0, 0);
             int w_issued = 0;
             if (first < tiles)
@@ -261,10 +267,12 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 }
                 tc_fence_after();
                 const int ch = kp * 64 + cq * 8;
+                // channel ch in the taps' group layout
+                const uint8_t* taps = dw_smem + (static_cast<size_t>(ch / tg) * 10 * tg + ch % tg) * 2;
                 float acc4[4][8];
                 {
                     float b8[8];
-                    const uint4 bv = *reinterpret_cast<const uint4*>(dw_smem + (9 * p.K + ch) * 2);
+                    const uint4 bv = *reinterpret_cast<const uint4*>(taps + 9 * tg * 2);
                     const uint32_t* bw = reinterpret_cast<const uint32_t*>(&bv);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
@@ -279,7 +287,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 uint32_t wv[9][4];
 #pragma unroll
                 for (int tap = 0; tap < 9; ++tap) {
-                    const uint4 q = *reinterpret_cast<const uint4*>(dw_smem + (tap * p.K + ch) * 2);
+                    const uint4 q = *reinterpret_cast<const uint4*>(taps + tap * tg * 2);
                     wv[tap][0] = q.x;
                     wv[tap][1] = q.y;
                     wv[tap][2] = q.z;

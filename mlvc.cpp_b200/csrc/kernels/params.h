@@ -135,6 +135,20 @@ constexpr int kDwTileW = 16, kDwTileH = 8;                        // output tile
 constexpr int kDwHaloPx = (kDwTileW + 2) * (kDwTileH + 2);        // 180 halo pixels per slice
 constexpr int kDwHaloBytes = (kDwHaloPx * 128 + 1023) / 1024 * 1024;  // one 64-channel halo slice in smem
 
+// Channels per depthwise-taps TMA box of mlvc_dwconv_tc: the largest multiple
+// of 64 that is at most 256 (a box dimension limit) and divides C, so the
+// boxes tile [10][C] exactly (C a multiple of 64).
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline int dw_tap_group(int c)
+{
+    for (int t = 256; t >= 64; t -= 64)
+        if (c % t == 0)
+            return t;
+    return 64;
+}
+
 struct DwConvTcParams {
     // map_b = W [C_out rows, C] (C_out x 64 boxes, 128-byte swizzle);
     // map_out / map_res / bias / epilogue / alpha describe the 1x1 conv's

@@ -176,13 +176,14 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
 def test_plan_mlvc_decoder_standin():
     """The MLVC-shaped stand-in plans on the tensor-core path: every 1x1 conv
     (256-channel blocks, up-sampling convs) on tcgen05, LeakyReLU / residual /
-    ReGLU in the conv epilogues, depthwise on the bandwidth kernel; graph I/O as
-    documented for the decoder."""
+    ReGLU in the conv epilogues, each 512-channel depthwise fused with the
+    projection after it (+ residual); graph I/O as documented for the decoder."""
     gb, inputs = build_mlvc_decoder_standin(width=640, height=368)
     graph, weights = gb.finish()
     be = plan(graph, weights)
     k = _kernels(be)
-    assert k.count("mlvc_conv1x1_tc") == 36 and k.count("mlvc_depthwise3x3_f16") == 7, k
+    assert k.count("mlvc_conv1x1_tc") == 29 and k.count("mlvc_dwconv_tc") == 7, k
+    assert "mlvc_depthwise3x3_f16" not in k
     assert "mlvc_conv_direct_f16" not in k and "mlvc_unary_f16" not in k and "mlvc_reglu_f16" not in k
     assert [tuple(s) for _, _, s in be.inputs] == [(1, 128, 3, 5), (1, 64, 23, 40), (1, 64, 23, 40),
                                                      (1, 256, 46, 80), (1,)]
@@ -230,7 +231,9 @@ def test_plan_mbconv_needs_single_consumers():
     (64, 64, 4, 2000, True),    # wide image (2-D tiles: any width)
     (48, 64, 8, 8, False),      # channels not a multiple of 64
     (64, 96, 8, 8, False),      # output channels not a multiple of 64
-    (320, 128, 8, 8, False),    # depthwise taps beyond one TMA box row (C > 256)
+    (512, 256, 8, 8, True),     # taps in two 256-channel TMA boxes
+    (320, 128, 8, 8, True),     # taps in a 256- and a 64-channel box
+    (576, 128, 8, 8, False),    # more channels than the kernel takes (C > 512)
 ])
 def test_plan_depthwise_fusion_predicates(c, c_out, h, w, fused):
     gb = GraphBuilder()

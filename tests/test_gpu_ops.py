@@ -136,6 +136,8 @@ DW_CASES = [  # (C, C_out, H, W, epilogue of the 1x1 conv)
     (128, 128, 9, 300, "leaky"),      # wide image
     (64, 64, 160, 160, "residual"),   # 200 tiles: two tiles per CTA
     (64, 256, 8, 8, None),            # 256 output columns (four staging panels)
+    (512, 256, 34, 60, "residual"),   # taps in two 256-channel boxes (MLVC-width block)
+    (320, 128, 13, 21, None),         # taps in a 256- and a 64-channel box
 ]
 
 
