@@ -931,7 +931,7 @@ void Backend::plan()
                 };
                 int best = 0, ctas_per_sm = 1;
                 for (int bn : cands)
-                    if (bn <= 128 && stages_for(bn, kTwoCtaSmem) >= 2 && m_tiles * (NN / bn) >= sm_count_) {
+                    if (!best && bn <= 128 && stages_for(bn, kTwoCtaSmem) >= 2 && m_tiles * (NN / bn) >= sm_count_) {
                         best = bn;
                         ctas_per_sm = 2;
                         break;
@@ -951,6 +951,19 @@ void Backend::plan()
                         }
                 if (!best && !cands.empty())
                     best = cands.back() >= 64 ? cands.back() : cands.front();
+                {
+                    // tuning override (sweeps): MLVC_B200_CONV1X1_BN = N tile when it is a
+                    // candidate, MLVC_B200_CONV1X1_CTAS = CTAs per SM (1 or 2)
+                    const char* e_bn = std::getenv("MLVC_B200_CONV1X1_BN");
+                    const char* e_ct = std::getenv("MLVC_B200_CONV1X1_CTAS");
+                    if (e_bn && std::find(cands.begin(), cands.end(), std::atoi(e_bn)) != cands.end()) {
+                        best = std::atoi(e_bn);
+                        ctas_per_sm = 1;
+                    }
+                    if (e_ct && (std::atoi(e_ct) == 1 ||
+                                 (std::atoi(e_ct) == 2 && best <= 128 && stages_for(best, kTwoCtaSmem) >= 2)))
+                        ctas_per_sm = std::atoi(e_ct);
+                }
                 if (best) {
                     const int BN = best, n_tiles = NN / BN;
                     std::vector<uint16_t> wp(static_cast<size_t>(NN) * K, 0), bp(NN, 0);
@@ -965,13 +978,29 @@ void Backend::plan()
                     }
                     const size_t w_off = prep(wp.data(), wp.size() * 2);
                     const size_t b_off = prep(bp.data(), bp.size() * 2);
-                    const int a_stages =
+                    int a_stages =
                         std::min(8, ctas_per_sm == 2 ? stages_for(BN, kTwoCtaSmem) : stages_for(BN, smem_cap + 1024));
+                    // Two output staging buffers when at least four A stages remain: a
+                    // tile's rows are then written while the previous tile's TMA store
+                    // still reads the other buffer (MLVC_B200_STAGE_BUFS=1: one buffer).
+                    int stage_bufs = 1;
+                    {
+                        const int cap = ctas_per_sm == 2 ? kTwoCtaSmem : smem_cap + 1024;
+                        const int with2 = (cap - header - 1024 - 2 * stage_for(BN) - k_panels * BN * 128) / 16384;
+                        const char* e = std::getenv("MLVC_B200_STAGE_BUFS");
+                        if (!(e && e[0] == '1') && with2 >= 4) {
+                            stage_bufs = 2;
+                            a_stages = std::min(8, with2);
+                        }
+                    }
+                    if (a_stages < 2)  // the A ring needs two slots (load one while the MMA reads the other)
+                        throw std::runtime_error("mlvc-b200: conv1x1 plan leaves fewer than two A stages");
                     const int slots = sm_count_ * ctas_per_sm;
                     const int grid = n_tiles * std::max(1, std::min(m_tiles, slots / n_tiles));
                     s.kernel = "mlvc_conv1x1_tc";
                     s.info.kernel = s.kernel;
-                    s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 + stage_for(BN) + 1024);
+                    s.smem = static_cast<unsigned>(header + k_panels * BN * 128 + a_stages * 16384 +
+                                                   stage_bufs * stage_for(BN) + 1024);
                     s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     const int M = IH * IW;
@@ -1023,6 +1052,7 @@ void Backend::plan()
                         p.clip_lo = lo;
                         p.clip_hi = hi;
                         p.a_stages = a_stages;
+                        p.stage_bufs = stage_bufs;
                         st.set(p);
                     };
                     steps_.push_back(std::move(s));

@@ -205,13 +205,17 @@ __device__ __forceinline__ void epilogue_rows(const ConvTcParams& p, const float
     }
 }
 
-// Leader thread, before a tile's rows are written: the previous tile's stores
-// must have read the staging buffer; then the residual tile is loaded into it
-// (load_residual) or the buffer is simply released.
+// Leader thread, before a tile's rows are written: the stores that last used
+// this staging buffer must have read it (with two buffers the previous tile's
+// store may still be reading the other one); then the residual tile is loaded
+// into it (load_residual) or the buffer is simply released.
 __device__ __forceinline__ void stage_prepare(const ConvTcParams& p, uint8_t* stage, int panels, int col0,
                                               const TileCoord& tc, bool kxk, bool load_residual, uint64_t* ready)
 {
-    bulk_wait_read<0>();
+    if (p.stage_bufs == 2)
+        bulk_wait_read<1>();
+    else
+        bulk_wait_read<0>();
     if (load_residual) {
         mbar_arrive_expect_tx(ready, static_cast<uint32_t>(panels) * 16384u);
         tile_copy(&p.map_res, true, stage, panels, col0, tc, kxk, ready);
@@ -274,10 +278,12 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
         tc.pixel0 = m_tile * kBM;
         tc.oy = m_tile / tiles_per_row;
         tc.ox0 = (m_tile % tiles_per_row) * kBM;
+        // staging buffer of this tile (two alternate when the host gave two)
+        uint8_t* st = stage + (p.stage_bufs == 2 ? static_cast<size_t>(it & 1u) * panels * kTcStagePanelBytes : 0);
         if (leader)
-            stage_prepare(p, stage, panels, n_tile * out_cols, tc, kxk, p.epilogue == kEpiResidual, ss.ready);
+            stage_prepare(p, st, panels, n_tile * out_cols, tc, kxk, p.epilogue == kEpiResidual, ss.ready);
         if (!epilogue_tile(p, sh.bias, sh.tmem_base + acc * p.BN, &sh.tmem_full[acc], acc_phase, &sh.tmem_empty[acc],
-                           ss, it, stage, nullptr, panels, n_tile * out_cols, tc, kxk, quadrant, group, lane, leader,
+                           ss, it, st, nullptr, panels, n_tile * out_cols, tc, kxk, quadrant, group, lane, leader,
                            &sh.abort_flag))
             break;
         if (t == first_tile && leader)
