@@ -567,6 +567,36 @@ void Backend::plan()
         return 1;
     };
 
+    // Channel concats read in place by the 1x1 conv right after them: a Concat
+    // of two NHWC tensors (channels multiples of 64) whose only consumer is the
+    // next node, a plain 1x1 conv with tensor-core output channels, is not
+    // materialised; the conv streams its K panels from both tensors
+    // (ConvTcParams::a_split).
+    struct ConcatSrc {
+        uint32_t a, b;
+        int c1;
+    };
+    std::map<uint32_t, ConcatSrc> concat_src;  // concat output -> its two sources
+    for (size_t j = 0; j + 1 < nodes.size(); ++j) {
+        const NodeDesc& c = nodes[j];
+        const NodeDesc& v = nodes[j + 1];
+        if (c.op != Op::kConcat || absorbed[j] || c.inputs.size() != 2 || v.op != Op::kConv ||
+            v.inputs[0] != c.output || !only_consumer(c.output))
+            continue;
+        const Value &o = values_[c.output], &va = values_[c.inputs[0]], &vb = values_[c.inputs[1]];
+        if (!o.nhwc || !va.nhwc || !vb.nhwc || o.shape.size() != 4 || o.shape[0] != 1 || va.shape.size() != 4 ||
+            vb.shape.size() != 4 || (c.axis != 1 && c.axis != -3))
+            continue;
+        const int c1 = static_cast<int>(va.shape[1]), c2 = static_cast<int>(vb.shape[1]);
+        const Value& wv = values_[v.inputs[1]];
+        if (c1 % 64 || c2 % 64 || c1 + c2 > 1024 || v.groups != 1 || v.strides[0] != 1 || v.strides[1] != 1 ||
+            v.pads[0] != 0 || v.pads[1] != 0 || wv.kind != Value::kWeight || wv.dtype != DType::kFp16 ||
+            wv.shape.size() != 4 || wv.shape[1] != c1 + c2 || wv.shape[2] != 1 || wv.shape[3] != 1 || wv.shape[0] % 8)
+            continue;
+        concat_src[c.output] = {c.inputs[0], c.inputs[1], c1};
+        absorbed[j] = true;
+    }
+
     for (size_t i = 0; i < nodes.size();) {
         const NodeDesc& n = nodes[i];
         if (absorbed[i]) {
@@ -608,8 +638,10 @@ void Backend::plan()
             if (bias)
                 std::copy(bias, bias + OC, bias_full.begin());
 
+            const auto split_it = concat_src.find(x_id);
+            const bool split_a = split_it != concat_src.end();  // x is a concat read in place (1x1 path only)
             Step s;
-            s.reads = {x_id};
+            s.reads = split_a ? std::vector<uint32_t>{split_it->second.a, split_it->second.b} : std::vector<uint32_t>{x_id};
             if (res_id)
                 s.reads.push_back(res_id);
             s.writes = {out_id};
@@ -628,7 +660,7 @@ void Backend::plan()
             const bool tc_shape = G == 1 && N == 1 && IC % 8 == 0 && OC % 8 == 0 && (!reglu || OC % 64 == 0);
             const int header = kTcHeaderBytes;
             const int smem_cap = max_smem_optin_ - 1024;  // slack for the in-kernel 1024-byte alignment
-            if (reglu && tc_shape && is1x1 && ffn_fusion_ && i + 5 < nodes.size() && IC % 64 == 0 && IC <= 256 &&
+            if (reglu && tc_shape && is1x1 && ffn_fusion_ && !split_a && i + 5 < nodes.size() && IC % 64 == 0 && IC <= 256 &&
                 (OC / 2) % kFfnChunk == 0 && OC / 2 <= kFfnMaxHidden) {
                 // ---- fused feed-forward block: this ReGLU conv and the 1x1 conv that
                 // consumes its output, with the hidden tensor kept on chip
@@ -756,7 +788,7 @@ void Backend::plan()
                     continue;
                 }
             }
-            if (tc_shape && is1x1 && !reglu && mb_fusion_ && (epi == kEpiBias || epi == kEpiLeaky) && IC % 64 == 0 &&
+            if (tc_shape && is1x1 && !reglu && mb_fusion_ && !split_a && (epi == kEpiBias || epi == kEpiLeaky) && IC % 64 == 0 &&
                 IC <= 128 && OC % 64 == 0 && OC <= kMbMaxExpand && i + consumed + 1 < nodes.size()) {
                 // ---- fused inverted-residual block: this expand conv, the depthwise
                 // 3x3 that consumes it and the 1x1 projection of the depthwise
@@ -1004,21 +1036,26 @@ void Backend::plan()
                     s.block = 320;
                     s.grid = static_cast<unsigned>(grid);
                     const int M = IH * IW;
+                    // A sources: x itself, or the two tensors of a concat read in place
+                    const uint32_t a0_id = split_a ? split_it->second.a : x_id;
+                    const uint32_t a1_id = split_a ? split_it->second.b : 0;
+                    const int c0 = split_a ? split_it->second.c1 : K;
                     s.build = [=, this](Step& st) {
                         ConvTcParams p{};
                         const CUdeviceptr wdev = prepped_dev_.get() + w_off;
                         const cuuint32_t elem1[2] = {1, 1};
-                        {
-                            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+                        auto encode_a = [&](CUtensorMap* map, uint32_t id, int channels, const char* what) {
+                            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(M)};
+                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(channels) * 2};
                             const cuuint32_t box[2] = {64, 128};
-                            check(cuTensorMapEncodeTiled(&p.map_a0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                                                         reinterpret_cast<void*>(values_[x_id].addr), dims, strides,
-                                                         box, elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            check(cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                                         reinterpret_cast<void*>(values_[id].addr), dims, strides, box,
+                                                         elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
-                                  "cuTensorMapEncodeTiled(conv1x1 A)");
-                        }
+                                  what);
+                        };
+                        encode_a(&p.map_a0, a0_id, c0, "cuTensorMapEncodeTiled(conv1x1 A)");
                         {
                             const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(NN)};
                             const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
@@ -1030,7 +1067,12 @@ void Backend::plan()
                                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
                                   "cuTensorMapEncodeTiled(conv1x1 B)");
                         }
-                        p.map_a1 = p.map_a0;
+                        if (a1_id) {
+                            encode_a(&p.map_a1, a1_id, K - c0, "cuTensorMapEncodeTiled(conv1x1 A, second concat operand)");
+                            p.a_split = c0 / 64;
+                        } else {
+                            p.map_a1 = p.map_a0;
+                        }
                         encode_tile_map(&p.map_out, values_[out_id].addr, reglu ? OC / 2 : OC, M, 0, 0,
                                         "cuTensorMapEncodeTiled(conv1x1 out)");
                         if (res_id)
@@ -1335,6 +1377,8 @@ void Backend::plan()
                     continue;
                 }
             }
+            if (split_a)  // the pre-pass only defers concats for convs with a tensor-core 1x1 plan
+                throw std::runtime_error("mlvc-b200: internal: concat read in place by a conv without a 1x1 plan");
             DirectConvParams dp{};
             dp.n = N;
             dp.ih = IH;

@@ -322,6 +322,8 @@ __device__ __forceinline__ TcShared* setup_shared(uint8_t* smem_raw, const ConvT
     }
     if (warp == 0 && elect_one()) {
         tma_prefetch_desc(&p.map_a0);
+        if (p.a_split)
+            tma_prefetch_desc(&p.map_a1);
         tma_prefetch_desc(&p.map_b);
         tma_prefetch_desc(&p.map_out);
         if (p.epilogue == kEpiResidual)
@@ -427,7 +429,10 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                     if (!mbar_wait(&sh->a_empty[stage], phase ^ 1u, &sh->abort_flag, kErrWaitProducer))
                         break;
                     mbar_arrive_expect_tx(&sh->a_full[stage], kAPanelBytes);
-                    tma_load_2d(a_smem + stage * kAPanelBytes, &p.map_a0, &sh->a_full[stage], kp * 64, m_tile * kBM);
+                    // K panels past a_split come from the second tensor of a concat
+                    const bool second = p.a_split > 0 && kp >= p.a_split;
+                    tma_load_2d(a_smem + stage * kAPanelBytes, second ? &p.map_a1 : &p.map_a0, &sh->a_full[stage],
+                                (second ? kp - p.a_split : kp) * 64, m_tile * kBM);
                     a_armed.arm(stage, phase);
                     if (++stage == p.a_stages) {
                         stage = 0;

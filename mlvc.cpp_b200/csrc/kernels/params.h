@@ -63,6 +63,8 @@ struct ConvTcParams {
     int kh, kw, stride, pad;
     int halo_px;                // pixels (or pixel pairs) per halo row
     int px_min;                 // leftmost halo offset relative to the tile start (<= 0)
+    int a_split;                // 1x1: K panels from this index on come from map_a1 (a channel concat of two
+                                // tensors read in place); 0: all from map_a0
     int stage_bufs;             // 1x1 / k x k: output staging buffers (2: a tile's rows are written while the
                                 // previous tile's TMA store still reads the other buffer; 0 or 1: one)
     // Optional phase trace (null in normal runs): kTracePoints %globaltimer

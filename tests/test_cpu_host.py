@@ -173,6 +173,27 @@ def test_plan_block_stack_fuses_like_the_reference(monkeypatch):
     assert "6-10" in nodes  # conv + slice + slice + clip + mul
 
 
+@pytest.mark.parametrize("c1,c2,oc,other_reader,absorbed", [
+    (128, 128, 256, False, True), (64, 192, 64, False, True),
+    (96, 128, 64, False, False),   # first operand not a multiple of 64 channels
+    (128, 128, 256, True, False),  # the concat has another reader
+])
+def test_plan_concat_read_in_place_by_1x1(c1, c2, oc, other_reader, absorbed):
+    """A channel concat whose only reader is the 1x1 conv right after it is
+    not materialised: the conv reads its K panels from both tensors."""
+    gb = GraphBuilder()
+    a = gb.input("a", [1, c1, 6, 20])
+    b = gb.input("b", [1, c2, 6, 20])
+    cat = gb.concat([a, b], 1)
+    gb.output(gb.conv(cat, gb.weight("w", np.zeros((oc, c1 + c2, 1, 1), np.float16))), "y")
+    if other_reader:
+        gb.output(gb.leaky_relu(cat, 0.1), "z")
+    k = _kernels(plan(*gb.finish()))
+    copies = sum(1 for x in k if x.startswith("mlvc_strided_copy"))
+    assert (copies == 0) == absorbed, k
+    assert "mlvc_conv1x1_tc" in k
+
+
 def test_plan_mlvc_decoder_standin():
     """The MLVC-shaped stand-in plans on the tensor-core path: every 1x1 conv
     (256-channel blocks, up-sampling convs) on tcgen05, LeakyReLU / residual /

@@ -374,6 +374,35 @@ def test_pixel_shuffle_order(factor):
     bits_equal(got[1], inputs[0])
 
 
+@pytest.mark.parametrize("c1,c2,oc,epilogue", [(128, 128, 256, "leaky"), (64, 192, 96, None), (256, 256, 256, "residual"),
+                                                (128, 64, 256, "reglu")])
+def test_conv1x1_concat_read_in_place(c1, c2, oc, epilogue):
+    """Concat -> 1x1 conv with the concat never materialised (the conv streams
+    its K panels from both tensors): parity with the oracle."""
+    rng = np.random.default_rng(23)
+    h, w = 23, 40
+    gb = GraphBuilder()
+    a = gb.input("a", [1, c1, h, w])
+    b = gb.input("b", [1, c2, h, w])
+    wt = gb.weight("w", (rng.standard_normal((oc, c1 + c2, 1, 1), dtype=np.float32) *
+                         np.sqrt(1.0 / (c1 + c2))).astype(np.float16))
+    y = gb.conv(gb.concat([a, b], 1), wt, gb.weight("bias", rng.uniform(-0.1, 0.1, oc).astype(np.float16)))
+    inputs = [rng.standard_normal((1, c, h, w), dtype=np.float32).astype(np.float16) for c in (c1, c2)]
+    if epilogue == "leaky":
+        y = gb.leaky_relu(y, 0.01)
+    elif epilogue == "residual":
+        y = gb.add(y, gb.input("r", [1, oc, h, w]))
+        inputs.append(rng.standard_normal((1, oc, h, w), dtype=np.float32).astype(np.float16))
+    elif epilogue == "reglu":  # node order of the exported ReGLU tail: slice, slice, clip, mul
+        gate, lin = gb.slice(y, 1, 0, oc // 2), gb.slice(y, 1, oc // 2, oc)
+        y = gb.mul(gb.clip(gate, 0.0, 1.0), lin)
+    gb.output(y, "y")
+    got, want, be = run_both(gb, inputs)
+    compare(got[0], want[0])
+    kernels = [s["kernel"] for s in be.steps() if s["kernel"] != "mlvc_boundary_f16"]
+    assert kernels == ["mlvc_conv1x1_tc"], kernels
+
+
 @pytest.mark.parametrize("c,h,w", [(64, 6, 10), (32, 4, 14), (24, 4, 6)])
 def test_pixel_shuffle_mid_graph(c, h, w):
     """Pixel shuffle / unshuffle between two other operators (not folded into
