@@ -1987,15 +1987,36 @@ void Backend::plan()
             continue;
         steps_.push_back(boundary_step(id, output_source[k].first, output_source[k].second, true, k));
     }
+    state_alias_.assign(bindings_.size(), false);
     for (const auto& b : bindings_) {
         const uint32_t out_id = graph_.outputs[b.output_index];
+        const uint32_t in_id = graph_.inputs[b.input_index];
+        const size_t bi = static_cast<size_t>(&b - bindings_.data());
+        // The output aliases the state buffer (the reference's contract: state
+        // aliases the final node's output) when every step that reads the state
+        // input runs before the first step that writes the output; otherwise it
+        // is copied into the state buffer after the frame.
+        long long last_read = -1, first_write = -1;
+        for (size_t k = 0; k < steps_.size(); ++k) {
+            for (uint32_t r : steps_[k].reads)
+                if (r == in_id)
+                    last_read = static_cast<long long>(k);
+            for (uint32_t w : steps_[k].writes)
+                if (w == out_id && first_write < 0)
+                    first_write = static_cast<long long>(k);
+        }
+        if (first_write >= 0 && last_read < first_write && values_[out_id].bytes == values_[in_id].bytes &&
+            values_[out_id].nhwc == values_[in_id].nhwc && values_[out_id].kind != Value::kWeight &&
+            values_[out_id].kind != Value::kInput && values_[out_id].kind != Value::kState) {
+            state_alias_[bi] = true;
+            continue;
+        }
         Step s;
         s.type = Step::kCopy;
         s.kernel = "state-copy";
         s.info.kernel = s.kernel;
         s.info.nodes = "state:" + graph_.tensors[out_id].name;
         s.reads = {out_id};
-        const size_t bi = static_cast<size_t>(&b - bindings_.data());
         s.build = [this, out_id, bi](Step& st) {
             st.src = values_[out_id].addr;
             st.dst = state_dev_.at(bi).get();
@@ -2114,6 +2135,9 @@ void Backend::build_schedule()
         else if (v.kind == Value::kWeight)
             v.addr = weights_dev_.get() + v.weight_off;
     }
+    for (size_t bi = 0; bi < bindings_.size(); ++bi)
+        if (bi < state_alias_.size() && state_alias_[bi])
+            values_[graph_.outputs[bindings_[bi].output_index]].addr = state_dev_.at(bi).get();
     for (auto id : graph_.outputs)
         if (!values_[id].addr &&
             std::find(absorbed_outputs_.begin(), absorbed_outputs_.end(), id) == absorbed_outputs_.end())

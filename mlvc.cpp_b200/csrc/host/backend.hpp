@@ -134,6 +134,9 @@ private:
     GraphDesc graph_;
     std::vector<uint8_t> weights_host_;
     std::vector<StateBinding> bindings_;
+    // per binding: the bound output is written straight into the state buffer
+    // (every read of the state input precedes the first write of the output)
+    std::vector<bool> state_alias_;
     std::vector<size_t> ext_inputs_;   // indices into graph_.inputs
     std::vector<size_t> ext_outputs_;  // indices into graph_.outputs
     std::vector<uint32_t> absorbed_outputs_;  // outputs written straight into host staging

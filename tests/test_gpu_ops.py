@@ -474,6 +474,45 @@ def test_state_binding_and_slots():
         bits_equal(be.slot_output(slot, 0), outs[i])
 
 
+def test_state_output_written_in_place():
+    """When every read of the state input precedes the step that writes the
+    bound output, the output is written straight into the state buffer (no
+    copy step; the reference requires the state to alias the final node's
+    output): frames still chain through the state exactly as with a copy."""
+    rng = np.random.default_rng(12)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 64, 6, 10])
+    ref = gb.input("ref", [1, 64, 6, 10])
+    w1 = gb.weight("w1", (rng.standard_normal((64, 64, 1, 1), dtype=np.float32) * 0.1).astype(np.float16))
+    w2 = gb.weight("w2", (rng.standard_normal((64, 64, 1, 1), dtype=np.float32) * 0.1).astype(np.float16))
+    y = gb.leaky_relu(gb.add(gb.conv(x, w1), ref), 0.1)  # last read of the state
+    feat = gb.conv(y, w2)                                # written after it
+    gb.output(y, "y")
+    gb.output(feat, "feature")
+    graph, weights = gb.finish()
+    be = Backend(0)
+    be.load_memory(graph, weights, [(1, 1)])
+    assert "state-copy" not in {s["kernel"] for s in be.steps()}
+    be.reset_state()
+    oracle = GraphOracle(graph, weights)
+    state = np.zeros((1, 64, 6, 10), np.float16)
+    frames = [_rand((1, 64, 6, 10), 20 + i) for i in range(3)]
+    outs = []
+    for f in frames:
+        (got,) = be.run([f])
+        want_y, want_feat = oracle.run([f, state])
+        compare(got, want_y)
+        state = want_feat
+        outs.append(got)
+    be.reset_state()
+    be.configure_slots(2)
+    for i, f in enumerate(frames):
+        be.slot_input(i % 2, 0)[...] = f
+        be.submit(i % 2)
+        be.wait_slot(i % 2)
+        bits_equal(be.slot_output(i % 2, 0), outs[i])
+
+
 def test_slot_pipeline_overlapped_frames():
     """Two slots in flight (host->device of one frame, the schedule of the
     previous one and its device->host copy overlap on separate streams):
