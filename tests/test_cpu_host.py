@@ -194,6 +194,28 @@ def test_plan_concat_read_in_place_by_1x1(c1, c2, oc, other_reader, absorbed):
     assert "mlvc_conv1x1_tc" in k
 
 
+@pytest.mark.parametrize("state_read_last", [False, True])
+def test_plan_state_output_aliases_state_buffer(state_read_last):
+    """A state-bound output is written in place into the state buffer when
+    every read of the state input precedes its first write; when a later step
+    still reads the state, the output is copied after the frame."""
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 64, 6, 10])
+    ref = gb.input("ref", [1, 64, 6, 10])
+    w = gb.weight("w", np.zeros((64, 64, 1, 1), np.float16))
+    y = gb.leaky_relu(gb.add(gb.conv(x, w), ref), 0.1)
+    feat = gb.conv(y, w)
+    if state_read_last:
+        gb.output(gb.add(feat, ref), "y")  # reads the state after the output is written
+    else:
+        gb.output(y, "y")
+    gb.output(feat, "feature")
+    graph, weights = gb.finish()
+    be = Backend(plan_only_for=B200)
+    be.load_memory(graph, weights, [(1, 1)])
+    assert ("state-copy" in _kernels(be)) == state_read_last
+
+
 def test_plan_mlvc_decoder_standin():
     """The MLVC-shaped stand-in plans on the tensor-core path: every 1x1 conv
     (256-channel blocks, up-sampling convs) on tcgen05, LeakyReLU / residual /
