@@ -123,6 +123,44 @@ int mlvc_b200_slot_input_yuv(mlvc_b200_backend* backend, size_t slot, uint8_t** 
 int mlvc_b200_slot_output_yuv(const mlvc_b200_backend* backend, size_t slot, const uint8_t** y, const uint8_t** u,
                               const uint8_t** v);
 
+/* Entropy-coder inputs on the GPU.  These need a backend from
+ * mlvc_b200_create but no loaded graph.
+ *
+ * mlvc_b200_scale_config carries the mlvc::ModelConfig fields that
+ * extract_scales reads (core/include/mlvc/core/model.hpp; plane sizes of
+ * core/src/model.cpp:94-126: ceil(model size / downsample_latent) for the
+ * latent plane, ceil(model size / (downsample_latent * downsample_hyperprior))
+ * for the hyper-latent plane) and the scale table's last index
+ * (GaussianPmf::scale_levels - 1, core/src/entropy.cpp:389-391). */
+typedef struct mlvc_b200_scale_config {
+    int32_t hyperprior_channels;
+    int32_t model_width;
+    int32_t model_height;
+    int32_t latent_channels;
+    int32_t downsample_latent;
+    int32_t downsample_hyperprior;
+    int32_t y_scale_repeat;
+    int32_t scale_max_index;
+} mlvc_b200_scale_config;
+
+/* Element counts of z_raw [1][hyper][zh][zw] and of each scale plane
+ * [latent / 2][yh][yw] for `config`; validates it like extract_scales. */
+int mlvc_b200_scale_shape(const mlvc_b200_scale_config* config, size_t* z_count, size_t* scale_count);
+
+/* extract_scales(z_raw, config, scale_max_index, scales_0, scales_1)
+ * (core/include/mlvc/core/scales.hpp:15-19, core/src/scales.cpp:25-105):
+ * z_raw as FP16 bits (z_count elements, which must match the model's plane),
+ * scales_0 / scales_1 with room for scale_count int32 each.  Errors carry the
+ * reference's messages. */
+int mlvc_b200_extract_scales(mlvc_b200_backend* backend, const uint16_t* z_raw, size_t z_count,
+                             const mlvc_b200_scale_config* config, int32_t* scales_0, int32_t* scales_1,
+                             size_t scale_count);
+
+/* integer_values(tensor, result) (core/src/entropy.cpp:201-226): FP16 bits ->
+ * int32 by truncation; fails with "entropy symbol is outside signed 16-bit
+ * range" when a value is not finite or outside [-32768, 32767]. */
+int mlvc_b200_integer_values(mlvc_b200_backend* backend, const uint16_t* values, size_t count, int32_t* symbols);
+
 /* Measurement hooks (no reference counterpart; the reference times whole
  * runs with steady_clock, codec/src/pipeline.cpp:341-415).  enqueue replays
  * the captured schedule on the backend's stream with the device-resident

@@ -2381,6 +2381,88 @@ void Backend::reset_state()
     state_ready_ = true;
 }
 
+// ------------------------------------------------- entropy-coder inputs
+void Backend::scale_plane(const ScaleConfig& c, int* z_height, int* z_width, int* y_height, int* y_width)
+{
+    if (c.hyperprior_channels <= 0 || c.model_width <= 0 || c.model_height <= 0 || c.latent_channels <= 0 ||
+        c.downsample_latent <= 0 || c.downsample_hyperprior <= 0 || c.y_scale_repeat <= 0 || c.scale_max_index < 0)
+        throw std::runtime_error("mlvc-b200: scale configuration values must be positive");
+    auto ceil_div = [](long long a, long long b) { return static_cast<int>((a + b - 1) / b); };
+    const long long zf = static_cast<long long>(c.downsample_latent) * c.downsample_hyperprior;
+    *z_height = ceil_div(c.model_height, zf);
+    *z_width = ceil_div(c.model_width, zf);
+    *y_height = ceil_div(c.model_height, c.downsample_latent);
+    *y_width = ceil_div(c.model_width, c.downsample_latent);
+    const int half = c.latent_channels / 2, base = c.latent_channels / c.y_scale_repeat;
+    if (base > c.hyperprior_channels)
+        throw std::runtime_error("scale decoder channel mapping is invalid");
+    // The reference indexes its base table with (channel + half) / repeat
+    // without a bound; reject the configurations where that leaves the table.
+    if (half == 0 || (2 * half - 1) / c.y_scale_repeat >= base)
+        throw std::runtime_error("scale decoder channel mapping is invalid");
+}
+
+void Backend::extract_scales(const uint16_t* z, const ScaleConfig& cfg, int32_t* scales_0, int32_t* scales_1)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    int zh = 0, zw = 0, yh = 0, yw = 0;
+    scale_plane(cfg, &zh, &zw, &yh, &yw);
+    const size_t z_count = static_cast<size_t>(cfg.hyperprior_channels) * zh * zw;
+    const size_t out_count = static_cast<size_t>(cfg.latent_channels / 2) * yh * yw;
+    ContextGuard guard(ctx_);
+    DeviceBuffer z_dev(z_count * 2), s_dev(out_count * 2 * sizeof(int32_t));
+    check(cuMemcpyHtoDAsync(z_dev.get(), z, z_count * 2, stream_), "cuMemcpyHtoDAsync(z)");
+    ScaleParams sp{};
+    sp.z = reinterpret_cast<const mlvc_half*>(z_dev.get());
+    sp.scales_0 = reinterpret_cast<int32_t*>(s_dev.get());
+    sp.scales_1 = reinterpret_cast<int32_t*>(s_dev.get()) + out_count;
+    sp.z_height = zh;
+    sp.z_width = zw;
+    sp.latent = cfg.latent_channels;
+    sp.repeat = cfg.y_scale_repeat;
+    sp.y_height = yh;
+    sp.y_width = yw;
+    sp.spatial = cfg.downsample_hyperprior;
+    sp.max_index = cfg.scale_max_index;
+    void* args[] = {&sp};
+    const unsigned grid = blocks_for(static_cast<long long>(out_count), 256, sm_count_);
+    check(cuLaunchKernel(fn("mlvc_extract_scales"), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr),
+          "mlvc_extract_scales");
+    check(cuMemcpyDtoHAsync(scales_0, s_dev.get(), out_count * sizeof(int32_t), stream_), "cuMemcpyDtoHAsync(scales_0)");
+    check(cuMemcpyDtoHAsync(scales_1, s_dev.get() + out_count * sizeof(int32_t), out_count * sizeof(int32_t), stream_),
+          "cuMemcpyDtoHAsync(scales_1)");
+    check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
+}
+
+void Backend::integer_values(const uint16_t* values, size_t count, int32_t* symbols)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    if (count == 0)
+        return;
+    ContextGuard guard(ctx_);
+    DeviceBuffer src(count * 2), dst(count * sizeof(int32_t) + 16);
+    const CUdeviceptr flag = dst.get() + count * sizeof(int32_t);
+    check(cuMemsetD8Async(flag, 0, sizeof(uint32_t), stream_), "cuMemsetD8Async(flag)");
+    check(cuMemcpyHtoDAsync(src.get(), values, count * 2, stream_), "cuMemcpyHtoDAsync(values)");
+    IntegerValuesParams ip{};
+    ip.src = reinterpret_cast<const mlvc_half*>(src.get());
+    ip.dst = reinterpret_cast<int32_t*>(dst.get());
+    ip.count = static_cast<long long>(count);
+    ip.out_of_range = reinterpret_cast<unsigned int*>(flag);
+    void* args[] = {&ip};
+    const unsigned grid = blocks_for(static_cast<long long>(count), 256, sm_count_);
+    check(cuLaunchKernel(fn("mlvc_integer_values_f16"), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr),
+          "mlvc_integer_values_f16");
+    uint32_t bad = 0;
+    check(cuMemcpyDtoHAsync(&bad, flag, sizeof(bad), stream_), "cuMemcpyDtoHAsync(flag)");
+    check(cuMemcpyDtoHAsync(symbols, dst.get(), count * sizeof(int32_t), stream_), "cuMemcpyDtoHAsync(symbols)");
+    check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
+    if (bad)
+        throw std::runtime_error("entropy symbol is outside signed 16-bit range");
+}
+
 void Backend::configure_slots(size_t count)
 {
     if (offline_)

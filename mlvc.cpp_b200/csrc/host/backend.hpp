@@ -37,6 +37,18 @@ struct StateBinding {
     size_t output_index;
 };
 
+// Entropy-coder scale extraction parameters: the mlvc::ModelConfig fields
+// extract_scales reads (core/src/scales.cpp:25-105) plus the scale table's
+// last index (GaussianPmf::scale_levels - 1).
+struct ScaleConfig {
+    int hyperprior_channels;
+    int model_width, model_height;
+    int latent_channels;
+    int downsample_latent, downsample_hyperprior;
+    int y_scale_repeat;
+    int scale_max_index;
+};
+
 struct StepInfo {
     std::string kernel;
     std::string nodes;   // graph node indices covered by the step
@@ -68,6 +80,16 @@ public:
 
     void run(const HostTensorRef* inputs, size_t n_in, HostTensorRef* outputs, size_t n_out);
     void reset_state();
+
+    // Entropy-coder inputs computed on the GPU; they need no loaded graph.
+    // extract_scales: z [1][hyper][zh][zw] FP16 bits -> scales_0 / scales_1
+    // int32 [latent / 2][yh][yw] (zh = ceil(model_height / (downsample_latent
+    // * downsample_hyperprior)), yh = ceil(model_height / downsample_latent)).
+    // integer_values: FP16 bits -> int32 by truncation; throws the reference's
+    // error when a value is not finite or outside [-32768, 32767].
+    static void scale_plane(const ScaleConfig& cfg, int* z_height, int* z_width, int* y_height, int* y_width);
+    void extract_scales(const uint16_t* z, const ScaleConfig& cfg, int32_t* scales_0, int32_t* scales_1);
+    void integer_values(const uint16_t* values, size_t count, int32_t* symbols);
 
     // Slot path: pinned host staging per slot, asynchronous submit, wait.
     void configure_slots(size_t count);

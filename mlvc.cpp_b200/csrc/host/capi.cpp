@@ -174,6 +174,56 @@ int mlvc_b200_reset_state(mlvc_b200_backend* backend)
     return guarded([&] { require(backend).reset_state(); });
 }
 
+namespace {
+mlvc_b200::ScaleConfig scale_config(const mlvc_b200_scale_config* c)
+{
+    if (!c)
+        throw std::runtime_error("mlvc-b200: null scale configuration");
+    return {c->hyperprior_channels, c->model_width,     c->model_height,          c->latent_channels,
+            c->downsample_latent,   c->downsample_hyperprior, c->y_scale_repeat, c->scale_max_index};
+}
+}  // namespace
+
+int mlvc_b200_scale_shape(const mlvc_b200_scale_config* config, size_t* z_count, size_t* scale_count)
+{
+    return guarded([&] {
+        const mlvc_b200::ScaleConfig c = scale_config(config);
+        int zh = 0, zw = 0, yh = 0, yw = 0;
+        mlvc_b200::Backend::scale_plane(c, &zh, &zw, &yh, &yw);
+        if (z_count)
+            *z_count = static_cast<size_t>(c.hyperprior_channels) * zh * zw;
+        if (scale_count)
+            *scale_count = static_cast<size_t>(c.latent_channels / 2) * yh * yw;
+    });
+}
+
+int mlvc_b200_extract_scales(mlvc_b200_backend* backend, const uint16_t* z_raw, size_t z_count,
+                             const mlvc_b200_scale_config* config, int32_t* scales_0, int32_t* scales_1,
+                             size_t scale_count)
+{
+    return guarded([&] {
+        const mlvc_b200::ScaleConfig c = scale_config(config);
+        int zh = 0, zw = 0, yh = 0, yw = 0;
+        mlvc_b200::Backend::scale_plane(c, &zh, &zw, &yh, &yw);
+        if (z_count != static_cast<size_t>(c.hyperprior_channels) * zh * zw)
+            throw std::runtime_error("z_raw shape or dtype does not match model metadata");
+        if (scale_count < static_cast<size_t>(c.latent_channels / 2) * yh * yw)
+            throw std::runtime_error("mlvc-b200: scale buffers are too small");
+        if (!z_raw || !scales_0 || !scales_1)
+            throw std::runtime_error("mlvc-b200: null scale buffer");
+        require(backend).extract_scales(z_raw, c, scales_0, scales_1);
+    });
+}
+
+int mlvc_b200_integer_values(mlvc_b200_backend* backend, const uint16_t* values, size_t count, int32_t* symbols)
+{
+    return guarded([&] {
+        if (count && (!values || !symbols))
+            throw std::runtime_error("mlvc-b200: null value buffer");
+        require(backend).integer_values(values, count, symbols);
+    });
+}
+
 int mlvc_b200_configure_slots(mlvc_b200_backend* backend, size_t slot_count)
 {
     return guarded([&] { require(backend).configure_slots(slot_count); });

@@ -465,6 +465,64 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_y1_tail_f16(const __grid_
     }
 }
 
+// ------------------------------------------------- entropy-coder inputs
+// Scale extraction (reference: extract_scales, core/src/scales.cpp:25-105).
+// One thread per output element (c, y, x), c < latent / 2: the base scales of
+// hyper-latent channels c / repeat ("first") and (c + latent / 2) / repeat
+// ("second") at the nearest z position, clamp(trunc(|z|), 0, max_index); a
+// non-finite z gives INT_MIN, the reference's compiled result for its
+// undefined float -> int cast there.  scales_0 takes first where x + y is
+// even, scales_1 the other one.
+__device__ __forceinline__ int32_t base_scale(const ScaleParams& p, int ch, int zy, int zx)
+{
+    const float a = fabsf(__half2float(p.z[(static_cast<long long>(ch) * p.z_height + zy) * p.z_width + zx]));
+    if (!isfinite(a))
+        return -2147483647 - 1;  // INT_MIN
+    return min(max(__float2int_rz(a), 0), p.max_index);
+}
+
+extern "C" __global__ void __launch_bounds__(256) mlvc_extract_scales(const __grid_constant__ ScaleParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int half = p.latent / 2;
+    const long long total = static_cast<long long>(half) * p.y_height * p.y_width;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int x = static_cast<int>(i % p.y_width);
+        const long long t = i / p.y_width;
+        const int y = static_cast<int>(t % p.y_height);
+        const int c = static_cast<int>(t / p.y_height);
+        const int zy = min(y / p.spatial, p.z_height - 1), zx = min(x / p.spatial, p.z_width - 1);
+        const int32_t first = base_scale(p, c / p.repeat, zy, zx);
+        const int32_t second = base_scale(p, (c + half) / p.repeat, zy, zx);
+        const bool even = ((x + y) & 1) == 0;
+        p.scales_0[i] = even ? first : second;
+        p.scales_1[i] = even ? second : first;
+    }
+}
+
+// FP16 latents -> int32 entropy symbols (reference: integer_values,
+// core/src/entropy.cpp:201-226): truncation; a value that is not finite or
+// lies outside [-32768, 32767] raises the out-of-range flag, which the host
+// turns into the reference's error.
+extern "C" __global__ void __launch_bounds__(256) mlvc_integer_values_f16(const __grid_constant__ IntegerValuesParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    bool bad = false;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const float v = __half2float(p.src[i]);
+        if (v >= -32768.0f && v <= 32767.0f)  // false for NaN
+            p.dst[i] = __float2int_rz(v);
+        else
+            bad = true;
+    }
+    if (bad)
+        atomicOr(p.out_of_range, 1u);
+}
+
 // ------------------------------------------------------------ codec I/O
 // YUV420 frame -> model input tensor (reference: prepare_model_input,
 // core/src/yuv.cpp:339-400).  One thread per tensor element; the 256-entry

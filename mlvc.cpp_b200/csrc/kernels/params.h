@@ -336,6 +336,29 @@ struct QuantTailParams {
 // replicate the last row / column into the padding; output bytes are
 // round(clamp(value / pixel_range, 0, 1) * 255), chroma from the mean of a
 // 2x2 block summed in raster order.
+// Scale extraction for the entropy coder (mlvc_extract_scales; reference
+// extract_scales, core/src/scales.cpp:25-105): z [hyper][zh][zw] FP16 ->
+// scales_0 / scales_1 int32 [latent / 2][yh][yw].
+struct ScaleParams {
+    const mlvc_half* z;
+    int32_t* scales_0;
+    int32_t* scales_1;
+    int z_height, z_width;
+    int latent, repeat;      // latent channels, y_scale_repeat
+    int y_height, y_width;
+    int spatial;             // downsample_hyperprior (nearest up-sampling factor)
+    int max_index;           // scale_max_index
+};
+
+// FP16 latents -> int32 entropy symbols (mlvc_integer_values_f16; reference
+// integer_values, core/src/entropy.cpp:201-226).
+struct IntegerValuesParams {
+    const mlvc_half* src;
+    int32_t* dst;
+    long long count;
+    unsigned int* out_of_range;  // set to 1 when a value is not finite or outside [-32768, 32767]
+};
+
 struct YuvParams {
     const uint8_t* yuv_in;    // to tensor: Y | U | V planes
     uint8_t* yuv_out;         // from tensor

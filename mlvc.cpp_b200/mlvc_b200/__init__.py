@@ -33,6 +33,12 @@ class StateBinding(ctypes.Structure):
     _fields_ = [("input_index", ctypes.c_size_t), ("output_index", ctypes.c_size_t)]
 
 
+class ScaleConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "hyperprior_channels", "model_width", "model_height", "latent_channels", "downsample_latent",
+        "downsample_hyperprior", "y_scale_repeat", "scale_max_index")]
+
+
 EXPORTS = {
     "mlvc_b200_abi_version": ([], ctypes.c_int),
     "mlvc_b200_last_error": ([], ctypes.c_char_p),
@@ -53,6 +59,12 @@ EXPORTS = {
     "mlvc_b200_run": ([ctypes.c_void_p, ctypes.POINTER(Tensor), ctypes.c_size_t, ctypes.POINTER(Tensor),
                        ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_reset_state": ([ctypes.c_void_p], ctypes.c_int),
+    "mlvc_b200_scale_shape": ([ctypes.POINTER(ScaleConfig), ctypes.POINTER(ctypes.c_size_t),
+                               ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "mlvc_b200_extract_scales": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ScaleConfig),
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_integer_values": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],
+                                 ctypes.c_int),
     "mlvc_b200_configure_slots": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_slot_count": ([ctypes.c_void_p], ctypes.c_size_t),
     "mlvc_b200_slot_input": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t], ctypes.c_void_p),
@@ -197,6 +209,34 @@ class Backend:
 
     def reset_state(self):
         _check(lib().mlvc_b200_reset_state(self._h))
+
+    # --------------------------------------------- entropy-coder inputs
+    def extract_scales(self, z_raw, model_width, model_height, latent_channels, downsample_latent=16,
+                       downsample_hyperprior=8, y_scale_repeat=2, scale_max_index=127):
+        """mlvc::extract_scales (core/src/scales.cpp:25-105) on the GPU:
+        z_raw float16 [1, hyper, zh, zw] -> (scales_0, scales_1) int32
+        [latent / 2, yh, yw].  Needs no loaded graph."""
+        z = np.ascontiguousarray(z_raw, np.float16)
+        cfg = ScaleConfig(int(z.shape[1]) if z.ndim == 4 else 0, model_width, model_height, latent_channels,
+                          downsample_latent, downsample_hyperprior, y_scale_repeat, scale_max_index)
+        zc, sc = ctypes.c_size_t(), ctypes.c_size_t()
+        _check(lib().mlvc_b200_scale_shape(ctypes.byref(cfg), ctypes.byref(zc), ctypes.byref(sc)))
+        yh = -(-model_height // downsample_latent)
+        yw = -(-model_width // downsample_latent)
+        s0 = np.empty((latent_channels // 2, yh, yw), np.int32)
+        s1 = np.empty_like(s0)
+        _check(lib().mlvc_b200_extract_scales(self._h, z.ctypes.data, z.size, ctypes.byref(cfg), s0.ctypes.data,
+                                              s1.ctypes.data, s0.size))
+        return s0, s1
+
+    def integer_values(self, values):
+        """mlvc::integer_values (core/src/entropy.cpp:201-226) on the GPU:
+        float16 values -> int32 symbols by truncation (same shape); raises
+        RuntimeError when a value is not finite or outside [-32768, 32767]."""
+        v = np.ascontiguousarray(values, np.float16)
+        out = np.empty(v.shape, np.int32)
+        _check(lib().mlvc_b200_integer_values(self._h, v.ctypes.data, v.size, out.ctypes.data))
+        return out
 
     # ----------------------------------------------------------- slots
     def configure_slots(self, n):

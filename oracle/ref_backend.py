@@ -39,6 +39,7 @@ def lib():
                                              ctypes.c_float, vp, vp, cp, sz]
         L.mlvc_ref_tensor_to_yuv.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                              ctypes.c_float, vp, cp, sz]
+        L.mlvc_ref_extract_scales.argtypes = [vp] + [ctypes.c_int] * 8 + [vp, vp, cp, sz]
         _lib = L
     return _lib
 
@@ -117,3 +118,22 @@ def ref_tensor_to_yuv(tensor, width, height, pixel_range=1.0):
     if lib().mlvc_ref_tensor_to_yuv(t.ctypes.data, mw, mh, width, height, pixel_range, out.ctypes.data, err, 512):
         raise RuntimeError(err.value.decode())
     return out
+
+
+def ref_extract_scales(z_raw, model_width, model_height, latent_channels, downsample_latent=16,
+                       downsample_hyperprior=8, y_scale_repeat=2, scale_max_index=127):
+    """The reference's extract_scales (core/src/scales.cpp:25-105) on a
+    [1, hyper, zh, zw] float16 z_raw: returns (scales_0, scales_1), int32
+    [latent / 2, yh, yw] each."""
+    import numpy as np
+    z = np.ascontiguousarray(z_raw, np.float16)
+    yh = -(-model_height // downsample_latent)
+    yw = -(-model_width // downsample_latent)
+    s0 = np.empty((latent_channels // 2, yh, yw), np.int32)
+    s1 = np.empty_like(s0)
+    err = ctypes.create_string_buffer(512)
+    if lib().mlvc_ref_extract_scales(z.ctypes.data, z.shape[1], model_width, model_height, latent_channels,
+                                     downsample_latent, downsample_hyperprior, y_scale_repeat, scale_max_index,
+                                     s0.ctypes.data, s1.ctypes.data, err, 512):
+        raise RuntimeError(err.value.decode())
+    return s0, s1

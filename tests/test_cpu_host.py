@@ -403,3 +403,37 @@ def test_plan_quantisation_tails_fused(monkeypatch):
     monkeypatch.setenv("MLVC_B200_TAIL_FUSION", "0")
     split = _kernels(plan(*gb.finish()))
     assert "mlvc_y0_tail_f16" not in split and split.count("mlvc_unary_f16") == 4  # clip, reciprocal, 2 rounds
+
+
+# ------------------------------------------------- entropy-coder inputs
+def test_scale_shape_and_validation():
+    """mlvc_b200_scale_shape follows the reference plane sizes
+    (core/src/model.cpp:94-126) and rejects the channel mappings that
+    extract_scales rejects or would read outside its base table with."""
+    import ctypes
+    lib = mlvc_b200.lib()
+
+    def shape(*fields):
+        zc, sc = ctypes.c_size_t(), ctypes.c_size_t()
+        rc = lib.mlvc_b200_scale_shape(ctypes.byref(mlvc_b200.ScaleConfig(*fields)), ctypes.byref(zc),
+                                       ctypes.byref(sc))
+        if rc:
+            raise RuntimeError(lib.mlvc_b200_last_error().decode())
+        return zc.value, sc.value
+
+    assert shape(128, 1920, 1080, 128, 16, 8, 2, 127) == (128 * 9 * 15, 64 * 68 * 120)
+    assert shape(128, 640, 368, 128, 16, 8, 2, 127) == (128 * 3 * 5, 64 * 23 * 40)
+    with pytest.raises(RuntimeError, match="channel mapping is invalid"):
+        shape(32, 640, 368, 128, 16, 8, 2, 127)   # base channels 64 > hyper 32
+    with pytest.raises(RuntimeError, match="channel mapping is invalid"):
+        shape(8, 640, 368, 5, 16, 8, 3, 127)      # (3 + 2) // 3 would leave the base table
+    with pytest.raises(RuntimeError, match="positive"):
+        shape(128, 640, 368, 128, 16, 0, 2, 127)
+
+
+def test_planning_only_backend_refuses_entropy_inputs():
+    be = Backend(plan_only_for=B200)
+    with pytest.raises(RuntimeError, match="planning-only"):
+        be.integer_values(np.zeros(4, np.float16))
+    with pytest.raises(RuntimeError, match="planning-only"):
+        be.extract_scales(np.zeros((1, 128, 3, 5), np.float16), 640, 368, 128)
