@@ -6,7 +6,9 @@ at N=1): the 8-block depthwise residual stack, C=128 @ 92x160 between
 pixel_unshuffle(2) and pixel_shuffle(2), input [1, 32, 184, 320] FP16,
 Kaiming-normal weights and N(0, 1) input from seed 0 (synthetic: no
 checkpoints exist for this network).  One step = one frame through the stack.
-`--workload conv3x3` runs configs[0] (one 3x3 64->64 conv @ 184x320) instead.
+`--workload conv3x3` runs configs[0] (one 3x3 64->64 conv @ 184x320) instead;
+`--workload entropy_1080p` times the entropy-coder inputs of one 1920x1088
+frame (scale extraction + FP16 -> int32 symbols of y_raw_1, y_raw_0, z_raw).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -214,6 +216,177 @@ def replica_throughput(local_ms, steps, world, device="cpu"):
     return world * steps / (ms_max / 1000.0), ms_max
 
 
+# ------------------------------------------------ entropy-coder inputs
+# One frame of the reference's encode prelude (core/src/entropy.cpp:389-394):
+# extract_scales(z_raw) and integer_values of y_raw_1, y_raw_0 and z_raw, at
+# the 1920x1088 plane sizes (latent 128 -> two 64 x 68 x 120 halves, z 128 x
+# 9 x 15; scale table 128 levels).
+ENTROPY_CFG = dict(model_width=1920, model_height=1088, latent_channels=128)
+ENTROPY_DESC = ("entropy-coder inputs of one 1920x1088 frame: extract_scales(z_raw [1,128,9,15]) -> 2 x int32 "
+                "[64,68,120], integer_values(y_raw_1, y_raw_0 [1,64,68,120], z_raw) -> int32; integer-valued FP16 "
+                "latents rint(N(0,1)*3), z rint(N(0,1)*4), seed 0")
+ENTROPY_METRIC = "entropy-coder input frames/s @1920x1088 (scale extraction + symbol conversion)"
+
+
+def entropy_inputs():
+    rng = np.random.default_rng(0)
+    z = np.rint(rng.standard_normal((1, 128, 9, 15)) * 4).astype(np.float16)
+    y1 = np.rint(rng.standard_normal((1, 64, 68, 120)) * 3).astype(np.float16)
+    y0 = np.rint(rng.standard_normal((1, 64, 68, 120)) * 3).astype(np.float16)
+    return z, y1, y0
+
+
+def entropy_cpu_frames_per_s(frames):
+    """The CPU prelude: the reference's compiled extract_scales (oracle/_ref)
+    and the numpy restatement of integer_values (entropy.cpp needs the absent
+    rANS coder).  One thread."""
+    from oracle import scales_oracle  # CPU baseline only
+    from oracle.ref_backend import ref_extract_scales
+    z, y1, y0 = entropy_inputs()
+    times = []
+    for _ in range(frames + 1):
+        t0 = time.perf_counter()
+        ref_extract_scales(z, **ENTROPY_CFG)
+        for v in (y1, y0, z):
+            scales_oracle.integer_values(v)
+        times.append(time.perf_counter() - t0)
+    times = times[1:]
+    return frames / sum(times), times
+
+
+def run_entropy_arm(args, rank, world, local_rank):
+    import torch
+    from mlvc_b200 import Backend
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device(f"cuda:{local_rank}")
+    z, y1, y0 = entropy_inputs()
+    be = Backend(local_rank)
+    stream = torch.cuda.ExternalStream(be.stream)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    zt, y1t, y0t = (torch.from_numpy(a).to(dev) for a in (z, y1, y0))
+    s0 = torch.empty((64, 68, 120), dtype=torch.int32, device=dev)
+    s1 = torch.empty_like(s0)
+    sy1, sy0 = (torch.empty(a.shape, dtype=torch.int32, device=dev) for a in (y1, y0))
+    sz = torch.empty(z.shape, dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+
+    def scales():
+        be.extract_scales_device(zt.data_ptr(), 128, 1920, 1088, 128, s0.data_ptr(), s1.data_ptr())
+
+    def symbols(src, dst):
+        be.integer_values_device(src.data_ptr(), src.numel(), dst.data_ptr(), flag.data_ptr())
+
+    def frame():
+        scales()
+        symbols(y1t, sy1)
+        symbols(y0t, sy0)
+        symbols(zt, sz)
+
+    def flush_l2():
+        with torch.cuda.stream(stream):
+            flush.fill_(1)
+
+    for _ in range(args.warmup):
+        flush_l2()
+        frame()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = vis.split(",")[local_rank] if vis else local_rank
+    with ClockSampler(gpu_index) as clocks:
+        for i in range(args.steps):
+            flush_l2()  # cold L2 at the start of every frame (untimed)
+            starts[i].record(stream)
+            frame()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    value, ms_max = replica_throughput(ms, args.steps, world, f"cuda:{local_rank}")
+    if int(flag.item()) != 0:
+        raise RuntimeError("symbol conversion reported an out-of-range value")
+    want0, want1 = be.extract_scales(z, **ENTROPY_CFG)
+    if not (np.array_equal(s0.cpu().numpy(), want0) and np.array_equal(s1.cpu().numpy(), want1)
+            and np.array_equal(sy1.cpu().numpy(), be.integer_values(y1))):
+        raise RuntimeError("device-pointer results differ from the host-buffer calls")
+
+    # per-kernel cold-L2 launch times (events around each launch)
+    def timed(fn, n=20):
+        total = 0.0
+        for _ in range(n):
+            flush_l2()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            total += a.elapsed_time(b)
+        return total / n
+    t_scales = timed(scales)
+    t_sym = timed(lambda: symbols(y1t, sy1))
+    n_out = s0.numel()
+    kernels = {
+        "mlvc_extract_scales": {"launches": 1, "us_cold_l2": 1e3 * t_scales,
+                                "algorithmic_bytes": z.nbytes + 8 * n_out},
+        "mlvc_integer_values_f16": {"launches": 3, "us_cold_l2_y_half": 1e3 * t_sym,
+                                    "algorithmic_bytes": 6 * (y1.size + y0.size + z.size)},
+    }
+    hbm, _, peak_kind = measured_peaks()
+    sym_bytes = 6.0 * y1.size
+    achieved = sym_bytes / (t_sym / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+            "peak_kind": peak_kind, "kernel": "mlvc_integer_values_f16",
+            "algorithmic_bytes_per_launch": sym_bytes, "avg_launch_us_cold_l2": 1e3 * t_sym,
+            "traffic": ncu_traffic().get(args.workload, {}).get("mlvc_integer_values_f16")}
+
+    # end to end through the public host-buffer calls (the reference's call shape)
+    def host_frame():
+        be.extract_scales(z, **ENTROPY_CFG)
+        for v in (y1, y0, z):
+            be.integer_values(v)
+    for _ in range(args.warmup):
+        host_frame()
+    e_st, e_en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e_st.record(stream)
+    for _ in range(args.steps):
+        host_frame()
+    e_en.record(stream)
+    torch.cuda.synchronize()
+    e2e_value, _ = replica_throughput(e_st.elapsed_time(e_en), args.steps, world, f"cuda:{local_rank}")
+    h2d = 2 * z.nbytes + y1.nbytes + y0.nbytes
+    d2h = 8 * n_out + 4 * (y1.size + y0.size + z.size) + 3 * 4
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": ENTROPY_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16->int32", "data": "synthetic",
+            "config": {"workload": ENTROPY_DESC, "global_batch": world,
+                       "parallelism": f"replicas x{world} (no collective)",
+                       "l2": "flushed before every timed frame (256 MiB fill, untimed)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world,
+                    "path": "mlvc_b200_extract_scales + 3 x mlvc_b200_integer_values on pageable host buffers "
+                            "(each call copies in, launches, copies out and waits)"},
+            "gpu_launches": 4 * args.steps,
+            "roofline": roof,
+            "kernels": kernels,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            fps, times = entropy_cpu_frames_per_s(1000)  # ~10 s of CPU work
+            line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": 1, "kind": "port",
+                                    "sample": f"{len(times)} frames: reference extract_scales compiled from "
+                                              "core/src/scales.cpp (oracle/_ref) + numpy restatement of "
+                                              f"integer_values, {sum(times):.2f} s"}
+    be.close()
+    return line
+
+
 # ------------------------------------------------------------------ CPU
 def reference_backend_frames_per_s(graph, weights, inputs, frames, warmup, threads):
     """Times the reference CPU backend (oracle/_ref) running the same graph."""
@@ -236,6 +409,22 @@ def reference_backend_frames_per_s(graph, weights, inputs, frames, warmup, threa
 
 
 def run_reference_arm(args, rank, world):
+    if args.workload == "entropy_1080p":
+        if rank != 0:
+            return 0
+        fps, times = entropy_cpu_frames_per_s(args.steps)
+        line = {
+            "impl": "reference", "metric": ENTROPY_METRIC, "value": fps, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16->int32",
+            "data": "synthetic", "config": {"workload": ENTROPY_DESC, "global_batch": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": 1, "kind": "port",
+                             "sample": f"{args.steps} frames: reference extract_scales (oracle/_ref) + numpy "
+                                       "restatement of integer_values"},
+            "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return 0
     graph, weights, inputs, desc, metric, _ = workload(args.workload)
     if rank != 0:
         return 0
@@ -431,7 +620,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv",
-                                                   "op_mbconv", "mlvc_dec_1080p", "mlvc_dec_640"], default="block_stack")
+                                                   "op_mbconv", "mlvc_dec_1080p", "mlvc_dec_640", "entropy_1080p"],
+                    default="block_stack")
     ap.add_argument("--cpu-frames", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -450,7 +640,8 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(f"cuda:{local_rank}"))
-    line = run_b200_arm(args, rank, world, local_rank)
+    arm = run_entropy_arm if args.workload == "entropy_1080p" else run_b200_arm
+    line = arm(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

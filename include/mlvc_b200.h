@@ -161,6 +161,18 @@ int mlvc_b200_extract_scales(mlvc_b200_backend* backend, const uint16_t* z_raw, 
  * range" when a value is not finite or outside [-32768, 32767]. */
 int mlvc_b200_integer_values(mlvc_b200_backend* backend, const uint16_t* values, size_t count, int32_t* symbols);
 
+/* Device-memory forms of the two calls above (no reference counterpart: the
+ * reference runs them on host tensors).  Pointers are device addresses
+ * (CUdeviceptr) on the backend's device, from any allocator; the kernels are
+ * enqueued on mlvc_b200_stream() and the calls return without waiting.  The
+ * caller zeroes the device uint32 *out_of_range before the call; it is
+ * non-zero afterwards when a value was not finite or outside [-32768, 32767]
+ * (that element's symbol is then left unwritten). */
+int mlvc_b200_extract_scales_device(mlvc_b200_backend* backend, uint64_t z_raw, const mlvc_b200_scale_config* config,
+                                    uint64_t scales_0, uint64_t scales_1);
+int mlvc_b200_integer_values_device(mlvc_b200_backend* backend, uint64_t values, size_t count, uint64_t symbols,
+                                    uint64_t out_of_range);
+
 /* Measurement hooks (no reference counterpart; the reference times whole
  * runs with steady_clock, codec/src/pipeline.cpp:341-415).  enqueue replays
  * the captured schedule on the backend's stream with the device-resident

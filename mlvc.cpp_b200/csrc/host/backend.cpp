@@ -256,6 +256,7 @@ Backend::~Backend()
     prepped_dev_.reset();
     arena_dev_.reset();
     flush_dev_.reset();
+    entropy_scratch_.reset();
     input_dev_.clear();
     input_stage_dev_.clear();
     output_stage_dev_.clear();
@@ -2402,21 +2403,18 @@ void Backend::scale_plane(const ScaleConfig& c, int* z_height, int* z_width, int
         throw std::runtime_error("scale decoder channel mapping is invalid");
 }
 
-void Backend::extract_scales(const uint16_t* z, const ScaleConfig& cfg, int32_t* scales_0, int32_t* scales_1)
+void Backend::extract_scales_device(CUdeviceptr z, const ScaleConfig& cfg, CUdeviceptr scales_0, CUdeviceptr scales_1)
 {
     if (offline_)
         throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
     int zh = 0, zw = 0, yh = 0, yw = 0;
     scale_plane(cfg, &zh, &zw, &yh, &yw);
-    const size_t z_count = static_cast<size_t>(cfg.hyperprior_channels) * zh * zw;
     const size_t out_count = static_cast<size_t>(cfg.latent_channels / 2) * yh * yw;
     ContextGuard guard(ctx_);
-    DeviceBuffer z_dev(z_count * 2), s_dev(out_count * 2 * sizeof(int32_t));
-    check(cuMemcpyHtoDAsync(z_dev.get(), z, z_count * 2, stream_), "cuMemcpyHtoDAsync(z)");
     ScaleParams sp{};
-    sp.z = reinterpret_cast<const mlvc_half*>(z_dev.get());
-    sp.scales_0 = reinterpret_cast<int32_t*>(s_dev.get());
-    sp.scales_1 = reinterpret_cast<int32_t*>(s_dev.get()) + out_count;
+    sp.z = reinterpret_cast<const mlvc_half*>(z);
+    sp.scales_0 = reinterpret_cast<int32_t*>(scales_0);
+    sp.scales_1 = reinterpret_cast<int32_t*>(scales_1);
     sp.z_height = zh;
     sp.z_width = zw;
     sp.latent = cfg.latent_channels;
@@ -2429,9 +2427,51 @@ void Backend::extract_scales(const uint16_t* z, const ScaleConfig& cfg, int32_t*
     const unsigned grid = blocks_for(static_cast<long long>(out_count), 256, sm_count_);
     check(cuLaunchKernel(fn("mlvc_extract_scales"), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr),
           "mlvc_extract_scales");
-    check(cuMemcpyDtoHAsync(scales_0, s_dev.get(), out_count * sizeof(int32_t), stream_), "cuMemcpyDtoHAsync(scales_0)");
-    check(cuMemcpyDtoHAsync(scales_1, s_dev.get() + out_count * sizeof(int32_t), out_count * sizeof(int32_t), stream_),
-          "cuMemcpyDtoHAsync(scales_1)");
+}
+
+void Backend::integer_values_device(CUdeviceptr values, size_t count, CUdeviceptr symbols, CUdeviceptr out_of_range)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    if (count == 0)
+        return;
+    ContextGuard guard(ctx_);
+    IntegerValuesParams ip{};
+    ip.src = reinterpret_cast<const mlvc_half*>(values);
+    ip.dst = reinterpret_cast<int32_t*>(symbols);
+    ip.count = static_cast<long long>(count);
+    ip.out_of_range = reinterpret_cast<unsigned int*>(out_of_range);
+    void* args[] = {&ip};
+    const unsigned grid = blocks_for(static_cast<long long>(count), 256, sm_count_);
+    check(cuLaunchKernel(fn("mlvc_integer_values_f16"), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr),
+          "mlvc_integer_values_f16");
+}
+
+CUdeviceptr Backend::entropy_scratch(size_t bytes)
+{
+    if (entropy_scratch_.bytes() < bytes) {
+        check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
+        entropy_scratch_ = DeviceBuffer(bytes);
+    }
+    return entropy_scratch_.get();
+}
+
+void Backend::extract_scales(const uint16_t* z, const ScaleConfig& cfg, int32_t* scales_0, int32_t* scales_1)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    int zh = 0, zw = 0, yh = 0, yw = 0;
+    scale_plane(cfg, &zh, &zw, &yh, &yw);
+    const size_t z_bytes = (static_cast<size_t>(cfg.hyperprior_channels) * zh * zw * 2 + 255) & ~size_t{255};
+    const size_t out_bytes = static_cast<size_t>(cfg.latent_channels / 2) * yh * yw * sizeof(int32_t);
+    ContextGuard guard(ctx_);
+    const CUdeviceptr buf = entropy_scratch(z_bytes + 2 * out_bytes);
+    const CUdeviceptr s0 = buf + z_bytes, s1 = s0 + out_bytes;
+    check(cuMemcpyHtoDAsync(buf, z, static_cast<size_t>(cfg.hyperprior_channels) * zh * zw * 2, stream_),
+          "cuMemcpyHtoDAsync(z)");
+    extract_scales_device(buf, cfg, s0, s1);
+    check(cuMemcpyDtoHAsync(scales_0, s0, out_bytes, stream_), "cuMemcpyDtoHAsync(scales_0)");
+    check(cuMemcpyDtoHAsync(scales_1, s1, out_bytes, stream_), "cuMemcpyDtoHAsync(scales_1)");
     check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
 }
 
@@ -2442,22 +2482,15 @@ void Backend::integer_values(const uint16_t* values, size_t count, int32_t* symb
     if (count == 0)
         return;
     ContextGuard guard(ctx_);
-    DeviceBuffer src(count * 2), dst(count * sizeof(int32_t) + 16);
-    const CUdeviceptr flag = dst.get() + count * sizeof(int32_t);
+    const size_t src_bytes = (count * 2 + 255) & ~size_t{255};
+    const CUdeviceptr src = entropy_scratch(src_bytes + count * sizeof(int32_t) + 16);
+    const CUdeviceptr dst = src + src_bytes, flag = dst + count * sizeof(int32_t);
     check(cuMemsetD8Async(flag, 0, sizeof(uint32_t), stream_), "cuMemsetD8Async(flag)");
-    check(cuMemcpyHtoDAsync(src.get(), values, count * 2, stream_), "cuMemcpyHtoDAsync(values)");
-    IntegerValuesParams ip{};
-    ip.src = reinterpret_cast<const mlvc_half*>(src.get());
-    ip.dst = reinterpret_cast<int32_t*>(dst.get());
-    ip.count = static_cast<long long>(count);
-    ip.out_of_range = reinterpret_cast<unsigned int*>(flag);
-    void* args[] = {&ip};
-    const unsigned grid = blocks_for(static_cast<long long>(count), 256, sm_count_);
-    check(cuLaunchKernel(fn("mlvc_integer_values_f16"), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr),
-          "mlvc_integer_values_f16");
+    check(cuMemcpyHtoDAsync(src, values, count * 2, stream_), "cuMemcpyHtoDAsync(values)");
+    integer_values_device(src, count, dst, flag);
     uint32_t bad = 0;
     check(cuMemcpyDtoHAsync(&bad, flag, sizeof(bad), stream_), "cuMemcpyDtoHAsync(flag)");
-    check(cuMemcpyDtoHAsync(symbols, dst.get(), count * sizeof(int32_t), stream_), "cuMemcpyDtoHAsync(symbols)");
+    check(cuMemcpyDtoHAsync(symbols, dst, count * sizeof(int32_t), stream_), "cuMemcpyDtoHAsync(symbols)");
     check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
     if (bad)
         throw std::runtime_error("entropy symbol is outside signed 16-bit range");

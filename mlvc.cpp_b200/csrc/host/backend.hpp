@@ -90,6 +90,10 @@ public:
     static void scale_plane(const ScaleConfig& cfg, int* z_height, int* z_width, int* y_height, int* y_width);
     void extract_scales(const uint16_t* z, const ScaleConfig& cfg, int32_t* scales_0, int32_t* scales_1);
     void integer_values(const uint16_t* values, size_t count, int32_t* symbols);
+    // Device-memory forms: launch on stream() without copies or a sync.  The
+    // caller zeroes *out_of_range (a device uint32) and reads it afterwards.
+    void extract_scales_device(CUdeviceptr z, const ScaleConfig& cfg, CUdeviceptr scales_0, CUdeviceptr scales_1);
+    void integer_values_device(CUdeviceptr values, size_t count, CUdeviceptr symbols, CUdeviceptr out_of_range);
 
     // Slot path: pinned host staging per slot, asynchronous submit, wait.
     void configure_slots(size_t count);
@@ -142,6 +146,7 @@ private:
     void check_status();
     void launch_steps(CUstream s);
     CUfunction fn(const char* name);
+    CUdeviceptr entropy_scratch(size_t bytes);  // grow-only staging of the host-buffer entropy calls
 
     int device_ = 0;
     CUdevice dev_ = 0;
@@ -175,7 +180,7 @@ private:
         size_t input = kNoCodecTensor, output = kNoCodecTensor;
     } codec_;
 
-    DeviceBuffer weights_dev_, prepped_dev_, arena_dev_, flush_dev_;
+    DeviceBuffer weights_dev_, prepped_dev_, arena_dev_, flush_dev_, entropy_scratch_;
     std::vector<DeviceBuffer> input_dev_, input_stage_dev_, output_stage_dev_, state_dev_;
     std::vector<uint8_t> prepped_host_;
 

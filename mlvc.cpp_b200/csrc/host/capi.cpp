@@ -215,6 +215,27 @@ int mlvc_b200_extract_scales(mlvc_b200_backend* backend, const uint16_t* z_raw, 
     });
 }
 
+int mlvc_b200_extract_scales_device(mlvc_b200_backend* backend, uint64_t z_raw, const mlvc_b200_scale_config* config,
+                                    uint64_t scales_0, uint64_t scales_1)
+{
+    return guarded([&] {
+        const mlvc_b200::ScaleConfig c = scale_config(config);
+        if (!z_raw || !scales_0 || !scales_1 || (z_raw & 1) || (scales_0 & 3) || (scales_1 & 3))
+            throw std::runtime_error("mlvc-b200: null or misaligned device pointer");
+        require(backend).extract_scales_device(z_raw, c, scales_0, scales_1);
+    });
+}
+
+int mlvc_b200_integer_values_device(mlvc_b200_backend* backend, uint64_t values, size_t count, uint64_t symbols,
+                                    uint64_t out_of_range)
+{
+    return guarded([&] {
+        if (count && (!values || !symbols || !out_of_range || (values & 1) || (symbols & 3) || (out_of_range & 3)))
+            throw std::runtime_error("mlvc-b200: null or misaligned device pointer");
+        require(backend).integer_values_device(values, count, symbols, out_of_range);
+    });
+}
+
 int mlvc_b200_integer_values(mlvc_b200_backend* backend, const uint16_t* values, size_t count, int32_t* symbols)
 {
     return guarded([&] {

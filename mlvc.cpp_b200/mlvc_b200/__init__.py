@@ -65,6 +65,10 @@ EXPORTS = {
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_integer_values": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p],
                                  ctypes.c_int),
+    "mlvc_b200_extract_scales_device": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ScaleConfig),
+                                         ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
+    "mlvc_b200_integer_values_device": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_uint64,
+                                         ctypes.c_uint64], ctypes.c_int),
     "mlvc_b200_configure_slots": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_slot_count": ([ctypes.c_void_p], ctypes.c_size_t),
     "mlvc_b200_slot_input": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t], ctypes.c_void_p),
@@ -237,6 +241,21 @@ class Backend:
         out = np.empty(v.shape, np.int32)
         _check(lib().mlvc_b200_integer_values(self._h, v.ctypes.data, v.size, out.ctypes.data))
         return out
+
+    def extract_scales_device(self, z_ptr, hyperprior_channels, model_width, model_height, latent_channels,
+                              scales_0_ptr, scales_1_ptr, downsample_latent=16, downsample_hyperprior=8,
+                              y_scale_repeat=2, scale_max_index=127):
+        """Device-pointer form of extract_scales (enqueued on self.stream, no
+        wait): z_ptr -> FP16 [hyper, zh, zw], scales_*_ptr -> int32 planes."""
+        cfg = ScaleConfig(hyperprior_channels, model_width, model_height, latent_channels, downsample_latent,
+                          downsample_hyperprior, y_scale_repeat, scale_max_index)
+        _check(lib().mlvc_b200_extract_scales_device(self._h, z_ptr, ctypes.byref(cfg), scales_0_ptr, scales_1_ptr))
+
+    def integer_values_device(self, values_ptr, count, symbols_ptr, out_of_range_ptr):
+        """Device-pointer form of integer_values (enqueued on self.stream, no
+        wait); the device uint32 at out_of_range_ptr, zeroed by the caller,
+        becomes non-zero when a value is out of range."""
+        _check(lib().mlvc_b200_integer_values_device(self._h, values_ptr, count, symbols_ptr, out_of_range_ptr))
 
     # ----------------------------------------------------------- slots
     def configure_slots(self, n):

@@ -82,3 +82,31 @@ def test_integer_values_out_of_range_raises(be, bad):
 
 def test_integer_values_empty(be):
     assert be.integer_values(np.zeros(0, np.float16)).shape == (0,)
+
+
+def test_device_forms_match_host_forms(be):
+    """The device-pointer entry points (buffers from another allocator, here
+    torch) give the same symbols and scales as the host-buffer calls, and
+    report out-of-range values through the caller's device flag."""
+    import torch
+    rng = np.random.default_rng(11)
+    z = (rng.standard_normal((1, 128, 3, 5)) * 50).astype(np.float16)
+    y = np.rint(rng.standard_normal((1, 64, 23, 40)) * 300).astype(np.float16)
+    dev = torch.device("cuda:0")
+    zt, yt = torch.from_numpy(z).to(dev), torch.from_numpy(y).to(dev)
+    s0 = torch.empty((64, 23, 40), dtype=torch.int32, device=dev)
+    s1 = torch.empty_like(s0)
+    sym = torch.empty(y.shape, dtype=torch.int32, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+    be.extract_scales_device(zt.data_ptr(), 128, 640, 368, 128, s0.data_ptr(), s1.data_ptr())
+    be.integer_values_device(yt.data_ptr(), y.size, sym.data_ptr(), flag.data_ptr())
+    torch.cuda.synchronize()
+    want0, want1 = be.extract_scales(z, 640, 368, 128)
+    assert np.array_equal(s0.cpu().numpy(), want0) and np.array_equal(s1.cpu().numpy(), want1)
+    assert np.array_equal(sym.cpu().numpy(), be.integer_values(y)) and int(flag.item()) == 0
+    yt[0, 3, 4, 5] = float("inf")
+    torch.cuda.synchronize()
+    be.integer_values_device(yt.data_ptr(), y.size, sym.data_ptr(), flag.data_ptr())
+    torch.cuda.synchronize()
+    assert int(flag.item()) != 0
