@@ -2423,8 +2423,9 @@ void Backend::extract_scales_device(CUdeviceptr z, const ScaleConfig& cfg, CUdev
     sp.y_width = yw;
     sp.spatial = cfg.downsample_hyperprior;
     sp.max_index = cfg.scale_max_index;
+    sp.vec4 = yw % 4 == 0 && scales_0 % 16 == 0 && scales_1 % 16 == 0;
     void* args[] = {&sp};
-    const unsigned grid = blocks_for(static_cast<long long>(out_count), 256, sm_count_);
+    const unsigned grid = blocks_for(static_cast<long long>(sp.vec4 ? out_count / 4 : out_count), 256, sm_count_);
     check(cuLaunchKernel(fn("mlvc_extract_scales"), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr),
           "mlvc_extract_scales");
 }
@@ -2441,8 +2442,9 @@ void Backend::integer_values_device(CUdeviceptr values, size_t count, CUdevicept
     ip.dst = reinterpret_cast<int32_t*>(symbols);
     ip.count = static_cast<long long>(count);
     ip.out_of_range = reinterpret_cast<unsigned int*>(out_of_range);
+    ip.vec8 = values % 16 == 0 && symbols % 16 == 0;
     void* args[] = {&ip};
-    const unsigned grid = blocks_for(static_cast<long long>(count), 256, sm_count_);
+    const unsigned grid = blocks_for(static_cast<long long>(ip.vec8 ? (count + 7) / 8 : count), 256, sm_count_);
     check(cuLaunchKernel(fn("mlvc_integer_values_f16"), grid, 1, 1, 256, 1, 1, 0, stream_, args, nullptr),
           "mlvc_integer_values_f16");
 }

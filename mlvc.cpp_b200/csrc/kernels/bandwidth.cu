@@ -481,41 +481,103 @@ __device__ __forceinline__ int32_t base_scale(const ScaleParams& p, int ch, int 
     return min(max(__float2int_rz(a), 0), p.max_index);
 }
 
+__device__ __forceinline__ void scale_pair(const ScaleParams& p, int c, int y, int x, int32_t& s0, int32_t& s1)
+{
+    const int half = p.latent / 2;
+    const int zy = min(y / p.spatial, p.z_height - 1), zx = min(x / p.spatial, p.z_width - 1);
+    const int32_t first = base_scale(p, c / p.repeat, zy, zx);
+    const int32_t second = base_scale(p, (c + half) / p.repeat, zy, zx);
+    const bool even = ((x + y) & 1) == 0;
+    s0 = even ? first : second;
+    s1 = even ? second : first;
+}
+
 extern "C" __global__ void __launch_bounds__(256) mlvc_extract_scales(const __grid_constant__ ScaleParams p)
 {
     pdl_launch_dependents();
     pdl_wait();
-    const int half = p.latent / 2;
-    const long long total = static_cast<long long>(half) * p.y_height * p.y_width;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long total = static_cast<long long>(p.latent / 2) * p.y_height * p.y_width;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    if (p.vec4) {
+        // four consecutive x of one row per thread, one 16-byte store per plane
+        // (host: y_width % 4 == 0, both planes 16-byte aligned)
+        const int qw = p.y_width / 4;
+        for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total / 4; i += stride) {
+            const int x0 = static_cast<int>(i % qw) * 4;
+            const long long t = i / qw;
+            const int y = static_cast<int>(t % p.y_height);
+            const int c = static_cast<int>(t / p.y_height);
+            int32_t a[4], b[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                scale_pair(p, c, y, x0 + k, a[k], b[k]);
+            reinterpret_cast<int4*>(p.scales_0)[i] = make_int4(a[0], a[1], a[2], a[3]);
+            reinterpret_cast<int4*>(p.scales_1)[i] = make_int4(b[0], b[1], b[2], b[3]);
+        }
+        return;
+    }
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
         const int x = static_cast<int>(i % p.y_width);
         const long long t = i / p.y_width;
-        const int y = static_cast<int>(t % p.y_height);
-        const int c = static_cast<int>(t / p.y_height);
-        const int zy = min(y / p.spatial, p.z_height - 1), zx = min(x / p.spatial, p.z_width - 1);
-        const int32_t first = base_scale(p, c / p.repeat, zy, zx);
-        const int32_t second = base_scale(p, (c + half) / p.repeat, zy, zx);
-        const bool even = ((x + y) & 1) == 0;
-        p.scales_0[i] = even ? first : second;
-        p.scales_1[i] = even ? second : first;
+        int32_t a, b;
+        scale_pair(p, static_cast<int>(t / p.y_height), static_cast<int>(t % p.y_height), x, a, b);
+        p.scales_0[i] = a;
+        p.scales_1[i] = b;
     }
 }
 
 // FP16 latents -> int32 entropy symbols (reference: integer_values,
 // core/src/entropy.cpp:201-226): truncation; a value that is not finite or
 // lies outside [-32768, 32767] raises the out-of-range flag, which the host
-// turns into the reference's error.
+// turns into the reference's error (that element's symbol is not written).
+__device__ __forceinline__ bool symbol_of(float v, int32_t& out)
+{
+    if (!(v >= -32768.0f && v <= 32767.0f))  // also true for NaN
+        return false;
+    out = __float2int_rz(v);
+    return true;
+}
+
 extern "C" __global__ void __launch_bounds__(256) mlvc_integer_values_f16(const __grid_constant__ IntegerValuesParams p)
 {
     pdl_launch_dependents();
     pdl_wait();
     bool bad = false;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const float v = __half2float(p.src[i]);
-        if (v >= -32768.0f && v <= 32767.0f)  // false for NaN
-            p.dst[i] = __float2int_rz(v);
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    const long long tid = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+    // vector body: 8 values per thread (one 16-byte load, two 16-byte stores;
+    // host: both pointers 16-byte aligned), then the scalar tail
+    const long long nvec = p.vec8 ? p.count / 8 : 0;
+    for (long long i = tid; i < nvec; i += stride) {
+        const uint4 raw = reinterpret_cast<const uint4*>(p.src)[i];
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        int32_t o[8];
+        bool ok[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+            ok[2 * k] = symbol_of(f.x, o[2 * k]);
+            ok[2 * k + 1] = symbol_of(f.y, o[2 * k + 1]);
+        }
+        bool all = true;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            all = all && ok[k];
+        if (all) {
+            reinterpret_cast<int4*>(p.dst)[2 * i] = make_int4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<int4*>(p.dst)[2 * i + 1] = make_int4(o[4], o[5], o[6], o[7]);
+        } else {
+            bad = true;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (ok[k])
+                    p.dst[8 * i + k] = o[k];
+        }
+    }
+    for (long long i = nvec * 8 + tid; i < p.count; i += stride) {
+        int32_t o;
+        if (symbol_of(__half2float(p.src[i]), o))
+            p.dst[i] = o;
         else
             bad = true;
     }

@@ -348,6 +348,7 @@ struct ScaleParams {
     int y_height, y_width;
     int spatial;             // downsample_hyperprior (nearest up-sampling factor)
     int max_index;           // scale_max_index
+    int vec4;                // 1: four outputs per thread (y_width % 4 == 0, planes 16-byte aligned)
 };
 
 // FP16 latents -> int32 entropy symbols (mlvc_integer_values_f16; reference
@@ -357,6 +358,7 @@ struct IntegerValuesParams {
     int32_t* dst;
     long long count;
     unsigned int* out_of_range;  // set to 1 when a value is not finite or outside [-32768, 32767]
+    int vec8;                    // 1: src and dst 16-byte aligned (8 values per thread)
 };
 
 struct YuvParams {
