@@ -202,6 +202,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                     tc_fence_after();
                     if (issued == 0)
                         trace(p, kTrFirstA);
+                    if (t == first && kp < 8)
+                        trace(p, kTrDwMma + kp);
                     const uint32_t a_st = a_addr + static_cast<uint32_t>(as) * kDwPanelBytes;
                     const uint32_t b_st = w_addr + static_cast<uint32_t>(ws) * w_bytes;
 #pragma unroll
@@ -254,8 +256,6 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
             tc.pixel0 = 0;
             tc.ox0 = (t % dp.tiles_x) * kDwTileW;
             tc.oy = (t / dp.tiles_x) * kDwTileH;
-            if (leader)  // residual tile into the staging buffer while the depthwise runs
-                stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
             const int ty = pg >> 2, tx = (pg & 3) * 4;  // the thread's 4 pixels: tile row ty, columns tx .. tx + 3
             const int x0 = tc.ox0 + tx;
             const int h0 = (ty + 1) * (kDwTileW + 2) + tx + 1;  // halo pixel of the first one
@@ -337,8 +337,18 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 }
                 fence_proxy_async_smem();  // the tensor core reads the panel through the async proxy
                 mbar_arrive(&sh->a_full[as]);
+                // Residual tile into the staging buffer while the remaining slices
+                // run.  Issued after the first slice, not before it: the leader's
+                // wait for the previous tile's output store to read the buffer
+                // would otherwise hold up the first slice's A panel.
+                if (leader && kp == 0)
+                    stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
                 if (leader && it == 0 && kp == 0)
                     trace(p, kTrDwFirstSlice);
+                if (leader && it == 0 && kp < 8)
+                    trace(p, kTrDwSlice + kp);
+                if (leader && it == 1 && kp == 0)
+                    trace(p, kTrDwTile1);
                 if (++hs == dp.h_stages) {
                     hs = 0;
                     hph ^= 1u;

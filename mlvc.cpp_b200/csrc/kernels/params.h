@@ -102,6 +102,12 @@ enum TracePoint : int {
     kTrMbChunk = 24,
     kTrMbExpandMma = 36,
     kTrMbProjMma = 40,
+    // fused depthwise (mlvc_dwconv_tc), first tile, slice s < 8: A panel
+    // written (kTrDwSlice + s), MMA issuer passed its waits (kTrDwMma + s);
+    // second tile's first slice written (kTrDwTile1)
+    kTrDwSlice = 24,
+    kTrDwTile1 = 32,
+    kTrDwMma = 36,
     kTracePoints = 48
 };
 
