@@ -149,6 +149,11 @@ struct Backend::Value {
     int consumers = 0;
     bool graph_output = false;
     size_t weight_off = 0;  // weights.bin offset for kWeight
+    // A Slice whose result is one contiguous byte range of its source is not
+    // materialised: the value lives inside the source's buffer, alias_off bytes
+    // in (alias_of = the source, never itself an alias; 0 = not an alias).
+    uint32_t alias_of = 0;
+    size_t alias_off = 0;
 
     // Physical element strides for logical (n, c, h, w).
     std::array<long long, 4> strides() const
@@ -1816,6 +1821,35 @@ void Backend::plan()
                 if (!stepv.empty())
                     step4[axis] = stepv[k];
             }
+            {
+                // Contiguous result (every dimension inside the sliced one whole,
+                // every one outside it of extent 1, unit steps, same layout): a
+                // view into the source at a 256-byte aligned offset, no copy.
+                const auto od4 = dims4(ov.shape);
+                const Value& src = av.alias_of ? values_[av.alias_of] : av;
+                const bool producible = src.kind == Value::kNone || src.kind == Value::kArena;
+                bool contiguous = ov.nhwc == av.nhwc && ov.dtype == av.dtype && producible && !src.graph_output &&
+                                  !ov.graph_output && step4 == std::array<long long, 4>{1, 1, 1, 1};
+                const int order_nhwc[4] = {0, 2, 3, 1}, order_nchw[4] = {0, 1, 2, 3};
+                const int* ord = av.nhwc ? order_nhwc : order_nchw;
+                int k = 3;  // innermost physical dimension that is not taken whole
+                while (k >= 0 && od4[ord[k]] == id4[ord[k]])
+                    --k;
+                for (int q = 0; contiguous && q < k; ++q)
+                    contiguous = od4[ord[q]] == 1;
+                const auto as = av.strides();
+                long long off = 0;
+                for (int l = 0; l < 4; ++l)
+                    off += start4[l] * as[l];
+                const size_t bytes_off = static_cast<size_t>(off) * 2 + (av.alias_of ? av.alias_off : 0);
+                if (contiguous && bytes_off % 256 == 0) {
+                    Value& o = values_[out_id];
+                    o.alias_of = av.alias_of ? av.alias_of : a;
+                    o.alias_off = bytes_off;
+                    ++i;
+                    continue;
+                }
+            }
             s.info.bytes += 2.0 * out_count;
             const bool nhwc = ov.nhwc;
             s.kernel = "mlvc_strided_copy_f16";
@@ -2043,7 +2077,7 @@ void Backend::build_schedule()
             v.last = std::max(v.last, si);
         }
         for (auto id : steps_[si].reads) {
-            Value& v = values_[id];
+            Value& v = values_[values_[id].alias_of ? values_[id].alias_of : id];
             if (v.kind == Value::kArena || v.kind == Value::kNone)
                 v.last = std::max(v.last, si);
         }
@@ -2139,6 +2173,9 @@ void Backend::build_schedule()
     for (size_t bi = 0; bi < bindings_.size(); ++bi)
         if (bi < state_alias_.size() && state_alias_[bi])
             values_[graph_.outputs[bindings_[bi].output_index]].addr = state_dev_.at(bi).get();
+    for (auto& v : values_)
+        if (v.alias_of)
+            v.addr = values_[v.alias_of].addr + v.alias_off;
     for (auto id : graph_.outputs)
         if (!values_[id].addr &&
             std::find(absorbed_outputs_.begin(), absorbed_outputs_.end(), id) == absorbed_outputs_.end())

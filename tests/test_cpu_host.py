@@ -226,6 +226,9 @@ def test_plan_mlvc_decoder_standin():
     be = plan(graph, weights)
     k = _kernels(be)
     assert k.count("mlvc_conv1x1_tc") == 29 and k.count("mlvc_dwconv_tc") == 7, k
+    # the hyperprior's row crop and full-width slice are views; the two channel
+    # slices and the latent concat are copies
+    assert k.count("mlvc_strided_copy_v8_f16") == 4, k
     assert "mlvc_depthwise3x3_f16" not in k
     assert "mlvc_conv_direct_f16" not in k and "mlvc_unary_f16" not in k and "mlvc_reglu_f16" not in k
     assert [tuple(s) for _, _, s in be.inputs] == [(1, 128, 3, 5), (1, 64, 23, 40), (1, 64, 23, 40),
@@ -437,3 +440,26 @@ def test_planning_only_backend_refuses_entropy_inputs():
         be.integer_values(np.zeros(4, np.float16))
     with pytest.raises(RuntimeError, match="planning-only"):
         be.extract_scales(np.zeros((1, 128, 3, 5), np.float16), 640, 368, 128)
+
+
+@pytest.mark.parametrize("shape,axis,start,end,aliased", [
+    ([1, 64, 16, 16], 2, 0, 8, True),    # leading rows of an NHWC tensor
+    ([1, 64, 16, 16], 2, 4, 12, True),   # a row range at a 256-byte aligned offset
+    ([1, 64, 16, 16], 3, 0, 16, True),   # full-width slice: the whole tensor
+    ([1, 64, 16, 16], 3, 0, 8, False),   # part of every row: strided
+    ([1, 64, 16, 16], 1, 0, 32, False),  # channel slice: strided
+    ([1, 8, 6, 5], 2, 1, 4, False),      # contiguous, but the offset (80 bytes) is not 256-byte aligned
+])
+def test_plan_contiguous_slice_is_a_view(shape, axis, start, end, aliased):
+    """A Slice whose result is one contiguous, aligned byte range of its
+    source becomes a view into the source's buffer instead of a copy."""
+    c = shape[1]
+    gb = GraphBuilder()
+    x = gb.input("x", shape)
+    t = gb.conv(x, gb.weight("w1", np.zeros((c, c, 1, 1), np.float16)))
+    s = gb.slice(t, axis, start, end)
+    cs = gb.shape(s)[1]
+    gb.output(gb.conv(s, gb.weight("w2", np.zeros((c, cs, 1, 1), np.float16))), "y")
+    k = _kernels(plan(*gb.finish()))
+    copies = [n for n in k if n.startswith("mlvc_strided_copy")]
+    assert (not copies) == aliased, k

@@ -598,3 +598,35 @@ def test_quantisation_tails_fused(q, h, w, monkeypatch):
     split.load_memory(graph, weights)
     for g, s in zip(got, split.run(inputs)):
         bits_equal(s, g)
+
+
+def test_slice_views_keep_their_source_alive():
+    """Contiguous slices are views into their source's buffer (no copy step).
+    The source stays allocated until the view's last reader: the convs
+    planned between the slice and its reader must not reuse its memory."""
+    from mlvc_b200.graph import kaiming_normal, small_bias
+    rng = np.random.default_rng(31)
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 64, 16, 24])
+
+    def conv(v, cin, cout, name):
+        return gb.conv(v, gb.weight(name + ".w", kaiming_normal(rng, (cout, cin, 1, 1), 1.0)),
+                       gb.weight(name + ".b", small_bias(rng, cout)))
+
+    t = conv(x, 64, 64, "c1")
+    s = gb.slice(t, 2, 4, 12)                  # rows 4..11 of t: a view at 12,288 bytes
+    u = gb.leaky_relu(conv(x, 64, 128, "c2"), 0.1)
+    u = conv(conv(u, 128, 64, "c3"), 64, 64, "c4")
+    y = gb.add(gb.slice(u, 2, 4, 12), s)      # both operands are views
+    gb.output(conv(y, 64, 64, "c5"), "y")
+    inputs = [rng.standard_normal((1, 64, 16, 24), dtype=np.float32).astype(np.float16)]
+    got, want, be = run_both(gb, inputs)
+    compare(got[0], want[0])
+    assert not [s_ for s_ in be.steps() if s_["kernel"].startswith("mlvc_strided_copy")], be.steps()
+    # the views are readable like any materialised tensor
+    graph, weights = gb.finish()
+    dbg = Backend(0, debug_tensors=True)
+    dbg.load_memory(graph, weights)
+    dbg.run(inputs)
+    from helpers import per_op_parity
+    assert per_op_parity(dbg, graph, weights, inputs) >= 6
