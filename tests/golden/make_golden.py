@@ -10,7 +10,7 @@ then two reference implementations produce the expected outputs:
                 (tests/unit/aot_tests.py:21-61, execute_graph), FP32 upcast.
 Inputs are seeded; everything is stored in <case>.npz next to the bundle.
 
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py [REFERENCE_TREE]
 """
 
 import os
