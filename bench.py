@@ -39,7 +39,8 @@ for p in (ROOT, ROOT / "mlvc.cpp_b200"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
 
-from mlvc_b200.graph import build_block_stack, build_conv3x3, build_mlvc_decoder_standin  # noqa: E402
+from mlvc_b200.graph import (build_block_stack, build_conv3x3, build_mlvc_decoder_standin,  # noqa: E402
+                             build_mlvcs_decoder_standin)
 
 METRIC = "conv-stack frames/s (config 2 block stack; stand-in for 1080p MLVC decode frames/s)"
 UNIT = "frames/s"
@@ -118,6 +119,16 @@ def workload(name):
         desc += ("; ref_feature <- feature bound as recurrent state (as the codec pipeline binds decoder input 3 to "
                  "output 1), so it stays on the device between frames")
         metric = f"MLVC-shaped decoder stand-in frames/s @{width}x{height} (stand-in for MLVC decode frames/s)"
+        graph, weights = gb.finish()
+        return graph, weights, inputs, desc, metric, [(3, 1)]
+    if name == "mlvcs_dec_640":
+        gb, inputs = build_mlvcs_decoder_standin(0, 640, 368)
+        desc = ("MLVC-S-shaped decoder stand-in @640x368 (the upstream MLVC-S architecture is absent): documented "
+                "small-profile sizes (feature 96, y/z 48 ch, hidden/recon 192, y_scale_repeat 4, mini hyperprior "
+                "z 1/64 with 2 blocks), x4 hyperprior up-sampling, QP-indexed dequantisation, 2+2+2 depth-conv "
+                "blocks (192 / 96 / 192 ch), x8 pixel-shuffle reconstruction; Kaiming-normal weights, seed 0; "
+                "ref_feature <- feature bound as recurrent state")
+        metric = "MLVC-S-shaped decoder stand-in frames/s @640x368 (stand-in for MLVC-S P-frame decode frames/s)"
         graph, weights = gb.finish()
         return graph, weights, inputs, desc, metric, [(3, 1)]
     if name == "conv3x3":
@@ -620,7 +631,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv",
-                                                   "op_mbconv", "mlvc_dec_1080p", "mlvc_dec_640", "entropy_1080p"],
+                                                   "op_mbconv", "mlvc_dec_1080p", "mlvc_dec_640", "mlvcs_dec_640",
+                                                   "entropy_1080p"],
                     default="block_stack")
     ap.add_argument("--cpu-frames", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -473,3 +473,75 @@ def build_mlvc_decoder_standin(seed=0, width=1920, height=1088, feature=256, lat
               _fp16(rng.standard_normal((1, feature, h8, w8), dtype=np.float32)),
               np.array([q_index], np.int32)]
     return gb, inputs
+
+
+def build_mlvcs_decoder_standin(seed=0, width=640, height=368, feature=96, latent=48, hyper=48, hidden=192,
+                                recon=192, y_scale_repeat=4, qp_num=72, q_index=21, hyper_blocks=2, blocks_y=2,
+                                blocks_feature=2, blocks_recon=2):
+    """MLVC-S-shaped decoder STAND-IN (the upstream MLVC-S architecture is
+    absent, like MLVC's).  Built from what the reference documents about the
+    small profile (models/profiles/profiles.json "mlvc-s-psnr-v1": hidden and
+    recon channels 192, two hyperprior blocks, y_scale_repeat 4, z and y 48
+    channels, the same depth-conv block; docs/design.md: feature 96 channels,
+    a mini hyperprior with a 6 x 10 z plane at 640x368, i.e. z at 1/64):
+
+    z_raw [1, 48, ceil(H/64), ceil(W/64)] -> 1x1 + LeakyReLU to 192 ->
+    hyper_blocks blocks -> two [1x1 to 4 x 192, pixel shuffle 2] stages ->
+    crop to the y plane -> prior (means 48 | context 144); y =
+    concat(y_raw_0, y_raw_1) * qscale[q] + means; concat(y, context) -> 1x1
+    -> blocks_y blocks at 1/16 (192) -> 1x1 to 4 x 96 + pixel shuffle 2 ->
+    concat(ref_feature) -> 1x1 -> blocks_feature blocks at 1/8 (96) = new
+    feature; 1x1 to 192 -> blocks_recon blocks -> 1x1 to 3 x 64 -> pixel
+    shuffle 8 = x_hat.  Weights and inputs as in build_mlvc_decoder_standin.
+    The 96- and 192-channel blocks take the kernels' general paths (separate
+    expand conv, stand-alone or fused depthwise, ReGLU GEMM + 1x1)."""
+    rng = np.random.default_rng(seed)
+    h8, w8 = -(-height // 8), -(-width // 8)
+    h16, w16 = -(-height // 16), -(-width // 16)
+    hz, wz = -(-height // 64), -(-width // 64)
+    if h8 != 2 * h16 or w8 != 2 * w16 or height != 8 * h8 or width != 8 * w8:
+        raise ValueError("stand-in needs H and W multiples of 16")
+    gb = GraphBuilder()
+    z = gb.input("z_raw", [1, hyper, hz, wz])
+    y0 = gb.input("y_raw_0", [1, latent // 2, h16, w16])
+    y1 = gb.input("y_raw_1", [1, latent // 2, h16, w16])
+    ref = gb.input("ref_feature", [1, feature, h8, w8])
+    q = gb.input("q_index_shifted", [1], "int32")
+
+    def conv1x1(x, cin, cout, name, gain=1.0):
+        w = gb.weight(name + ".weight", kaiming_normal(rng, (cout, cin, 1, 1), gain))
+        return gb.conv(x, w, gb.weight(name + ".bias", small_bias(rng, cout)))
+
+    # mini hyperprior decoder: 1/64 -> 1/16 (x4), cropped to the y plane
+    t = gb.leaky_relu(conv1x1(z, hyper, hidden, "hyper.in", np.sqrt(2.0)), 0.01)
+    for i in range(hyper_blocks):
+        t = _depth_conv_block(gb, rng, t, hidden, f"hyper.block{i}.", 0.25)
+    for i in range(2):
+        t = gb.depth_to_space(conv1x1(t, hidden, 4 * hidden, f"hyper.up{i}"), 2)
+    t = gb.slice(gb.slice(t, 2, 0, h16), 3, 0, w16)
+    means = gb.slice(t, 1, 0, latent)
+    context = gb.slice(t, 1, latent, hidden)
+    table = gb.weight("qscale", rng.uniform(0.5, 2.0, (qp_num, latent, 1, 1)).astype(np.float16))
+    y = gb.add(gb.mul(gb.concat([y0, y1], 1), gb.gather(table, q)), means)
+    # contextual decoder: 1/16 -> 1/8, joined with the reference feature
+    t = conv1x1(gb.concat([y, context], 1), hidden, hidden, "ctx.in")
+    for i in range(blocks_y):
+        t = _depth_conv_block(gb, rng, t, hidden, f"ctx.block{i}.", 0.25)
+    t = gb.depth_to_space(conv1x1(t, hidden, 4 * feature, "ctx.up"), 2)
+    t = conv1x1(gb.concat([t, ref], 1), 2 * feature, feature, "feat.in")
+    for i in range(blocks_feature):
+        t = _depth_conv_block(gb, rng, t, feature, f"feat.block{i}.", 0.25)
+    new_feature = t
+    # reconstruction: 1/8 -> full resolution
+    r = conv1x1(t, feature, recon, "recon.in")
+    for i in range(blocks_recon):
+        r = _depth_conv_block(gb, rng, r, recon, f"recon.block{i}.", 0.25)
+    x_hat = gb.depth_to_space(conv1x1(r, recon, 3 * 64, "recon.out"), 8)
+    gb.output(x_hat, "x_hat")
+    gb.output(new_feature, "feature")
+    inputs = [np.rint(rng.standard_normal((1, hyper, hz, wz)) * 4).astype(np.float16),
+              np.rint(rng.standard_normal((1, latent // 2, h16, w16)) * 3).astype(np.float16),
+              np.rint(rng.standard_normal((1, latent // 2, h16, w16)) * 3).astype(np.float16),
+              _fp16(rng.standard_normal((1, feature, h8, w8), dtype=np.float32)),
+              np.array([q_index], np.int32)]
+    return gb, inputs

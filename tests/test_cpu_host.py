@@ -236,6 +236,25 @@ def test_plan_mlvc_decoder_standin():
     assert [tuple(s) for _, _, s in be.outputs] == [(1, 3, 368, 640), (1, 256, 46, 80)]
 
 
+def test_plan_mlvcs_decoder_standin():
+    """The MLVC-S-shaped stand-in (96 / 192-channel blocks, 48-channel
+    latents) plans on the general paths: every 1x1 conv on tcgen05 (output
+    channels not a multiple of 64 included), the 384-channel depthwise fused
+    with its 192-channel projection, the 192-channel depthwise of the
+    96-channel blocks stand-alone (a 96-column output is no whole 64-column
+    panel), no scalar fallback; documented I/O shapes."""
+    from mlvc_b200.graph import build_mlvcs_decoder_standin
+    gb, inputs = build_mlvcs_decoder_standin(width=640, height=368)
+    be = plan(*gb.finish())
+    k = _kernels(be)
+    assert k.count("mlvc_conv1x1_tc") == 34 and k.count("mlvc_dwconv_tc") == 6, k
+    assert k.count("mlvc_depthwise3x3_f16") == 2, k
+    assert "mlvc_conv_direct_f16" not in k and "mlvc_unary_f16" not in k and "mlvc_reglu_f16" not in k
+    assert [tuple(s) for _, _, s in be.inputs] == [(1, 48, 6, 10), (1, 24, 23, 40), (1, 24, 23, 40),
+                                                     (1, 96, 46, 80), (1,)]
+    assert [tuple(s) for _, _, s in be.outputs] == [(1, 3, 368, 640), (1, 96, 46, 80)]
+
+
 @pytest.mark.parametrize("c,e,c_out,leaky,fused", [
     (128, 256, 128, True, True), (64, 64, 64, False, True), (64, 192, 128, True, True), (128, 128, 64, True, True),
     (192, 256, 128, True, False),  # input channels above two 64-channel halo slices

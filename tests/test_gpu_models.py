@@ -94,6 +94,20 @@ def test_mlvc_decoder_standin(width, height, tmp_path):
     _stack_check([x_hat, feature], graph, weights, inputs, tmp_path)
 
 
+@pytest.mark.parametrize("width,height", [(256, 128), (640, 368)])
+def test_mlvcs_decoder_standin(width, height, tmp_path):
+    """The MLVC-S-shaped stand-in (96 / 192-channel blocks, 48-channel
+    latents, x4 mini-hyperprior up-sampling): every materialised step against
+    the oracle, then the whole graph against the reference CPU backend."""
+    from mlvc_b200.graph import build_mlvcs_decoder_standin
+    gb, inputs = build_mlvcs_decoder_standin(seed=5, width=width, height=height)
+    be, graph, weights = _load(gb)
+    x_hat, feature = be.run(inputs)
+    assert x_hat.shape == (1, 3, height, width) and feature.shape == (1, 96, height // 8, width // 8)
+    assert per_op_parity(be, graph, weights, inputs, conv_impl="gemm") >= 40
+    _stack_check([x_hat, feature], graph, weights, inputs, tmp_path)
+
+
 def test_conv3x3_config1_per_op():
     gb, inputs = build_conv3x3(0)
     be, graph, weights = _load(gb)
