@@ -173,6 +173,23 @@ int mlvc_b200_extract_scales_device(mlvc_b200_backend* backend, uint64_t z_raw, 
 int mlvc_b200_integer_values_device(mlvc_b200_backend* backend, uint64_t values, size_t count, uint64_t symbols,
                                     uint64_t out_of_range);
 
+/* integer_values without any device allocation (no counterpart in the
+ * reference).  For callers that cannot allocate device memory: a device
+ * allocation synchronises the whole GPU, which a real-time encoder thread
+ * with a per-frame latency budget cannot afford, and a process whose device
+ * memory is owned by another framework's pool must not allocate behind its
+ * back.  Same arguments, results and errors as mlvc_b200_integer_values, but
+ * the staging of values and symbols and the out-of-range word live in a fixed
+ * array inside the library (about 12 MiB, held by every GPU that loads the
+ * library until the process exits), so needs no backend handle.  Limits:
+ * at most 2,097,152 values per call (larger calls fail with an error); runs
+ * on the calling thread's current device (cudaSetDevice, device 0 by
+ * default) and returns when the work is done; every call on a device shares
+ * the one array, so calls from several host threads at once race; the first
+ * call on a device looks the array's address up, so make it before any
+ * stream capture on that device. */
+int mlvc_b200_integer_values_noalloc(const uint16_t* values, size_t count, int32_t* symbols);
+
 /* Measurement hooks (no reference counterpart; the reference times whole
  * runs with steady_clock, codec/src/pipeline.cpp:341-415).  enqueue replays
  * the captured schedule on the backend's stream with the device-resident

@@ -7,6 +7,9 @@
    loaded at run time with cuModuleLoadData.
 3. g++ compiles the C++ host runtime (Driver API) and the C ABI and links
    against libcuda.
+4. nvcc compiles csrc/noalloc/*.cu (host and device code, CUDA runtime API)
+   into an object linked with the static CUDA runtime, so the library still
+   has no link-time dependency on libcudart or libcuda.
 
 Outputs: mlvc.cpp_b200/lib/libmlvc_b200.so (git-ignored, travels with the
 repository snapshot to the GPU machine).  Usage: python mlvc.cpp_b200/build.py
@@ -69,9 +72,16 @@ def build(force=False, verbose=False):
     # crashed the Python host, so prefer it over wrapper toolchains.
     cxx = "/usr/bin/g++" if Path("/usr/bin/g++").exists() else os.environ.get("CXX", "g++")
     host = sorted((HERE / "csrc" / "host").glob("*.cpp"))
+    rt_objs = []
+    for cu in sorted((HERE / "csrc" / "noalloc").glob("*.cu")):
+        obj = BUILD / (cu.stem + ".o")
+        _run([nvcc, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-ccbin", cxx, "-Xcompiler", "-fPIC", "-c",
+              "-o", str(obj), str(cu)])
+        rt_objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
     _run([cxx, "-std=c++20", "-O2", "-fPIC", "-shared", "-Wall", "-Wno-unused-function",
-          f"-I{CUDA / 'include'}", *map(str, host), str(blob),
+          f"-I{CUDA / 'include'}", *map(str, host), str(blob), *rt_objs,
+          f"-L{CUDA / 'lib64'}", "-lcudart_static", "-lrt", "-lpthread",
           "-ldl", "-o", str(tmp)])
     os.replace(tmp, LIB)
     if verbose:

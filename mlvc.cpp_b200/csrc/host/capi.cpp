@@ -14,6 +14,11 @@ struct mlvc_b200_backend {
     std::unique_ptr<mlvc_b200::Backend> impl;
 };
 
+namespace mlvc_b200 {
+// csrc/noalloc/integer_values_noalloc.cu
+void integer_values_noalloc(const uint16_t* values, size_t count, int32_t* symbols);
+}  // namespace mlvc_b200
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -243,6 +248,11 @@ int mlvc_b200_integer_values(mlvc_b200_backend* backend, const uint16_t* values,
             throw std::runtime_error("mlvc-b200: null value buffer");
         require(backend).integer_values(values, count, symbols);
     });
+}
+
+int mlvc_b200_integer_values_noalloc(const uint16_t* values, size_t count, int32_t* symbols)
+{
+    return guarded([&] { mlvc_b200::integer_values_noalloc(values, count, symbols); });
 }
 
 int mlvc_b200_configure_slots(mlvc_b200_backend* backend, size_t slot_count)

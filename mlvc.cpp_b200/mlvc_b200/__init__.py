@@ -69,6 +69,7 @@ EXPORTS = {
                                          ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
     "mlvc_b200_integer_values_device": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_uint64,
                                          ctypes.c_uint64], ctypes.c_int),
+    "mlvc_b200_integer_values_noalloc": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p], ctypes.c_int),
     "mlvc_b200_configure_slots": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_slot_count": ([ctypes.c_void_p], ctypes.c_size_t),
     "mlvc_b200_slot_input": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t], ctypes.c_void_p),
