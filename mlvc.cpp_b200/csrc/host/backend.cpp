@@ -578,11 +578,42 @@ void Backend::plan()
     // next node, a plain 1x1 conv with tensor-core output channels, is not
     // materialised; the conv streams its K panels from both tensors
     // (ConvTcParams::a_split).
+    // An operand that is a channel slice of a wider NHWC tensor, consumed only
+    // by the concat, is read in place as well: its A map starts at the slice's
+    // first channel and steps by the wider tensor's row (the slice is not
+    // materialised either).
     struct ConcatSrc {
-        uint32_t a, b;
-        int c1;
+        uint32_t a, b;  // tensors the two K ranges are read from
+        int c1;         // channels of the first operand
+        int a_off, a_row, b_off, b_row;  // first channel and row width (channels) within a / b
     };
     std::map<uint32_t, ConcatSrc> concat_src;  // concat output -> its two sources
+    auto channel_view = [&](uint32_t id, uint32_t& base, int& off, int& row, size_t& slice_node) -> bool {
+        if (!only_consumer(id))
+            return false;
+        for (size_t q = 0; q < nodes.size(); ++q) {
+            const NodeDesc& sl = nodes[q];
+            if (sl.output != id)
+                continue;
+            if (sl.op != Op::kSlice || absorbed[q])
+                return false;
+            const uint32_t src = sl.inputs[0];
+            const Value& sv = values_[src];
+            if (!sv.nhwc || sv.dtype != DType::kFp16 || sv.kind == Value::kWeight || sv.shape.size() != 4 ||
+                sv.shape[1] % 8)
+                return false;
+            const auto starts = int64s(sl.inputs[1]);
+            if (starts.size() != 1 || starts[0] < 0 || starts[0] % 8 ||
+                !is_channel_slice(sl, src, starts[0], starts[0] + values_[id].shape[1]))
+                return false;
+            base = src;
+            off = static_cast<int>(starts[0]);
+            row = static_cast<int>(sv.shape[1]);
+            slice_node = q;
+            return true;
+        }
+        return false;
+    };
     for (size_t j = 0; j + 1 < nodes.size(); ++j) {
         const NodeDesc& c = nodes[j];
         const NodeDesc& v = nodes[j + 1];
@@ -599,8 +630,28 @@ void Backend::plan()
             v.pads[0] != 0 || v.pads[1] != 0 || wv.kind != Value::kWeight || wv.dtype != DType::kFp16 ||
             wv.shape.size() != 4 || wv.shape[1] != c1 + c2 || wv.shape[2] != 1 || wv.shape[3] != 1 || wv.shape[0] % 8)
             continue;
-        concat_src[c.output] = {c.inputs[0], c.inputs[1], c1};
+        ConcatSrc cs{c.inputs[0], c.inputs[1], c1, 0, c1, 0, c2};
+        uint32_t base = 0;
+        int off = 0, row = 0;
+        size_t qa = 0, qb = 0;
+        const bool view_a = channel_view(c.inputs[0], base, off, row, qa);
+        if (view_a) {
+            cs.a = base;
+            cs.a_off = off;
+            cs.a_row = row;
+        }
+        const bool view_b = channel_view(c.inputs[1], base, off, row, qb);
+        if (view_b) {
+            cs.b = base;
+            cs.b_off = off;
+            cs.b_row = row;
+        }
+        concat_src[c.output] = cs;
         absorbed[j] = true;
+        if (view_a)
+            absorbed[qa] = true;
+        if (view_b)
+            absorbed[qb] = true;
     }
 
     for (size_t i = 0; i < nodes.size();) {
@@ -1046,22 +1097,27 @@ void Backend::plan()
                     const uint32_t a0_id = split_a ? split_it->second.a : x_id;
                     const uint32_t a1_id = split_a ? split_it->second.b : 0;
                     const int c0 = split_a ? split_it->second.c1 : K;
+                    const int a0_off = split_a ? split_it->second.a_off : 0, a0_row = split_a ? split_it->second.a_row : K;
+                    const int a1_off = split_a ? split_it->second.b_off : 0, a1_row = split_a ? split_it->second.b_row : 0;
                     s.build = [=, this](Step& st) {
                         ConvTcParams p{};
                         const CUdeviceptr wdev = prepped_dev_.get() + w_off;
                         const cuuint32_t elem1[2] = {1, 1};
-                        auto encode_a = [&](CUtensorMap* map, uint32_t id, int channels, const char* what) {
+                        // channels [off, off + channels) of a tensor whose rows hold `row` channels
+                        auto encode_a = [&](CUtensorMap* map, uint32_t id, int channels, int off, int row,
+                                            const char* what) {
                             const cuuint64_t dims[2] = {static_cast<cuuint64_t>(channels), static_cast<cuuint64_t>(M)};
-                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(channels) * 2};
+                            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row) * 2};
                             const cuuint32_t box[2] = {64, 128};
                             check(cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                                                         reinterpret_cast<void*>(values_[id].addr), dims, strides, box,
+                                                         reinterpret_cast<void*>(values_[id].addr + off * 2), dims,
+                                                         strides, box,
                                                          elem1, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
                                   what);
                         };
-                        encode_a(&p.map_a0, a0_id, c0, "cuTensorMapEncodeTiled(conv1x1 A)");
+                        encode_a(&p.map_a0, a0_id, c0, a0_off, a0_row, "cuTensorMapEncodeTiled(conv1x1 A)");
                         {
                             const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(NN)};
                             const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
@@ -1074,7 +1130,8 @@ void Backend::plan()
                                   "cuTensorMapEncodeTiled(conv1x1 B)");
                         }
                         if (a1_id) {
-                            encode_a(&p.map_a1, a1_id, K - c0, "cuTensorMapEncodeTiled(conv1x1 A, second concat operand)");
+                            encode_a(&p.map_a1, a1_id, K - c0, a1_off, a1_row,
+                                     "cuTensorMapEncodeTiled(conv1x1 A, second concat operand)");
                             p.a_split = c0 / 64;
                         } else {
                             p.map_a1 = p.map_a0;

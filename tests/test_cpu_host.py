@@ -194,6 +194,28 @@ def test_plan_concat_read_in_place_by_1x1(c1, c2, oc, other_reader, absorbed):
     assert "mlvc_conv1x1_tc" in k
 
 
+@pytest.mark.parametrize("start,end,other_reader,absorbed", [
+    (128, 256, False, True), (64, 128, False, True),
+    (4, 68, False, False),     # slice start not 16-byte aligned (4 channels)
+    (128, 256, True, False),   # the slice has another reader: materialised, then read in place
+])
+def test_plan_concat_of_channel_slice_read_in_place(start, end, other_reader, absorbed):
+    """A concat operand that is a channel slice of a wider tensor, read only
+    by the concat, is read in place by the 1x1 conv (no copy at all)."""
+    gb = GraphBuilder()
+    t = gb.leaky_relu(gb.input("t", [1, 256, 6, 20]), 0.1)
+    b = gb.input("b", [1, 128, 6, 20])
+    sl = gb.slice(t, 1, start, end)
+    cat = gb.concat([b, sl], 1)
+    gb.output(gb.conv(cat, gb.weight("w", np.zeros((64, 128 + end - start, 1, 1), np.float16))), "y")
+    if other_reader:
+        gb.output(gb.leaky_relu(sl, 0.2), "z")
+    k = _kernels(plan(*gb.finish()))
+    copies = sum(1 for x in k if x.startswith("mlvc_strided_copy"))
+    assert (copies == 0) == absorbed, k
+    assert "mlvc_conv1x1_tc" in k
+
+
 @pytest.mark.parametrize("state_read_last", [False, True])
 def test_plan_state_output_aliases_state_buffer(state_read_last):
     """A state-bound output is written in place into the state buffer when
@@ -226,9 +248,10 @@ def test_plan_mlvc_decoder_standin():
     be = plan(graph, weights)
     k = _kernels(be)
     assert k.count("mlvc_conv1x1_tc") == 29 and k.count("mlvc_dwconv_tc") == 7, k
-    # the hyperprior's row crop and full-width slice are views; the two channel
-    # slices and the latent concat are copies
-    assert k.count("mlvc_strided_copy_v8_f16") == 4, k
+    # the hyperprior's row crop and full-width slice are views, the context
+    # channel slice is read in place by the 1x1 conv after its concat; the
+    # means slice and the latent concat are copies
+    assert k.count("mlvc_strided_copy_v8_f16") == 3, k
     assert "mlvc_depthwise3x3_f16" not in k
     assert "mlvc_conv_direct_f16" not in k and "mlvc_unary_f16" not in k and "mlvc_reglu_f16" not in k
     assert [tuple(s) for _, _, s in be.inputs] == [(1, 128, 3, 5), (1, 64, 23, 40), (1, 64, 23, 40),

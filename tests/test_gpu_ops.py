@@ -403,6 +403,39 @@ def test_conv1x1_concat_read_in_place(c1, c2, oc, epilogue):
     assert kernels == ["mlvc_conv1x1_tc"], kernels
 
 
+@pytest.mark.parametrize("first,second", [((256, 128, 256), None), (None, (192, 64, 128)), ((128, 0, 64), (128, 64, 128))])
+def test_conv1x1_concat_of_channel_slices_read_in_place(first, second):
+    """Concat operands that are channel slices of wider tensors (each slice's
+    only reader being the concat) are read in place too: the conv's A map
+    starts at the slice's first channel and steps by the wider tensor's row.
+    first / second: (channels of the wider tensor, slice start, slice end), or
+    None for a plain tensor of 128 channels."""
+    rng = np.random.default_rng(29)
+    h, w = 17, 30
+    gb = GraphBuilder()
+    inputs = []
+
+    def operand(spec, name):
+        if spec is None:
+            inputs.append(rng.standard_normal((1, 128, h, w), dtype=np.float32).astype(np.float16))
+            return gb.input(name, [1, 128, h, w]), 128
+        c, lo, hi = spec
+        wide = gb.input(name, [1, c, h, w])
+        inputs.append(rng.standard_normal((1, c, h, w), dtype=np.float32).astype(np.float16))
+        # the wider tensor is produced on the device (a LeakyReLU), as in the decoder graphs
+        return gb.slice(gb.leaky_relu(wide, 0.1), 1, lo, hi), hi - lo
+
+    a, c1 = operand(first, "a")
+    b, c2 = operand(second, "b")
+    wt = gb.weight("w", (rng.standard_normal((128, c1 + c2, 1, 1), dtype=np.float32) *
+                         np.sqrt(1.0 / (c1 + c2))).astype(np.float16))
+    gb.output(gb.conv(gb.concat([a, b], 1), wt, gb.weight("bias", rng.uniform(-0.1, 0.1, 128).astype(np.float16))), "y")
+    got, want, be = run_both(gb, inputs)
+    compare(got[0], want[0])
+    kernels = [s["kernel"] for s in be.steps() if s["kernel"] not in ("mlvc_boundary_f16", "mlvc_unary_f16")]
+    assert kernels == ["mlvc_conv1x1_tc"], kernels
+
+
 @pytest.mark.parametrize("c,h,w", [(64, 6, 10), (32, 4, 14), (24, 4, 6)])
 def test_pixel_shuffle_mid_graph(c, h, w):
     """Pixel shuffle / unshuffle between two other operators (not folded into
