@@ -424,6 +424,66 @@ void Backend::plan()
     std::vector<size_t> prepped_for_weight;  // not used yet
     (void)prepped_for_weight;
 
+    // ---- operand extents of the data-movement and elementwise operators.
+    // Their kernels index operands by the output's extents, so a graph whose
+    // declared shapes disagree would read or write past a buffer: reject it.
+    for (const auto& n : graph_.nodes) {
+        const auto od = dims4(values_[n.output].shape);
+        const int rank = static_cast<int>(values_[n.output].shape.size());
+        if (n.op == Op::kConcat) {
+            int axis = n.axis < 0 ? n.axis + rank : n.axis;
+            if (axis < 0 || axis >= rank)
+                throw std::runtime_error("mlvc-b200: Concat axis out of range");
+            axis += 4 - rank;
+            long long sum = 0;
+            for (auto id : n.inputs) {
+                const auto d = dims4(values_[id].shape);
+                for (int l = 0; l < 4; ++l)
+                    if (l != axis && d[l] != od[l])
+                        throw std::runtime_error("mlvc-b200: Concat operand shapes do not match its output");
+                sum += d[axis];
+            }
+            if (sum != od[axis])
+                throw std::runtime_error("mlvc-b200: Concat operand shapes do not match its output");
+        } else if (n.op == Op::kSlice) {
+            const Value& av = values_[n.inputs[0]];
+            const int arank = static_cast<int>(av.shape.size());
+            if (arank != rank)
+                throw std::runtime_error("mlvc-b200: Slice changes the tensor rank");
+            const auto id4 = dims4(av.shape);
+            const auto starts = int64s(n.inputs[1]);
+            const auto axes = n.inputs.size() > 3 && n.inputs[3] ? int64s(n.inputs[3]) : std::vector<int64_t>{};
+            const auto stepv = n.inputs.size() > 4 && n.inputs[4] ? int64s(n.inputs[4]) : std::vector<int64_t>{};
+            std::array<long long, 4> start4{0, 0, 0, 0}, step4{1, 1, 1, 1};
+            for (size_t k = 0; k < starts.size(); ++k) {
+                long long axis = axes.empty() ? static_cast<long long>(k) : axes.at(k);
+                if (axis < 0)
+                    axis += arank;
+                if (axis < 0 || axis >= arank)
+                    throw std::runtime_error("mlvc-b200: Slice axis out of range");
+                axis += 4 - arank;
+                long long st0 = starts[k];
+                if (st0 < 0)
+                    st0 += id4[axis];
+                start4[axis] = st0;
+                if (!stepv.empty())
+                    step4[axis] = stepv.at(k);
+            }
+            for (int l = 0; l < 4; ++l) {
+                const long long last = start4[l] + (od[l] - 1) * step4[l];
+                if (start4[l] < 0 || start4[l] >= id4[l] || last < 0 || last >= id4[l])
+                    throw std::runtime_error("mlvc-b200: Slice output exceeds its input");
+            }
+        } else if (n.op == Op::kAdd || n.op == Op::kSub || n.op == Op::kMul) {
+            for (auto id : n.inputs) {
+                const auto d = dims4(values_[id].shape);
+                for (int l = 0; l < 4; ++l)
+                    if (d[l] != 1 && d[l] != od[l])
+                        throw std::runtime_error("mlvc-b200: binary operand does not broadcast to the output shape");
+            }
+        }
+    }
+
     // ---- boundary: NCHW host layout <-> NHWC device layout.  A SpaceToDepth
     // that is the only consumer of a graph input, and a DepthToSpace that
     // produces a graph output from a private tensor, are folded into the

@@ -505,3 +505,51 @@ def test_plan_contiguous_slice_is_a_view(shape, axis, start, end, aliased):
     k = _kernels(plan(*gb.finish()))
     copies = [n for n in k if n.startswith("mlvc_strided_copy")]
     assert (not copies) == aliased, k
+
+
+@pytest.mark.parametrize("case,copies", [("input_rows", 1), ("view_of_view", 0), ("input_channels_concat", 0)])
+def test_plan_slice_views_of_inputs_and_chains(case, copies):
+    """A row slice of a graph input is copied (only values the schedule
+    produces become views); a contiguous slice of a contiguous slice is a
+    view of the first source; a channel slice of an input is still read in
+    place by the 1x1 conv after its concat."""
+    gb = GraphBuilder()
+    w = lambda cin: gb.weight("w", np.zeros((64, cin, 1, 1), np.float16))  # noqa: E731
+    if case == "input_rows":
+        x = gb.input("x", [1, 64, 16, 16])
+        gb.output(gb.conv(gb.slice(x, 2, 0, 8), w(64)), "y")
+    elif case == "view_of_view":
+        t = gb.leaky_relu(gb.input("x", [1, 64, 16, 16]), 0.1)
+        gb.output(gb.conv(gb.slice(gb.slice(t, 2, 0, 12), 2, 4, 12), w(64)), "y")
+    else:
+        x = gb.input("x", [1, 128, 16, 16])
+        b = gb.input("b", [1, 64, 16, 16])
+        gb.output(gb.conv(gb.concat([b, gb.slice(x, 1, 64, 128)], 1), w(128)), "y")
+    k = _kernels(plan(*gb.finish()))
+    assert sum(1 for n in k if n.startswith("mlvc_strided_copy")) == copies, k
+
+
+def _bad_shape_graph(what):
+    gb = GraphBuilder()
+    a = gb.input("a", [1, 64, 8, 16])
+    b = gb.input("b", [1, 64, 16, 16])
+    if what == "concat":      # operands disagree outside the concat axis
+        y = gb.concat([a, b], 1)
+    elif what == "slice":     # declared output runs past the input
+        y = gb.slice(b, 2, 4, 16)
+        gb.tensors[y].shape[2] = 16
+    else:                     # operand neither 1 nor the output's extent
+        y = gb.add(a, a)
+        gb.tensors[y].shape[2] = 16
+    gb.output(gb.leaky_relu(y, 0.1), "y")
+    return gb.finish()
+
+
+@pytest.mark.parametrize("what,message", [("concat", "Concat operand shapes"), ("slice", "exceeds its input"),
+                                          ("binary", "does not broadcast")])
+def test_plan_rejects_inconsistent_operand_extents(what, message):
+    """Copy and elementwise kernels index their operands by the output's
+    extents; a graph whose declared shapes disagree is rejected at load
+    instead of reading or writing past a buffer."""
+    with pytest.raises(RuntimeError, match=message):
+        plan(*_bad_shape_graph(what))
