@@ -481,6 +481,19 @@ void Backend::plan()
                     if (d[l] != 1 && d[l] != od[l])
                         throw std::runtime_error("mlvc-b200: binary operand does not broadcast to the output shape");
             }
+        } else if (n.op == Op::kLeakyRelu || n.op == Op::kClip || n.op == Op::kSigmoid || n.op == Op::kReciprocal ||
+                   n.op == Op::kRound) {
+            if (dims4(values_[n.inputs[0]].shape) != od)
+                throw std::runtime_error("mlvc-b200: elementwise operator changes the tensor shape");
+        } else if (n.op == Op::kDepthToSpace || n.op == Op::kSpaceToDepth) {
+            const auto d = dims4(values_[n.inputs[0]].shape);
+            const long long r = n.block, rr = r * r;
+            const std::array<long long, 4> want =
+                n.op == Op::kDepthToSpace ? std::array<long long, 4>{d[0], d[1] / rr, d[2] * r, d[3] * r}
+                                          : std::array<long long, 4>{d[0], d[1] * rr, d[2] / r, d[3] / r};
+            const bool divisible = n.op == Op::kDepthToSpace ? d[1] % rr == 0 : d[2] % r == 0 && d[3] % r == 0;
+            if (!divisible || want[0] != od[0] || want[1] != od[1] || want[2] != od[2] || want[3] != od[3])
+                throw std::runtime_error("mlvc-b200: pixel (un)shuffle output shape does not match its input");
         }
     }
 

@@ -538,15 +538,22 @@ def _bad_shape_graph(what):
     elif what == "slice":     # declared output runs past the input
         y = gb.slice(b, 2, 4, 16)
         gb.tensors[y].shape[2] = 16
-    else:                     # operand neither 1 nor the output's extent
+    elif what == "binary":    # operand neither 1 nor the output's extent
         y = gb.add(a, a)
         gb.tensors[y].shape[2] = 16
+    elif what == "unary":     # elementwise output larger than its input
+        y = gb.leaky_relu(a, 0.2)
+        gb.tensors[y].shape[2] = 16
+    else:                     # pixel shuffle output that does not follow from its input
+        y = gb.depth_to_space(b, 2)
+        gb.tensors[y].shape[1] = 32
     gb.output(gb.leaky_relu(y, 0.1), "y")
     return gb.finish()
 
 
 @pytest.mark.parametrize("what,message", [("concat", "Concat operand shapes"), ("slice", "exceeds its input"),
-                                          ("binary", "does not broadcast")])
+                                          ("binary", "does not broadcast"), ("unary", "changes the tensor shape"),
+                                          ("shuffle", "pixel .un.shuffle output shape")])
 def test_plan_rejects_inconsistent_operand_extents(what, message):
     """Copy and elementwise kernels index their operands by the output's
     extents; a graph whose declared shapes disagree is rejected at load
