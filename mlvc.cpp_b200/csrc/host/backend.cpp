@@ -485,6 +485,19 @@ void Backend::plan()
                    n.op == Op::kRound) {
             if (dims4(values_[n.inputs[0]].shape) != od)
                 throw std::runtime_error("mlvc-b200: elementwise operator changes the tensor shape");
+        } else if (n.op == Op::kConv) {
+            const auto& x = values_[n.inputs[0]].shape;
+            const auto& w = values_[n.inputs[1]].shape;
+            const auto& o = values_[n.output].shape;
+            if (x.size() == 4 && w.size() == 4 && o.size() == 4) {
+                const long long g = n.groups, sh = n.strides[0], sw = n.strides[1], ph = n.pads[0], pw = n.pads[1];
+                const long long oh = (x[2] + 2 * ph - w[2]) / sh + 1, ow = (x[3] + 2 * pw - w[3]) / sw + 1;
+                const bool bias_ok = n.inputs.size() < 3 || !n.inputs[2] ||
+                                     element_count(values_[n.inputs[2]].shape) == w[0];
+                if (sh <= 0 || sw <= 0 || x[2] + 2 * ph < w[2] || x[3] + 2 * pw < w[3] || o[0] != x[0] ||
+                    o[1] != w[0] || x[1] != w[1] * g || w[0] % g || o[2] != oh || o[3] != ow || !bias_ok)
+                    throw std::runtime_error("mlvc-b200: Conv shapes do not match its input, weights and attributes");
+            }
         } else if (n.op == Op::kDepthToSpace || n.op == Op::kSpaceToDepth) {
             const auto d = dims4(values_[n.inputs[0]].shape);
             const long long r = n.block, rr = r * r;

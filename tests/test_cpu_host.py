@@ -544,16 +544,20 @@ def _bad_shape_graph(what):
     elif what == "unary":     # elementwise output larger than its input
         y = gb.leaky_relu(a, 0.2)
         gb.tensors[y].shape[2] = 16
-    else:                     # pixel shuffle output that does not follow from its input
+    elif what == "shuffle":   # pixel shuffle output that does not follow from its input
         y = gb.depth_to_space(b, 2)
         gb.tensors[y].shape[1] = 32
+    else:                     # conv output larger than stride / padding allow
+        y = gb.conv(b, gb.weight("w", np.zeros((64, 64, 3, 3), np.float16)), None, (2, 2), (1, 1))
+        gb.tensors[y].shape[2] = 16
     gb.output(gb.leaky_relu(y, 0.1), "y")
     return gb.finish()
 
 
 @pytest.mark.parametrize("what,message", [("concat", "Concat operand shapes"), ("slice", "exceeds its input"),
                                           ("binary", "does not broadcast"), ("unary", "changes the tensor shape"),
-                                          ("shuffle", "pixel .un.shuffle output shape")])
+                                          ("shuffle", "pixel .un.shuffle output shape"),
+                                          ("conv", "Conv shapes do not match")])
 def test_plan_rejects_inconsistent_operand_extents(what, message):
     """Copy and elementwise kernels index their operands by the output's
     extents; a graph whose declared shapes disagree is rejected at load
