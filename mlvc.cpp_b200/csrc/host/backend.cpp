@@ -485,6 +485,13 @@ void Backend::plan()
                    n.op == Op::kRound) {
             if (dims4(values_[n.inputs[0]].shape) != od)
                 throw std::runtime_error("mlvc-b200: elementwise operator changes the tensor shape");
+        } else if (n.op == Op::kGather) {
+            // one row of the table per index; the kernel copies one row
+            const auto& dshape = values_[n.inputs[0]].shape;
+            const long long idx = element_count(values_[n.inputs[1]].shape);
+            const long long row = dshape.empty() || dshape[0] <= 0 ? 0 : element_count(dshape) / dshape[0];
+            if (idx != 1 || element_count(values_[n.output].shape) != row)
+                throw std::runtime_error("mlvc-b200: Gather takes one index and produces one table row");
         } else if (n.op == Op::kConv) {
             const auto& x = values_[n.inputs[0]].shape;
             const auto& w = values_[n.inputs[1]].shape;

@@ -547,6 +547,10 @@ def _bad_shape_graph(what):
     elif what == "shuffle":   # pixel shuffle output that does not follow from its input
         y = gb.depth_to_space(b, 2)
         gb.tensors[y].shape[1] = 32
+    elif what == "gather":    # declared output larger than one table row
+        table = gb.weight("table", np.zeros((4, 64, 1, 1), np.float16))
+        y = gb.mul(a, gb.gather(table, gb.input("q", [1], "int32")))
+        gb.tensors[gb.nodes[-2].output].shape[0] = 2
     else:                     # conv output larger than stride / padding allow
         y = gb.conv(b, gb.weight("w", np.zeros((64, 64, 3, 3), np.float16)), None, (2, 2), (1, 1))
         gb.tensors[y].shape[2] = 16
@@ -557,7 +561,8 @@ def _bad_shape_graph(what):
 @pytest.mark.parametrize("what,message", [("concat", "Concat operand shapes"), ("slice", "exceeds its input"),
                                           ("binary", "does not broadcast"), ("unary", "changes the tensor shape"),
                                           ("shuffle", "pixel .un.shuffle output shape"),
-                                          ("conv", "Conv shapes do not match")])
+                                          ("conv", "Conv shapes do not match"),
+                                          ("gather", "Gather takes one index")])
 def test_plan_rejects_inconsistent_operand_extents(what, message):
     """Copy and elementwise kernels index their operands by the output's
     extents; a graph whose declared shapes disagree is rejected at load
