@@ -1603,7 +1603,12 @@ void Backend::plan()
         }
 
         // ---- latent quantisation tails (reference matchers:
-        // fusion_registry.cpp:14-225 for y0, :226-404 for y1)
+        // fusion_registry.cpp:14-225 for y0, :226-404 for y1; the CPU twins
+        // backends/cpu/src/fusion_matcher.cpp:543-850).  As there, the operands
+        // of the Adds and Muls may come in either order, the Clip's upper bound
+        // may be absent or >= 65504 (the reference's exporter writes 65504), and
+        // in the y0 tail an optional Mul of the reciprocal by an FP16 scalar 1
+        // may follow the Reciprocal.
         if (tail_fusion_ && (n.op == Op::kSlice || n.op == Op::kSub)) {
             const bool y0 = n.op == Op::kSlice;
             static constexpr Op kY0[19] = {Op::kSlice, Op::kSlice, Op::kClip,   Op::kReciprocal, Op::kMul,
@@ -1613,17 +1618,44 @@ void Backend::plan()
             static constexpr Op kY1[15] = {Op::kSub, Op::kMul,   Op::kSlice, Op::kSlice, Op::kAdd,
                                            Op::kRound, Op::kSlice, Op::kSlice, Op::kAdd,   Op::kMul,
                                            Op::kAdd, Op::kMul,   Op::kConcat, Op::kAdd,  Op::kMul};
+            auto is_one = [&](uint32_t id) {
+                if (id == 0 || values_[id].kind != Value::kWeight || values_[id].dtype != DType::kFp16 ||
+                    element_count(values_[id].shape) != 1)
+                    return false;
+                return std::fabs(half_bits_to_float(wdata(id)[0]) - 1.0f) <= 1e-4f;
+            };
+            // y0 with the Mul-by-one: chain nodes 4.. sit one index later
+            size_t extra = 0;
+            if (y0 && i + 20 <= nodes.size() && nodes[i + 3].op == Op::kReciprocal && nodes[i + 4].op == Op::kMul &&
+                nodes[i + 5].op == Op::kMul && nodes[i + 4].inputs.size() == 2 && !absorbed[i + 4]) {
+                const auto& m = nodes[i + 4].inputs;
+                const uint32_t r = nodes[i + 3].output;
+                if ((m[0] == r && is_one(m[1])) || (m[1] == r && is_one(m[0])))
+                    extra = 1;
+            }
+            auto at = [&](size_t k) { return i + k + (k >= 4 ? extra : 0); };
             const Op* pat = y0 ? kY0 : kY1;
-            const size_t len = y0 ? 19 : 15;
+            const size_t chain = y0 ? 19 : 15;
+            const size_t len = chain + extra;
             bool ok = i + len <= nodes.size();
-            for (size_t k = 0; ok && k < len; ++k)
-                ok = nodes[i + k].op == pat[k] && !absorbed[i + k];
-            auto out = [&](size_t k) { return nodes[i + k].output; };
-            auto in = [&](size_t k) -> const std::vector<uint32_t>& { return nodes[i + k].inputs; };
+            for (size_t k = 0; ok && k < chain; ++k)
+                ok = nodes[at(k)].op == pat[k] && !absorbed[at(k)];
+            auto out = [&](size_t k) { return nodes[at(k)].output; };
+            auto in = [&](size_t k) -> const std::vector<uint32_t>& { return nodes[at(k)].inputs; };
             auto vec = [](std::initializer_list<uint32_t> l) { return std::vector<uint32_t>(l); };
+            auto pair = [&](size_t k, uint32_t a, uint32_t b) {  // inputs are {a, b} in either order
+                const auto& v = in(k);
+                return v.size() == 2 && ((v[0] == a && v[1] == b) || (v[0] == b && v[1] == a));
+            };
+            auto other = [&](size_t k, uint32_t a) -> uint32_t {  // the operand beside `a`, or 0
+                const auto& v = in(k);
+                if (v.size() != 2)
+                    return 0;
+                return v[0] == a ? v[1] : v[1] == a ? v[0] : 0;
+            };
             auto rt = [&](uint32_t id) {  // runtime NHWC FP16 rank-4 value
                 const Value& v = values_[id];
-                return v.present && v.nhwc && v.dtype == DType::kFp16 && v.shape.size() == 4;
+                return id != 0 && v.present && v.nhwc && v.dtype == DType::kFp16 && v.shape.size() == 4;
             };
             auto cons = [&](uint32_t id, int c) { return values_[id].consumers == c && !values_[id].graph_output; };
             // chain offsets of: scaled, y_raw, prior slices, updates (y0 numbering minus 5 for y1)
@@ -1632,47 +1664,43 @@ void Backend::plan()
             int Q = 0;
             if (ok) {
                 const uint32_t scaled = out(6 - d), y_raw = out(10 - d);
-                ok = in(7 - d).size() >= 1 && in(7 - d)[0] == scaled && in(8 - d).size() >= 1 && in(8 - d)[0] == scaled &&
-                     in(9 - d) == vec({out(7 - d), out(8 - d)}) && in(10 - d) == vec({out(9 - d)}) &&
-                     in(13 - d) == vec({y_raw, out(11 - d)}) && in(14 - d).size() == 2 && in(14 - d)[0] == out(13 - d) &&
-                     in(15 - d) == vec({y_raw, out(12 - d)}) && in(16 - d).size() == 2 && in(16 - d)[0] == out(15 - d) &&
-                     in(17 - d) == vec({out(14 - d), out(16 - d)}) && rt(y_raw);
+                qs_id = other(6 - d, out(5 - d));
+                us0_id = other(14 - d, out(13 - d));
+                us1_id = other(16 - d, out(15 - d));
+                ok = rt(y_raw) && pair(9 - d, out(7 - d), out(8 - d)) && in(10 - d) == vec({out(9 - d)}) &&
+                     pair(13 - d, y_raw, out(11 - d)) && pair(15 - d, y_raw, out(12 - d)) &&
+                     in(17 - d) == vec({out(14 - d), out(16 - d)}) && rt(qs_id) && rt(us0_id) && rt(us1_id);
                 if (ok) {
                     Q = static_cast<int>(values_[y_raw].shape[1]);
-                    qs_id = in(6 - d)[1];
-                    us0_id = in(14 - d)[1];
-                    us1_id = in(16 - d)[1];
-                    ok = Q % 8 == 0 && in(6 - d).size() == 2 && in(6 - d)[0] == out(5 - d) && rt(qs_id) && rt(us0_id) &&
-                         rt(us1_id) && cons(out(5 - d), 1) && cons(scaled, 2) && cons(out(7 - d), 1) &&
-                         cons(out(8 - d), 1) && cons(out(9 - d), 1) && values_[y_raw].consumers == 2 &&
-                         cons(out(11 - d), 1) && cons(out(12 - d), 1) && cons(out(13 - d), 1) && cons(out(14 - d), 1) &&
-                         cons(out(15 - d), 1) && cons(out(16 - d), 1) &&
-                         (nodes[i + 17 - d].axis == 1 || nodes[i + 17 - d].axis == -3);
+                    ok = Q % 8 == 0 && is_channel_slice(nodes[at(7 - d)], scaled, 0, Q) &&
+                         is_channel_slice(nodes[at(8 - d)], scaled, Q, 2 * Q) && cons(out(5 - d), 1) &&
+                         cons(scaled, 2) && cons(out(7 - d), 1) && cons(out(8 - d), 1) && cons(out(9 - d), 1) &&
+                         values_[y_raw].consumers >= 2 && cons(out(11 - d), 1) && cons(out(12 - d), 1) &&
+                         cons(out(13 - d), 1) && cons(out(14 - d), 1) && cons(out(15 - d), 1) &&
+                         cons(out(16 - d), 1) && (nodes[at(17 - d)].axis == 1 || nodes[at(17 - d)].axis == -3);
                 }
             }
             if (ok && y0) {
                 prior_id = n.inputs[0];
-                latent_id = in(4).size() == 2 ? in(4)[0] : 0;
+                const uint32_t inv = extra ? nodes[i + 4].output : out(3);
+                latent_id = other(4, inv);
                 ok = in(1)[0] == prior_id && rt(prior_id) && values_[prior_id].shape[1] == 4 * Q &&
                      is_channel_slice(nodes[i], prior_id, 0, 2 * Q) && is_channel_slice(nodes[i + 1], prior_id, 2 * Q, 4 * Q) &&
-                     in(2).size() >= 2 && in(2)[0] == out(0) && in(3) == vec({out(2)}) && in(4).size() == 2 &&
-                     in(4)[1] == out(3) && rt(latent_id) && in(5) == vec({out(4), out(1)}) &&
-                     in(11)[0] == out(1) && in(12)[0] == out(1) && is_channel_slice(nodes[i + 7], out(6), 0, Q) &&
-                     is_channel_slice(nodes[i + 8], out(6), Q, 2 * Q) && is_channel_slice(nodes[i + 11], out(1), 0, Q) &&
-                     is_channel_slice(nodes[i + 12], out(1), Q, 2 * Q) && in(18) == vec({out(17), prior_id}) &&
-                     (nodes[i + 18].axis == 1 || nodes[i + 18].axis == -3) && cons(out(0), 1) && cons(out(1), 3) &&
-                     cons(out(3), 1) && values_[prior_id].consumers == 3 && rt(out(18)) &&
-                     (in(2).size() < 3 || in(2)[2] == 0);
+                     in(2).size() >= 2 && in(2)[0] == out(0) &&
+                     (in(2).size() < 3 || in(2)[2] == 0 || scalar(in(2)[2], INFINITY) >= 65504.0f) &&
+                     in(3) == vec({out(2)}) && rt(latent_id) && in(5) == vec({out(4), out(1)}) &&
+                     is_channel_slice(nodes[at(11)], out(1), 0, Q) && is_channel_slice(nodes[at(12)], out(1), Q, 2 * Q) &&
+                     in(18) == vec({out(17), prior_id}) && (nodes[at(18)].axis == 1 || nodes[at(18)].axis == -3) &&
+                     cons(out(0), 1) && cons(out(1), 3) && cons(out(3), 1) && (!extra || cons(inv, 1)) &&
+                     values_[prior_id].consumers >= 3 && rt(out(18));
             } else if (ok) {
                 norm_id = n.inputs[0];
                 prior_id = n.inputs.size() == 2 ? n.inputs[1] : 0;
-                c2_id = in(13).size() == 2 ? in(13)[0] : 0;
-                cl_id = in(14).size() == 2 ? in(14)[1] : 0;
-                ok = rt(norm_id) && rt(prior_id) && rt(c2_id) && rt(cl_id) && in(13).size() == 2 && in(13)[1] == out(12) &&
-                     in(14).size() == 2 && in(14)[0] == out(13) && in(6)[0] == prior_id && in(7)[0] == prior_id &&
-                     is_channel_slice(nodes[i + 2], out(1), 0, Q) && is_channel_slice(nodes[i + 3], out(1), Q, 2 * Q) &&
-                     is_channel_slice(nodes[i + 6], prior_id, 0, Q) && is_channel_slice(nodes[i + 7], prior_id, Q, 2 * Q) &&
-                     values_[prior_id].consumers == 3 && cons(out(12), 1) && cons(out(13), 1) && rt(out(14));
+                c2_id = other(13, out(12));
+                cl_id = other(14, out(13));
+                ok = rt(norm_id) && rt(prior_id) && rt(c2_id) && rt(cl_id) && is_channel_slice(nodes[at(6)], prior_id, 0, Q) &&
+                     is_channel_slice(nodes[at(7)], prior_id, Q, 2 * Q) && values_[prior_id].consumers >= 3 &&
+                     cons(out(12), 1) && cons(out(13), 1) && rt(out(14));
             }
             if (ok) {
                 const std::vector<int64_t> raw = values_[out(10 - d)].shape;

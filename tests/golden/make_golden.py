@@ -8,9 +8,17 @@ then two reference implementations produce the expected outputs:
                 (oracle/_ref), scalar ISA (MLVC_CPU_ISA=scalar) and AVX2;
   * replay    - the reference's independent PyTorch replay of the graph
                 (tests/unit/aot_tests.py:21-61, execute_graph), FP32 upcast.
+The tail cases (feature_update_enc, feature_update_dec, quant_tails) hold
+the operator chains the reference fuses into one kernel each (Sigmoid,
+Reciprocal, Round; backends/cpu/src/fusion_matcher.cpp:413-850, kernels at
+backends/cpu/src/kernels_scalar.cpp:324-537); they also record the reference
+CPU backend with fusion disabled (MLVC_CPU_DISABLE_FUSION=1), i.e. operator
+by operator.  The AVX2 sigmoid is an approximation, so the scalar ISA is the
+bit-level reference for sigmoid-bearing cases.
 Inputs are seeded; everything is stored in <case>.npz next to the bundle.
 
-    python tests/golden/make_golden.py [REFERENCE_TREE]
+    python tests/golden/make_golden.py REFERENCE_TREE [CASE ...]
+    MLVC_REFERENCE_DIR=REFERENCE_TREE python tests/golden/make_golden.py [CASE ...]
 """
 
 import os
@@ -23,7 +31,14 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+_ARGS = sys.argv[1:]
+if _ARGS and Path(_ARGS[0]).is_dir():
+    REF = Path(_ARGS.pop(0))
+elif os.environ.get("MLVC_REFERENCE_DIR"):
+    REF = Path(os.environ["MLVC_REFERENCE_DIR"])
+else:
+    sys.exit("usage: make_golden.py REFERENCE_TREE [CASE ...] (or set MLVC_REFERENCE_DIR)")
+ONLY = set(_ARGS)
 sys.path[:0] = [str(REF / "tools" / "python"), str(REF / "tests" / "unit"), str(ROOT)]
 
 import torch  # noqa: E402
@@ -101,6 +116,64 @@ class Spatial(torch.nn.Module):
         return self.OutputType(y, self.s2(y), self.k2(x) + 0.5)
 
 
+class FeatureUpdate(torch.nn.Module):
+    """The recurrent-feature update: three channel thirds (a, b, g) of t, a
+    sigmoid-gated blend of the history with a, a sigmoid gate and a
+    per-channel scale.  encoder form: the concat of (scaled, blended) is the
+    next node (fusion_matcher.cpp Case A); decoder form: scaled also feeds a
+    LeakyReLU -> conv branch first and the concat comes later (Case B)."""
+
+    def __init__(self, c, decoder):
+        super().__init__()
+        self.decoder = decoder
+        self.scale = torch.nn.Parameter((torch.rand(1, c, 1, 1) + 0.5).half())
+        if decoder:
+            self.out = torch.nn.Conv2d(c, c, 1).half()
+        names = "recon feature" if decoder else "feature"
+        self.OutputType = namedtuple("Outputs", names)
+
+    InputType = namedtuple("Inputs", "t hist")
+
+    def forward(self, t, hist):
+        a, b, g = t.chunk(3, 1)
+        sb = torch.sigmoid(b)
+        sg = torch.sigmoid(g)
+        blended = sb * hist + (1 - sb) * a
+        scaled = sg * blended * self.scale
+        if not self.decoder:
+            return self.OutputType(torch.cat((scaled, blended), 1))
+        recon = self.out(F.leaky_relu(scaled, 0.1))
+        return self.OutputType(recon, torch.cat((scaled, blended), 1))
+
+
+class QuantTails(torch.nn.Module):
+    """The latent quantisation tails in the node order the reference fuses
+    (fusion_matcher.cpp try_y0_tail / try_y1_tail): y0 = round of the summed
+    halves of (latent / clip(prior head, 0.11) - prior tail) * qs0, the
+    dequantised update of both halves, the concat with the prior; y1 the same
+    against prior2, added to the y0 update and multiplied by the clipped
+    prior head."""
+    InputType = namedtuple("Inputs", "prior latent qs0 us00 us01 prior2 qs1 us10 us11")
+    OutputType = namedtuple("Outputs", "y_raw_0 y_raw_1 decoder_input prior_concat")
+
+    def forward(self, prior, latent, qs0, us00, us01, prior2, qs1, us10, us11):
+        s0, s1 = prior.chunk(2, 1)
+        clipped = s0.clamp_min(0.11)
+        norm = latent * clipped.reciprocal()
+        scaled = (norm - s1) * qs0
+        a0, a1 = scaled.chunk(2, 1)
+        y0 = (a0 + a1).round()
+        p0, p1 = s1.chunk(2, 1)
+        c2 = torch.cat(((y0 + p0) * us00, (y0 + p1) * us01), 1)
+        c3 = torch.cat((c2, prior), 1)
+        sc = (norm - prior2) * qs1
+        b0, b1 = sc.chunk(2, 1)
+        y1 = (b0 + b1).round()
+        q0, q1 = prior2.chunk(2, 1)
+        c4 = torch.cat(((y1 + q0) * us10, (y1 + q1) * us11), 1)
+        return self.OutputType(y0, y1, (c2 + c4) * clipped, c3)
+
+
 @case
 def example_q():
     torch.manual_seed(7)
@@ -126,7 +199,38 @@ def spatial_convs():
     return m, (torch.randn(1, 16, 13, 17).half(),)
 
 
-def ref_cpu(bundle, part, inputs, isa):
+@case
+def feature_update_enc():
+    torch.manual_seed(17)
+    m = FeatureUpdate(8, decoder=False).eval()
+    return m, (torch.randn(1, 24, 6, 10).half() * 2, torch.randn(1, 8, 6, 10).half())
+
+
+@case
+def feature_update_dec():
+    torch.manual_seed(19)
+    m = FeatureUpdate(16, decoder=True).eval()
+    return m, (torch.randn(1, 48, 5, 9).half() * 2, torch.randn(1, 16, 5, 9).half())
+
+
+@case
+def quant_tails():
+    torch.manual_seed(23)
+    q, h, w = 8, 5, 7
+
+    def u(c, lo, hi):
+        return (torch.rand(1, c, h, w) * (hi - lo) + lo).half()
+
+    inputs = (u(4 * q, -0.2, 2.0), (torch.randn(1, 2 * q, h, w) * 3).half(), u(2 * q, 0.25, 2.0),
+              u(q, 0.25, 2.0), u(q, 0.25, 2.0), (torch.randn(1, 2 * q, h, w) * 3).half(), u(2 * q, 0.25, 2.0),
+              u(q, 0.25, 2.0), u(q, 0.25, 2.0))
+    return QuantTails().eval(), inputs
+
+
+TAIL_CASES = {"feature_update_enc", "feature_update_dec", "quant_tails"}
+
+
+def ref_cpu(bundle, part, inputs, isa, fusion=True):
     code = (
         "import sys, numpy as np; sys.path.insert(0, %r);"
         "from oracle.ref_backend import RefCpuBackend;"
@@ -135,6 +239,8 @@ def ref_cpu(bundle, part, inputs, isa):
         "np.savez(%r, *outs)" % (str(ROOT), str(bundle / "inputs.npz"), str(bundle), part,
                                  str(bundle / f"out_{isa}.npz")))
     env = dict(os.environ, MLVC_CPU_ISA=isa)
+    if not fusion:
+        env["MLVC_CPU_DISABLE_FUSION"] = "1"
     subprocess.run([sys.executable, "-c", code], check=True, env=env)
     d = np.load(bundle / f"out_{isa}.npz")
     outs = [d[f"arr_{i}"] for i in range(len(d.files))]
@@ -146,6 +252,8 @@ def main():
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "ref", f"REF={REF}"], check=True)
     from aot_tests import execute_graph
     for name, make in CASES.items():
+        if ONLY and name not in ONLY:
+            continue
         model, inputs = make()
         bundle = HERE / name
         part = bundle / "aot" / "model"
@@ -156,6 +264,10 @@ def main():
         np.savez(bundle / "inputs.npz", **{f"in{i}": a for i, a in enumerate(np_inputs)})
         scalar = ref_cpu(bundle, "model", np_inputs, "scalar")
         avx2 = ref_cpu(bundle, "model", np_inputs, "avx2")
+        extra = {}
+        if name in TAIL_CASES:
+            unfused = ref_cpu(bundle, "model", np_inputs, "scalar", fusion=False)
+            extra = {f"ref_cpu_scalar_unfused_{i}": a for i, a in enumerate(unfused)}
         replay = [t.float().numpy().astype(np.float16) for t in execute_graph(part, inputs)]
         with torch.inference_mode():
             eager = [t.float().numpy().astype(np.float16) for t in model(*inputs)]
@@ -163,7 +275,7 @@ def main():
                  **{f"ref_cpu_scalar_{i}": a for i, a in enumerate(scalar)},
                  **{f"ref_cpu_avx2_{i}": a for i, a in enumerate(avx2)},
                  **{f"replay_{i}": a for i, a in enumerate(replay)},
-                 **{f"eager_{i}": a for i, a in enumerate(eager)})
+                 **{f"eager_{i}": a for i, a in enumerate(eager)}, **extra)
         print(name, [a.shape for a in scalar])
 
 
