@@ -1,22 +1,27 @@
 #!/usr/bin/env python3
 """Throughput benchmark of the B200 FP16 conv-stack backend.
 
-Workload (the benchmark this backend is measured on
-at N=1): the 8-block depthwise residual stack, C=128 @ 92x160 between
-pixel_unshuffle(2) and pixel_shuffle(2), input [1, 32, 184, 320] FP16,
-Kaiming-normal weights and N(0, 1) input from seed 0 (synthetic: no
-checkpoints exist for this network).  One step = one frame through the stack.
-`--workload conv3x3` runs configs[0] (one 3x3 64->64 conv @ 184x320) instead;
-`--workload entropy_1080p` times the entropy-coder inputs of one 1920x1088
-frame (scale extraction + FP16 -> int32 symbols of y_raw_1, y_raw_0, z_raw).
+Default workload (the configuration the metric is
+quoted on): 1920x1088 decode on the MLVC-shaped decoder stand-in (the
+upstream MLVC network is absent; mlvc_b200.graph.build_mlvc_decoder_standin
+assembles one from the reference's documented decoder I/O, plane sizes and
+depth-conv block), 8 independent streams, each a sequence of 64-frame GOPs
+with its own recurrent feature state (I-frame = state reset), split 8/N per
+GPU, one backend instance per stream.  One step = one frame of every stream
+a GPU serves.  Random-init FP16 weights and seeded integer-valued latents
+(synthetic: no checkpoints exist here).
+
+Other workloads: `block_stack` (configs[1], the 8-block depthwise residual
+stack), `conv3x3`, `mlvc_dec_1080p` / `mlvc_dec_640` /
+`mlvcs_dec_640` (one stream of a stand-in), single-operator graphs `op_*`
+for kernel work, `entropy_1080p` (scale extraction + FP16 -> int32 symbols).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-N>1 runs under torchrun, one process and one independent backend per GPU (the
-stack has no cross-GPU exchange: frames of different streams are independent),
-timed on the device, max over ranks.  `--impl reference` times the reference's
-own CPU backend (compiled from its sources into oracle/_ref) on the host cores.
-Prints one JSON line (rank 0).
+N>1 runs under torchrun, one process per GPU; streams and replicas are
+independent (no data-path collective), timed on the device, max over ranks.
+`--impl reference` times the reference's own CPU backend (compiled from its
+sources into oracle/_ref) on the host cores.  Prints one JSON line (rank 0).
 """
 
 from __future__ import annotations
@@ -436,6 +441,26 @@ def run_reference_arm(args, rank, world):
         }
         print(json.dumps(line), flush=True)
         return 0
+    if args.workload == STREAMS_WORKLOAD:
+        if rank != 0:
+            return 0
+        graph, weights, inputs = streams_graph()
+        threads = os.cpu_count() or 1
+        fps, times = reference_stream_frames_per_s(graph, weights, inputs, args.steps, args.warmup, threads)
+        line = {
+            "impl": "reference", "metric": STREAMS_METRIC, "value": fps, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": STREAMS_DESC, "global_batch": STREAMS, "parallelism": "cpu-threads",
+                       "step": "one frame of one stream (a bounded sample: the CPU decodes the 8 streams' frames one "
+                               "after another, so frames/s is the per-frame rate)"},
+            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": f"{args.steps} frames (streams in turn, recurrent state carried) on the "
+                                       "reference backends/cpu (AVX2, fusion on)"},
+            "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return 0
     graph, weights, inputs, desc, metric, _ = workload(args.workload)
     if rank != 0:
         return 0
@@ -452,6 +477,285 @@ def run_reference_arm(args, rank, world):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+
+# ------------------------------------------------------------ roofline
+def kernel_roofline(be, workload_name):
+    """Per-kernel device times of one backend's schedule (in-stack shares from
+    back-to-back launches, cold-L2 times from launches after a 256 MiB flush,
+    CUDA events on the backend's stream) and the roofline line of the kernel
+    with the largest in-stack share.  Algorithmic work per launch is the
+    planner's count: one HBM read of each distinct input and weight tensor,
+    one write of each output, FP16 = 2 B; FLOPs = 2 * MACs.  Both roofs are
+    reported; `bound` is the one the kernel's intensity puts it under (the
+    measured ridge = bf16 peak / copy bandwidth)."""
+    steps = be.steps()
+    warm = be.time_steps(20, 0)
+    cold = be.time_steps(10, FLUSH_BYTES)
+    per_kernel = {}
+    for st, w_ms, c_ms in zip(steps, warm, cold):
+        k = per_kernel.setdefault(st["kernel"], {"launches": 0, "warm_ms": 0.0, "cold_ms": 0.0, "bytes": 0.0,
+                                                 "flops": 0.0})
+        k["launches"] += 1
+        k["warm_ms"] += w_ms
+        k["cold_ms"] += c_ms
+        k["bytes"] += st["bytes"]
+        k["flops"] += st["flops"]
+    total_warm = sum(v["warm_ms"] for v in per_kernel.values())
+    dom_name, dom = max(per_kernel.items(), key=lambda kv: kv[1]["warm_ms"])
+    hbm, tflops_peak, peak_kind = measured_peaks()
+    ridge = tflops_peak * 1e12 / (hbm * 1e9)
+    intensity = dom["flops"] / max(dom["bytes"], 1.0)
+    tensor_achieved = dom["flops"] / (dom["cold_ms"] / 1e3) / 1e12
+    hbm_achieved = dom["bytes"] / (dom["cold_ms"] / 1e3) / 1e9
+    if intensity >= ridge:
+        roof = {"bound": "tensor", "achieved": tensor_achieved, "peak": tflops_peak, "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": hbm_achieved, "peak": hbm, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_kind"] = peak_kind
+    roof["kernel"] = dom_name
+    roof["intensity_flop_per_byte"] = intensity
+    roof["ridge_flop_per_byte"] = ridge
+    roof["tensor_roof"] = {"achieved_tflops": tensor_achieved, "peak_tflops": tflops_peak,
+                           "frac": tensor_achieved / tflops_peak}
+    roof["hbm_roof"] = {"achieved_gbs": hbm_achieved, "peak_gbs": hbm, "frac": hbm_achieved / hbm}
+    roof["launches_per_step"] = dom["launches"]
+    roof["algorithmic_bytes_per_launch"] = dom["bytes"] / dom["launches"]
+    roof["algorithmic_flops_per_launch"] = dom["flops"] / dom["launches"]
+    roof["avg_launch_us_cold_l2"] = 1e3 * dom["cold_ms"] / dom["launches"]
+    roof["avg_launch_us_in_stack"] = 1e3 * dom["warm_ms"] / dom["launches"]
+    roof["share_in_stack"] = dom["warm_ms"] / total_warm
+    roof["traffic"] = ncu_traffic().get(workload_name, {}).get(dom_name)
+    kernels = {k: {"launches": v["launches"], "share": v["warm_ms"] / total_warm,
+                   "us_in_stack": 1e3 * v["warm_ms"], "us_cold_l2": 1e3 * v["cold_ms"],
+                   "tflops_in_stack": v["flops"] / (v["warm_ms"] / 1e3) / 1e12 if v["flops"] else 0.0,
+                   "tflops_cold": v["flops"] / (v["cold_ms"] / 1e3) / 1e12 if v["flops"] else 0.0,
+                   "gbs_cold": v["bytes"] / (v["cold_ms"] / 1e3) / 1e9}
+               for k, v in per_kernel.items()}
+    return roof, kernels
+
+
+# ------------------------------------------- config 5: 8 streams at 1080p
+STREAMS = 8
+GOP = 64
+STREAMS_WORKLOAD = "mlvc_dec_1080p_8s"
+STREAMS_Q = 21
+STREAMS_DESC = ("BASELINE config 5 on the MLVC-shaped decoder stand-in @1920x1088 (the upstream MLVC architecture is "
+                "absent): 8 independent streams of 64-frame GOPs, each with its own recurrent feature state (bound "
+                "ref_feature <- feature on the device, reset at every I-frame), split 8/N per GPU with one backend "
+                "instance per stream; one step = one frame of every stream on that GPU; decoder I/O z_raw 1/128, "
+                "y_raw_0/1 1/16, q_index 21 -> x_hat (8-bit YUV420 1920x1080 through the codec output conversion "
+                "on the e2e path); 2+2+2 depth-conv blocks at 256 ch, x8 pixel-shuffle reconstruction; "
+                "Kaiming-normal weights, seed 0; integer-valued latents seeded per stream and frame")
+STREAMS_METRIC = ("1080p decode frames/s, 8 independent streams (MLVC-shaped decoder stand-in for the 1080p MLVC "
+                  "decode of BASELINE config 5)")
+
+
+def streams_graph():
+    gb, inputs = build_mlvc_decoder_standin(0, 1920, 1088, q_index=STREAMS_Q)
+    graph, weights = gb.finish()
+    return graph, weights, inputs
+
+
+def stream_latents(inputs, stream, frame):
+    """Seeded integer-valued latents (z_raw, y_raw_0, y_raw_1) of one frame of one stream."""
+    rng = np.random.default_rng((stream << 20) + frame)
+    return [np.rint(rng.standard_normal(inputs[k].shape) * scale).astype(np.float16)
+            for k, scale in zip(range(3), (4, 3, 3))]
+
+
+def reference_stream_frames_per_s(graph, weights, inputs, frames, warmup, threads):
+    """The reference CPU backend decoding frames of the streams in turn, its
+    recurrent feature state carried (ref_feature <- feature) and reset at
+    every GOP start."""
+    from oracle.ref_backend import RefCpuBackend  # reference arm / CPU baseline only
+    q = np.array([STREAMS_Q], np.int32)
+    with tempfile.TemporaryDirectory() as d:
+        part = Path(d) / "aot" / "MLVCDecoder"
+        part.mkdir(parents=True)
+        (part / "graph.pb").write_bytes(graph)
+        (part / "weights.bin").write_bytes(weights)
+        ref = RefCpuBackend(d, "MLVCDecoder", threads, state_bindings=[(3, 1, list(inputs[3].shape))])
+        times = []
+        for f in range(warmup + frames):
+            lat = stream_latents(inputs, f % STREAMS, f // STREAMS)
+            if f % (STREAMS * GOP) == 0:
+                ref.reset_state()
+            t0 = time.perf_counter()
+            ref.run(lat + [q])
+            if f >= warmup:
+                times.append(time.perf_counter() - t0)
+        ref.close()
+    return frames / sum(times), times
+
+
+def run_streams_arm(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from mlvc_b200 import Backend
+
+    if STREAMS % world:
+        raise SystemExit(f"--gpus must divide the {STREAMS} streams")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device(f"cuda:{local_rank}")
+    n_local = STREAMS // world
+    stream_ids = list(range(rank * n_local, (rank + 1) * n_local))
+    graph, weights, inputs = streams_graph()
+    q = np.array([STREAMS_Q], np.int32)
+    backends = []
+    for sid in stream_ids:
+        be = Backend(local_rank)
+        be.load_memory(graph, weights, [(3, 1)])
+        be.reset_state()
+        outs = be.run(stream_latents(inputs, sid, 0) + [q])  # inputs now resident on the device
+        if not all(np.isfinite(o.astype(np.float32)).all() for o in outs):
+            raise RuntimeError("non-finite output")
+        be.reset_state()
+        backends.append(be)
+    cstreams = [torch.cuda.ExternalStream(be.stream, device=dev) for be in backends]
+    s0 = cstreams[0]
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step(i):
+        """One frame of every local stream, each on its own CUDA stream, all
+        started after an L2 flush on stream 0 and joined back into it."""
+        with torch.cuda.stream(s0):
+            flush.fill_(1)
+        start = torch.cuda.Event(enable_timing=True)
+        start.record(s0)
+        for cs, be in zip(cstreams, backends):
+            if cs is not s0:
+                cs.wait_event(start)
+            be.enqueue()
+        for cs in cstreams[1:]:
+            done = torch.cuda.Event()
+            done.record(cs)
+            s0.wait_event(done)
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(s0)
+        return start, end
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = vis.split(",")[local_rank] if vis else local_rank
+    with ClockSampler(gpu_index) as clocks:
+        marks = [step(i) for i in range(args.steps)]
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in marks)
+    frames_local = args.steps * n_local
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = STREAMS * args.steps / (ms_max / 1e3)
+
+    # ---- end to end through the public slot API: per stream two slots,
+    # latents in from pinned host memory, submit(slot, shifted_q), the decoded
+    # frame out as 8-bit YUV420 through the codec output conversion
+    width, height = 1920, 1080
+    for be in backends:
+        be.reset_state()
+        be.configure_codec_io(width, height, 1920, 1088, 1.0, slots=2, output_index=0)
+    lat_cache = {}
+
+    def frame_inputs(sid, f):
+        key = (sid, f % 4)  # four distinct latent sets per stream, cycled
+        if key not in lat_cache:
+            lat_cache[key] = stream_latents(inputs, sid, f % 4)
+        return lat_cache[key]
+
+    def pipeline(first, n):
+        for i in range(first, first + n):
+            slot = i % 2
+            with torch.cuda.stream(s0):
+                flush.fill_(1)  # cold L2 before every step, inside the timed region
+            fl = torch.cuda.Event()
+            fl.record(s0)
+            for sid, cs, be in zip(stream_ids, cstreams, backends):
+                if i >= 2:
+                    be.wait_slot(slot)
+                if i % GOP == 0 and i > 0:
+                    be.reset_state()  # I-frame: a new GOP starts from a zeroed feature
+                for k, a in enumerate(frame_inputs(sid, i)):
+                    be.slot_input(slot, k)[...] = a
+                cs.wait_event(fl)
+                be.submit(slot, shifted_q=STREAMS_Q)
+        for be in backends:
+            for slot in range(min(first + n, 2)):
+                be.wait_slot(slot)
+
+    pipeline(0, max(2, args.warmup))
+    for be in backends:
+        be.reset_state()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_st, e_en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_st.record(s0)
+    pipeline(0, args.steps)
+    e_en.record(s0)
+    torch.cuda.synchronize()
+    t = torch.tensor([e_st.elapsed_time(e_en)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = STREAMS * args.steps / (float(t.item()) / 1e3)
+    h2d = sum(a.nbytes for a in inputs[:3]) + 4
+    d2h = width * height * 3 // 2
+    # the slot path still decodes after the timed run (first frame of a fresh GOP, stream 0)
+    be = backends[0]
+    be.reset_state()
+    for k, a in enumerate(frame_inputs(stream_ids[0], 0)):
+        be.slot_input(0, k)[...] = a
+    be.submit(0, shifted_q=STREAMS_Q)
+    be.wait_slot(0)
+    got = np.concatenate([pl.reshape(-1) for pl in be.slot_output_yuv(0)])
+    if got.size != d2h or float(got.std()) == 0.0:
+        raise RuntimeError("slot path produced no decoded frame")
+
+    roof, kernels = kernel_roofline(backends[0], args.workload)
+    line = None
+    if rank == 0:
+        line = {
+            "metric": STREAMS_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": STREAMS_DESC, "global_batch": STREAMS, "streams_per_gpu": n_local,
+                       "parallelism": f"{STREAMS} independent streams over {world} GPU(s), {n_local} per GPU "
+                                      "(no collective)",
+                       "step": f"one frame of each of the {n_local} streams on a GPU ({STREAMS} frames per step "
+                               "job-wide)",
+                       "l2": "flushed before every timed step (256 MiB fill; untimed on the device path, inside "
+                             "the timed region on the e2e path)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * STREAMS,
+                    "d2h_bytes_per_step": d2h * STREAMS,
+                    "path": ("mlvc_b200 slot API per stream, 2 slots: latents (z_raw, y_raw_0, y_raw_1) from pinned "
+                             "host memory, submit(slot, shifted_q), schedule, x_hat -> 8-bit YUV420 1920x1080 on the "
+                             "GPU, pinned D2H; GOP reset every 64 frames; timed on the device over the whole run")},
+            "gpu_launches": sum(b.kernel_launches for b in backends) * args.steps,
+            "roofline": roof,
+            "kernels": kernels,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            try:
+                fps, times = reference_stream_frames_per_s(graph, weights, inputs, args.cpu_frames, 1, threads)
+                line["cpu_baseline"] = {"value": fps, "unit": UNIT, "cores": threads, "kind": "reference",
+                                        "sample": f"{args.cpu_frames} frames (streams in turn, state carried) on "
+                                                  f"the reference backends/cpu (AVX2, fusion on), {sum(times):.1f} s"}
+            except Exception as e:  # reported, never silently replaced
+                line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": threads, "kind": "reference",
+                                        "sample": f"unavailable: {e}"}
+    for be in backends:
+        be.close()
+    return line
 
 
 # ------------------------------------------------------------------ GPU
@@ -552,46 +856,7 @@ def run_b200_arm(args, rank, world, local_rank):
     if not np.array_equal(first.view(np.uint16), want.view(np.uint16)):
         raise RuntimeError("slot path output differs from run()")
 
-    # ---- per-kernel timings: in-stack (warm) shares and cold-L2 launches
-    steps = be.steps()
-    warm = be.time_steps(20, 0)
-    cold = be.time_steps(10, FLUSH_BYTES)
-    per_kernel = {}
-    for s, w_ms, c_ms in zip(steps, warm, cold):
-        k = per_kernel.setdefault(s["kernel"], {"launches": 0, "warm_ms": 0.0, "cold_ms": 0.0, "bytes": 0.0,
-                                                "flops": 0.0})
-        k["launches"] += 1
-        k["warm_ms"] += w_ms
-        k["cold_ms"] += c_ms
-        k["bytes"] += s["bytes"]
-        k["flops"] += s["flops"]
-    total_warm = sum(v["warm_ms"] for v in per_kernel.values())
-    dom_name, dom = max(per_kernel.items(), key=lambda kv: kv[1]["warm_ms"])
-    hbm, tflops_peak, peak_kind = measured_peaks()
-    intensity = dom["flops"] / max(dom["bytes"], 1.0)
-    ridge = tflops_peak * 1e12 / (hbm * 1e9)
-    if intensity >= ridge:
-        achieved = dom["flops"] / (dom["cold_ms"] / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s"}
-    else:
-        achieved = dom["bytes"] / (dom["cold_ms"] / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["peak_kind"] = peak_kind
-    roof["kernel"] = dom_name
-    roof["launches_per_step"] = dom["launches"]
-    roof["algorithmic_bytes_per_launch"] = dom["bytes"] / dom["launches"]
-    roof["algorithmic_flops_per_launch"] = dom["flops"] / dom["launches"]
-    roof["avg_launch_us_cold_l2"] = 1e3 * dom["cold_ms"] / dom["launches"]
-    roof["avg_launch_us_in_stack"] = 1e3 * dom["warm_ms"] / dom["launches"]
-    roof["share_in_stack"] = dom["warm_ms"] / total_warm
-    tr = ncu_traffic().get(args.workload, {}).get(dom_name)
-    roof["traffic"] = tr
-    kernels = {k: {"launches": v["launches"], "share": v["warm_ms"] / total_warm,
-                   "us_in_stack": 1e3 * v["warm_ms"], "us_cold_l2": 1e3 * v["cold_ms"],
-                   "tflops_cold": v["flops"] / (v["cold_ms"] / 1e3) / 1e12 if v["flops"] else 0.0,
-                   "gbs_cold": v["bytes"] / (v["cold_ms"] / 1e3) / 1e9}
-               for k, v in per_kernel.items()}
+    roof, kernels = kernel_roofline(be, args.workload)
 
     line = None
     if rank == 0:
@@ -632,9 +897,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv",
                                                    "op_mbconv", "mlvc_dec_1080p", "mlvc_dec_640", "mlvcs_dec_640",
-                                                   "entropy_1080p"],
-                    default="block_stack")
-    ap.add_argument("--cpu-frames", type=int, default=5)
+                                                   "entropy_1080p", STREAMS_WORKLOAD],
+                    default=STREAMS_WORKLOAD)
+    ap.add_argument("--cpu-frames", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -652,7 +917,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device(f"cuda:{local_rank}"))
-    arm = run_entropy_arm if args.workload == "entropy_1080p" else run_b200_arm
+    arm = {"entropy_1080p": run_entropy_arm, STREAMS_WORKLOAD: run_streams_arm}.get(args.workload, run_b200_arm)
     line = arm(args, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist

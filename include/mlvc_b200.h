@@ -103,6 +103,12 @@ size_t mlvc_b200_slot_count(const mlvc_b200_backend* backend);
 void* mlvc_b200_slot_input(mlvc_b200_backend* backend, size_t slot, size_t input_index);
 const void* mlvc_b200_slot_output(const mlvc_b200_backend* backend, size_t slot, size_t output_index);
 int mlvc_b200_submit(mlvc_b200_backend* backend, size_t slot);
+/* submit_encoder(slot, shifted_q) / submit_decoder(slot, shifted_q)
+ * (backend.hpp:87, 92): stores shifted_q in the slot's buffer of the int32 [1]
+ * graph input named "q_index_shifted" and submits the slot, like the
+ * reference's set_q_index (backends/driver_cubin/src/cuda_graph_executor.cpp:
+ * 66-82, 286, 353).  Fails when the graph has no such input. */
+int mlvc_b200_submit_q(mlvc_b200_backend* backend, size_t slot, int32_t shifted_q);
 int mlvc_b200_wait_slot(mlvc_b200_backend* backend, size_t slot);
 
 /* BufferedCodecBackend codec I/O (backend.hpp:69-93): CodecIoConfig {width,
@@ -216,6 +222,20 @@ int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend);
 int mlvc_b200_trace_step(mlvc_b200_backend* backend, size_t index, uint64_t* stamps, size_t capacity,
                          size_t* count);
 size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend);
+
+/* Failure-detection test hook (no reference counterpart; the reference's
+ * kernels have no bounded waits).  Relaunches step `step_index`, which must
+ * be a mlvc_conv1x1_tc step of the loaded schedule, once with every bounded
+ * device wait of this backend limited to `limit_ns` (at most 2 s) and CTA 0's
+ * TMA producer withholding its first activation panel: no copy is issued or
+ * armed for it, so the tensor-core issuer's wait for it runs out, the CTA
+ * sets its abort flag, every role winds down (producer drains the copies it
+ * armed, epilogue drains its residual load) and the kernel returns.  Then
+ * waits, restores the 2 s limit and stores the module status word in *status
+ * (0x2 = the issuer's wait ran out), clearing it.  The step's output is left
+ * incomplete; the next run recomputes it.  Uses the device state of the last
+ * run. */
+int mlvc_b200_test_wait_expiry(mlvc_b200_backend* backend, size_t step_index, uint64_t limit_ns, uint32_t* status);
 
 /* Debug dump of one named tensor of the last run, NCHW on the host: the
  * reference's --debug-dir tensor dumps (codec/src/pipeline.cpp:225-266).

@@ -804,8 +804,9 @@ void Backend::plan()
             }
             s.info.flops = 2.0 * N * OH * OW * static_cast<double>(OC) * ICG * KH * KW;
             const double out_elems = static_cast<double>(element_count(values_[out_id].shape));
+            // algorithmic bytes: one read of each distinct tensor, one write of the output
             s.info.bytes = 2.0 * (element_count(xv.shape) + element_count(wv.shape) + (bias ? OC : 0) + out_elems +
-                                  (res_id ? out_elems : 0));
+                                  (res_id && res_id != x_id ? out_elems : 0));
 
             const bool tc_shape = G == 1 && N == 1 && IC % 8 == 0 && OC % 8 == 0 && (!reglu || OC % 64 == 0);
             const int header = kTcHeaderBytes;
@@ -880,7 +881,8 @@ void Backend::plan()
                     }
                     f.info.flops = 2.0 * M * (static_cast<double>(OC) * IC + static_cast<double>(OC2) * H);
                     f.info.bytes = 2.0 * (static_cast<double>(M) * IC + static_cast<double>(OC) * IC + OC +
-                                          static_cast<double>(OC2) * H + OC2 + static_cast<double>(M) * OC2 * (res2 ? 2 : 1));
+                                          static_cast<double>(OC2) * H + OC2 +
+                                          static_cast<double>(M) * OC2 * (res2 && res2 != x_id ? 2 : 1));
                     f.kernel = "mlvc_ffn_tc";
                     f.info.kernel = f.kernel;
                     f.smem = static_cast<unsigned>(ffn_smem);
@@ -1007,7 +1009,8 @@ void Backend::plan()
                     f.info.nodes = std::to_string(i) + "-" + std::to_string(pj + consumed2 - 1);
                     f.info.flops = 2.0 * M * static_cast<double>(IC) * OC + 18.0 * M * OC + 2.0 * M * static_cast<double>(OC) * OC2;
                     f.info.bytes = 2.0 * (static_cast<double>(M) * IC + static_cast<double>(OC) * IC + OC + 10.0 * OC +
-                                          static_cast<double>(OC2) * OC + OC2 + static_cast<double>(M) * OC2 * (res2 ? 2 : 1));
+                                          static_cast<double>(OC2) * OC + OC2 +
+                                          static_cast<double>(M) * OC2 * (res2 && res2 != x_id ? 2 : 1));
                     f.kernel = "mlvc_mbconv_tc";
                     f.info.kernel = f.kernel;
                     f.smem = static_cast<unsigned>(mb_smem);
@@ -1454,7 +1457,7 @@ void Backend::plan()
                     f.info.nodes = std::to_string(i) + "-" + std::to_string(i + consumed2);
                     f.info.flops = 2.0 * M * IC * 9 + 2.0 * M * static_cast<double>(IC) * OC2;
                     f.info.bytes = 2.0 * (static_cast<double>(M) * IC + 9.0 * IC + IC + static_cast<double>(OC2) * IC +
-                                          OC2 + static_cast<double>(M) * OC2 * (res2 ? 2 : 1));
+                                          OC2 + static_cast<double>(M) * OC2 * (res2 && res2 != x_id ? 2 : 1));
                     f.kernel = "mlvc_dwconv_tc";
                     f.info.kernel = f.kernel;
                     f.smem = static_cast<unsigned>(fixed + h_stages * halo_stride);
@@ -2480,6 +2483,45 @@ std::vector<uint64_t> Backend::trace_step(size_t index)
     return out;
 }
 
+uint32_t Backend::test_wait_expiry(size_t index, uint64_t limit_ns)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    if (!loaded_)
+        throw std::runtime_error("mlvc-b200: load() must be called before test_wait_expiry()");
+    Step& st = steps_.at(index);
+    if (st.kernel != "mlvc_conv1x1_tc")
+        throw std::runtime_error("mlvc-b200: the wait-expiry test relaunches a mlvc_conv1x1_tc step");
+    constexpr uint64_t kDefaultLimit = 2000000000ull;  // the kernels' kWaitLimitNs
+    if (limit_ns == 0 || limit_ns > kDefaultLimit)
+        throw std::runtime_error("mlvc-b200: wait limit must be in (0, 2 s]");
+    ContextGuard guard(ctx_);
+    check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
+    check_status();
+    CUdeviceptr limit_ptr = 0;
+    size_t limit_size = 0;
+    check(cuModuleGetGlobal(&limit_ptr, &limit_size, module_, "mlvc_b200_wait_limit_ns"),
+          "cuModuleGetGlobal(mlvc_b200_wait_limit_ns)");
+    const unsigned long long shortened = limit_ns, restored = kDefaultLimit;
+    check(cuMemcpyHtoD(limit_ptr, &shortened, sizeof(shortened)), "cuMemcpyHtoD(wait limit)");
+    std::vector<uint8_t> params = st.params;
+    const int withhold = 1;
+    std::memcpy(params.data() + offsetof(ConvTcParams, withhold_a), &withhold, sizeof(withhold));
+    void* args[] = {params.data()};
+    CUresult launched = cuLaunchKernel(st.f, st.grid, st.grid_y, st.grid_z, st.block, st.block_y, 1, st.smem, stream_,
+                                       args, nullptr);
+    const CUresult finished = launched == CUDA_SUCCESS ? cuStreamSynchronize(stream_) : launched;
+    const CUresult reset = cuMemcpyHtoD(limit_ptr, &restored, sizeof(restored));
+    check(launched, "cuLaunchKernel(wait expiry)");
+    check(finished, "cuStreamSynchronize(wait expiry)");
+    check(reset, "cuMemcpyHtoD(wait limit)");
+    unsigned int status = 0;
+    check(cuMemcpyDtoH(&status, status_ptr_, sizeof(status)), "cuMemcpyDtoH(status)");
+    const unsigned int zero = 0;
+    check(cuMemcpyHtoD(status_ptr_, &zero, sizeof(zero)), "cuMemcpyHtoD(status)");
+    return status;
+}
+
 void Backend::set_keep_all_values(bool keep)
 {
     if (loaded_)
@@ -2908,6 +2950,23 @@ void Backend::submit(size_t slot)
         check(cuMemcpyDtoHAsync(s.out[k].get(), s.dout[k].get(), s.out[k].bytes(), copy_out_), "cuMemcpyDtoHAsync(slot)");
     check(cuEventRecord(s.done.get(), copy_out_), "cuEventRecord(done)");
     s.pending = true;
+}
+
+void Backend::submit_q(size_t slot, int shifted_q)
+{
+    size_t index = ext_inputs_.size();
+    for (size_t k = 0; k < ext_inputs_.size(); ++k)
+        if (input_desc(k).name == "q_index_shifted")
+            index = k;
+    if (index == ext_inputs_.size())
+        throw std::runtime_error("mlvc-b200: graph has no q_index_shifted input");
+    const auto& d = input_desc(index);
+    if (d.dtype != DType::kInt32 || d.shape != std::vector<int64_t>{1} || index == codec_.input)
+        throw std::runtime_error("mlvc-b200: invalid q_index_shifted input");
+    if (slots_.at(slot).pending)
+        throw std::runtime_error("mlvc-b200: slot resubmitted before wait_slot()");
+    std::memcpy(slot_input(slot, index), &shifted_q, sizeof(shifted_q));
+    submit(slot);
 }
 
 void Backend::wait_slot(size_t slot)

@@ -101,6 +101,10 @@ public:
     void* slot_input(size_t slot, size_t i);
     const void* slot_output(size_t slot, size_t i) const;
     void submit(size_t slot);
+    // submit_encoder / submit_decoder(slot, shifted_q): writes shifted_q into
+    // the slot's buffer of the int32 [1] graph input "q_index_shifted", then
+    // submits (set_q_index, backends/driver_cubin/src/cuda_graph_executor.cpp:66-82).
+    void submit_q(size_t slot, int shifted_q);
     void wait_slot(size_t slot);
 
     // Codec I/O on the slot path: the graph input `input_index` takes a YUV420
@@ -131,6 +135,14 @@ public:
     // enabled and returns kTracePoints %globaltimer stamps per CTA (0 = not
     // reached).  Uses the device state of the last run.
     std::vector<uint64_t> trace_step(size_t index);
+    // Failure-detection test: relaunches 1x1 tensor-core conv step `index`
+    // once with every bounded wait of this backend's module limited to
+    // `limit_ns` and CTA 0's producer withholding its first activation panel
+    // (nothing is loaded or armed for it), waits for the launch, restores the
+    // 2 s limit and returns the module status word it left (then cleared):
+    // the MMA issuer's wait bit when the abort path ran.  Uses the device
+    // state of the last run; the step's output is left incomplete.
+    uint32_t test_wait_expiry(size_t index, uint64_t limit_ns);
     // Before load(): give every materialised tensor its own arena slot so
     // read_value() sees all of them after a run (costs memory; debug only).
     void set_keep_all_values(bool keep);

@@ -313,6 +313,21 @@ int mlvc_b200_submit(mlvc_b200_backend* backend, size_t slot)
     return guarded([&] { require(backend).submit(slot); });
 }
 
+int mlvc_b200_test_wait_expiry(mlvc_b200_backend* backend, size_t step_index, uint64_t limit_ns,
+                               uint32_t* status)
+{
+    return guarded([&] {
+        if (!status)
+            throw std::runtime_error("mlvc-b200: status pointer is null");
+        *status = require(backend).test_wait_expiry(step_index, limit_ns);
+    });
+}
+
+int mlvc_b200_submit_q(mlvc_b200_backend* backend, size_t slot, int32_t shifted_q)
+{
+    return guarded([&] { require(backend).submit_q(slot, shifted_q); });
+}
+
 int mlvc_b200_wait_slot(mlvc_b200_backend* backend, size_t slot)
 {
     return guarded([&] { require(backend).wait_slot(slot); });

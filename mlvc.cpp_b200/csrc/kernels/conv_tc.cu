@@ -272,6 +272,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
     const StageSync ss{&sh.stg_ready, &sh.stg_full};
     const int tiles_per_row = kxk ? (p.out_w + kBM - 1) / kBM : 1;
     uint32_t acc = 0, acc_phase = 0, it = 0;
+    bool aborted = false;
     for (int t = first_tile; t < total_tiles; t += tile_step, ++it) {
         const int m_tile = t / p.n_tiles;
         TileCoord tc;
@@ -284,14 +285,24 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
             stage_prepare(p, st, panels, n_tile * out_cols, tc, kxk, p.epilogue == kEpiResidual, ss.ready);
         if (!epilogue_tile(p, sh.bias, sh.tmem_base + acc * p.BN, &sh.tmem_full[acc], acc_phase, &sh.tmem_empty[acc],
                            ss, it, st, nullptr, panels, n_tile * out_cols, tc, kxk, quadrant, group, lane, leader,
-                           &sh.abort_flag))
+                           &sh.abort_flag)) {
+            aborted = true;
             break;
+        }
         if (t == first_tile && leader)
             trace(p, kTrFirstAcc);
         acc ^= 1u;
         acc_phase ^= (acc == 0) ? 1u : 0u;
     }
     if (leader) {
+        // On abort, a residual tile this leader loaded for tile `it` may still
+        // be in flight: wait (bounded) for its barrier phase before the CTA's
+        // shared memory retires.  When the phase already completed, the wait
+        // returns at once.
+        if (aborted && p.epilogue == kEpiResidual) {
+            volatile int never = 0;
+            mbar_wait(ss.ready, it & 1u, &never, kErrWaitEpilogue);
+        }
         bulk_wait_all();  // stores complete before the CTA (and its shared memory) retires
         trace(p, kTrEpilogueDone);
     }
@@ -423,17 +434,21 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
             pdl_wait();  // activations are written by the previous kernel
             int stage = 0;
             uint32_t phase = 0;
+            int panel = 0;  // A panels this CTA has handled (wait-expiry test)
+            const int withhold = blockIdx.x == 0 ? p.withhold_a : 0;
             for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {
                 const int m_tile = t / p.n_tiles;
                 for (int kp = 0; kp < k_panels; ++kp) {
                     if (!mbar_wait(&sh->a_empty[stage], phase ^ 1u, &sh->abort_flag, kErrWaitProducer))
                         break;
-                    mbar_arrive_expect_tx(&sh->a_full[stage], kAPanelBytes);
-                    // K panels past a_split come from the second tensor of a concat
-                    const bool second = p.a_split > 0 && kp >= p.a_split;
-                    tma_load_2d(a_smem + stage * kAPanelBytes, second ? &p.map_a1 : &p.map_a0, &sh->a_full[stage],
-                                (second ? kp - p.a_split : kp) * 64, m_tile * kBM);
-                    a_armed.arm(stage, phase);
+                    if (++panel != withhold) {
+                        mbar_arrive_expect_tx(&sh->a_full[stage], kAPanelBytes);
+                        // K panels past a_split come from the second tensor of a concat
+                        const bool second = p.a_split > 0 && kp >= p.a_split;
+                        tma_load_2d(a_smem + stage * kAPanelBytes, second ? &p.map_a1 : &p.map_a0,
+                                    &sh->a_full[stage], (second ? kp - p.a_split : kp) * 64, m_tile * kBM);
+                        a_armed.arm(stage, phase);
+                    }
                     if (++stage == p.a_stages) {
                         stage = 0;
                         phase ^= 1u;

@@ -70,6 +70,11 @@ struct ConvTcParams {
     // Optional phase trace (null in normal runs): kTracePoints %globaltimer
     // stamps per CTA, written by the role that reaches each point.
     unsigned long long* trace;
+    // Wait-expiry test only (0 in every normal launch): k > 0 makes CTA 0's
+    // producer leave its k-th A panel unloaded -- no TMA is issued and the
+    // stage's barrier is never armed -- so the MMA issuer's bounded wait for
+    // it runs out and the CTA takes its abort path.  1x1 kernel only.
+    int withhold_a;
 };
 
 // Phase trace points of the tensor-core conv kernels.

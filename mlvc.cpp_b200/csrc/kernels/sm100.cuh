@@ -17,6 +17,9 @@
 // Module-wide error status (0 = ok).  Read by the host through
 // cuModuleGetGlobal("mlvc_b200_status") after every synchronising call.
 extern "C" __device__ unsigned int mlvc_b200_status;
+// Limit of every bounded wait in nanoseconds (module-wide, kWaitLimitNs
+// unless the host's wait-expiry test shortens it for one launch).
+extern "C" __device__ unsigned long long mlvc_b200_wait_limit_ns;
 
 namespace mlvc_b200 {
 
@@ -106,12 +109,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity))
         return true;
     const unsigned long long start = globaltimer_ns();
+    const unsigned long long limit = mlvc_b200_wait_limit_ns;
     while (true) {
         if (mbar_try_wait(bar, parity))
             return true;
         if (*abort_flag)
             return false;
-        if (globaltimer_ns() - start > kWaitLimitNs) {
+        if (globaltimer_ns() - start > limit) {
             *abort_flag = 1;
             atomicOr(&mlvc_b200_status, code);
             return false;

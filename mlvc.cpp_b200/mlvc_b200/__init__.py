@@ -82,6 +82,7 @@ EXPORTS = {
     "mlvc_b200_slot_output_yuv": ([ctypes.c_void_p, ctypes.c_size_t] + [ctypes.POINTER(ctypes.c_void_p)] * 3,
                                   ctypes.c_int),
     "mlvc_b200_submit": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
+    "mlvc_b200_submit_q": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32], ctypes.c_int),
     "mlvc_b200_wait_slot": ([ctypes.c_void_p, ctypes.c_size_t], ctypes.c_int),
     "mlvc_b200_enqueue": ([ctypes.c_void_p], ctypes.c_int),
     "mlvc_b200_synchronize": ([ctypes.c_void_p], ctypes.c_int),
@@ -97,6 +98,8 @@ EXPORTS = {
     "mlvc_b200_device_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
     "mlvc_b200_trace_step": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t,
                               ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "mlvc_b200_test_wait_expiry": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint64,
+                                    ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
     "mlvc_b200_set_debug_tensors": ([ctypes.c_void_p, ctypes.c_int], ctypes.c_int),
     "mlvc_b200_read_tensor": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_size_t,
                                ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
@@ -309,8 +312,14 @@ class Backend:
         """(Y, U, V) numpy views of the slot's decoded YUV420 frame."""
         return self._planes(lib().mlvc_b200_slot_output_yuv, slot)
 
-    def submit(self, slot):
-        _check(lib().mlvc_b200_submit(self._h, slot))
+    def submit(self, slot, shifted_q=None):
+        """submit(slot), or with shifted_q the reference's submit_encoder /
+        submit_decoder(slot, shifted_q): the q_index_shifted input of the slot
+        is set to shifted_q first."""
+        if shifted_q is None:
+            _check(lib().mlvc_b200_submit(self._h, slot))
+        else:
+            _check(lib().mlvc_b200_submit_q(self._h, slot, int(shifted_q)))
 
     def wait_slot(self, slot):
         _check(lib().mlvc_b200_wait_slot(self._h, slot))
@@ -355,6 +364,15 @@ class Backend:
         buf = (ctypes.c_uint64 * n.value)()
         _check(lib().mlvc_b200_trace_step(self._h, index, buf, n.value, ctypes.byref(n)))
         return np.frombuffer(buf, np.uint64).reshape(-1, 48).copy()
+
+    def test_wait_expiry(self, step_index, limit_ns):
+        """Failure-detection test: relaunch a mlvc_conv1x1_tc step with its
+        bounded waits limited to limit_ns and one activation panel withheld;
+        returns the device status word the aborted launch left (see
+        include/mlvc_b200.h)."""
+        status = ctypes.c_uint32()
+        _check(lib().mlvc_b200_test_wait_expiry(self._h, step_index, int(limit_ns), ctypes.byref(status)))
+        return status.value
 
     @property
     def kernel_launches(self):

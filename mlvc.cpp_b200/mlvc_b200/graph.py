@@ -395,8 +395,40 @@ def _depth_conv_block(gb, rng, h, c, prefix, branch_gain=1.0):
     return gb.add(h, gb.conv(f, w4, b4))
 
 
+def _recon_out(gb, rng, r, cin, name, gain):
+    """Final 1x1 conv to 3 x 64 channels ahead of the x8 pixel shuffle: weights
+    Kaiming-normal scaled by `gain`, bias 0.5 + U(-0.1, 0.1), so that x_hat
+    lies mostly inside [0, 1] (the range the codec's YUV conversion keeps;
+    with unit gain nearly every sample would clip to 0 or 255)."""
+    w = gb.weight(name + ".weight", _fp16(kaiming_normal(rng, (3 * 64, cin, 1, 1), 1.0) * gain))
+    b = gb.weight(name + ".bias", _fp16(small_bias(rng, 3 * 64).astype(np.float32) + 0.5))
+    return gb.depth_to_space(gb.conv(r, w, b), 8)
+
+
+def synthetic_yuv420(frame, width, height, seed=0, shift=2, sigma=8.0):
+    """Seeded synthetic 8-bit YUV420 content of BASELINE configs 3-5: a smooth
+    diagonal luma gradient and two chroma gradients plus Gaussian noise
+    (sigma 8 on luma, sigma / 2 on chroma), moving `shift` pixels to the
+    right per frame (a global translation: frame f is the content window at
+    x offset shift * f).  Returns (Y [h, w], U [h/2, w/2], V [h/2, w/2]) uint8."""
+    rng = np.random.default_rng(seed)
+    span = width + shift * 64  # a window that holds 64 frames of motion
+    noise_y = rng.standard_normal((height, span)).astype(np.float32) * sigma
+    noise_c = rng.standard_normal((2, height // 2, span // 2)).astype(np.float32) * (sigma / 2)
+    off = (shift * frame) % (span - width + 1)
+    xs = np.arange(off, off + width, dtype=np.float32)[None, :]
+    ys = np.arange(height, dtype=np.float32)[:, None]
+    y = 32.0 + 160.0 * (xs / span + ys / height) / 2.0 + noise_y[:, off:off + width]
+    cx, cy = xs[:, ::2] / span, ys[::2] / height
+    coff = off // 2
+    u = 96.0 + 64.0 * cx + noise_c[0, :, coff:coff + width // 2]
+    v = 160.0 - 64.0 * cy + noise_c[1, :, coff:coff + width // 2]
+    q = lambda a: np.clip(np.rint(a), 0, 255).astype(np.uint8)
+    return q(y), q(u), q(v)
+
+
 def build_mlvc_decoder_standin(seed=0, width=1920, height=1088, feature=256, latent=128, hyper=128, qp_num=72,
-                               q_index=21, blocks_y=2, blocks_feature=2, blocks_recon=2):
+                               q_index=21, blocks_y=2, blocks_feature=2, blocks_recon=2, recon_gain=0.02):
     """MLVC-shaped decoder STAND-IN.  The upstream MLVC architecture source is
     absent from the reference (tools/python/mlvc_tools/source.py imports it from
     an external package), so this is not the MLVC network; it is assembled from
@@ -416,7 +448,8 @@ def build_mlvc_decoder_standin(seed=0, width=1920, height=1088, feature=256, lat
     contextual decoder concat(y, context) -> 1x1 -> blocks_y blocks at 1/16 ->
     1x1 + pixel shuffle 2 -> concat(ref_feature) -> 1x1 -> blocks_feature
     blocks at 1/8 = new feature; reconstruction blocks_recon blocks -> 1x1 to
-    3 x 64 -> pixel shuffle 8 = x_hat.  Weights Kaiming-normal (gain as in
+    3 x 64 (gain recon_gain, bias 0.5: x_hat within [0, 1]) -> pixel shuffle
+    8 = x_hat.  Weights Kaiming-normal (gain as in
     build_block_stack), the residual-branch output convs scaled by 0.25 (with
     full gain the un-normalised 256-channel residual stream grows to std ~100
     and the two CPU implementations differ by 10 % rel-L2 at the output; at
@@ -464,7 +497,7 @@ def build_mlvc_decoder_standin(seed=0, width=1920, height=1088, feature=256, lat
     r = t
     for i in range(blocks_recon):
         r = _depth_conv_block(gb, rng, r, feature, f"recon.block{i}.", 0.25)
-    x_hat = gb.depth_to_space(conv1x1(r, feature, 3 * 64, "recon.out"), 8)
+    x_hat = _recon_out(gb, rng, r, feature, "recon.out", recon_gain)
     gb.output(x_hat, "x_hat")
     gb.output(new_feature, "feature")
     inputs = [np.rint(rng.standard_normal((1, hyper, hz, wz)) * 4).astype(np.float16),
@@ -477,7 +510,7 @@ def build_mlvc_decoder_standin(seed=0, width=1920, height=1088, feature=256, lat
 
 def build_mlvcs_decoder_standin(seed=0, width=640, height=368, feature=96, latent=48, hyper=48, hidden=192,
                                 recon=192, y_scale_repeat=4, qp_num=72, q_index=21, hyper_blocks=2, blocks_y=2,
-                                blocks_feature=2, blocks_recon=2):
+                                blocks_feature=2, blocks_recon=2, recon_gain=0.02):
     """MLVC-S-shaped decoder STAND-IN (the upstream MLVC-S architecture is
     absent, like MLVC's).  Built from what the reference documents about the
     small profile (models/profiles/profiles.json "mlvc-s-psnr-v1": hidden and
@@ -491,8 +524,8 @@ def build_mlvcs_decoder_standin(seed=0, width=640, height=368, feature=96, laten
     concat(y_raw_0, y_raw_1) * qscale[q] + means; concat(y, context) -> 1x1
     -> blocks_y blocks at 1/16 (192) -> 1x1 to 4 x 96 + pixel shuffle 2 ->
     concat(ref_feature) -> 1x1 -> blocks_feature blocks at 1/8 (96) = new
-    feature; 1x1 to 192 -> blocks_recon blocks -> 1x1 to 3 x 64 -> pixel
-    shuffle 8 = x_hat.  Weights and inputs as in build_mlvc_decoder_standin.
+    feature; 1x1 to 192 -> blocks_recon blocks -> 1x1 to 3 x 64 (gain
+    recon_gain, bias 0.5) -> pixel shuffle 8 = x_hat.  Weights and inputs as in build_mlvc_decoder_standin.
     The 96- and 192-channel blocks take the kernels' general paths (separate
     expand conv, stand-alone or fused depthwise, ReGLU GEMM + 1x1)."""
     rng = np.random.default_rng(seed)
@@ -536,7 +569,7 @@ def build_mlvcs_decoder_standin(seed=0, width=640, height=368, feature=96, laten
     r = conv1x1(t, feature, recon, "recon.in")
     for i in range(blocks_recon):
         r = _depth_conv_block(gb, rng, r, recon, f"recon.block{i}.", 0.25)
-    x_hat = gb.depth_to_space(conv1x1(r, recon, 3 * 64, "recon.out"), 8)
+    x_hat = _recon_out(gb, rng, r, recon, "recon.out", recon_gain)
     gb.output(x_hat, "x_hat")
     gb.output(new_feature, "feature")
     inputs = [np.rint(rng.standard_normal((1, hyper, hz, wz)) * 4).astype(np.float16),

@@ -81,6 +81,12 @@ class RefCpuBackend:
             outs.append(o)
         return outs
 
+    def reset_state(self):
+        """InferenceBackend::reset_state(): zeroes every bound state (a new GOP)."""
+        err = ctypes.create_string_buffer(1024)
+        if lib().mlvc_ref_reset_state(self._h, err, 1024) != 0:
+            raise RuntimeError(err.value.decode())
+
     def close(self):
         if self._h:
             lib().mlvc_ref_destroy(self._h)

@@ -12,7 +12,7 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 
 
-@pytest.mark.parametrize("workload", ["block_stack", "entropy_1080p"])
+@pytest.mark.parametrize("workload", ["mlvc_dec_1080p_8s", "block_stack", "entropy_1080p"])
 def test_reference_arm_prints_one_contract_line(workload):
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload", workload,
                           "--steps", "2", "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=ROOT)
@@ -30,3 +30,25 @@ def test_bench_rejects_short_warmup():
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--warmup", "2"], capture_output=True, text=True,
                          timeout=120, cwd=ROOT)
     assert out.returncode != 0 and "--warmup must be >= 3" in out.stderr
+
+
+def test_default_workload_is_the_metric_configuration():
+    """The default workload is BASELINE config 5 (1080p, 8 independent
+    streams), and both arms report it under the same metric and scaling."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([l for l in out.stdout.splitlines() if l.startswith("{")][0])
+    assert d["metric"] == bench.STREAMS_METRIC and d["scaling"] == "strong"
+    assert d["config"]["workload"] == bench.STREAMS_DESC and d["config"]["global_batch"] == bench.STREAMS == 8
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun with N > 1 only rank 0 runs the reference arm."""
+    import os
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "3"], capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
+    assert out.returncode == 0 and not [l for l in out.stdout.splitlines() if l.startswith("{")]

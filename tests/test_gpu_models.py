@@ -80,12 +80,14 @@ def test_block_stack_config2_full(tmp_path):
     assert np.array_equal(y.view(np.uint16), y2.view(np.uint16))
 
 
-@pytest.mark.parametrize("width,height", [(256, 128), (640, 368)])
+@pytest.mark.parametrize("width,height", [(256, 128), (640, 368), (1920, 1088)])
 def test_mlvc_decoder_standin(width, height, tmp_path):
     """The MLVC-shaped decoder stand-in (256-channel blocks on the unfused
     tensor-core path, pixel shuffle x2 / x8, spatial crops, channel concats,
     QP-indexed Gather): every materialised step against the oracle, then the
-    whole graph against the reference CPU backend."""
+    whole graph against the reference CPU backend.  1920x1088 is the
+    benchmark's configuration: 510-tile 1x1 convs and the
+    512-channel fused depthwise + projection at 136 x 240."""
     gb, inputs = build_mlvc_decoder_standin(seed=5, width=width, height=height)
     be, graph, weights = _load(gb)
     x_hat, feature = be.run(inputs)
