@@ -45,7 +45,7 @@ for p in (ROOT, ROOT / "mlvc.cpp_b200"):
         sys.path.insert(0, str(p))
 
 from mlvc_b200.graph import (build_block_stack, build_conv3x3, build_mlvc_decoder_standin,  # noqa: E402
-                             build_mlvcs_decoder_standin)
+                             build_mlvc_encoder_standin, build_mlvcs_decoder_standin)
 
 METRIC = "conv-stack frames/s (config 2 block stack; stand-in for 1080p MLVC decode frames/s)"
 UNIT = "frames/s"
@@ -126,6 +126,17 @@ def workload(name):
         metric = f"MLVC-shaped decoder stand-in frames/s @{width}x{height} (stand-in for MLVC decode frames/s)"
         graph, weights = gb.finish()
         return graph, weights, inputs, desc, metric, [(3, 1)]
+    if name.startswith("mlvc_enc_"):
+        width, height = {"mlvc_enc_1080p": (1920, 1088), "mlvc_enc_640": (640, 368)}[name]
+        gb, inputs = build_mlvc_encoder_standin(0, width, height)
+        desc = (f"MLVC-shaped encoder stand-in @{width}x{height} (the upstream MLVC architecture is absent): "
+                "documented encoder I/O (x [1,3,H,W], ref_feature 256ch 1/8, q_index int32 -> feature, z_raw 1/128, "
+                "y_raw_0/1 1/16), pixel-unshuffle x8 analysis with 3x3 s2 down-sampling, hyperprior encoder and "
+                "decoder, the y0 / y1 latent quantisation tails, the recurrent feature update; Kaiming-normal "
+                "weights, seed 0; ref_feature <- feature bound as recurrent state (input 1 <- output 0)")
+        metric = f"MLVC-shaped encoder stand-in frames/s @{width}x{height} (stand-in for MLVC encode frames/s)"
+        graph, weights = gb.finish()
+        return graph, weights, inputs, desc, metric, [(1, 0)]
     if name == "mlvcs_dec_640":
         gb, inputs = build_mlvcs_decoder_standin(0, 640, 368)
         desc = ("MLVC-S-shaped decoder stand-in @640x368 (the upstream MLVC-S architecture is absent): documented "
@@ -897,7 +908,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["block_stack", "conv3x3", "op_dw3x3", "op_conv1x1", "op_ffn", "op_dwconv",
                                                    "op_mbconv", "mlvc_dec_1080p", "mlvc_dec_640", "mlvcs_dec_640",
-                                                   "entropy_1080p", STREAMS_WORKLOAD],
+                                                   "mlvc_enc_1080p", "mlvc_enc_640", "entropy_1080p",
+                                                   STREAMS_WORKLOAD],
                     default=STREAMS_WORKLOAD)
     ap.add_argument("--cpu-frames", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -193,7 +193,9 @@ int mlvc_b200_integer_values_device(mlvc_b200_backend* backend, uint64_t values,
  * default) and returns when the work is done; every call on a device shares
  * the one array, so calls from several host threads at once race; the first
  * call on a device looks the array's address up, so make it before any
- * stream capture on that device. */
+ * stream capture on that device, and do not call it after a
+ * cudaDeviceReset of that device (or anything else that destroys its primary
+ * context) in the same process: it keeps the address it looked up. */
 int mlvc_b200_integer_values_noalloc(const uint16_t* values, size_t count, int32_t* symbols);
 
 /* Measurement hooks (no reference counterpart; the reference times whole

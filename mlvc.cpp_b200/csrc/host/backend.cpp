@@ -465,7 +465,9 @@ void Backend::plan()
                 long long st0 = starts[k];
                 if (st0 < 0)
                     st0 += id4[axis];
-                start4[axis] = st0;
+                // clamped to [0, dim] like the reference CPU plan
+                // (backends/cpu/src/execution_plan.cpp:596-599)
+                start4[axis] = std::clamp<long long>(st0, 0, id4[axis]);
                 if (!stepv.empty())
                     step4[axis] = stepv.at(k);
             }
@@ -496,7 +498,11 @@ void Backend::plan()
             const auto& x = values_[n.inputs[0]].shape;
             const auto& w = values_[n.inputs[1]].shape;
             const auto& o = values_[n.output].shape;
-            if (x.size() == 4 && w.size() == 4 && o.size() == 4) {
+            // the conv kernels index NCHW / OIHW operands: every Conv is rank 4
+            // (the reference's exporter emits nothing else, aot.py:161-168)
+            if (x.size() != 4 || w.size() != 4 || o.size() != 4)
+                throw std::runtime_error("mlvc-b200: Conv input, weights and output must be rank 4");
+            {
                 const long long g = n.groups, sh = n.strides[0], sw = n.strides[1], ph = n.pads[0], pw = n.pads[1];
                 const long long oh = (x[2] + 2 * ph - w[2]) / sh + 1, ow = (x[3] + 2 * pw - w[3]) / sw + 1;
                 const bool bias_ok = n.inputs.size() < 3 || !n.inputs[2] ||
@@ -1998,7 +2004,9 @@ void Backend::plan()
                 long long st0 = starts[k];
                 if (st0 < 0)
                     st0 += id4[axis];
-                start4[axis] = st0;
+                // clamped to [0, dim] like the reference CPU plan
+                // (backends/cpu/src/execution_plan.cpp:596-599)
+                start4[axis] = std::clamp<long long>(st0, 0, id4[axis]);
                 if (!stepv.empty())
                     step4[axis] = stepv[k];
             }
@@ -2571,13 +2579,14 @@ void Backend::check_status()
     if (status) {
         const unsigned int zero = 0;
         cuMemcpyHtoD(status_ptr_, &zero, sizeof(zero));
-        throw std::runtime_error("mlvc-b200: a device-side wait timed out (status 0x" +
-                                 [&] {
-                                     std::ostringstream os;
-                                     os << std::hex << status;
-                                     return os.str();
-                                 }() +
-                                 ")");
+        std::ostringstream os;
+        os << "mlvc-b200:";
+        if (status & 0xffu)  // wait-timeout / alignment bits of the tensor-core kernels
+            os << " a device-side wait timed out or a TMA destination was misaligned;";
+        if (status & 0x100u)  // mlvc_gather_rows_f16 (reference: "cpu: GATHER index out of range")
+            os << " GATHER index out of range;";
+        os << " status 0x" << std::hex << status;
+        throw std::runtime_error(os.str());
     }
 }
 

@@ -684,8 +684,13 @@ extern "C" __global__ void mlvc_gather_rows_f16(const __grid_constant__ GatherPa
     int row = p.index[0];
     if (row < 0)
         row += p.rows;
-    if (row < 0 || row >= p.rows)
+    if (row < 0 || row >= p.rows) {
+        // the reference CPU backend raises "GATHER index out of range"
+        // (backends/cpu/src/execution_plan.cpp:119-124); here the run reports it
+        if (blockIdx.x == 0 && threadIdx.x == 0)
+            atomicOr(&mlvc_b200_status, mlvc_b200::kStatusGatherIndex);
         return;
+    }
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.row_elems; i += stride)
         p.dst[i] = p.src[row * p.row_elems + i];

@@ -251,7 +251,9 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
         bool ok = mbar_wait(&sh->dw_full, 0, &sh->abort_flag, kErrWaitEpilogue);
         int hs = 0, as = 0;
         uint32_t hph = 0, aph = 0, acc = 0, acc_phase = 0, it = 0;
+        bool res_issued = false;  // the leader issued tile `it`'s residual load
         for (int t = first; ok && t < tiles; t += step, ++it) {
+            res_issued = false;
             TileCoord tc;
             tc.pixel0 = 0;
             tc.ox0 = (t % dp.tiles_x) * kDwTileW;
@@ -341,8 +343,10 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 // run.  Issued after the first slice, not before it: the leader's
                 // wait for the previous tile's output store to read the buffer
                 // would otherwise hold up the first slice's A panel.
-                if (leader && kp == 0)
+                if (leader && kp == 0) {
                     stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
+                    res_issued = p.epilogue == kEpiResidual;
+                }
                 if (leader && it == 0 && kp == 0)
                     trace(p, kTrDwFirstSlice);
                 if (leader && it == 0 && kp < 8)
@@ -362,14 +366,23 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 break;
             if (!epilogue_tile(p, sh->bias, sh->tmem_base + acc * p.BN, &sh->acc_full[acc], acc_phase, &sh->acc_empty[acc],
                                ss, it, stage_smem, nullptr, panels, 0, tc, true, quadrant, group, lane, leader,
-                               &sh->abort_flag))
+                               &sh->abort_flag)) {
+                ok = false;
                 break;
+            }
             if (leader && it == 0)
                 trace(p, kTrFirstAcc);
             acc ^= 1u;
             acc_phase ^= (acc == 0) ? 1u : 0u;
         }
         if (leader) {
+            // An aborted tile's residual load may still be in flight: wait
+            // (bounded) for its barrier phase before shared memory retires; a
+            // phase that already completed returns at once.
+            if (!ok && res_issued) {
+                volatile int never = 0;
+                mbar_wait(ss.ready, it & 1u, &never, kErrWaitEpilogue);
+            }
             bulk_wait_all();
             trace(p, kTrEpilogueDone);
         }

@@ -435,6 +435,7 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
             ok = mbar_wait(&sh->dw_full, 0, &sh->abort_flag, kErrWaitEpilogue);
             int as = 0;
             uint32_t aph = 0;
+            bool res_issued = false;  // the leader issued tile `it`'s residual load
             for (int t = first; ok && t < tiles; t += step, ++it) {
                 TileCoord tc;
                 tc.pixel0 = 0;
@@ -442,6 +443,7 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
                 tc.oy = (t / mp.tiles_x) * kDwTileH;
                 if (leader)  // residual tile into the staging buffer while the block runs
                     stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
+                res_issued = p.epilogue == kEpiResidual;
                 const int x0 = tc.ox0 + bx;
                 for (int c = 0; c < nch; ++c, ++kc) {
                     const uint32_t buf = kc & 1u, use = kc >> 1;
@@ -531,12 +533,20 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
                     break;
                 if (!epilogue_tile(p, sh->bias2, sh->tmem_base + kMbAcc2Col, &sh->acc2_full, it & 1u, &sh->acc2_empty,
                                    ss, it, stage_smem, nullptr, panels, 0, tc, true, quadrant, group, lane, leader,
-                                   &sh->abort_flag))
+                                   &sh->abort_flag)) {
+                    ok = false;
                     break;
+                }
                 if (leader && it == 0)
                     trace(p, kTrFirstAcc);
             }
             if (leader) {
+                // An aborted tile's residual load may still be in flight: wait
+                // (bounded) for its barrier phase before shared memory retires.
+                if (!ok && res_issued) {
+                    volatile int never = 0;
+                    mbar_wait(ss.ready, it & 1u, &never, kErrWaitEpilogue);
+                }
                 bulk_wait_all();
                 trace(p, kTrEpilogueDone);
             }

@@ -24,6 +24,9 @@ extern "C" __device__ unsigned long long mlvc_b200_wait_limit_ns;
 namespace mlvc_b200 {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+// Status bit of a Gather whose index is outside the table (the wait-timeout
+// bits of the tensor-core kernels are 0x1 .. 0x80).
+constexpr unsigned int kStatusGatherIndex = 0x100u;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns()
 {

@@ -19,7 +19,11 @@
 //   * the work runs on the calling thread's current device (cudaSetDevice;
 //     device 0 by default) and its per-thread default stream;
 //   * the first call on a device looks the array's device address up; make
-//     that first call before any stream capture on that device.
+//     that first call before any stream capture on that device;
+//   * that address belongs to the device's primary context: do not call this
+//     entry point after a cudaDeviceReset (or anything else that destroys the
+//     primary context) in the same process, since it would still use the old
+//     address.
 //
 // The arithmetic is the one of mlvc_integer_values_f16 (reference
 // integer_values, core/src/entropy.cpp:201-226): truncation towards zero, and

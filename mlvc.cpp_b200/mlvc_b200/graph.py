@@ -508,6 +508,137 @@ def build_mlvc_decoder_standin(seed=0, width=1920, height=1088, feature=256, lat
     return gb, inputs
 
 
+def build_mlvc_encoder_standin(seed=0, width=1920, height=1088, feature=256, latent=128, hyper=128, qp_num=72,
+                               q_index=21, blocks_analysis=1, blocks_latent=1, blocks_mirror=1, ref_gain=0.25,
+                               mirror_gain=0.25):
+    """MLVC-shaped encoder STAND-IN (the upstream MLVC architecture is absent).
+    Built from what the reference documents about the encoder:
+
+    * graph I/O (docs/design.md, "Fixed graph I/O"): x [1, 3, H, W] pixels in
+      [0, 1], ref_feature [1, feature, H/8, W/8], q_index_shifted [1] int32 ->
+      feature [1, feature, H/8, W/8] (the new DPB feature, the final node, so a
+      state binding input 1 <- output 0 aliases it), z_raw
+      [1, hyper, ceil(H/128), ceil(W/128)], y_raw_0 / y_raw_1
+      [1, latent/2, ceil(H/16), ceil(W/16)], all integer-valued latents;
+    * the latent quantisation tails in the node order the reference fuses
+      (y0 then y1: backends/cpu/src/fusion_matcher.cpp:543-850,
+      backends/driver_cubin/src/fusion_registry.cpp:14-404), fed by a
+      hyperprior that mirrors the decoder stand-in's;
+    * the recurrent-feature update in its encoder form (three channel thirds,
+      two sigmoids, a gated blend with the previous feature, a per-channel
+      scale, then the concat: fusion_matcher.cpp:413-541 Case A);
+    * the profile's depth-conv block (_depth_conv_block), native CRD pixel
+      (un)shuffle and strided 3 x 3 convolutions for down-sampling.
+
+    Layout: x -> pixel unshuffle 8 -> 1x1 + LeakyReLU -> concat(ref_feature)
+    -> 1x1 -> blocks_analysis blocks at 1/8 -> 3x3 s2 + LeakyReLU ->
+    blocks_latent blocks at 1/16 -> 1x1 = y; hyperprior encoder: three 3x3 s2
+    convs (1/32, 1/64, 1/128) -> Round = z_raw; hyperprior decoder as in the
+    decoder stand-in -> prior (4 x latent/2 channels); quantisation scales
+    qs0 / qs1 = clip(1x1(prior), 0.25, 4) x the QP-indexed scale row,
+    update scales clip(1x1(prior), 0.25, 4), second prior 1x1(prior); y0
+    tail -> y_raw_0, y1 tail -> y_raw_1 and the dequantised latent; the
+    mirror of the decoder's context path: concat(dequantised latent, prior
+    concat) -> 1x1 to 4 x feature -> pixel shuffle 2 -> concat(ref_feature)
+    -> 1x1 -> blocks_mirror blocks -> 1x1 to 3 x feature/2 -> feature update
+    with the previous feature's second half as history = feature.  Weights
+    as in build_mlvc_decoder_standin, seeded."""
+    rng = np.random.default_rng(seed)
+    h8, w8 = -(-height // 8), -(-width // 8)
+    h16, w16 = -(-height // 16), -(-width // 16)
+    if h8 != 2 * h16 or w8 != 2 * w16 or height != 8 * h8 or width != 8 * w8:
+        raise ValueError("stand-in needs H and W multiples of 16")
+    q = latent // 2
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 3, height, width])
+    ref = gb.input("ref_feature", [1, feature, h8, w8])
+    qi = gb.input("q_index_shifted", [1], "int32")
+
+    def conv1x1(v, cin, cout, name, gain=1.0, damp_from=None):
+        """damp_from: input channels from this index on (the previous
+        feature's part of a concat) get weights scaled by ref_gain."""
+        w = kaiming_normal(rng, (cout, cin, 1, 1), gain)
+        if damp_from is not None:
+            w = w.astype(np.float32)
+            w[:, damp_from:] *= ref_gain
+            w = _fp16(w)
+        return gb.conv(v, gb.weight(name + ".weight", w), gb.weight(name + ".bias", small_bias(rng, cout)))
+
+    def conv3x3s2(v, cin, cout, name, gain=1.0):
+        w = gb.weight(name + ".weight", kaiming_normal(rng, (cout, cin, 3, 3), gain))
+        return gb.conv(v, w, gb.weight(name + ".bias", small_bias(rng, cout)), (2, 2), (1, 1))
+
+    # analysis: 1/8 with the reference feature, then 1/16
+    t = gb.leaky_relu(conv1x1(gb.space_to_depth(x, 8), 3 * 64, feature, "ana.in", np.sqrt(2.0)), 0.01)
+    t = conv1x1(gb.concat([t, ref], 1), 2 * feature, feature, "ana.ctx", damp_from=feature)
+    for i in range(blocks_analysis):
+        t = _depth_conv_block(gb, rng, t, feature, f"ana.block{i}.", 0.25)
+    t = gb.leaky_relu(conv3x3s2(t, feature, feature, "ana.down", np.sqrt(2.0)), 0.01)
+    for i in range(blocks_latent):
+        t = _depth_conv_block(gb, rng, t, feature, f"lat.block{i}.", 0.25)
+    y = conv1x1(t, feature, latent, "lat.out")
+    # hyperprior encoder: 1/16 -> 1/128, rounded
+    hz = gb.leaky_relu(conv3x3s2(y, latent, hyper, "hyenc.0", np.sqrt(2.0)), 0.01)
+    hz = gb.leaky_relu(conv3x3s2(hz, hyper, hyper, "hyenc.1", np.sqrt(2.0)), 0.01)
+    z = gb.unary("Round", conv3x3s2(hz, hyper, hyper, "hyenc.2", 2.0))
+    # hyperprior decoder (as in the decoder stand-in), cropped to the y plane
+    p = gb.leaky_relu(conv1x1(z, hyper, feature, "hyper.in", np.sqrt(2.0)), 0.01)
+    p = _depth_conv_block(gb, rng, p, feature, "hyper.block0.", 0.25)
+    for i in range(3):
+        p = gb.depth_to_space(conv1x1(p, feature, 4 * feature, f"hyper.up{i}"), 2)
+    prior = gb.slice(gb.slice(p, 2, 0, h16), 3, 0, w16)  # [1, feature = 4q, h16, w16]
+    table = gb.weight("qscale", rng.uniform(0.5, 2.0, (qp_num, latent, 1, 1)).astype(np.float16))
+    qrow = gb.gather(table, qi)
+    qs0 = gb.mul(gb.clip(conv1x1(prior, feature, latent, "qs0"), 0.25, 4.0), qrow)
+    qs1 = gb.mul(gb.clip(conv1x1(prior, feature, latent, "qs1"), 0.25, 4.0), qrow)
+    us0 = gb.clip(conv1x1(prior, feature, q, "us0"), 0.25, 4.0)
+    us1 = gb.clip(conv1x1(prior, feature, q, "us1"), 0.25, 4.0)
+    prior2 = conv1x1(prior, feature, latent, "prior2")
+    # y0 tail (19 operators in the exported order)
+    s0 = gb.slice(prior, 1, 0, 2 * q)
+    s1 = gb.slice(prior, 1, 2 * q, 4 * q)
+    clipped = gb.clip(s0, 0.11, 65504.0)
+    norm = gb.mul(y, gb.unary("Reciprocal", clipped))
+    scaled = gb.mul(gb.sub(norm, s1), qs0)
+    a0, a1 = gb.slice(scaled, 1, 0, q), gb.slice(scaled, 1, q, 2 * q)
+    y0 = gb.unary("Round", gb.add(a0, a1))
+    p0, p1 = gb.slice(s1, 1, 0, q), gb.slice(s1, 1, q, 2 * q)
+    c2 = gb.concat([gb.mul(gb.add(y0, p0), us0), gb.mul(gb.add(y0, p1), us1)], 1)
+    c3 = gb.concat([c2, prior], 1)
+    # y1 tail (15 operators)
+    sc = gb.mul(gb.sub(norm, prior2), qs1)
+    b0, b1 = gb.slice(sc, 1, 0, q), gb.slice(sc, 1, q, 2 * q)
+    y1 = gb.unary("Round", gb.add(b0, b1))
+    r0, r1 = gb.slice(prior2, 1, 0, q), gb.slice(prior2, 1, q, 2 * q)
+    c4 = gb.concat([gb.mul(gb.add(y1, r0), us0), gb.mul(gb.add(y1, r1), us1)], 1)
+    y_hat = gb.mul(gb.add(c2, c4), clipped)
+    # mirror of the decoder's context path, then the recurrent-feature update
+    m = conv1x1(gb.concat([y_hat, c3], 1), 2 * latent + feature, 4 * feature, "mir.up", mirror_gain)
+    m = conv1x1(gb.concat([gb.depth_to_space(m, 2), ref], 1), 2 * feature, feature, "mir.in", damp_from=feature)
+    for i in range(blocks_mirror):
+        m = _depth_conv_block(gb, rng, m, feature, f"mir.block{i}.", 0.25)
+    half = feature // 2
+    u = conv1x1(m, feature, 3 * half, "upd.in")
+    hist = gb.slice(ref, 1, half, feature)
+    ua, ub, ug = gb.slice(u, 1, 0, half), gb.slice(u, 1, half, 2 * half), gb.slice(u, 1, 2 * half, 3 * half)
+    sb, sg = gb.unary("Sigmoid", ub), gb.unary("Sigmoid", ug)
+    blended = gb.add(gb.mul(sb, hist), gb.mul(gb.sub(gb.weight("upd.one", np.array([1.0], np.float16)), sb), ua))
+    scale = gb.weight("upd.scale", rng.uniform(0.5, 1.5, (1, half, 1, 1)).astype(np.float16))
+    new_feature = gb.concat([gb.mul(gb.mul(sg, blended), scale), blended], 1)
+    gb.output(new_feature, "feature")
+    gb.output(z, "z_raw")
+    gb.output(y0, "y_raw_0")
+    gb.output(y1, "y_raw_1")
+    Y, U, V = synthetic_yuv420(0, width, height - 8 if height % 16 == 0 else height, seed)
+    xin = np.zeros((1, 3, height, width), np.float16)
+    xin[0, 0, :Y.shape[0]] = Y / 255.0
+    xin[0, 1, :Y.shape[0]] = np.repeat(np.repeat(U, 2, 0), 2, 1) / 255.0
+    xin[0, 2, :Y.shape[0]] = np.repeat(np.repeat(V, 2, 0), 2, 1) / 255.0
+    inputs = [xin, _fp16(rng.standard_normal((1, feature, h8, w8), dtype=np.float32)),
+              np.array([q_index], np.int32)]
+    return gb, inputs
+
+
 def build_mlvcs_decoder_standin(seed=0, width=640, height=368, feature=96, latent=48, hyper=48, hidden=192,
                                 recon=192, y_scale_repeat=4, qp_num=72, q_index=21, hyper_blocks=2, blocks_y=2,
                                 blocks_feature=2, blocks_recon=2, recon_gain=0.02):

@@ -211,6 +211,8 @@ class GraphOracle:
             for s, ax, st in zip(starts, axes, steps):
                 ax = int(ax) + (x.ndim if ax < 0 else 0)
                 s = int(s) + (x.shape[ax] if s < 0 else 0)
+                # clamped to [0, dim] (backends/cpu/src/execution_plan.cpp:596-599)
+                s = min(max(s, 0), x.shape[ax])
                 sl[ax] = slice(s, s + int(st) * out_shape[ax], int(st))
             y = np.ascontiguousarray(x[tuple(sl)])
         elif op == "Concat":

@@ -569,3 +569,45 @@ def test_plan_rejects_inconsistent_operand_extents(what, message):
     instead of reading or writing past a buffer."""
     with pytest.raises(RuntimeError, match=message):
         plan(*_bad_shape_graph(what))
+
+
+def test_plan_rejects_conv_that_is_not_rank_4():
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 64, 16, 16])
+    y = gb.conv(x, gb.weight("w", np.zeros((64, 64, 1, 1), np.float16)))
+    gb.tensors[x].shape = [64, 16, 16]  # rank-3 input
+    gb.output(y, "y")
+    with pytest.raises(RuntimeError, match="Conv input, weights and output must be rank 4"):
+        plan(*gb.finish())
+
+
+def _slice_from(start, dim=8):
+    """Slice of rows [start, start + 4) of a [1, 16, dim, 12] input, with the
+    start literal written as given (the builder would normalise it)."""
+    gb = GraphBuilder()
+    x = gb.input("x", [1, 16, dim, 12])
+    y = gb.slice(x, 2, 0, 4)
+    gb.tensors[gb.nodes[-1].inputs[1]].data = np.array([start], np.int64)
+    gb.output(gb.leaky_relu(y, 0.5), "y")
+    return gb.finish()
+
+
+def test_plan_clamps_slice_start_like_the_reference(tmp_path):
+    """A start below -dim wraps to a negative value, which the reference CPU
+    plan clamps to 0 (backends/cpu/src/execution_plan.cpp:596-599): the graph
+    loads and slices from row 0, like the reference CPU backend."""
+    from oracle.ref_backend import LIB_PATH, RefCpuBackend
+    graph, weights = _slice_from(-9)
+    plan(graph, weights)  # accepted
+    x = np.random.default_rng(0).standard_normal((1, 16, 8, 12)).astype(np.float16)
+    want = GraphOracle(graph, weights).run([x])[0]
+    assert np.array_equal(want, GraphOracle(*_slice_from(0)).run([x])[0])
+    if LIB_PATH.exists():
+        part = tmp_path / "aot" / "m"
+        part.mkdir(parents=True)
+        (part / "graph.pb").write_bytes(graph)
+        (part / "weights.bin").write_bytes(weights)
+        (ref,) = RefCpuBackend(tmp_path, "m", 1).run([x])
+        assert np.array_equal(ref.view(np.uint16), want.view(np.uint16))
+    with pytest.raises(RuntimeError, match="exceeds its input"):
+        plan(*_slice_from(6))  # rows 6..9 of 8

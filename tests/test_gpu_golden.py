@@ -64,3 +64,11 @@ def test_example_q_all_qp_rows():
         ins = [x, ref, np.array([q], np.int32)]
         for got, want in zip(be.run(ins), oracle.run(ins)):
             compare_scaled(got, want)
+    # an index outside the 4-row table is an error, as in the reference CPU
+    # backend ("cpu: GATHER index out of range"), and the backend stays usable
+    for q in (4, -5):
+        with pytest.raises(RuntimeError, match="GATHER index out of range"):
+            be.run([x, ref, np.array([q], np.int32)])
+    ins = [x, ref, np.array([1], np.int32)]
+    for got, want in zip(be.run(ins), oracle.run(ins)):
+        compare_scaled(got, want)

@@ -16,7 +16,7 @@ CPU-vs-CPU spread (or within 1e-3), measured on the same inputs.
 import numpy as np
 import pytest
 
-from helpers import compare_scaled, per_op_parity
+from helpers import bits_equal, compare_scaled, per_op_parity
 from mlvc_b200 import Backend
 from mlvc_b200.graph import build_block_stack, build_conv3x3, build_mlvc_decoder_standin
 from oracle.graph_oracle import GraphOracle
@@ -116,3 +116,58 @@ def test_conv3x3_config1_per_op():
     (y,) = be.run(inputs)
     (want,) = GraphOracle(graph, weights, "gemm").run(inputs)
     compare_scaled(y, want)
+
+
+@pytest.mark.parametrize("width,height", [(256, 128), (640, 368), (1920, 1088)])
+def test_mlvc_encoder_standin(width, height, tmp_path):
+    """The MLVC-shaped encoder stand-in (strided 3x3 analysis convs, the y0 /
+    y1 quantisation tails and the encoder-form feature update as fused
+    kernels): every materialised step against the oracle on the GPU's own
+    step inputs -- integer-valued z_raw / y_raw_0 / y_raw_1 exactly, since
+    Round outputs pass the per-op check only when equal -- then all four
+    outputs against the reference CPU backend within twice the CPU-vs-CPU
+    spread (symbols differ only where an upstream FP16 rounding difference
+    crosses a rounding boundary).  A P-frame: the reference feature is a
+    previous feature (not zero)."""
+    from mlvc_b200.graph import build_mlvc_encoder_standin
+    gb, inputs = build_mlvc_encoder_standin(seed=4, width=width, height=height)
+    inputs[1] = (inputs[1].astype(np.float32) * 0.15).astype(np.float16)
+    be, graph, weights = _load(gb)
+    outs = be.run(inputs)
+    kernels = {s["kernel"] for s in be.steps()}
+    assert {"mlvc_y0_tail_f16", "mlvc_y1_tail_f16", "mlvc_feature_update_f16", "mlvc_convkxk_tc"} <= kernels
+    assert [o.shape for o in outs] == [(1, 256, height // 8, width // 8), (1, 128, -(-height // 128), -(-width // 128)),
+                                       (1, 64, height // 16, width // 16), (1, 64, height // 16, width // 16)]
+    for o in outs[1:]:
+        assert np.array_equal(o, np.rint(o)), "latents must be integer-valued"
+    assert per_op_parity(be, graph, weights, inputs, conv_impl="gemm") >= 40
+    _stack_check(outs, graph, weights, inputs, tmp_path)
+
+
+def test_mlvc_encoder_slot_path_with_yuv_input(tmp_path):
+    """Encoder through the slot API with the codec's YUV420 input conversion
+    and submit(slot, shifted_q) (the reference's encoder_input_yuv /
+    submit_encoder / encoder_outputs, cuda_graph_executor.cpp:243-312): the
+    outputs equal run() on the tensor the reference's prepare_model_input
+    makes from the same frame, frame after frame with the state carried."""
+    from mlvc_b200.graph import build_mlvc_encoder_standin, synthetic_yuv420
+    from oracle.ref_backend import ref_yuv_to_tensor
+    W, H, MW, MH = 256, 120, 256, 128
+    gb, inputs = build_mlvc_encoder_standin(seed=6, width=MW, height=MH)
+    graph, weights = gb.finish()
+    slots, plain = Backend(0), Backend(0)
+    for b in (slots, plain):
+        b.load_memory(graph, weights, [(1, 0)])
+        b.reset_state()
+    slots.configure_codec_io(W, H, MW, MH, 1.0, slots=2, input_index=0)
+    for frame, q in enumerate((21, 21, 0, 51)):
+        slot = frame % 2
+        y, u, v = synthetic_yuv420(frame, W, H)
+        py, pu, pv = slots.slot_input_yuv(slot)
+        py[...], pu[...], pv[...] = y, u, v
+        slots.submit(slot, shifted_q=q)
+        slots.wait_slot(slot)
+        x, _ = ref_yuv_to_tensor(np.concatenate([y.reshape(-1), u.reshape(-1), v.reshape(-1)]), W, H, MW, MH)
+        want = plain.run([x, np.array([q], np.int32)])
+        for k, w in enumerate(want):
+            bits_equal(slots.slot_output(slot, k), w)

@@ -61,3 +61,56 @@ def test_noalloc_clears_its_out_of_range_word():
         noalloc(bad)
     good = np.array([3.5, -2.5, 32752, -32768, 0.25], np.float16)
     assert noalloc(good).tolist() == be.integer_values(good).tolist() == [3, -2, 32752, -32768, 0]
+
+
+@pytest.mark.gpu
+def test_noalloc_matches_the_oracle_restatement():
+    """Independently of the GPU's allocating path: the numpy restatement of the
+    reference's integer_values (core/src/entropy.cpp:201-226), on every
+    finite FP16 value inside [-32768, 32767] and on the same values shuffled."""
+    from oracle import scales_oracle
+    bits = np.arange(1 << 16, dtype=np.uint16).view(np.float16)
+    ok = np.isfinite(bits) & (bits >= -32768) & (bits <= 32767)
+    values = bits[ok]
+    assert np.array_equal(noalloc(values), scales_oracle.integer_values(values))
+    shuffled = np.random.default_rng(3).permutation(values)
+    assert np.array_equal(noalloc(shuffled), scales_oracle.integer_values(shuffled))
+
+
+@pytest.mark.gpu
+def test_noalloc_as_the_first_device_work_of_a_process():
+    """The per-device set-up runs in the first call; here that call is the
+    process's first CUDA work (no backend exists yet), and a backend created
+    afterwards on the same thread agrees with it."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    code = (
+        "import sys; sys.path[:0] = [%r, %r]\n"
+        "import numpy as np, mlvc_b200\n"
+        "from mlvc_b200 import Backend\n"
+        "v = np.rint(np.random.default_rng(5).standard_normal(70001) * 500).astype(np.float16)\n"
+        "out = np.empty(v.shape, np.int32)\n"
+        "assert mlvc_b200.lib().mlvc_b200_integer_values_noalloc(v.ctypes.data, v.size, out.ctypes.data) == 0\n"
+        "be = Backend(0)\n"
+        "assert np.array_equal(out, be.integer_values(v))\n"
+        "print('ok')\n" % (str(root), str(root / "mlvc.cpp_b200")))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
+@pytest.mark.gpu
+def test_noalloc_on_a_second_device():
+    """The set-up is per device: with device 1 current, the call uses device
+    1's copy of the array.  Needs two visible GPUs."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("one GPU visible")
+    torch.cuda.set_device(1)  # makes device 1 current for the CUDA runtime of this thread
+    try:
+        v = np.rint(np.random.default_rng(6).standard_normal(9001) * 700).astype(np.float16)
+        be = Backend(1)
+        assert np.array_equal(noalloc(v), be.integer_values(v))
+    finally:
+        torch.cuda.set_device(0)
