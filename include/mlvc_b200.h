@@ -212,10 +212,19 @@ size_t mlvc_b200_step_count(const mlvc_b200_backend* backend);
 int mlvc_b200_step_info(const mlvc_b200_backend* backend, size_t index, const char** kernel, const char** nodes,
                         double* flops, double* bytes, uint32_t* grid, uint32_t* block, uint32_t* smem);
 int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, size_t flush_bytes, float* ms_per_step);
+/* In-frame kernel spans (no reference counterpart): consecutive kernels of a
+ * replayed frame overlap (programmatic dependent launch), so CUDA events
+ * between them cannot separate them without removing the overlap.  The
+ * schedule is captured once more with the phase trace of every tensor-core
+ * step enabled and replayed `iterations` times like a frame (flush_bytes > 0:
+ * an L2 flush before each); for those steps ms_per_step[i] = the last CTA's
+ * exit minus the first CTA's passing of griddepcontrol.wait (%globaltimer,
+ * written by the kernel), averaged; 0 for other steps. */
+int mlvc_b200_trace_spans(mlvc_b200_backend* backend, int iterations, size_t flush_bytes, float* ms_per_step);
 int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend);
 
 /* Phase trace of one tensor-core conv or fused FFN step: relaunches it once
- * with %globaltimer stamps enabled; writes 48 stamps per CTA (CTA start,
+ * with %globaltimer stamps enabled; writes 64 stamps per CTA (CTA start,
  * setup done, weights issued, weights landed, first activation panel, last
  * MMA commit, first accumulator seen by the epilogue, epilogue done, exit,
  * then fused-FFN, fused-depthwise and fused-block chunk events; 0 = not

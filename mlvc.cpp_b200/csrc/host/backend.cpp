@@ -2449,6 +2449,113 @@ void Backend::capture()
     check(cuGraphInstantiateWithFlags(&graph_exec_, graph_handle_, 0), "cuGraphInstantiate");
 }
 
+// In-graph kernel spans.  Consecutive kernels of a replayed frame overlap
+// (programmatic dependent launch), so events between them would separate
+// them only by removing the overlap.  Instead the schedule is captured once
+// more with the phase trace of every tensor-core step enabled and replayed
+// exactly like a frame; each such step's span is its last CTA's exit stamp
+// minus its first CTA's entry stamp (%globaltimer, written by the kernel),
+// averaged over the replays.  Steps without a trace report 0.
+std::vector<float> Backend::trace_spans(int iterations, size_t flush_bytes)
+{
+    if (offline_)
+        throw std::runtime_error("mlvc-b200: planning-only backend cannot execute");
+    if (!loaded_)
+        throw std::runtime_error("mlvc-b200: load() must be called before trace_spans()");
+    if (iterations < 1)
+        throw std::runtime_error("mlvc-b200: trace_spans needs at least one iteration");
+    ContextGuard guard(ctx_);
+    auto traced = [](const Step& st) {
+        return st.type == Step::kKernel &&
+               (st.kernel == "mlvc_conv1x1_tc" || st.kernel == "mlvc_convkxk_tc" || st.kernel == "mlvc_ffn_tc" ||
+                st.kernel == "mlvc_dwconv_tc" || st.kernel == "mlvc_mbconv_tc");
+    };
+    std::vector<size_t> offs(steps_.size(), 0);
+    size_t total = 0;
+    for (size_t k = 0; k < steps_.size(); ++k)
+        if (traced(steps_[k])) {
+            offs[k] = total;
+            total += static_cast<size_t>(steps_[k].grid) * kTracePoints;
+        }
+    std::vector<float> out(steps_.size(), 0.0f);
+    if (total == 0)
+        return out;
+    DeviceBuffer buf(total * sizeof(uint64_t));
+    if (flush_bytes && flush_dev_.bytes() < flush_bytes)
+        flush_dev_ = DeviceBuffer(flush_bytes);
+    // patch the trace pointers in, capture, restore the normal parameters
+    std::vector<std::vector<uint8_t>> saved(steps_.size());
+    for (size_t k = 0; k < steps_.size(); ++k)
+        if (traced(steps_[k])) {
+            saved[k] = steps_[k].params;
+            unsigned long long* ptr = reinterpret_cast<unsigned long long*>(buf.get() + offs[k] * sizeof(uint64_t));
+            std::memcpy(steps_[k].params.data() + offsetof(ConvTcParams, trace), &ptr, sizeof(ptr));
+        }
+    CUgraph g = nullptr;
+    CUgraphExec ge = nullptr;
+    CUresult rc = cuStreamBeginCapture(stream_, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL);
+    if (rc == CUDA_SUCCESS) {
+        try {
+            launch_steps(stream_);
+        } catch (...) {
+            rc = CUDA_ERROR_UNKNOWN;
+        }
+        const CUresult end = cuStreamEndCapture(stream_, &g);
+        if (rc == CUDA_SUCCESS)
+            rc = end;
+        if (rc == CUDA_SUCCESS)
+            rc = cuGraphInstantiateWithFlags(&ge, g, 0);
+    }
+    for (size_t k = 0; k < steps_.size(); ++k)
+        if (!saved[k].empty())
+            steps_[k].params = std::move(saved[k]);
+    if (rc != CUDA_SUCCESS) {
+        if (g)
+            cuGraphDestroy(g);
+        check(rc, "capture (trace_spans)");
+    }
+    std::vector<uint64_t> host(total);
+    std::vector<double> acc(steps_.size(), 0.0);
+    try {
+        for (int it = 0; it < iterations; ++it) {
+            if (flush_bytes)
+                check(cuMemsetD8Async(flush_dev_.get(), static_cast<unsigned char>(it), flush_bytes, stream_),
+                      "cuMemsetD8Async(flush)");
+            check(cuMemsetD8Async(buf.get(), 0, buf.bytes(), stream_), "cuMemsetD8Async(trace)");
+            check(cuGraphLaunch(ge, stream_), "cuGraphLaunch(trace_spans)");
+            check(cuStreamSynchronize(stream_), "cuStreamSynchronize");
+            check(cuMemcpyDtoH(host.data(), buf.get(), buf.bytes()), "cuMemcpyDtoH(trace)");
+            for (size_t k = 0; k < steps_.size(); ++k) {
+                if (!traced(steps_[k]))
+                    continue;
+                // from the first CTA whose producer passed griddepcontrol.wait
+                // (the previous kernel's outputs visible; the prologue before it
+                // overlaps the previous kernel) to the last CTA's exit
+                uint64_t first = UINT64_MAX, last = 0;
+                for (unsigned c = 0; c < steps_[k].grid; ++c) {
+                    const uint64_t* s = host.data() + offs[k] + static_cast<size_t>(c) * kTracePoints;
+                    const uint64_t start = s[kTrDepReady] ? s[kTrDepReady] : s[kTrEntry];
+                    if (start)
+                        first = std::min<uint64_t>(first, start);
+                    last = std::max<uint64_t>(last, s[kTrExit]);
+                }
+                if (first != UINT64_MAX && last > first)
+                    acc[k] += static_cast<double>(last - first) * 1e-6;  // ns -> ms
+            }
+        }
+    } catch (...) {
+        cuGraphExecDestroy(ge);
+        cuGraphDestroy(g);
+        throw;
+    }
+    cuGraphExecDestroy(ge);
+    cuGraphDestroy(g);
+    check_status();
+    for (size_t k = 0; k < steps_.size(); ++k)
+        out[k] = static_cast<float>(acc[k] / iterations);
+    return out;
+}
+
 int Backend::kernel_launches_per_run() const
 {
     int n = 0;

@@ -121,6 +121,9 @@ public:
     void enqueue();
     void synchronize();
     std::vector<float> time_steps(int iterations, size_t flush_bytes);
+    // Per-step device span inside a replayed frame for the tensor-core steps
+    // (%globaltimer stamps of the kernels; 0 for other steps).
+    std::vector<float> trace_spans(int iterations, size_t flush_bytes);
     const std::vector<StepInfo>& steps() const { return step_info_; }
     int kernel_launches_per_run() const;
     CUstream stream() const { return stream_; }

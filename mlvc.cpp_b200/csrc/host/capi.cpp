@@ -384,6 +384,15 @@ int mlvc_b200_time_steps(mlvc_b200_backend* backend, int iterations, size_t flus
     });
 }
 
+int mlvc_b200_trace_spans(mlvc_b200_backend* backend, int iterations, size_t flush_bytes, float* ms_per_step)
+{
+    return guarded([&] {
+        const auto t = require(backend).trace_spans(iterations, flush_bytes);
+        for (size_t i = 0; i < t.size(); ++i)
+            ms_per_step[i] = t[i];
+    });
+}
+
 int mlvc_b200_kernel_launches(const mlvc_b200_backend* backend)
 {
     return backend && backend->impl ? backend->impl->kernel_launches_per_run() : -1;

@@ -289,6 +289,8 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
             aborted = true;
             break;
         }
+        if (leader && it < 4)
+            trace(p, kTrConvTile + 4 * static_cast<int>(it) + 2);
         if (t == first_tile && leader)
             trace(p, kTrFirstAcc);
         acc ^= 1u;
@@ -432,6 +434,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                 tma_load_2d(b_smem + kp * b_panel_bytes, &p.map_b, &sh->b_full[0], kp * 64, n_tile * p.BN);
             trace(p, kTrWeightsIssued);
             pdl_wait();  // activations are written by the previous kernel
+            trace(p, kTrDepReady);
             int stage = 0;
             uint32_t phase = 0;
             int panel = 0;  // A panels this CTA has handled (wait-expiry test)
@@ -472,10 +475,13 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                 int stage = 0;
                 uint32_t phase = 0, acc = 0, acc_phase = 0;
                 const uint32_t b_addr = smem_u32(b_smem), a_addr = smem_u32(a_smem);
-                for (int t = first; t < total_tiles; t += step) {
+                int tile_no = 0;
+                for (int t = first; t < total_tiles; t += step, ++tile_no) {
                     if (!mbar_wait(&sh->tmem_empty[acc], acc_phase ^ 1u, &sh->abort_flag, kErrWaitMma))
                         break;
                     tc_fence_after();
+                    if (tile_no < 4)
+                        trace(p, kTrConvTile + 4 * tile_no);
                     const uint32_t d = sh->tmem_base + acc * static_cast<uint32_t>(p.BN);
                     bool ok = true;
                     for (int kp = 0; kp < k_panels; ++kp) {
@@ -504,6 +510,8 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                     if (!ok)
                         break;
                     umma_commit(&sh->tmem_full[acc]);
+                    if (tile_no < 4)
+                        trace(p, kTrConvTile + 4 * tile_no + 1);
                     acc ^= 1u;
                     acc_phase ^= (acc == 0) ? 1u : 0u;
                 }
@@ -568,6 +576,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_convkxk_tc(const 
                 b_armed.arm(0, 0);
             }
             pdl_wait();  // activations are written by the previous kernel
+            trace(p, kTrDepReady);
             int as = 0, bs = 0;
             uint32_t aph = 0, bph = 0;
             for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {

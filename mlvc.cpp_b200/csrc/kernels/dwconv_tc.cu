@@ -142,6 +142,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                     issue_w(w_issued);
             trace(p, kTrWeightsIssued);
             pdl_wait();  // x is written by the previous kernel
+            trace(p, kTrDepReady);
             int local = 0;
             bool ok = true;
             for (int t = first; ok && t < tiles && !sh->abort_flag; t += step, ++local) {

@@ -179,6 +179,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_ffn_tc(const __gr
                     issue_w(widx);
             trace(p, kTrWeightsIssued);
             pdl_wait();  // X is written by the previous kernel
+            trace(p, kTrDepReady);
             int local = 0;
             for (int t = first; t < tiles && !sh->abort_flag; t += step, ++local) {
                 if (!mbar_wait(&sh->x_empty[xs], xph ^ 1u, &sh->abort_flag, kErrWaitProducer))

@@ -253,6 +253,7 @@ extern "C" __global__ void __launch_bounds__(kMbThreads, 1) mlvc_mbconv_tc(const
                     issue_w(w_issued);
             trace(p, kTrWeightsIssued);
             pdl_wait();  // x is written by the previous kernel
+            trace(p, kTrDepReady);
             bool ok = true;
             int local = 0;
             for (int t = first; ok && t < tiles && !sh->abort_flag; t += step, ++local) {

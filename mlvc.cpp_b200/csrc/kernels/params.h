@@ -100,6 +100,7 @@ enum TracePoint : int {
     kTrFfnG2First = 18,      // fused FFN: MMA issuer passed the waits of GEMM2 chunk 0
     kTrFfnChunk1Done = 19,   // fused FFN: epilogue released hidden chunk 1
     kTrDwFirstSlice = 20,    // fused depthwise (+ expand): first depthwise slice written as an A panel
+    kTrDepReady = 21,        // producer's griddepcontrol.wait returned: the previous kernel's outputs are visible
     // fused block, first tile, expand chunk c < 4: compute leader saw the expand
     // accumulator (kTrMbChunk + 3c), the chunk complete in shared memory
     // (+1), its A panel written (+2); MMA issuer passed the waits of the expand
@@ -113,7 +114,11 @@ enum TracePoint : int {
     kTrDwSlice = 24,
     kTrDwTile1 = 32,
     kTrDwMma = 36,
-    kTracePoints = 48
+    // 1x1 / k x k conv, the CTA's tiles i < 4: MMA issuer began the tile
+    // (accumulator free: kTrConvTile + 4i), committed it (+1), the epilogue
+    // finished it (stores issued, +2)
+    kTrConvTile = 48,
+    kTracePoints = 64
 };
 
 // Fused feed-forward block (mlvc_ffn_tc):

@@ -94,6 +94,8 @@ EXPORTS = {
                              ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)], ctypes.c_int),
     "mlvc_b200_time_steps": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.POINTER(ctypes.c_float)],
                              ctypes.c_int),
+    "mlvc_b200_trace_spans": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.POINTER(ctypes.c_float)],
+                              ctypes.c_int),
     "mlvc_b200_kernel_launches": ([ctypes.c_void_p], ctypes.c_int),
     "mlvc_b200_device_bytes": ([ctypes.c_void_p], ctypes.c_size_t),
     "mlvc_b200_trace_step": ([ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t,
@@ -356,14 +358,23 @@ class Backend:
         _check(lib().mlvc_b200_time_steps(self._h, iterations, flush_bytes, buf))
         return list(buf[:n])
 
+    def trace_spans(self, iterations=10, flush_bytes=0):
+        """Per-step device span (ms) of the tensor-core steps inside a replayed
+        frame, from the kernels' own %globaltimer stamps (0 for other steps);
+        see include/mlvc_b200.h."""
+        n = lib().mlvc_b200_step_count(self._h)
+        buf = (ctypes.c_float * max(1, n))()
+        _check(lib().mlvc_b200_trace_spans(self._h, iterations, flush_bytes, buf))
+        return list(buf[:n])
+
     def trace_step(self, index):
-        """[CTAs, 48] %globaltimer stamps of one tensor-core conv or fused FFN
+        """[CTAs, 64] %globaltimer stamps of one tensor-core conv or fused FFN
         step (see include/mlvc_b200.h); requires a previous run()."""
         n = ctypes.c_size_t()
         _check(lib().mlvc_b200_trace_step(self._h, index, None, 0, ctypes.byref(n)))
         buf = (ctypes.c_uint64 * n.value)()
         _check(lib().mlvc_b200_trace_step(self._h, index, buf, n.value, ctypes.byref(n)))
-        return np.frombuffer(buf, np.uint64).reshape(-1, 48).copy()
+        return np.frombuffer(buf, np.uint64).reshape(-1, 64).copy()
 
     def test_wait_expiry(self, step_index, limit_ns):
         """Failure-detection test: relaunch a mlvc_conv1x1_tc step with its

@@ -70,8 +70,10 @@ def test_noalloc_matches_the_oracle_restatement():
     finite FP16 value inside [-32768, 32767] and on the same values shuffled."""
     from oracle import scales_oracle
     bits = np.arange(1 << 16, dtype=np.uint16).view(np.float16)
-    ok = np.isfinite(bits) & (bits >= -32768) & (bits <= 32767)
+    f = bits.astype(np.float32)  # compared in FP32: 32767 as an FP16 scalar would round to 32768
+    ok = np.isfinite(f) & (f >= -32768.0) & (f <= 32767.0)
     values = bits[ok]
+    assert values.size == 61441 and 32752.0 in values and -32768.0 in values and 32768.0 not in values
     assert np.array_equal(noalloc(values), scales_oracle.integer_values(values))
     shuffled = np.random.default_rng(3).permutation(values)
     assert np.array_equal(noalloc(shuffled), scales_oracle.integer_values(shuffled))
