@@ -124,10 +124,19 @@ def test_mlvc_encoder_standin(width, height, tmp_path):
     y1 quantisation tails and the encoder-form feature update as fused
     kernels): every materialised step against the oracle on the GPU's own
     step inputs -- integer-valued z_raw / y_raw_0 / y_raw_1 exactly, since
-    Round outputs pass the per-op check only when equal -- then all four
-    outputs against the reference CPU backend within twice the CPU-vs-CPU
-    spread (symbols differ only where an upstream FP16 rounding difference
-    crosses a rounding boundary).  A P-frame: the reference feature is a
+    Round outputs pass the per-op check only when equal.  That is the exact
+    criterion.  The whole graph is then compared with the reference CPU
+    backend as a sanity check with explicit bounds: a symbol differs only
+    where an upstream FP16 rounding difference crosses a rounding boundary,
+    and one z_raw symbol that flips changes the prior of every y symbol below
+    it, so whole-graph differences come in cascades.  Measured between two
+    CPU implementations (the reference backend and the oracle's GEMM form)
+    on these graphs: up to 2.4 % of the y symbols and a feature rel-L2 up to
+    4.7e-2; the GPU against the reference lies in the same range (up to 3.4 %
+    and 7.5e-2 at 640x368 with seed 4, where two z symbols flip).  Bounds: at
+    most 0.3 % of z_raw symbols differ (2 of 1920 measured), by 1; at most 6 %
+    of y symbols; the
+    feature within 0.15 rel-L2.  A P-frame: the reference feature is a
     previous feature (not zero)."""
     from mlvc_b200.graph import build_mlvc_encoder_standin
     gb, inputs = build_mlvc_encoder_standin(seed=4, width=width, height=height)
@@ -141,7 +150,17 @@ def test_mlvc_encoder_standin(width, height, tmp_path):
     for o in outs[1:]:
         assert np.array_equal(o, np.rint(o)), "latents must be integer-valued"
     assert per_op_parity(be, graph, weights, inputs, conv_impl="gemm") >= 40
-    _stack_check(outs, graph, weights, inputs, tmp_path)
+    part = tmp_path / "aot" / "m"
+    part.mkdir(parents=True)
+    (part / "graph.pb").write_bytes(graph)
+    (part / "weights.bin").write_bytes(weights)
+    refs = RefCpuBackend(tmp_path, "m", 0).run(inputs)
+    z, zr = outs[1].astype(np.float64), refs[1].astype(np.float64)
+    assert (z != zr).mean() <= 3e-3 and np.abs(z - zr).max() <= 1, (int((z != zr).sum()), z.size)
+    for k in (2, 3):
+        y, yr = outs[k].astype(np.float64), refs[k].astype(np.float64)
+        assert (y != yr).mean() <= 0.06, (k, int((y != yr).sum()), y.size)
+    assert _rel(outs[0], refs[0]) <= 0.15
 
 
 def test_mlvc_encoder_slot_path_with_yuv_input(tmp_path):
