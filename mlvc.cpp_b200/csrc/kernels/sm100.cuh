@@ -104,6 +104,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: while the phase is incomplete the thread
+// may be suspended (woken when the phase completes, at the latest after
+// hint_ns) instead of returning at once, so waiting warps stop taking issue
+// slots from the single-thread producer and MMA roles on their sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Suspend-time hint of the bounded wait's loop: the abort flag and the time
+// limit are still checked at least this often.
+constexpr uint32_t kWaitSuspendNs = 100000;  // 100 us
+
 // Bounded wait on `bar` completing the phase with the given parity.  Returns
 // false (after recording `code`) when the CTA is aborting or the wait ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -114,7 +135,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     const unsigned long long start = globaltimer_ns();
     const unsigned long long limit = mlvc_b200_wait_limit_ns;
     while (true) {
-        if (mbar_try_wait(bar, parity))
+        if (mbar_try_wait_suspend(bar, parity, kWaitSuspendNs))
             return true;
         if (*abort_flag)
             return false;
