@@ -239,11 +239,13 @@ size_t mlvc_b200_device_bytes(const mlvc_b200_backend* backend);
  * be a mlvc_conv1x1_tc step of the loaded schedule, once with every bounded
  * device wait of this backend limited to `limit_ns` (at most 2 s) and CTA 0's
  * TMA producer withholding its first activation panel: no copy is issued or
- * armed for it, so the tensor-core issuer's wait for it runs out, the CTA
- * sets its abort flag, every role winds down (producer drains the copies it
- * armed, epilogue drains its residual load) and the kernel returns.  Then
- * waits, restores the 2 s limit and stores the module status word in *status
- * (0x2 = the issuer's wait ran out), clearing it.  The step's output is left
+ * armed for it, so the tensor-core issuer stalls on it (and behind it the
+ * epilogue and the producer); the first of those bounded waits to run out
+ * sets the CTA's abort flag, every role winds down (producer drains the
+ * copies it armed, epilogue drains its residual load) and the kernel
+ * returns.  Then waits, restores the 2 s limit and stores the module status
+ * word in *status (wait bits: 0x1 producer, 0x2 tensor-core issuer, 0x4
+ * epilogue), clearing it.  The step's output is left
  * incomplete; the next run recomputes it.  Uses the device state of the last
  * run. */
 int mlvc_b200_test_wait_expiry(mlvc_b200_backend* backend, size_t step_index, uint64_t limit_ns, uint32_t* status);

@@ -143,7 +143,7 @@ public:
     // `limit_ns` and CTA 0's producer withholding its first activation panel
     // (nothing is loaded or armed for it), waits for the launch, restores the
     // 2 s limit and returns the module status word it left (then cleared):
-    // the MMA issuer's wait bit when the abort path ran.  Uses the device
+    // the wait bit of the role whose wait ran out first.  Uses the device
     // state of the last run; the step's output is left incomplete.
     uint32_t test_wait_expiry(size_t index, uint64_t limit_ns);
     // Before load(): give every materialised tensor its own arena slot so
