@@ -230,6 +230,23 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+def pin_host_cores(local_rank, local_world):
+    """Gives each rank of a multi-GPU run its own contiguous share of the host
+    cores this process may use, so the ranks' host threads (slot copies,
+    submits, waits) neither migrate nor contend for the same cores.  Returns
+    the cores kept, or None when there are fewer cores than ranks."""
+    try:
+        cores = sorted(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return None
+    share = len(cores) // max(1, local_world)
+    if share < 1:
+        return None
+    mine = cores[local_rank * share:(local_rank + 1) * share]
+    os.sched_setaffinity(0, mine)
+    return mine
+
+
 def replica_throughput(local_ms, steps, world, device="cpu"):
     """Whole-job frames/s of `world` independent replicas that each ran `steps`
     frames in `local_ms` device milliseconds: the slowest rank bounds the job
@@ -734,10 +751,18 @@ def run_streams_arm(args, rank, world, local_rank):
     pipeline(0, args.steps)
     e_en.record(s0)
     torch.cuda.synchronize()
-    t = torch.tensor([e_st.elapsed_time(e_en)], dtype=torch.float64, device=dev)
+    e2e_local = e_st.elapsed_time(e_en)
+    t = torch.tensor([e2e_local], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = STREAMS * args.steps / (float(t.item()) / 1e3)
+    # per-rank device times (value path, e2e path) for the line's diagnostics
+    per_rank = torch.tensor([[ms, e2e_local]], dtype=torch.float64, device=dev)
+    if world > 1:
+        gathered = [torch.zeros_like(per_rank) for _ in range(world)]
+        dist.all_gather(gathered, per_rank)
+        per_rank = torch.cat(gathered)
+    per_rank_ms = per_rank.cpu().tolist()
     h2d = sum(a.nbytes for a in inputs[:3]) + 4
     d2h = width * height * 3 // 2
     # the slot path still decodes after the timed run (first frame of a fresh GOP, stream 0)
@@ -769,7 +794,9 @@ def run_streams_arm(args, rank, world, local_rank):
                     "d2h_bytes_per_step": d2h * STREAMS,
                     "path": ("mlvc_b200 slot API per stream, 2 slots: latents (z_raw, y_raw_0, y_raw_1) from pinned "
                              "host memory, submit(slot, shifted_q), schedule, x_hat -> 8-bit YUV420 1920x1080 on the "
-                             "GPU, pinned D2H; GOP reset every 64 frames; timed on the device over the whole run")},
+                             "GPU, pinned D2H; GOP reset every 64 frames; timed on the device over the whole run"),
+                    "per_rank_ms": [r[1] for r in per_rank_ms]},
+            "per_rank_ms": [r[0] for r in per_rank_ms],
             "gpu_launches": sum(b.kernel_launches for b in backends) * args.steps,
             "roofline": roof,
             "kernels": kernels,
@@ -945,6 +972,7 @@ def main():
     if world > 1:
         import datetime
 
+        pin_host_cores(local_rank, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)

@@ -52,3 +52,20 @@ def test_reference_arm_other_ranks_exit_quietly():
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
                           "--warmup", "3"], capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
     assert out.returncode == 0 and not [l for l in out.stdout.splitlines() if l.startswith("{")]
+
+
+def test_ranks_get_disjoint_host_cores():
+    """Under torchrun each rank keeps its own share of the host cores (no
+    migration or contention between the ranks' host threads)."""
+    import ast
+    import os
+    cores = sorted(os.sched_getaffinity(0))
+    if len(cores) < 2:
+        pytest.skip("one host core")
+    got = []
+    for rank in (0, 1):
+        code = f"import sys; sys.path.insert(0, {str(ROOT)!r}); import bench; print(bench.pin_host_cores({rank}, 2))"
+        out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120, cwd=ROOT)
+        assert out.returncode == 0, out.stderr[-2000:]
+        got.append(set(ast.literal_eval(out.stdout.strip().splitlines()[-1])))
+    assert got[0] and got[1] and not (got[0] & got[1]) and (got[0] | got[1]) <= set(cores)
