@@ -746,16 +746,20 @@ def run_streams_arm(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    # whole GOPs per stream (at least K frames): the window the codec decodes
+    # between two I-frames, long enough that host jitter of one rank does not
+    # set the max over ranks
+    e2e_frames = GOP * max(1, -(-args.steps // GOP))
     e_st, e_en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_st.record(s0)
-    pipeline(0, args.steps)
+    pipeline(0, e2e_frames)
     e_en.record(s0)
     torch.cuda.synchronize()
     e2e_local = e_st.elapsed_time(e_en)
     t = torch.tensor([e2e_local], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_value = STREAMS * args.steps / (float(t.item()) / 1e3)
+    e2e_value = STREAMS * e2e_frames / (float(t.item()) / 1e3)
     # per-rank device times (value path, e2e path) for the line's diagnostics
     per_rank = torch.tensor([[ms, e2e_local]], dtype=torch.float64, device=dev)
     if world > 1:
@@ -763,6 +767,10 @@ def run_streams_arm(args, rank, world, local_rank):
         dist.all_gather(gathered, per_rank)
         per_rank = torch.cat(gathered)
     per_rank_ms = per_rank.cpu().tolist()
+    try:
+        host_cores = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        host_cores = os.cpu_count()
     h2d = sum(a.nbytes for a in inputs[:3]) + 4
     d2h = width * height * 3 // 2
     # the slot path still decodes after the timed run (first frame of a fresh GOP, stream 0)
@@ -794,8 +802,11 @@ def run_streams_arm(args, rank, world, local_rank):
                     "d2h_bytes_per_step": d2h * STREAMS,
                     "path": ("mlvc_b200 slot API per stream, 2 slots: latents (z_raw, y_raw_0, y_raw_1) from pinned "
                              "host memory, submit(slot, shifted_q), schedule, x_hat -> 8-bit YUV420 1920x1080 on the "
-                             "GPU, pinned D2H; GOP reset every 64 frames; timed on the device over the whole run"),
-                    "per_rank_ms": [r[1] for r in per_rank_ms]},
+                             "GPU, pinned D2H; GOP reset every 64 frames; timed on the device over whole 64-frame GOPs "
+                             "(at least K frames) per stream"),
+                    "frames_per_stream": e2e_frames,
+                    "per_rank_ms": [r[1] for r in per_rank_ms],
+                    "host_cores_per_rank": host_cores},
             "per_rank_ms": [r[0] for r in per_rank_ms],
             "gpu_launches": sum(b.kernel_launches for b in backends) * args.steps,
             "roofline": roof,

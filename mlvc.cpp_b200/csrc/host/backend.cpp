@@ -1106,10 +1106,18 @@ void Backend::plan()
                 const int k_panels = (K + 63) / 64;
                 const int m_tiles = (IH * IW + 127) / 128;
                 // Candidate N tiles divide NN and keep the CTA's weight slice resident.
-                // Prefer a footprint that lets two CTAs share an SM (<= 113 KB of smem,
-                // 2 x BN TMEM columns <= 512): one CTA's epilogue then overlaps the
-                // other's loads and MMAs.  Among those, the largest BN that still
-                // gives one tile per SM; otherwise fall back to one CTA per SM.
+                // Every N tile re-reads the activations from L2, and L2 -> SM traffic
+                // paces these GEMMs once four A panels are in flight (a deeper ring
+                // measured no faster), so the widest N tile that keeps four A stages
+                // at one CTA per SM comes first (at 136 x 240: expand 256 -> 512
+                // 17.3 -> 14.9 us, 256 -> 192 8.5 -> 6.7 us against 64-column tiles
+                // at two CTAs per SM), as long as its tiles still occupy 80 % of the
+                // SMs (on smaller planes the fill matters more: at 640 x 368 the
+                // wide tiles cost 3-6 % of the frame).  Otherwise
+                // (MLVC_B200_CONV1X1_POLICY=pair, or no such tile) a footprint that
+                // lets two CTAs share an SM (<= 113 KB of smem, 2 x BN TMEM columns
+                // <= 512), the largest BN that still gives one tile per SM, else
+                // one CTA per SM.
                 constexpr int kTwoCtaSmem = 233472 / 2 - 1024;
                 auto stage_for = [&](int bn) { return (reglu ? bn / 2 : bn) / 64 * kTcStagePanelBytes; };
                 std::vector<int> cands;
@@ -1121,6 +1129,10 @@ void Backend::plan()
                     return (cap - header - 1024 - stage_for(bn) - k_panels * bn * 128) / 16384;
                 };
                 int best = 0, ctas_per_sm = 1;
+                if (const char* e_pol = std::getenv("MLVC_B200_CONV1X1_POLICY"); !(e_pol && std::string(e_pol) == "pair"))
+                    for (int bn : cands)  // largest N tile that keeps four A stages at one CTA per SM
+                        if (!best && stages_for(bn, smem_cap + 1024) >= 4 && 5 * m_tiles * (NN / bn) >= 4 * sm_count_)
+                            best = bn;
                 for (int bn : cands)
                     if (!best && bn <= 128 && stages_for(bn, kTwoCtaSmem) >= 2 && m_tiles * (NN / bn) >= sm_count_) {
                         best = bn;
@@ -1183,6 +1195,12 @@ void Backend::plan()
                             stage_bufs = 2;
                             a_stages = std::min(8, with2);
                         }
+                    }
+                    {
+                        // tuning override (sweeps): MLVC_B200_CONV1X1_STAGES caps the A ring depth
+                        const char* e_st = std::getenv("MLVC_B200_CONV1X1_STAGES");
+                        if (e_st && std::atoi(e_st) >= 2)
+                            a_stages = std::min(a_stages, std::atoi(e_st));
                     }
                     if (a_stages < 2)  // the A ring needs two slots (load one while the MMA reads the other)
                         throw std::runtime_error("mlvc-b200: conv1x1 plan leaves fewer than two A stages");
@@ -1467,7 +1485,7 @@ void Backend::plan()
                     f.kernel = "mlvc_dwconv_tc";
                     f.info.kernel = f.kernel;
                     f.smem = static_cast<unsigned>(fixed + h_stages * halo_stride);
-                    f.block = 320;
+                    f.block = kDwThreads;
                     f.grid = static_cast<unsigned>(std::min(m_tiles, sm_count_));
                     f.build = [=, this](Step& st) {
                         DwConvTcParams dwp_{};

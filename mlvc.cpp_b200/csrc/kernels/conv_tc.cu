@@ -124,17 +124,17 @@ struct StageSync {
     uint64_t* full;
 };
 
-// One thread's row of the tile: for the 32-column chunks c0 = 32 group + 64 k
-// it reads 32 accumulators, applies bias and the fused operator with the
-// graph's rounding and writes the row into the staging panels.  `res` is the
-// residual tile (same layout), read before the row is overwritten.
+// One thread's row of the tile: for the 32-column chunks c0 = 32 (group +
+// groups k) it reads 32 accumulators, applies bias and the fused operator with
+// the graph's rounding and writes the row into the staging panels.  `res` is
+// the residual tile (same layout), read before the row is overwritten.
 __device__ __forceinline__ void epilogue_rows(const ConvTcParams& p, const float* bias, uint32_t lane_addr, int group,
-                                              int row, uint8_t* stage, const uint8_t* res)
+                                              int row, uint8_t* stage, const uint8_t* res, int groups)
 {
     if (p.epilogue == kEpiReglu) {
         const int half = p.BN / 2;
         const __half2 lo2 = __float2half2_rn(p.clip_lo), hi2 = __float2half2_rn(p.clip_hi);
-        for (int c0 = group * 32; c0 < half; c0 += 64) {
+        for (int c0 = group * 32; c0 < half; c0 += 32 * groups) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 uint32_t gr[16], lr[16];
@@ -163,7 +163,7 @@ __device__ __forceinline__ void epilogue_rows(const ConvTcParams& p, const float
         }
         return;
     }
-    for (int c0 = group * 32; c0 < p.BN; c0 += 64) {
+    for (int c0 = group * 32; c0 < p.BN; c0 += 32 * groups) {
         uint32_t a[32];
         tmem_ld32_nowait(lane_addr + c0, a);
         tmem_wait_ld();
@@ -226,12 +226,14 @@ __device__ __forceinline__ void stage_prepare(const ConvTcParams& p, uint8_t* st
 
 // All epilogue threads, one tile: wait for the accumulator and the staging
 // buffer, convert, release the accumulator, and let the leader store the tile.
-// `it` counts the CTA's tiles (barrier parities).  Returns false on abort.
+// `it` counts the CTA's tiles (barrier parities); `groups` warps share each
+// TMEM lane quadrant (column chunks split between them).  Returns false on abort.
 __device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float* bias, uint32_t tmem_acc,
                                               uint64_t* acc_full, uint32_t acc_parity, uint64_t* acc_empty,
                                               const StageSync& ss, uint32_t it, uint8_t* stage, const uint8_t* res,
                                               int panels, int col0, const TileCoord& tc, bool kxk, int quadrant,
-                                              int group, int lane, bool leader, volatile int* abort_flag)
+                                              int group, int lane, bool leader, volatile int* abort_flag,
+                                              int groups = 2)
 {
     if (!mbar_wait(acc_full, acc_parity, abort_flag, kErrWaitEpilogue))
         return false;
@@ -239,7 +241,7 @@ __device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float
     if (!mbar_wait(ss.ready, it & 1u, abort_flag, kErrWaitEpilogue))
         return false;
     epilogue_rows(p, bias, tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16), group, quadrant * 32 + lane, stage,
-                  res ? res : stage);
+                  res ? res : stage, groups);
     tc_fence_before();
     mbar_arrive(acc_empty);
     fence_proxy_async_smem();  // staging rows become visible to the TMA store (async proxy)

@@ -28,10 +28,12 @@
 // stand-alone depthwise kernel's, so the result is bit-identical to the
 // unfused pair.
 //
-// Roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2..9 = depthwise compute, then the output epilogue.  All waits
-// are bounded (%globaltimer) and abort the CTA with an error bit in
-// mlvc_b200_status.
+// Roles (448 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer, warps 2..9 = depthwise compute, warps 10..13 = output epilogue (one
+// per TMEM lane quadrant).  The accumulator is double-buffered, so tile t's
+// epilogue (TMEM -> bias, fused operator -> staging -> TMA store) overlaps
+// tile t + 1's depthwise slices.  All waits are bounded (%globaltimer) and
+// abort the CTA with an error bit in mlvc_b200_status.
 namespace mlvc_b200 {
 
 struct DwShared {
@@ -51,7 +53,7 @@ static_assert(offsetof(DwShared, bias) % 16 == 0, "vector bias reads");
 
 constexpr uint32_t kDwPanelBytes = kBM * 128;  // one 128-pixel x 64-channel FP16 panel
 
-extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const __grid_constant__ DwConvTcParams dp)
+extern "C" __global__ void __launch_bounds__(kDwThreads, 1) mlvc_dwconv_tc(const __grid_constant__ DwConvTcParams dp)
 {
     const ConvTcParams& p = dp.c;
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
@@ -78,16 +80,16 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
             p.trace[blockIdx.x * kTracePoints + kTrEntry] = globaltimer_ns();
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sh->h_full[s], 1);
-            mbar_init(&sh->h_empty[s], kEpilogueThreads);
-            mbar_init(&sh->a_full[s], kEpilogueThreads);
+            mbar_init(&sh->h_empty[s], kDwComputeThreads);
+            mbar_init(&sh->a_full[s], kDwComputeThreads);
             mbar_init(&sh->a_empty[s], 1);
             mbar_init(&sh->w_full[s], 1);
             mbar_init(&sh->w_empty[s], 1);
             mbar_init(&sh->acc_full[s], 1);
-            mbar_init(&sh->acc_empty[s], kEpilogueThreads);
+            mbar_init(&sh->acc_empty[s], kDwEpilogueThreads);
         }
         mbar_init(&sh->stg_ready, 1);
-        mbar_init(&sh->stg_full, kEpilogueThreads);
+        mbar_init(&sh->stg_full, kDwEpilogueThreads);
         mbar_init(&sh->dw_full, 1);
         mbar_init(&sh->drain, 1);
         sh->abort_flag = 0;
@@ -175,11 +177,11 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------ TMEM owner + MMA issuer
-        // accumulators (two buffers of BN columns), published to the other
-        // warps through named barrier 1 (256 depthwise/epilogue threads + this warp)
+        // accumulators (two buffers of BN columns), published to the epilogue
+        // warps through named barrier 1 (128 epilogue threads + this warp)
         tmem_alloc(&sh->tmem_base, tmem_cols_for(p.BN));
         tc_fence_before();
-        asm volatile("bar.arrive 1, %0;" ::"n"(kEpilogueThreads + 32) : "memory");
+        asm volatile("bar.arrive 1, %0;" ::"n"(kDwEpilogueThreads + 32) : "memory");
         __syncwarp();
         tc_fence_after();
         if (elect_one()) {
@@ -233,34 +235,20 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
             trace(p, kTrLastCommit);
         }
         __syncwarp();
-    } else {
-        // ------------------------------------------------ depthwise + epilogue warps
-        const int quadrant = warp & 3;
-        const int group = (warp - 2) / 4;
+    } else if (warp < 2 + kDwComputeThreads / 32) {
+        // ------------------------------------------------ depthwise warps
         const int et_id = (warp - 2) * 32 + lane;
         const bool leader = et_id == 0;
         const int cq = et_id & 7;     // 8-channel chunk of the slice
         const int pg = et_id >> 3;    // pixels 4 pg .. 4 pg + 3 of the tile
-        for (int i = et_id; i < p.BN; i += kEpilogueThreads)
-            sh->bias[i] = (p.bias && i < p.N) ? __half2float(p.bias[i]) : 0.0f;
-        asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads + 32) : "memory");  // bias + TMEM address
-        tc_fence_after();
-        pdl_wait();  // output writes follow the previous kernel
-        const StageSync ss{&sh->stg_ready, &sh->stg_full};
-        const int panels = p.BN / 64;
         const int W = dp.width;
         bool ok = mbar_wait(&sh->dw_full, 0, &sh->abort_flag, kErrWaitEpilogue);
         int hs = 0, as = 0;
-        uint32_t hph = 0, aph = 0, acc = 0, acc_phase = 0, it = 0;
-        bool res_issued = false;  // the leader issued tile `it`'s residual load
+        uint32_t hph = 0, aph = 0, it = 0;
         for (int t = first; ok && t < tiles; t += step, ++it) {
-            res_issued = false;
-            TileCoord tc;
-            tc.pixel0 = 0;
-            tc.ox0 = (t % dp.tiles_x) * kDwTileW;
-            tc.oy = (t / dp.tiles_x) * kDwTileH;
+            const int ox0 = (t % dp.tiles_x) * kDwTileW;
             const int ty = pg >> 2, tx = (pg & 3) * 4;  // the thread's 4 pixels: tile row ty, columns tx .. tx + 3
-            const int x0 = tc.ox0 + tx;
+            const int x0 = ox0 + tx;
             const int h0 = (ty + 1) * (kDwTileW + 2) + tx + 1;  // halo pixel of the first one
             for (int kp = 0; kp < kpan; ++kp) {
                 if (!mbar_wait(&sh->h_full[hs], hph, &sh->abort_flag, kErrWaitEpilogue) ||
@@ -340,14 +328,6 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                 }
                 fence_proxy_async_smem();  // the tensor core reads the panel through the async proxy
                 mbar_arrive(&sh->a_full[as]);
-                // Residual tile into the staging buffer while the remaining slices
-                // run.  Issued after the first slice, not before it: the leader's
-                // wait for the previous tile's output store to read the buffer
-                // would otherwise hold up the first slice's A panel.
-                if (leader && kp == 0) {
-                    stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
-                    res_issued = p.epilogue == kEpiResidual;
-                }
                 if (leader && it == 0 && kp == 0)
                     trace(p, kTrDwFirstSlice);
                 if (leader && it == 0 && kp < 8)
@@ -363,14 +343,42 @@ extern "C" __global__ void __launch_bounds__(kThreads, 1) mlvc_dwconv_tc(const _
                     aph ^= 1u;
                 }
             }
-            if (!ok)
-                break;
+        }
+    } else {
+        // ------------------------------------------------ output epilogue warps
+        // (one per TMEM lane quadrant): tile t's accumulator is stored while
+        // the depthwise warps compute tile t + 1
+        const int quadrant = warp & 3;
+        const int e_id = (warp - 2 - kDwComputeThreads / 32) * 32 + lane;
+        const bool leader = e_id == 0;
+        for (int i = e_id; i < p.BN; i += kDwEpilogueThreads)
+            sh->bias[i] = (p.bias && i < p.N) ? __half2float(p.bias[i]) : 0.0f;
+        asm volatile("bar.sync 1, %0;" ::"n"(kDwEpilogueThreads + 32) : "memory");  // bias + TMEM address
+        tc_fence_after();
+        pdl_wait();  // residual reads and output writes follow the previous kernel
+        const StageSync ss{&sh->stg_ready, &sh->stg_full};
+        const int panels = p.BN / 64;
+        uint32_t acc = 0, acc_phase = 0, it = 0;
+        bool ok = true;
+        bool res_issued = false;  // the leader issued tile `it`'s residual load
+        for (int t = first; t < tiles; t += step, ++it) {
+            TileCoord tc;
+            tc.pixel0 = 0;
+            tc.ox0 = (t % dp.tiles_x) * kDwTileW;
+            tc.oy = (t / dp.tiles_x) * kDwTileH;
+            // the previous tile's store must have read the staging buffer; the
+            // residual tile then lands in it while the depthwise runs
+            if (leader) {
+                stage_prepare(p, stage_smem, panels, 0, tc, true, p.epilogue == kEpiResidual, ss.ready);
+                res_issued = p.epilogue == kEpiResidual;
+            }
             if (!epilogue_tile(p, sh->bias, sh->tmem_base + acc * p.BN, &sh->acc_full[acc], acc_phase, &sh->acc_empty[acc],
-                               ss, it, stage_smem, nullptr, panels, 0, tc, true, quadrant, group, lane, leader,
-                               &sh->abort_flag)) {
+                               ss, it, stage_smem, nullptr, panels, 0, tc, true, quadrant, 0, lane, leader,
+                               &sh->abort_flag, 1)) {
                 ok = false;
                 break;
             }
+            res_issued = false;
             if (leader && it == 0)
                 trace(p, kTrFirstAcc);
             acc ^= 1u;

@@ -154,6 +154,12 @@ constexpr int kDwHeaderBytes = 2048;
 constexpr int kDwTileW = 16, kDwTileH = 8;                        // output tile (pixels)
 constexpr int kDwHaloPx = (kDwTileW + 2) * (kDwTileH + 2);        // 180 halo pixels per slice
 constexpr int kDwHaloBytes = (kDwHaloPx * 128 + 1023) / 1024 * 1024;  // one 64-channel halo slice in smem
+// Fused depthwise CTA: TMA warp, MMA warp, 8 depthwise warps, then 4 output
+// epilogue warps (one per TMEM lane quadrant) that drain tile t's accumulator
+// while the depthwise warps compute tile t + 1.
+constexpr int kDwComputeThreads = 256;
+constexpr int kDwEpilogueThreads = 128;
+constexpr int kDwThreads = 64 + kDwComputeThreads + kDwEpilogueThreads;
 
 // Channels per depthwise-taps TMA box of mlvc_dwconv_tc: the largest multiple
 // of 64 that is at most 256 (a box dimension limit) and divides C, so the
