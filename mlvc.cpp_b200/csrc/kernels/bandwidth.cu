@@ -83,11 +83,59 @@ extern "C" __global__ void mlvc_binary_same_f16(const __grid_constant__ Elementw
 }
 
 // General broadcast: output is dense in (n, h, w, c) order, operands are
-// addressed through per-dimension strides (0 on broadcast dimensions).
+// addressed through per-dimension strides (0 on broadcast dimensions).  When
+// the channel extent and every stride are multiples of 8, `a` is contiguous in
+// c and `b` is contiguous in c or constant along it (e.g. a per-channel scale
+// row, or a per-pixel value), and all three pointers are 16-byte aligned, each
+// thread handles 8 channels with 16-byte accesses and 32-bit index arithmetic
+// (the same per-element FP32 operation and rounding as the scalar loop).
 extern "C" __global__ void mlvc_binary_bcast_f16(const __grid_constant__ ElementwiseParams p)
 {
     pdl_launch_dependents();
     pdl_wait();
+    const bool b_vec = p.sb[3] == 1, b_const_c = p.sb[3] == 0;
+    const bool vec = p.dims[3] % 8 == 0 && p.sa[3] == 1 && (b_vec || b_const_c) && p.count < (1ll << 31) &&
+                     p.sa[0] % 8 == 0 && p.sa[1] % 8 == 0 && p.sa[2] % 8 == 0 &&
+                     (b_const_c || (p.sb[0] % 8 == 0 && p.sb[1] % 8 == 0 && p.sb[2] % 8 == 0)) &&
+                     ((reinterpret_cast<uintptr_t>(p.a) | reinterpret_cast<uintptr_t>(p.b) |
+                       reinterpret_cast<uintptr_t>(p.out)) & 15u) == 0;
+    if (vec) {
+        const unsigned cv = static_cast<unsigned>(p.dims[3]) / 8, W = p.dims[2], H = p.dims[1];
+        const unsigned total = static_cast<unsigned>(p.count / 8);
+        const unsigned stride = gridDim.x * blockDim.x;
+        for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+            unsigned r = i;
+            const unsigned c = (r % cv) * 8;
+            r /= cv;
+            const unsigned w = r % W;
+            r /= W;
+            const unsigned h = r % H, n = r / H;
+            uint4 va = *reinterpret_cast<const uint4*>(p.a + n * p.sa[0] + h * p.sa[1] + w * p.sa[2] + c);
+            const mlvc_half* bp = p.b + n * p.sb[0] + h * p.sb[1] + w * p.sb[2];
+            uint32_t* wa = reinterpret_cast<uint32_t*>(&va);
+            if (b_vec) {
+                const uint4 vb = *reinterpret_cast<const uint4*>(bp + c);
+                const uint32_t* wb = reinterpret_cast<const uint32_t*>(&vb);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float a0, a1, b0, b1;
+                    unpack_h2(wa[k], a0, a1);
+                    unpack_h2(wb[k], b0, b1);
+                    wa[k] = pack_h2(binary_op(a0, b0, p.op), binary_op(a1, b1, p.op));
+                }
+            } else {
+                const float b0 = __half2float(*bp);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float a0, a1;
+                    unpack_h2(wa[k], a0, a1);
+                    wa[k] = pack_h2(binary_op(a0, b0, p.op), binary_op(a1, b0, p.op));
+                }
+            }
+            *reinterpret_cast<uint4*>(p.out + static_cast<size_t>(i) * 8) = va;
+        }
+        return;
+    }
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
         long long r = i;
@@ -123,25 +171,35 @@ extern "C" __global__ void mlvc_strided_copy_f16(const __grid_constant__ CopyPar
 }
 
 // Same as above, moving 8 consecutive elements (16 bytes) per step; used when
-// the innermost extent is a multiple of 8 and contiguous on both sides.
+// the innermost extent is a multiple of 8 and contiguous on both sides.  The
+// index decomposition runs in 32 bits when the element count allows it (a
+// 64-bit division costs several times a 32-bit one).
+template <typename I>
+__device__ __forceinline__ void strided_copy_v8(const CopyParams& p)
+{
+    const I stride = static_cast<I>(gridDim.x) * blockDim.x;
+    const I inner = static_cast<I>(p.dims[3] / 8), d2 = p.dims[2], d1 = p.dims[1];
+    const I total = static_cast<I>(p.count / 8);
+    for (I i = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        I r = i;
+        const I i3 = (r % inner) * 8;
+        r /= inner;
+        const I i2 = r % d2;
+        r /= d2;
+        const I i1 = r % d1, i0 = r / d1;
+        *reinterpret_cast<uint4*>(p.dst + i0 * p.ds[0] + i1 * p.ds[1] + i2 * p.ds[2] + i3) =
+            *reinterpret_cast<const uint4*>(p.src + i0 * p.ss[0] + i1 * p.ss[1] + i2 * p.ss[2] + i3);
+    }
+}
+
 extern "C" __global__ void mlvc_strided_copy_v8_f16(const __grid_constant__ CopyParams p)
 {
     pdl_launch_dependents();
     pdl_wait();
-    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    const long long inner = p.dims[3] / 8;
-    const long long total = p.count / 8;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
-        long long r = i;
-        const long long i3 = (r % inner) * 8;
-        r /= inner;
-        const long long i2 = r % p.dims[2];
-        r /= p.dims[2];
-        const long long i1 = r % p.dims[1];
-        const long long i0 = r / p.dims[1];
-        *reinterpret_cast<uint4*>(p.dst + i0 * p.ds[0] + i1 * p.ds[1] + i2 * p.ds[2] + i3) =
-            *reinterpret_cast<const uint4*>(p.src + i0 * p.ss[0] + i1 * p.ss[1] + i2 * p.ss[2] + i3);
-    }
+    if (p.count < (1ll << 31))
+        strided_copy_v8<unsigned>(p);
+    else
+        strided_copy_v8<long long>(p);
 }
 
 // NCHW <-> NHWC with pixel (un)shuffle fused, through shared memory.  One
@@ -183,18 +241,36 @@ __device__ __forceinline__ void boundary_vec(const BoundaryParams& p, mlvc_half*
         __syncthreads();
         for (int e = threadIdx.x; e < nx * dcv; e += blockDim.x) {
             const int j = e / dcv, kv = e - (e / dcv) * dcv;
-            uint16_t h[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int k = kv * 8 + i;  // device channel c*R*R + dy*R + dx
-                const int c = k / RR, dy = (k % RR) / R, dx = k % R;
-                h[i] = reinterpret_cast<const uint16_t*>(tile)[(c * R + dy) * kPitch + j * R + dx];
-            }
             uint4 o;
-            o.x = h[0] | (static_cast<uint32_t>(h[1]) << 16);
-            o.y = h[2] | (static_cast<uint32_t>(h[3]) << 16);
-            o.z = h[4] | (static_cast<uint32_t>(h[5]) << 16);
-            o.w = h[6] | (static_cast<uint32_t>(h[7]) << 16);
+            if constexpr (R >= 2) {
+                // device channels kv*8 .. kv*8+7 = 8/R runs of R sub-pixels dx
+                // (c, dy fixed per run), each contiguous in one tile row
+                uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+                for (int q = 0; q < 8 / R; ++q) {
+                    const int k = kv * 8 + q * R;  // device channel c*R*R + dy*R
+                    const int c = k / RR, dy = (k % RR) / R;
+                    const mlvc_half* src = tile + (c * R + dy) * kPitch + j * R;
+                    if constexpr (R == 8) {
+                        o = *reinterpret_cast<const uint4*>(src);
+                    } else if constexpr (R == 4) {
+                        const uint2 v = *reinterpret_cast<const uint2*>(src);
+                        ow[2 * q] = v.x;
+                        ow[2 * q + 1] = v.y;
+                    } else {
+                        ow[q] = *reinterpret_cast<const uint32_t*>(src);
+                    }
+                }
+            } else {
+                uint16_t h[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)  // device channel kv*8+i = host row, column j
+                    h[i] = reinterpret_cast<const uint16_t*>(tile)[(kv * 8 + i) * kPitch + j];
+                o.x = h[0] | (static_cast<uint32_t>(h[1]) << 16);
+                o.y = h[2] | (static_cast<uint32_t>(h[3]) << 16);
+                o.z = h[4] | (static_cast<uint32_t>(h[5]) << 16);
+                o.w = h[6] | (static_cast<uint32_t>(h[7]) << 16);
+            }
             *reinterpret_cast<uint4*>(p.dst + dev_base + static_cast<size_t>(e) * 8) = o;
         }
     } else {
@@ -202,12 +278,25 @@ __device__ __forceinline__ void boundary_vec(const BoundaryParams& p, mlvc_half*
             const int j = e / dcv, kv = e - (e / dcv) * dcv;
             const uint4 v = *reinterpret_cast<const uint4*>(p.src + dev_base + static_cast<size_t>(e) * 8);
             const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+            if constexpr (R >= 2) {
+                // 8/R runs of R sub-pixels, each contiguous in one tile row
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int k = kv * 8 + i;
-                const int c = k / RR, dy = (k % RR) / R, dx = k % R;
-                reinterpret_cast<uint16_t*>(tile)[(c * R + dy) * kPitch + j * R + dx] =
-                    static_cast<uint16_t>(w4[i / 2] >> (16 * (i % 2)));
+                for (int q = 0; q < 8 / R; ++q) {
+                    const int k = kv * 8 + q * R;
+                    const int c = k / RR, dy = (k % RR) / R;
+                    mlvc_half* dst = tile + (c * R + dy) * kPitch + j * R;
+                    if constexpr (R == 8)
+                        *reinterpret_cast<uint4*>(dst) = v;
+                    else if constexpr (R == 4)
+                        *reinterpret_cast<uint2*>(dst) = make_uint2(w4[2 * q], w4[2 * q + 1]);
+                    else
+                        *reinterpret_cast<uint32_t*>(dst) = w4[q];
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    reinterpret_cast<uint16_t*>(tile)[(kv * 8 + i) * kPitch + j] =
+                        static_cast<uint16_t>(w4[i / 2] >> (16 * (i % 2)));
             }
         }
         __syncthreads();
@@ -722,27 +811,27 @@ extern "C" __global__ void mlvc_depth_to_space_f16(const __grid_constant__ Pixel
 // input pixel and 8 output channels (4 x 16-byte loads of 32 input channels,
 // 4 x 16-byte stores, one per output sub-pixel s = dy * 2 + dx, which takes
 // input channels 4 j + s).  `count` = input pixels x output channels / 8.
-extern "C" __global__ void __launch_bounds__(256) mlvc_depth_to_space_r2_v8_f16(const __grid_constant__ PixelShuffleParams p)
+template <typename I>
+__device__ __forceinline__ void depth_to_space_r2_v8(const PixelShuffleParams& p)
 {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int ocv = p.c / 32;  // 8-channel output blocks per pixel
-    const int ow = p.w * 2;
-    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < p.count; i += stride) {
-        const int m = static_cast<int>(i % ocv);
-        const long long px = i / ocv;  // input pixel (n, y, x)
-        const int x = static_cast<int>(px % p.w);
-        const long long ny = px / p.w;  // n * h + y
-        const uint4* src = reinterpret_cast<const uint4*>(p.src + px * p.c + m * 32);
-        uint32_t w[16];
+    const I ocv = p.c / 32;  // 8-channel output blocks per pixel
+    const I w = p.w, ow = w * 2;
+    const I count = static_cast<I>(p.count);
+    const I stride = static_cast<I>(gridDim.x) * blockDim.x;
+    for (I i = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+        const I m = i % ocv;
+        const I px = i / ocv;  // input pixel (n, y, x)
+        const I x = px % w;
+        const I ny = px / w;  // n * h + y
+        const uint4* src = reinterpret_cast<const uint4*>(p.src + static_cast<size_t>(px) * p.c + m * 32);
+        uint32_t wv[16];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const uint4 v = src[q];
-            w[4 * q] = v.x;
-            w[4 * q + 1] = v.y;
-            w[4 * q + 2] = v.z;
-            w[4 * q + 3] = v.w;
+            wv[4 * q] = v.x;
+            wv[4 * q + 1] = v.y;
+            wv[4 * q + 2] = v.z;
+            wv[4 * q + 3] = v.w;
         }
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
@@ -751,11 +840,21 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_depth_to_space_r2_v8_f16(
             uint32_t o[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-                o[k] = __byte_perm(w[4 * k + (s >> 1)], w[4 * k + 2 + (s >> 1)], sel);
-            const long long orow = (ny * 2 + dy) * ow + 2 * x + dx;  // output pixel (n, 2y + dy, 2x + dx)
+                o[k] = __byte_perm(wv[4 * k + (s >> 1)], wv[4 * k + 2 + (s >> 1)], sel);
+            const size_t orow = (static_cast<size_t>(ny) * 2 + dy) * ow + 2 * x + dx;  // output pixel (n, 2y + dy, 2x + dx)
             *reinterpret_cast<uint4*>(p.dst + orow * (p.c / 4) + m * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
+}
+
+extern "C" __global__ void __launch_bounds__(256) mlvc_depth_to_space_r2_v8_f16(const __grid_constant__ PixelShuffleParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    if (p.count < (1ll << 31))
+        depth_to_space_r2_v8<unsigned>(p);
+    else
+        depth_to_space_r2_v8<long long>(p);
 }
 
 // SpaceToDepth with r = 2, input channels a multiple of 8: one thread per

@@ -374,6 +374,21 @@ def test_pixel_shuffle_order(factor):
     bits_equal(got[1], inputs[0])
 
 
+@pytest.mark.parametrize("factor,c", [(2, 2), (2, 6), (4, 2), (8, 3)])
+def test_pixel_shuffle_boundary_vector_paths(factor, c):
+    """Unshuffle at a graph input and shuffle at a graph output with extents
+    that take the boundary kernel's 16-byte paths (device channels and host
+    row spans multiples of 8), a partial 32-pixel band included."""
+    h, w = factor * 3, factor * 40
+    gb = GraphBuilder()
+    x = gb.input("x", [1, c, h, w])
+    u = gb.space_to_depth(x, factor)
+    gb.output(gb.depth_to_space(gb.mul(u, gb.weight("s", _rand((1, c * factor * factor, 1, 1), 4))), factor), "y")
+    inputs = [_rand((1, c, h, w), 6)]
+    got, want, _ = run_both(gb, inputs)
+    bits_equal(got[0], want[0])
+
+
 @pytest.mark.parametrize("c1,c2,oc,epilogue", [(128, 128, 256, "leaky"), (64, 192, 96, None), (256, 256, 256, "residual"),
                                                 (128, 64, 256, "reglu")])
 def test_conv1x1_concat_read_in_place(c1, c2, oc, epilogue):
