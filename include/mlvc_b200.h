@@ -128,6 +128,10 @@ int mlvc_b200_configure_codec_io(mlvc_b200_backend* backend, int width, int heig
 int mlvc_b200_slot_input_yuv(mlvc_b200_backend* backend, size_t slot, uint8_t** y, uint8_t** u, uint8_t** v);
 int mlvc_b200_slot_output_yuv(const mlvc_b200_backend* backend, size_t slot, const uint8_t** y, const uint8_t** u,
                               const uint8_t** v);
+/* Diagnostic (no reference counterpart): *fused = 1 when the slot graphs
+ * convert the decoded frame to YUV420 straight from the NHWC tensor of the x8
+ * output pixel shuffle (the output boundary step is left out of them), else 0. */
+int mlvc_b200_codec_output_fused(const mlvc_b200_backend* backend, int* fused);
 
 /* Entropy-coder inputs on the GPU.  These need a backend from
  * mlvc_b200_create but no loaded graph.

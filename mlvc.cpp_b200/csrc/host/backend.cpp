@@ -2413,7 +2413,7 @@ void Backend::build_schedule()
     }
 }
 
-void Backend::launch_steps(CUstream s)
+void Backend::launch_steps(CUstream s, size_t skip)
 {
     // Kernels are launched with programmatic stream serialisation: each one
     // may start its prologue (barriers, TMEM, weight loads) while its
@@ -2421,7 +2421,10 @@ void Backend::launch_steps(CUstream s)
     // touches activations.  MLVC_B200_PDL=0 turns this off.
     const char* env = std::getenv("MLVC_B200_PDL");
     const bool pdl = !(env && env[0] == '0');
-    for (auto& st : steps_) {
+    for (size_t i = 0; i < steps_.size(); ++i) {
+        if (i == skip)
+            continue;
+        auto& st = steps_[i];
         if (st.type == Step::kCopy) {
             check(cuMemcpyDtoDAsync(st.dst, st.src, st.bytes, s), "cuMemcpyDtoDAsync");
             continue;
@@ -2926,6 +2929,37 @@ void Backend::configure_slots(size_t count)
         yp.pixel_range = codec_.pixel_range;
         return yp;
     };
+    // The decoded frame straight from the NHWC tensor that the x8 output
+    // boundary would convert (mlvc_nhwc8_to_yuv420): the boundary step is left
+    // out of the slot graphs when the frame is not rotated and sits on the
+    // canvas at multiples of 8 (MLVC_B200_YUV_FUSION=0: boundary + conversion).
+    size_t& fused_yuv_step = fused_yuv_step_;
+    fused_yuv_step = static_cast<size_t>(-1);
+    CUdeviceptr fused_yuv_src = 0;
+    {
+        const char* env = std::getenv("MLVC_B200_YUV_FUSION");
+        const bool allowed = !(env && env[0] == '0');
+        if (allowed && codec_.output != kNoCodecTensor && !codec_.rotated && codec_.width % 8 == 0 &&
+            codec_.height % 8 == 0 && codec_.pad_left % 8 == 0 && codec_.pad_top % 8 == 0 &&
+            codec_.pad_left + codec_.width <= codec_.model_width && codec_.pad_top + codec_.height <= codec_.model_height &&
+            output_stage_dev_.at(codec_.output)) {
+            const CUdeviceptr stage = output_stage_dev_[codec_.output].get();
+            for (size_t i = 0; i < steps_.size(); ++i) {
+                const Step& st = steps_[i];
+                if (st.type != Step::kKernel || st.kernel != "mlvc_boundary_f16" ||
+                    st.params.size() != sizeof(BoundaryParams))
+                    continue;
+                BoundaryParams bp;
+                std::memcpy(&bp, st.params.data(), sizeof(bp));
+                if (bp.to_host && bp.r == 8 && bp.c == 192 && bp.n == 1 &&
+                    reinterpret_cast<CUdeviceptr>(bp.dst) == stage && bp.w * 8 == codec_.model_width &&
+                    bp.h * 8 == codec_.model_height && reinterpret_cast<uintptr_t>(bp.src) % 16 == 0) {
+                    fused_yuv_step = i;
+                    fused_yuv_src = reinterpret_cast<CUdeviceptr>(bp.src);
+                }
+            }
+        }
+    }
     for (auto& s : slots_) {
         for (size_t k = 0; k < ext_inputs_.size(); ++k) {
             const auto& d = input_desc(k);
@@ -2958,11 +2992,16 @@ void Backend::configure_slots(size_t count)
                     check(cuMemcpyDtoDAsync(dst, s.din[k].get(), s.in[k].bytes(), stream_), "cuMemcpyDtoDAsync(slot in)");
                 }
             }
-            launch_steps(stream_);
+            launch_steps(stream_, fused_yuv_step);
             for (size_t k = 0; k < ext_outputs_.size(); ++k) {
                 const uint32_t id = graph_.outputs[ext_outputs_[k]];
                 const CUdeviceptr src = output_stage_dev_[k] ? output_stage_dev_[k].get() : values_[id].addr;
-                if (k == codec_.output) {
+                if (k == codec_.output && fused_yuv_src) {
+                    YuvParams yp = yuv_params();
+                    yp.t_in = reinterpret_cast<const mlvc_half*>(fused_yuv_src);
+                    yp.yuv_out = reinterpret_cast<uint8_t*>(s.dout[k].get());
+                    yuv_launch("mlvc_nhwc8_to_yuv420", yp, static_cast<long long>(codec_.width) * codec_.height / 8);
+                } else if (k == codec_.output) {
                     YuvParams yp = yuv_params();
                     yp.t_in = reinterpret_cast<const mlvc_half*>(src);
                     yp.yuv_out = reinterpret_cast<uint8_t*>(s.dout[k].get());

@@ -98,6 +98,7 @@ public:
     // Slot path: pinned host staging per slot, asynchronous submit, wait.
     void configure_slots(size_t count);
     size_t slot_count() const;
+    bool codec_output_fused() const { return fused_yuv_step_ != static_cast<size_t>(-1); }
     void* slot_input(size_t slot, size_t i);
     const void* slot_output(size_t slot, size_t i) const;
     void submit(size_t slot);
@@ -159,7 +160,9 @@ private:
     void build_schedule();
     void capture();
     void check_status();
-    void launch_steps(CUstream s);
+    // Launches every step in order on `s` (skip: index of a step left out, e.g. the
+    // output boundary that the slot path's fused YUV conversion replaces).
+    void launch_steps(CUstream s, size_t skip = static_cast<size_t>(-1));
     CUfunction fn(const char* name);
     CUdeviceptr entropy_scratch(size_t bytes);  // grow-only staging of the host-buffer entropy calls
 
@@ -194,6 +197,7 @@ private:
         bool rotated = false;
         size_t input = kNoCodecTensor, output = kNoCodecTensor;
     } codec_;
+    size_t fused_yuv_step_ = static_cast<size_t>(-1);  // output boundary replaced in the slot graphs
 
     DeviceBuffer weights_dev_, prepped_dev_, arena_dev_, flush_dev_, entropy_scratch_;
     std::vector<DeviceBuffer> input_dev_, input_stage_dev_, output_stage_dev_, state_dev_;

@@ -289,6 +289,15 @@ int mlvc_b200_configure_codec_io(mlvc_b200_backend* backend, int width, int heig
     });
 }
 
+int mlvc_b200_codec_output_fused(const mlvc_b200_backend* backend, int* fused)
+{
+    return guarded([&] {
+        if (!fused)
+            throw std::invalid_argument("mlvc-b200: null output pointer");
+        *fused = require(backend).codec_output_fused() ? 1 : 0;
+    });
+}
+
 int mlvc_b200_slot_input_yuv(mlvc_b200_backend* backend, size_t slot, uint8_t** y, uint8_t** u, uint8_t** v)
 {
     return guarded([&] {

@@ -747,6 +747,68 @@ extern "C" __global__ void __launch_bounds__(256) mlvc_tensor_to_yuv420(const __
     }
 }
 
+// Model output -> YUV420 straight from the NHWC tensor that the output
+// boundary turns into x_hat with an x8 pixel shuffle (3 x 64 channels per
+// 1/8-scale pixel; channel c * 64 + dy * 8 + dx is x_hat[c][8 y + dy][8 x + dx]),
+// so in the codec's slot path x_hat is never written.  Used when the frame is
+// not rotated and its size and position on the canvas are multiples of 8.
+// Every sample takes mlvc_tensor_to_yuv420's arithmetic (FP32 division by
+// pixel_range, the same order of the chroma sums), so the bytes are the same.
+// One thread per 1/8-scale pixel and row dy: 8 luma bytes (one 16-byte load,
+// one 8-byte store) and, for even dy, 4 U and 4 V bytes from rows dy, dy + 1.
+extern "C" __global__ void __launch_bounds__(256) mlvc_nhwc8_to_yuv420(const __grid_constant__ YuvParams p)
+{
+    pdl_launch_dependents();
+    pdl_wait();
+    const int fw8 = p.width / 8, fh8 = p.height / 8, mw8 = p.model_width / 8;
+    const int total = fw8 * fh8 * 8;
+    const int y_count = p.width * p.height, uv_width = p.width / 2, uv_count = y_count / 4;
+    const float pr = p.pixel_range;
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+        const int dy = t & 7, q = t >> 3;
+        const int fy8 = q / fw8, fx8 = q - fy8 * fw8;
+        const mlvc_half* base =
+            p.t_in + (static_cast<size_t>(fy8 + p.pad_top / 8) * mw8 + fx8 + p.pad_left / 8) * 192;
+        {
+            const uint4 v = *reinterpret_cast<const uint4*>(base + dy * 8);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float a, b;
+                unpack_h2(w[k], a, b);
+                const uint32_t pair = quantize_byte(__fdiv_rn(a, pr)) | (quantize_byte(__fdiv_rn(b, pr)) << 8);
+                if (k < 2)
+                    lo |= pair << (16 * k);
+                else
+                    hi |= pair << (16 * (k - 2));
+            }
+            *reinterpret_cast<uint2*>(p.yuv_out + static_cast<size_t>(fy8 * 8 + dy) * p.width + fx8 * 8) =
+                make_uint2(lo, hi);
+        }
+        if (dy & 1)
+            continue;
+#pragma unroll
+        for (int ch = 1; ch <= 2; ++ch) {
+            const uint4 r0 = *reinterpret_cast<const uint4*>(base + ch * 64 + dy * 8);
+            const uint4 r1 = *reinterpret_cast<const uint4*>(base + ch * 64 + dy * 8 + 8);
+            const uint32_t w0[4] = {r0.x, r0.y, r0.z, r0.w}, w1[4] = {r1.x, r1.y, r1.z, r1.w};
+            uint32_t out = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // chroma column 4 fx8 + j: luma columns 2j, 2j + 1
+                float a0, b0, a1, b1;
+                unpack_h2(w0[j], a0, b0);
+                unpack_h2(w1[j], a1, b1);
+                float s = __fadd_rn(__fdiv_rn(a0, pr), __fdiv_rn(b0, pr));
+                s = __fadd_rn(__fadd_rn(s, __fdiv_rn(a1, pr)), __fdiv_rn(b1, pr));
+                out |= static_cast<uint32_t>(quantize_byte(__fmul_rn(s, 0.25f))) << (8 * j);
+            }
+            *reinterpret_cast<uint32_t*>(p.yuv_out + y_count + (ch - 1) * uv_count +
+                                         static_cast<size_t>(fy8 * 4 + dy / 2) * uv_width + fx8 * 4) = out;
+        }
+    }
+}
+
 extern "C" __global__ void __launch_bounds__(256) mlvc_boundary_f16(const __grid_constant__ BoundaryParams p)
 {
     pdl_launch_dependents();

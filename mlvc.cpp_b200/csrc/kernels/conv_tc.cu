@@ -233,22 +233,32 @@ __device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float
                                               const StageSync& ss, uint32_t it, uint8_t* stage, const uint8_t* res,
                                               int panels, int col0, const TileCoord& tc, bool kxk, int quadrant,
                                               int group, int lane, bool leader, volatile int* abort_flag,
-                                              int groups = 2)
+                                              int groups = 2, int trace_at = -1)
 {
+    // trace_at >= 0: the leader stamps the phases of this tile at trace_at + 0..3
+    const bool stamp = leader && trace_at >= 0;
     if (!mbar_wait(acc_full, acc_parity, abort_flag, kErrWaitEpilogue))
         return false;
     tc_fence_after();
+    if (stamp)
+        trace(p, trace_at);
     if (!mbar_wait(ss.ready, it & 1u, abort_flag, kErrWaitEpilogue))
         return false;
+    if (stamp)
+        trace(p, trace_at + 1);
     epilogue_rows(p, bias, tmem_acc + (static_cast<uint32_t>(quadrant * 32) << 16), group, quadrant * 32 + lane, stage,
                   res ? res : stage, groups);
     tc_fence_before();
     mbar_arrive(acc_empty);
     fence_proxy_async_smem();  // staging rows become visible to the TMA store (async proxy)
     mbar_arrive(ss.full);
+    if (stamp)
+        trace(p, trace_at + 2);
     if (leader) {
         if (!mbar_wait(ss.full, it & 1u, abort_flag, kErrWaitEpilogue))
             return false;
+        if (stamp)
+            trace(p, trace_at + 3);
         tile_copy(&p.map_out, false, stage, panels, col0, tc, kxk, nullptr);
         bulk_commit();
     }
@@ -287,7 +297,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
             stage_prepare(p, st, panels, n_tile * out_cols, tc, kxk, p.epilogue == kEpiResidual, ss.ready);
         if (!epilogue_tile(p, sh.bias, sh.tmem_base + acc * p.BN, &sh.tmem_full[acc], acc_phase, &sh.tmem_empty[acc],
                            ss, it, st, nullptr, panels, n_tile * out_cols, tc, kxk, quadrant, group, lane, leader,
-                           &sh.abort_flag)) {
+                           &sh.abort_flag, 2, it < 4 ? kTrConvEpi + 4 * static_cast<int>(it) : -1)) {
             aborted = true;
             break;
         }

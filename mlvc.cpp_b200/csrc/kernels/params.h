@@ -116,7 +116,10 @@ enum TracePoint : int {
     kTrDwMma = 36,
     // 1x1 / k x k conv, the CTA's tiles i < 4: MMA issuer began the tile
     // (accumulator free: kTrConvTile + 4i), committed it (+1), the epilogue
-    // finished it (stores issued, +2)
+    // finished it (stores issued, +2); epilogue leader saw the accumulator
+    // (kTrConvEpi + 4i), the staging buffer ready (+1), wrote its rows (+2),
+    // saw every row written (+3)
+    kTrConvEpi = 24,
     kTrConvTile = 48,
     kTracePoints = 64
 };

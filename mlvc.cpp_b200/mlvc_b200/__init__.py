@@ -77,6 +77,7 @@ EXPORTS = {
     "mlvc_b200_configure_codec_io": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_float, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t],
                                      ctypes.c_int),
+    "mlvc_b200_codec_output_fused": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "mlvc_b200_slot_input_yuv": ([ctypes.c_void_p, ctypes.c_size_t] + [ctypes.POINTER(ctypes.c_void_p)] * 3,
                                  ctypes.c_int),
     "mlvc_b200_slot_output_yuv": ([ctypes.c_void_p, ctypes.c_size_t] + [ctypes.POINTER(ctypes.c_void_p)] * 3,
@@ -305,6 +306,13 @@ class Backend:
         shapes = ((h, w), (h // 2, w // 2), (h // 2, w // 2))
         return tuple(np.frombuffer((ctypes.c_char * n).from_address(q.value), np.uint8).reshape(s)
                      for q, n, s in zip(ptrs, sizes, shapes))
+
+    def codec_output_fused(self):
+        """True when the slot graphs convert the decoded frame to YUV420 straight
+        from the NHWC tensor of the x8 output pixel shuffle."""
+        v = ctypes.c_int()
+        _check(lib().mlvc_b200_codec_output_fused(self._h, ctypes.byref(v)))
+        return bool(v.value)
 
     def slot_input_yuv(self, slot):
         """(Y, U, V) numpy views of the slot's pinned YUV420 input frame."""

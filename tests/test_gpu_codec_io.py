@@ -86,3 +86,49 @@ def test_codec_io_output_only_and_errors():
     (xh,) = GraphOracle(graph, weights).run([x, a])
     got = np.concatenate([p.reshape(-1) for p in be.slot_output_yuv(0)])
     assert np.array_equal(got, yuv_oracle.tensor_to_yuv(xh, 60, 44))
+
+
+def _x8_graph(mw, mh):
+    """x_hat from a 192-channel 1/8-scale tensor through the x8 pixel shuffle,
+    as the MLVC decoders produce it (the output boundary folds the shuffle)."""
+    gb = GraphBuilder()
+    f = gb.input("f", [1, 192, mh // 8, mw // 8])
+    s = gb.weight("s", (np.random.default_rng(3).random((1, 192, 1, 1)) + 0.5).astype(np.float16))
+    gb.output(gb.depth_to_space(gb.mul(f, s), 8), "x_hat")
+    return gb.finish()
+
+
+@pytest.mark.parametrize("w,h,pr,fused", [(64, 48, 1.0, True), (64, 40, 1.0, True), (56, 48, 255.0, True),
+                                          (58, 40, 1.0, False), (40, 64, 1.0, False)])
+def test_codec_output_from_nhwc_x8(w, h, pr, fused, monkeypatch):
+    """The slot path converts the decoded frame to YUV420 straight from the
+    NHWC tensor of the x8 pixel shuffle when the frame is not rotated and its
+    size is a multiple of 8 (58 x 40: width not a multiple of 8; 40 x 64:
+    rotated onto the 64 x 48 canvas, both through the boundary kernel and the
+    NCHW conversion).  Either way the bytes equal the oracle's conversion of
+    the oracle's x_hat, and the fused path equals the unfused one."""
+    mw, mh = 64, 48
+    graph, weights = _x8_graph(mw, mh)
+    rng = np.random.default_rng(w * 3 + h)
+    frames = [(rng.random((1, 192, mh // 8, mw // 8)) * 1.1 * pr - 0.05 * pr).astype(np.float16) for _ in range(3)]
+    oracle = GraphOracle(graph, weights)
+    want = [yuv_oracle.tensor_to_yuv(oracle.run([f])[0], w, h, pr) for f in frames]
+    outs = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("MLVC_B200_YUV_FUSION", mode)
+        be = Backend(0)
+        be.load_memory(graph, weights)
+        be.reset_state()
+        be.configure_codec_io(w, h, mw, mh, pr, slots=1, input_index=None, output_index=0)
+        assert be.codec_output_fused() == (fused and mode == "1")
+        got = []
+        for f in frames:
+            be.slot_input(0, 0)[...] = f
+            be.submit(0)
+            be.wait_slot(0)
+            got.append(np.concatenate([p.reshape(-1) for p in be.slot_output_yuv(0)]).copy())
+        outs[mode] = got
+        be.close()
+    for g1, g0, wnt in zip(outs["1"], outs["0"], want):
+        assert np.array_equal(g1, wnt), np.flatnonzero(g1 != wnt)[:10]
+        assert np.array_equal(g0, wnt)
