@@ -589,6 +589,8 @@ def kernel_roofline(be, workload_name, frame_ms=None):
 # ------------------------------------------- config 5: 8 streams at 1080p
 STREAMS = 8
 GOP = 64
+# frames of different streams in flight on one GPU at a time (--concurrency)
+STREAM_LANES = 2
 STREAMS_WORKLOAD = "mlvc_dec_1080p_8s"
 STREAMS_Q = 21
 STREAMS_DESC = ("BASELINE config 5 on the MLVC-shaped decoder stand-in @1920x1088 (the upstream MLVC architecture is "
@@ -667,21 +669,35 @@ def run_streams_arm(args, rank, world, local_rank):
     s0 = cstreams[0]
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
+    # The local streams run in `lanes` lanes: stream j starts after the L2
+    # flush (j < lanes) or after stream j - lanes finished its frame, so at
+    # most `lanes` frames are in flight on the GPU.  Fewer concurrent frames
+    # keep more of each one's producer -> consumer tensors in the 126 MB L2.
+    lanes = max(1, min(args.concurrency, n_local))
+
+    def chain(j, cs, after_flush, done):
+        if j < lanes:
+            if cs is not s0:
+                cs.wait_event(after_flush)
+        else:
+            cs.wait_event(done[j - lanes])
+
     def step(i):
-        """One frame of every local stream, each on its own CUDA stream, all
-        started after an L2 flush on stream 0 and joined back into it."""
+        """One frame of every local stream, each on its own CUDA stream, in
+        lanes after an L2 flush on stream 0, joined back into stream 0."""
         with torch.cuda.stream(s0):
             flush.fill_(1)
         start = torch.cuda.Event(enable_timing=True)
         start.record(s0)
-        for cs, be in zip(cstreams, backends):
-            if cs is not s0:
-                cs.wait_event(start)
+        done = []
+        for j, (cs, be) in enumerate(zip(cstreams, backends)):
+            chain(j, cs, start, done)
             be.enqueue()
-        for cs in cstreams[1:]:
-            done = torch.cuda.Event()
-            done.record(cs)
-            s0.wait_event(done)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+            done.append(ev)
+        for j in range(max(1, n_local - lanes), n_local):
+            s0.wait_event(done[j])
         end = torch.cuda.Event(enable_timing=True)
         end.record(s0)
         return start, end
@@ -727,15 +743,19 @@ def run_streams_arm(args, rank, world, local_rank):
                 flush.fill_(1)  # cold L2 before every step, inside the timed region
             fl = torch.cuda.Event()
             fl.record(s0)
-            for sid, cs, be in zip(stream_ids, cstreams, backends):
+            done = []
+            for j, (sid, cs, be) in enumerate(zip(stream_ids, cstreams, backends)):
                 if i >= 2:
                     be.wait_slot(slot)
                 if i % GOP == 0 and i > 0:
                     be.reset_state()  # I-frame: a new GOP starts from a zeroed feature
                 for k, a in enumerate(frame_inputs(sid, i)):
                     be.slot_input(slot, k)[...] = a
-                cs.wait_event(fl)
+                chain(j, cs, fl, done)  # the same lanes as the device-timed steps
                 be.submit(slot, shifted_q=STREAMS_Q)
+                ev = torch.cuda.Event()
+                ev.record(cs)
+                done.append(ev)
         for be in backends:
             for slot in range(min(first + n, 2)):
                 be.wait_slot(slot)
@@ -791,7 +811,7 @@ def run_streams_arm(args, rank, world, local_rank):
             "metric": STREAMS_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": STREAMS_DESC, "global_batch": STREAMS, "streams_per_gpu": n_local,
+            "config": {"workload": STREAMS_DESC, "global_batch": STREAMS, "streams_per_gpu": n_local, "concurrent_streams_per_gpu": lanes,
                        "parallelism": f"{STREAMS} independent streams over {world} GPU(s), {n_local} per GPU "
                                       "(no collective)",
                        "step": f"one frame of each of the {n_local} streams on a GPU ({STREAMS} frames per step "
@@ -970,6 +990,8 @@ def main():
                                                    "mlvc_enc_1080p", "mlvc_enc_640", "entropy_1080p",
                                                    STREAMS_WORKLOAD],
                     default=STREAMS_WORKLOAD)
+    ap.add_argument("--concurrency", type=int, default=STREAM_LANES,
+                    help="streams of one GPU decoding at the same time (the others queue behind them)")
     ap.add_argument("--cpu-frames", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
