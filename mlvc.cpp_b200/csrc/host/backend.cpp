@@ -364,6 +364,8 @@ void Backend::plan()
         mb_fusion_ = !(env && env[0] == '0');
         env = std::getenv("MLVC_B200_TAIL_FUSION");
         tail_fusion_ = !(env && env[0] == '0');
+        env = std::getenv("MLVC_B200_D2S_FUSION");
+        d2s_fusion_ = !(env && env[0] == '0');
     }
     const size_t nt = graph_.tensors.size();
     values_.assign(nt, Value{});
@@ -1104,7 +1106,21 @@ void Backend::plan()
                 // stores 64-column panels (ReGLU: 64 output columns = 128 weight rows).
                 const int K = IC, NN = (OC + 63) / 64 * 64;
                 const int k_panels = (K + 63) / 64;
-                const int m_tiles = (IH * IW + 127) / 128;
+                // A 2x pixel shuffle (CRD) that is the only consumer of the conv's
+                // output (after a bias or LeakyReLU epilogue) is folded into the
+                // store: weight rows ordered [sub-pixel][channel], row-aligned
+                // tiles, each 64-column panel stored through a 5-D view of the
+                // shuffled output, so the 4C-channel tensor is never written.
+                uint32_t d2s_out = 0;
+                if (!reglu && epi != kEpiResidual && OC % 256 == 0 && i + consumed < nodes.size() && d2s_fusion_) {
+                    const size_t di = i + consumed;
+                    const NodeDesc& dn = nodes[di];
+                    if (dn.op == Op::kDepthToSpace && dn.block == 2 && dn.inputs[0] == out_id && !absorbed[di] &&
+                        only_consumer(out_id) && !values_[out_id].graph_output && values_[dn.output].nhwc)
+                        d2s_out = dn.output;
+                }
+                const int row_tiles = (IW + 127) / 128;
+                const int m_tiles = d2s_out ? IH * row_tiles : (IH * IW + 127) / 128;
                 // Candidate N tiles divide NN and keep the CTA's weight slice resident.
                 // Every N tile re-reads the activations from L2, and L2 -> SM traffic
                 // paces these GEMMs once four A panels are in flight (a deeper ring
@@ -1169,12 +1185,22 @@ void Backend::plan()
                 }
                 if (best) {
                     const int BN = best, n_tiles = NN / BN;
+                    if (d2s_out) {  // the step now also covers the pixel shuffle
+                        out_id = d2s_out;
+                        consumed += 1;
+                        s.writes = {out_id};
+                        s.info.nodes = std::to_string(i) + "-" + std::to_string(i + consumed - 1);
+                    }
                     std::vector<uint16_t> wp(static_cast<size_t>(NN) * K, 0), bp(NN, 0);
                     for (int r = 0; r < OC; ++r) {
                         int src = r;
                         if (reglu) {  // interleave gate/linear halves per N tile
                             const int t = r / BN, j = r % BN, half = BN / 2, c = OC / 2;
                             src = j < half ? t * half + j : c + t * half + (j - half);
+                        }
+                        if (d2s_out) {  // row sub * C + c <- conv channel c * 4 + sub (CRD order)
+                            const int C = OC / 4;
+                            src = (r % C) * 4 + r / C;
                         }
                         std::memcpy(&wp[static_cast<size_t>(r) * K], w + static_cast<size_t>(src) * K, K * 2);
                         bp[r] = bias_full[src];
@@ -1256,8 +1282,28 @@ void Backend::plan()
                         } else {
                             p.map_a1 = p.map_a0;
                         }
-                        encode_tile_map(&p.map_out, values_[out_id].addr, reglu ? OC / 2 : OC, M, 0, 0,
-                                        "cuTensorMapEncodeTiled(conv1x1 out)");
+                        if (d2s_out) {
+                            // {C, dx, x, dy, y}: the packed [2 IH][2 IW][C] output seen from the input pixels
+                            const cuuint64_t C = static_cast<cuuint64_t>(OC / 4);
+                            const cuuint64_t dims[5] = {C, 2, static_cast<cuuint64_t>(IW), 2, static_cast<cuuint64_t>(IH)};
+                            const cuuint64_t strides[4] = {C * 2, 2 * C * 2, 2 * static_cast<cuuint64_t>(IW) * C * 2,
+                                                           4 * static_cast<cuuint64_t>(IW) * C * 2};
+                            const cuuint32_t box[5] = {64, 1, 128, 1, 1};
+                            const cuuint32_t elem5[5] = {1, 1, 1, 1, 1};
+                            check(cuTensorMapEncodeTiled(&p.map_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                                                         reinterpret_cast<void*>(values_[out_id].addr), dims, strides,
+                                                         box, elem5, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE),
+                                  "cuTensorMapEncodeTiled(conv1x1 out, pixel shuffle)");
+                            p.d2s_c = OC / 4;
+                            p.row_tiles = row_tiles;
+                            p.in_w = IW;
+                            p.in_h = IH;
+                        } else {
+                            encode_tile_map(&p.map_out, values_[out_id].addr, reglu ? OC / 2 : OC, M, 0, 0,
+                                            "cuTensorMapEncodeTiled(conv1x1 out)");
+                        }
                         if (res_id)
                             encode_tile_map(&p.map_res, values_[res_id].addr, OC, M, 0, 0,
                                             "cuTensorMapEncodeTiled(conv1x1 residual)");

@@ -221,6 +221,9 @@ private:
     // Recurrent-feature update chain in one kernel; MLVC_B200_TAIL_FUSION=0
     // runs its operators one by one (same results, for comparison).
     bool tail_fusion_ = true;
+    // A 2x pixel shuffle after a 1x1 conv folded into the conv's store;
+    // MLVC_B200_D2S_FUSION=0 plans it as its own step (same results).
+    bool d2s_fusion_ = true;
     bool keep_all_values_ = false;
 };
 

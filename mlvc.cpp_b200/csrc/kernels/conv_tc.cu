@@ -259,7 +259,18 @@ __device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float
             return false;
         if (stamp)
             trace(p, trace_at + 3);
-        tile_copy(&p.map_out, false, stage, panels, col0, tc, kxk, nullptr);
+        if (p.d2s_c) {
+            // pixel shuffle folded into the store: output column n = sub * C + c
+            // (sub = dy * 2 + dx) of input pixel (x, y) goes to output pixel
+            // (2 x + dx, 2 y + dy), channel c; a 64-column panel never spans two
+            // sub-pixels (C is a multiple of 64)
+            for (int i = 0; i < panels; ++i) {
+                const int n = col0 + 64 * i, sub = n / p.d2s_c;
+                tma_store_5d(&p.map_out, stage + i * 16384, n - sub * p.d2s_c, sub & 1, tc.ox0, sub >> 1, tc.oy);
+            }
+        } else {
+            tile_copy(&p.map_out, false, stage, panels, col0, tc, kxk, nullptr);
+        }
         bulk_commit();
     }
     return true;
@@ -282,15 +293,16 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
     const int out_cols = p.epilogue == kEpiReglu ? p.BN / 2 : p.BN;
     const int panels = out_cols / 64;
     const StageSync ss{&sh.stg_ready, &sh.stg_full};
-    const int tiles_per_row = kxk ? (p.out_w + kBM - 1) / kBM : 1;
+    // row-aligned tiles: k x k convs, and 1x1 convs with a folded pixel shuffle
+    const int tiles_per_row = kxk ? (p.out_w + kBM - 1) / kBM : (p.row_tiles ? p.row_tiles : 1);
     uint32_t acc = 0, acc_phase = 0, it = 0;
     bool aborted = false;
     for (int t = first_tile; t < total_tiles; t += tile_step, ++it) {
         const int m_tile = t / p.n_tiles;
         TileCoord tc;
-        tc.pixel0 = m_tile * kBM;
         tc.oy = m_tile / tiles_per_row;
         tc.ox0 = (m_tile % tiles_per_row) * kBM;
+        tc.pixel0 = p.row_tiles ? tc.oy * p.in_w + tc.ox0 : m_tile * kBM;
         // staging buffer of this tile (two alternate when the host gave two)
         uint8_t* st = stage + (p.stage_bufs == 2 ? static_cast<size_t>(it & 1u) * panels * kTcStagePanelBytes : 0);
         if (leader)
@@ -453,6 +465,9 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
             const int withhold = blockIdx.x == 0 ? p.withhold_a : 0;
             for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {
                 const int m_tile = t / p.n_tiles;
+                // first pixel of the tile (row-aligned tiles: row m_tile / row_tiles)
+                const int pixel0 = p.row_tiles ? (m_tile / p.row_tiles) * p.in_w + (m_tile % p.row_tiles) * kBM
+                                               : m_tile * kBM;
                 for (int kp = 0; kp < k_panels; ++kp) {
                     if (!mbar_wait(&sh->a_empty[stage], phase ^ 1u, &sh->abort_flag, kErrWaitProducer))
                         break;
@@ -461,7 +476,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
                         // K panels past a_split come from the second tensor of a concat
                         const bool second = p.a_split > 0 && kp >= p.a_split;
                         tma_load_2d(a_smem + stage * kAPanelBytes, second ? &p.map_a1 : &p.map_a0,
-                                    &sh->a_full[stage], (second ? kp - p.a_split : kp) * 64, m_tile * kBM);
+                                    &sh->a_full[stage], (second ? kp - p.a_split : kp) * 64, pixel0);
                         a_armed.arm(stage, phase);
                     }
                     if (++stage == p.a_stages) {

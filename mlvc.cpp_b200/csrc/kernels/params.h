@@ -75,6 +75,13 @@ struct ConvTcParams {
     // stage's barrier is never armed -- so the MMA issuer's bounded wait for
     // it runs out and the CTA takes its abort path.  1x1 kernel only.
     int withhold_a;
+    // 1x1 with a pixel shuffle (r = 2) after it, folded into the store: the
+    // tiles are row-aligned (row_tiles per input row of in_w pixels, in_h
+    // rows), weight rows are ordered [sub-pixel dy * 2 + dx][channel], and
+    // map_out is the 5-D view {C, dx, x, dy, y} of the [2 in_h, 2 in_w, C]
+    // output with C = d2s_c.  0 / 0: linear pixel tiles, 2-D output map.
+    int d2s_c;
+    int row_tiles;
 };
 
 // Phase trace points of the tensor-core conv kernels.

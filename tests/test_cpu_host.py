@@ -252,6 +252,8 @@ def test_plan_mlvc_decoder_standin():
     # channel slice is read in place by the 1x1 conv after its concat; the
     # means slice and the latent concat are copies
     assert k.count("mlvc_strided_copy_v8_f16") == 3, k
+    # the four x2 up-sampling pixel shuffles are folded into the 1x1 convs before them
+    assert "mlvc_depth_to_space_r2_v8_f16" not in k and "mlvc_depth_to_space_f16" not in k, k
     assert "mlvc_depthwise3x3_f16" not in k
     assert "mlvc_conv_direct_f16" not in k and "mlvc_unary_f16" not in k and "mlvc_reglu_f16" not in k
     assert [tuple(s) for _, _, s in be.inputs] == [(1, 128, 3, 5), (1, 64, 23, 40), (1, 64, 23, 40),
@@ -611,3 +613,29 @@ def test_plan_clamps_slice_start_like_the_reference(tmp_path):
         assert np.array_equal(ref.view(np.uint16), want.view(np.uint16))
     with pytest.raises(RuntimeError, match="exceeds its input"):
         plan(*_slice_from(6))  # rows 6..9 of 8
+
+
+@pytest.mark.parametrize("fold", [True, False])
+def test_plan_pixel_shuffle_folded_into_1x1(fold, monkeypatch):
+    """A 2x pixel shuffle that is the only consumer of a 1x1 conv (+ LeakyReLU)
+    with channels in multiples of 256 joins the conv's step; not when the conv
+    output has another reader, a residual epilogue, or the switch is off."""
+    if not fold:
+        monkeypatch.setenv("MLVC_B200_D2S_FUSION", "0")
+    rng = np.random.default_rng(0)
+
+    def graph(extra_reader=False, oc=512):
+        gb = GraphBuilder()
+        x = gb.input("x", [1, 64, 6, 10])
+        y = gb.leaky_relu(gb.conv(x, gb.weight("w", (rng.standard_normal((oc, 64, 1, 1)) * 0.1).astype(np.float16))),
+                          0.01)
+        one = gb.weight("one", np.ones((1, 1, 1, 1), np.float16))
+        gb.output(gb.mul(gb.depth_to_space(y, 2), one), "y")  # (a shuffle straight into an output joins the boundary)
+        if extra_reader:
+            gb.output(y, "pre")
+        return gb.finish()
+
+    k = _kernels(plan(*graph()))
+    assert ("mlvc_depth_to_space_r2_v8_f16" in k) == (not fold), k
+    assert "mlvc_depth_to_space_r2_v8_f16" in _kernels(plan(*graph(extra_reader=True)))
+    assert "mlvc_depth_to_space_r2_v8_f16" in _kernels(plan(*graph(oc=384)))  # 96 channels: not a multiple of 64

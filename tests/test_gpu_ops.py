@@ -473,6 +473,35 @@ def test_pixel_shuffle_mid_graph(c, h, w):
     assert ("mlvc_space_to_depth_r2_v8_f16" in kernels) == (c % 8 == 0), kernels
 
 
+@pytest.mark.parametrize("c,h,w,ic,epilogue", [(64, 6, 10, 64, None), (128, 9, 120, 256, "leaky"),
+                                               (64, 5, 240, 128, None), (256, 4, 130, 256, "leaky"),
+                                               (128, 3, 17, 64, "leaky")])
+def test_conv1x1_pixel_shuffle_folded(c, h, w, ic, epilogue, monkeypatch):
+    """1x1 conv (4c outputs, + LeakyReLU) -> DepthToSpace(2): the shuffle is
+    folded into the conv's store (row-aligned tiles, weights in sub-pixel
+    order, 5-D output view), so the 4c-channel tensor is never written.
+    Widths below, at and above the 128-pixel tile (partial last tiles of a
+    row).  Against the oracle, and bit-identical to the two-step plan."""
+    x = lcg_fast(ic * h * w, 11).reshape(1, ic, h, w)
+    wt = lcg_fast(4 * c * ic, 12).reshape(4 * c, ic, 1, 1)
+    b = lcg_fast(4 * c, 13)
+    gb = GraphBuilder()
+    xi = gb.input("x", [1, ic, h, w])
+    y = gb.conv(xi, gb.weight("w", wt), gb.weight("b", b))
+    if epilogue == "leaky":
+        y = gb.leaky_relu(y, 0.01)
+    one = gb.weight("one", np.ones((1, 1, 1, 1), np.float16))
+    gb.output(gb.mul(gb.depth_to_space(y, 2), one), "y")
+    got, want, be = run_both(gb, [x])
+    compare(got[0], want[0])
+    kernels = [s["kernel"] for s in be.steps()]
+    assert "mlvc_depth_to_space_r2_v8_f16" not in kernels and "mlvc_conv1x1_tc" in kernels, kernels
+    monkeypatch.setenv("MLVC_B200_D2S_FUSION", "0")
+    got2, _, be2 = run_both(gb, [x])
+    assert "mlvc_depth_to_space_r2_v8_f16" in [s["kernel"] for s in be2.steps()]
+    bits_equal(got[0], got2[0])
+
+
 def test_reglu_standalone():
     gb = GraphBuilder()
     x = gb.input("x", [1, 48, 5, 7])
