@@ -168,6 +168,7 @@ struct Backend::Value {
 struct Backend::Step {
     enum Type { kKernel, kCopy, kMemset } type = kKernel;
     std::string kernel;
+    std::string symbol;  // cubin entry point when it is a variant of `kernel` (empty: `kernel` itself)
     CUfunction f = nullptr;
     unsigned grid = 1, block = 256, smem = 0;
     unsigned grid_y = 1, grid_z = 1, block_y = 1;
@@ -1188,6 +1189,7 @@ void Backend::plan()
                     if (d2s_out) {  // the step now also covers the pixel shuffle
                         out_id = d2s_out;
                         consumed += 1;
+                        s.symbol = "mlvc_conv1x1_d2s_tc";
                         s.writes = {out_id};
                         s.info.nodes = std::to_string(i) + "-" + std::to_string(i + consumed - 1);
                     }
@@ -2438,8 +2440,10 @@ void Backend::build_schedule()
     // every step that launches it: set it once to the largest request.
     std::map<std::string, unsigned> smem_max;
     for (const auto& st : steps_)
-        if (st.type == Step::kKernel)
-            smem_max[st.kernel] = std::max(smem_max[st.kernel], st.smem);
+        if (st.type == Step::kKernel) {
+            const std::string& sym = st.symbol.empty() ? st.kernel : st.symbol;
+            smem_max[sym] = std::max(smem_max[sym], st.smem);
+        }
     for (const auto& [name, bytes] : smem_max)
         if (bytes > 48 * 1024)
             check(cuFuncSetAttribute(fn(name.c_str()), CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
@@ -2448,7 +2452,7 @@ void Backend::build_schedule()
     step_info_.clear();
     for (auto& st : steps_) {
         if (st.type == Step::kKernel)
-            st.f = fn(st.kernel.c_str());
+            st.f = fn((st.symbol.empty() ? st.kernel : st.symbol).c_str());
         if (st.build)
             st.build(st);
         st.info.kernel = st.kernel;

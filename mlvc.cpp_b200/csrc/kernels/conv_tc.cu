@@ -228,6 +228,9 @@ __device__ __forceinline__ void stage_prepare(const ConvTcParams& p, uint8_t* st
 // buffer, convert, release the accumulator, and let the leader store the tile.
 // `it` counts the CTA's tiles (barrier parities); `groups` warps share each
 // TMEM lane quadrant (column chunks split between them).  Returns false on abort.
+// kShuffle: the 1x1 conv's variant that can store through the folded pixel
+// shuffle (p.d2s_c); the other kernels instantiate the plain store only.
+template <bool kShuffle = false>
 __device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float* bias, uint32_t tmem_acc,
                                               uint64_t* acc_full, uint32_t acc_parity, uint64_t* acc_empty,
                                               const StageSync& ss, uint32_t it, uint8_t* stage, const uint8_t* res,
@@ -259,7 +262,7 @@ __device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float
             return false;
         if (stamp)
             trace(p, trace_at + 3);
-        if (p.d2s_c) {
+        if (kShuffle && p.d2s_c) {
             // pixel shuffle folded into the store: output column n = sub * C + c
             // (sub = dy * 2 + dx) of input pixel (x, y) goes to output pixel
             // (2 x + dx, 2 y + dy), channel c; a 64-column panel never spans two
@@ -276,6 +279,9 @@ __device__ __forceinline__ bool epilogue_tile(const ConvTcParams& p, const float
     return true;
 }
 
+// kShuffle: the 1x1 conv's instantiation with the folded pixel shuffle
+// (row-aligned tiles, p.row_tiles, and the 5-D store of p.d2s_c).
+template <bool kShuffle = false>
 __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& sh, uint8_t* stage, int warp, int lane,
                                               int n_tile, int first_tile, int tile_step, int total_tiles, bool kxk)
 {
@@ -294,7 +300,7 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
     const int panels = out_cols / 64;
     const StageSync ss{&sh.stg_ready, &sh.stg_full};
     // row-aligned tiles: k x k convs, and 1x1 convs with a folded pixel shuffle
-    const int tiles_per_row = kxk ? (p.out_w + kBM - 1) / kBM : (p.row_tiles ? p.row_tiles : 1);
+    const int tiles_per_row = kxk ? (p.out_w + kBM - 1) / kBM : (kShuffle ? p.row_tiles : 1);
     uint32_t acc = 0, acc_phase = 0, it = 0;
     bool aborted = false;
     for (int t = first_tile; t < total_tiles; t += tile_step, ++it) {
@@ -302,14 +308,17 @@ __device__ __forceinline__ void epilogue_role(const ConvTcParams& p, TcShared& s
         TileCoord tc;
         tc.oy = m_tile / tiles_per_row;
         tc.ox0 = (m_tile % tiles_per_row) * kBM;
-        tc.pixel0 = p.row_tiles ? tc.oy * p.in_w + tc.ox0 : m_tile * kBM;
+        tc.pixel0 = kShuffle ? tc.oy * p.in_w + tc.ox0 : m_tile * kBM;
         // staging buffer of this tile (two alternate when the host gave two)
         uint8_t* st = stage + (p.stage_bufs == 2 ? static_cast<size_t>(it & 1u) * panels * kTcStagePanelBytes : 0);
         if (leader)
             stage_prepare(p, st, panels, n_tile * out_cols, tc, kxk, p.epilogue == kEpiResidual, ss.ready);
-        if (!epilogue_tile(p, sh.bias, sh.tmem_base + acc * p.BN, &sh.tmem_full[acc], acc_phase, &sh.tmem_empty[acc],
-                           ss, it, st, nullptr, panels, n_tile * out_cols, tc, kxk, quadrant, group, lane, leader,
-                           &sh.abort_flag, 2, it < 4 ? kTrConvEpi + 4 * static_cast<int>(it) : -1)) {
+        const int trace_at = it < 4 ? kTrConvEpi + 4 * static_cast<int>(it) : -1;
+        const bool tile_ok =
+            epilogue_tile<kShuffle>(p, sh.bias, sh.tmem_base + acc * p.BN, &sh.tmem_full[acc], acc_phase,
+                                    &sh.tmem_empty[acc], ss, it, st, nullptr, panels, n_tile * out_cols, tc, kxk,
+                                    quadrant, group, lane, leader, &sh.abort_flag, 2, trace_at);
+        if (!tile_ok) {
             aborted = true;
             break;
         }
@@ -429,7 +438,8 @@ __device__ __forceinline__ void drain_armed(uint64_t* bars, const ArmedSlots& a,
 }
 
 // ===================================================== 1x1 conv (GEMM)
-extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const __grid_constant__ ConvTcParams p)
+template <bool kShuffle>
+__device__ __forceinline__ void conv1x1_tc(const ConvTcParams& p)
 {
     extern __shared__ __align__(1024) uint8_t smem_dyn[];
     // 1024-byte alignment for the swizzled operand tiles.
@@ -466,7 +476,7 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
             for (int t = first; t < total_tiles && !sh->abort_flag; t += step) {
                 const int m_tile = t / p.n_tiles;
                 // first pixel of the tile (row-aligned tiles: row m_tile / row_tiles)
-                const int pixel0 = p.row_tiles ? (m_tile / p.row_tiles) * p.in_w + (m_tile % p.row_tiles) * kBM
+                const int pixel0 = kShuffle ? (m_tile / p.row_tiles) * p.in_w + (m_tile % p.row_tiles) * kBM
                                                : m_tile * kBM;
                 for (int kp = 0; kp < k_panels; ++kp) {
                     if (!mbar_wait(&sh->a_empty[stage], phase ^ 1u, &sh->abort_flag, kErrWaitProducer))
@@ -547,9 +557,20 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const 
         }
         __syncwarp();
     } else {
-        epilogue_role(p, *sh, stage_smem, warp, lane, n_tile, first, step, total_tiles, false);
+        epilogue_role<kShuffle>(p, *sh, stage_smem, warp, lane, n_tile, first, step, total_tiles, false);
     }
     teardown(p, sh, warp, mma_thread, issued);
+}
+
+extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_tc(const __grid_constant__ ConvTcParams p)
+{
+    conv1x1_tc<false>(p);
+}
+
+// the same GEMM with a 2x pixel shuffle folded into its store (see ConvTcParams::d2s_c)
+extern "C" __global__ void __launch_bounds__(kThreads, 2) mlvc_conv1x1_d2s_tc(const __grid_constant__ ConvTcParams p)
+{
+    conv1x1_tc<true>(p);
 }
 
 // ===================================================== k x k conv
